@@ -1,0 +1,321 @@
+"""numpy front end to ``liboracle.so`` (the C restatement) and, where it was
+built, to the reference-compiled checker libraries in ``oracle/_ref``.
+
+TEST INFRASTRUCTURE ONLY (see ``uk_oracle.h`` for the reference functions
+each routine restates).  Also holds the parity metric used by the tests:
+``rel_err`` below.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+_LIB = None
+_REF = None
+_EMIT = None
+
+f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+I, L64 = C.c_int, C.c_int64
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        path = HERE / "_build" / "liboracle.so"
+        if not path.exists():
+            from . import build
+            build.build_oracle()
+        l = C.CDLL(str(path))
+        sig = {
+            "or_initA": (C.c_float, [I]), "or_initB": (C.c_float, [I]), "or_initW": (C.c_float, [I]),
+            "or_fill_initA": (None, [f32p, L64]), "or_fill_initB": (None, [f32p, L64]),
+            "or_fill_initW": (None, [f32p, L64]),
+            "or_f32_to_f16_n": (None, [f32p, u16p, L64]), "or_f16_to_f32_n": (None, [u16p, f32p, L64]),
+            "or_gemm_f32": (None, [f32p, f32p, f32p, I, I, I, I, I, I]),
+            "or_gemm_f64": (None, [f32p, f32p, f64p, I, I, I, I, I, I]),
+            "or_gemm_f16": (None, [u16p, u16p, f32p, I, I, I, I, I, I]),
+            "or_gemm_f16_f64": (None, [u16p, u16p, f64p, I, I, I, I, I, I]),
+            "or_gemm_f16_dot_f64": (C.c_double, [u16p, u16p, I, I, I, I]),
+            "or_conv_f32": (None, [f32p, f32p, f32p, I, I, I, I, I, I, I]),
+            "or_conv_f64": (None, [f32p, f32p, f64p, I, I, I, I, I, I, I]),
+            "or_conv_nchw_f64": (None, [f32p, f32p, C.c_void_p, f64p] + [I] * 11),
+            "or_conv_nchw_f32": (None, [f32p, f32p, C.c_void_p, f32p] + [I] * 11),
+            "or_reduce_f32": (C.c_float, [f32p, L64]),
+            "or_reduce_blocked_f32": (C.c_float, [f32p, L64, I]),
+            "or_reduce_f64": (C.c_double, [f32p, L64]),
+            "or_row_reduce_f32": (None, [f32p, f32p, L64, L64, I, I]),
+            "or_row_reduce_f64": (None, [f32p, f64p, L64, L64, I]),
+            "or_softmax_f32": (None, [f32p, f32p, L64, L64, I]),
+            "or_softmax_f64": (None, [f32p, f64p, L64, L64, I]),
+            "or_rmsnorm_f32": (None, [f32p, f32p, f32p, L64, L64, C.c_float, I]),
+            "or_rmsnorm_f64": (None, [f32p, f32p, f64p, L64, L64, C.c_double, I]),
+            "or_channelscale_f32": (None, [f32p, f32p, f32p, L64, L64, I]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(l, name)
+            fn.restype, fn.argtypes = res, args
+        _LIB = l
+    return _LIB
+
+
+def ref():
+    """The reference's own sources compiled as a shared library, or None."""
+    global _REF
+    if _REF is None:
+        path = HERE / "_ref" / "libukref.so"
+        if not path.exists():
+            return None
+        l = C.CDLL(str(path))
+        l.ref_cpu_conv.argtypes = [f32p, f32p, f32p] + [I] * 6
+        l.ref_cpu_reduce.restype = C.c_float
+        l.ref_cpu_reduce.argtypes = [f32p, C.c_longlong]
+        l.ref_cpu_reduce_blocked.restype = C.c_float
+        l.ref_cpu_reduce_blocked.argtypes = [f32p, C.c_longlong, I]
+        l.ref_tolerance_for.restype = C.c_double
+        l.ref_tolerance_for.argtypes = [I]
+        for n in ("ref_kml_check", "ref_kml_export", "ref_hcs_check"):
+            getattr(l, n).argtypes = [C.c_char_p, C.c_char_p, I]
+        l.ref_ledger_key.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, I]
+        l.ref_emit_program.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, I]
+        l.ref_workload.argtypes = [C.c_char_p, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]
+        l.ref_solve_tile.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(I), C.POINTER(I)]
+        _REF = l
+    return _REF
+
+
+def emit():
+    """CPU references cut out of the reference's emitted programs, or None."""
+    global _EMIT
+    if _EMIT is None:
+        path = HERE / "_ref" / "libukemit.so"
+        if not path.exists():
+            return None
+        l = C.CDLL(str(path))
+        for n in ("emit_initA", "emit_initB", "emit_initX", "emit_initW", "emit_initS"):
+            getattr(l, n).restype = C.c_float
+            getattr(l, n).argtypes = [I]
+        l.emit_gemm_cpu_ref.argtypes = [f32p, f32p, f32p, I, I, I]
+        l.emit_gemm_f16_cpu_ref.argtypes = [f32p, f32p, f32p, I, I, I]
+        l.emit_conv.argtypes = [f32p, f32p, f32p] + [I] * 6
+        l.emit_reduce.restype = C.c_float
+        l.emit_reduce.argtypes = [f32p, C.c_longlong]
+        l.emit_softmax.argtypes = [f32p, f32p, I, I]
+        l.emit_rmsnorm.argtypes = [f32p, f32p, f32p, I, I]
+        l.emit_channelscale.argtypes = [f32p, f32p, f32p, I, I]
+        _EMIT = l
+    return _EMIT
+
+
+def ref_str(fn, *args, cap=1 << 20):
+    buf = C.create_string_buffer(cap)
+    rc = fn(*[a.encode() if isinstance(a, str) else a for a in args], buf, cap)
+    return rc, buf.value.decode()
+
+
+def nthreads():
+    return os.cpu_count() or 1
+
+
+# ---- numpy wrappers -------------------------------------------------------
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def sawtooth(kind: str, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    getattr(lib(), "or_fill_init" + kind)(out, n)
+    return out
+
+
+def f32_to_f16(x):
+    x = _c(x, np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().or_f32_to_f16_n(x.reshape(-1), out.reshape(-1), x.size)
+    return out
+
+
+def f16_to_f32(h):
+    h = _c(h, np.uint16)
+    out = np.empty(h.shape, np.float32)
+    lib().or_f16_to_f32_n(h.reshape(-1), out.reshape(-1), h.size)
+    return out
+
+
+def gemm_f32(A, B, rows=None, threads=1):
+    A, B = _c(A, np.float32), _c(B, np.float32)
+    M, K = A.shape
+    N = B.shape[1]
+    r0, r1 = rows or (0, M)
+    Cm = np.zeros((M, N), np.float32)
+    lib().or_gemm_f32(A, B, Cm, M, N, K, r0, r1, threads)
+    return Cm
+
+
+def gemm_f64(A, B, rows=None, threads=1):
+    A, B = _c(A, np.float32), _c(B, np.float32)
+    M, K = A.shape
+    N = B.shape[1]
+    r0, r1 = rows or (0, M)
+    Cm = np.zeros((M, N), np.float64)
+    lib().or_gemm_f64(A, B, Cm, M, N, K, r0, r1, threads)
+    return Cm
+
+
+def gemm_f16(Ah, Bh, rows=None, threads=1):
+    Ah, Bh = _c(Ah, np.uint16), _c(Bh, np.uint16)
+    M, K = Ah.shape
+    N = Bh.shape[1]
+    r0, r1 = rows or (0, M)
+    Cm = np.zeros((M, N), np.float32)
+    lib().or_gemm_f16(Ah, Bh, Cm, M, N, K, r0, r1, threads)
+    return Cm
+
+
+def gemm_f16_f64(Ah, Bh, rows=None, threads=1):
+    Ah, Bh = _c(Ah, np.uint16), _c(Bh, np.uint16)
+    M, K = Ah.shape
+    N = Bh.shape[1]
+    r0, r1 = rows or (0, M)
+    Cm = np.zeros((M, N), np.float64)
+    lib().or_gemm_f16_f64(Ah, Bh, Cm, M, N, K, r0, r1, threads)
+    return Cm
+
+
+def gemm_f16_dots_f64(Ah, Bh, ij):
+    """Double-precision dot products C[i, j] for the (i, j) pairs in `ij`."""
+    Ah, Bh = _c(Ah, np.uint16), _c(Bh, np.uint16)
+    K = Ah.shape[1]
+    N = Bh.shape[1]
+    f = lib().or_gemm_f16_dot_f64
+    return np.array([f(Ah, Bh, N, K, int(i), int(j)) for i, j in ij], np.float64)
+
+
+def conv_f32(x, wt, H, W, Cc, Kh, Kw, Oc, threads=1):
+    x, wt = _c(x, np.float32).reshape(-1), _c(wt, np.float32).reshape(-1)
+    y = np.zeros(Oc * (H - Kh + 1) * (W - Kw + 1), np.float32)
+    lib().or_conv_f32(x, wt, y, H, W, Cc, Kh, Kw, Oc, threads)
+    return y
+
+
+def conv_f64(x, wt, H, W, Cc, Kh, Kw, Oc, threads=1):
+    x, wt = _c(x, np.float32).reshape(-1), _c(wt, np.float32).reshape(-1)
+    y = np.zeros(Oc * (H - Kh + 1) * (W - Kw + 1), np.float64)
+    lib().or_conv_f64(x, wt, y, H, W, Cc, Kh, Kw, Oc, threads)
+    return y
+
+
+def conv_nchw(x, w, s, pad, images=None, threads=None, f32=False):
+    """x[N][C][H][W], w[Oc][C][Kh][Kw], optional s[Oc] -> y[N][Oc][Ho][Wo]."""
+    x, w = _c(x, np.float32), _c(w, np.float32)
+    N, Cc, H, W = x.shape
+    Oc, _, Kh, Kw = w.shape
+    Ho, Wo = H + 2 * pad - Kh + 1, W + 2 * pad - Kw + 1
+    n0, n1 = images or (0, N)
+    y = np.zeros((N, Oc, Ho, Wo), np.float32 if f32 else np.float64)
+    sp = None
+    if s is not None:
+        s = _c(s, np.float32)
+        sp = s.ctypes.data
+    fn = lib().or_conv_nchw_f32 if f32 else lib().or_conv_nchw_f64
+    fn(x.reshape(-1), w.reshape(-1), sp, y.reshape(-1), N, Cc, H, W, Oc, Kh, Kw, pad,
+       n0, n1, threads or nthreads())
+    return y
+
+
+def reduce_f32(x):
+    x = _c(x, np.float32).reshape(-1)
+    return lib().or_reduce_f32(x, x.size)
+
+
+def reduce_blocked_f32(x, width=1024):
+    x = _c(x, np.float32).reshape(-1)
+    return lib().or_reduce_blocked_f32(x, x.size, width)
+
+
+def reduce_f64(x):
+    x = _c(x, np.float32).reshape(-1)
+    return lib().or_reduce_f64(x, x.size)
+
+
+def row_reduce_f32(x, width=1024, threads=None):
+    x = _c(x, np.float32)
+    rows, cols = x.shape
+    y = np.zeros(rows, np.float32)
+    lib().or_row_reduce_f32(x, y, rows, cols, width, threads or nthreads())
+    return y
+
+
+def row_reduce_f64(x, threads=None):
+    x = _c(x, np.float32)
+    rows, cols = x.shape
+    y = np.zeros(rows, np.float64)
+    lib().or_row_reduce_f64(x, y, rows, cols, threads or nthreads())
+    return y
+
+
+def softmax_f32(X, threads=None):
+    X = _c(X, np.float32)
+    Y = np.empty_like(X)
+    lib().or_softmax_f32(X, Y, X.shape[0], X.shape[1], threads or nthreads())
+    return Y
+
+
+def softmax_f64(X, threads=None):
+    X = _c(X, np.float32)
+    Y = np.empty(X.shape, np.float64)
+    lib().or_softmax_f64(X, Y, X.shape[0], X.shape[1], threads or nthreads())
+    return Y
+
+
+def rmsnorm_f32(X, W, eps=1e-6, threads=None):
+    X, W = _c(X, np.float32), _c(W, np.float32)
+    Y = np.empty_like(X)
+    lib().or_rmsnorm_f32(X, W, Y, X.shape[0], X.shape[1], eps, threads or nthreads())
+    return Y
+
+
+def rmsnorm_f64(X, W, eps=1e-6, threads=None):
+    X, W = _c(X, np.float32), _c(W, np.float32)
+    Y = np.empty(X.shape, np.float64)
+    lib().or_rmsnorm_f64(X, W, Y, X.shape[0], X.shape[1], float(np.float32(eps)), threads or nthreads())
+    return Y
+
+
+def channelscale_f32(X, S, threads=None):
+    X, S = _c(X, np.float32), _c(S, np.float32)
+    Y = np.empty_like(X)
+    lib().or_channelscale_f32(X, S, Y, X.shape[0], X.shape[1], threads or nthreads())
+    return Y
+
+
+# ---- parity metric ---------------------------------------------------------
+
+def rel_err(got, ref, tau):
+    """max_i |got_i - ref_i| / max(|ref_i|, tau).
+
+    The reference's own verify uses a 1e-6 floor (src/codegen_hip.cpp:1410-1416),
+    which is unbounded for random inputs whose exact results come near zero.
+    Callers pass tau = 1e-3 * RMS(ref) for sums of signed terms (gemm, conv,
+    reduce) and a tiny tau for outputs bounded away from zero or exactly
+    scaled (softmax, rmsnorm, channelscale)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    den = np.maximum(np.abs(ref), tau)
+    return float(np.max(np.abs(got - ref) / den)) if ref.size else 0.0
+
+
+def rms(a):
+    a = np.asarray(a, np.float64)
+    return float(np.sqrt(np.mean(a * a))) if a.size else 0.0
+
+
+def ref_rel(got, ref):
+    """The reference's own per-element metric (floor 1e-6), for transparency."""
+    return rel_err(got, ref, 1e-6)
