@@ -1,0 +1,112 @@
+/*
+ * unikern_cuda.h -- C ABI of libunikern_cuda.so, the B200 (sm_100a) path of
+ * the UNIKERN KML operator set.
+ *
+ * Conventions
+ *   - All tensors are caller-owned DEVICE memory of the current device
+ *     (cudaMalloc'd or equivalent).  Host, managed or another device's memory
+ *     is refused with UK_ERESIDENCY (the reference refuses non-device-resident
+ *     allocations as oversubscription, src/codegen_hip.cpp:209-293).
+ *   - Every call is stream-ordered on `stream` (a cudaStream_t; NULL = the
+ *     legacy default stream) and returns before the kernel finishes.
+ *   - No call allocates or frees memory.  Calls that need scratch memory take
+ *     a caller-provided workspace whose size a *_workspace_size() call gives.
+ *   - Return value: UK_OK (0) or an error code; uk_cuda_last_error() gives
+ *     the text of the last failure on the calling thread.
+ *   - Layouts are the KML contract's "NT" tag: row-major A[M][K], B[K][N],
+ *     C[M][N] (src/codegen.hpp codegen_layout_supported, src/codegen_hip.cpp:72).
+ *   - Reentrant across streams; the library keeps no per-call state except
+ *     the thread-local error text and per-device cached attributes.
+ *
+ * Each entry point replaces the device kernel(s) the reference generates for
+ * the op (file:line within the UNIKERN project).
+ */
+#ifndef UNIKERN_CUDA_H
+#define UNIKERN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UK_OK 0
+#define UK_EVERIFY 1    /* runner level: result outside the tolerance */
+#define UK_EINVAL 2     /* invalid argument (sizes, NULL, alignment) */
+#define UK_ECUDA 4      /* CUDA error, or a refused configuration */
+#define UK_ERESIDENCY 5 /* pointer is not device-resident on this device */
+
+/* text of the last failure on this thread ("" if none) */
+const char* uk_cuda_last_error(void);
+/* ABI version: major * 10000 + minor * 100 + patch */
+int uk_cuda_abi_version(void);
+/* 1 when the current device is an sm_100 part this library can run on */
+int uk_cuda_device_supported(void);
+
+/* ---- channelscale ----------------------------------------------------------
+ * Y[i*C + c] = X[i*C + c] * S[c] for i < L, c < C.  Bit-exact to the reference.
+ * Replaces uk_channelscale (src/codegen_hip.cpp:2329-2335). */
+int uk_cuda_channelscale_f32(const float* X, const float* S, float* Y, int64_t L,
+                             int64_t C, void* stream);
+
+/* ---- reduce ----------------------------------------------------------------
+ * Y[r] = sum_c X[r*cols + c] (fp32) for r < rows.  rows = 1 is the KML
+ * `reduce` op (a length-L vector to one scalar); cols = 0 writes zeros.
+ * Deterministic: the same inputs give the same bits on every call.
+ * Replaces uk_reduce_part + uk_reduce_sum (src/codegen_hip.cpp:818-833) and
+ * the width plan uk_reduce_width_plan (:874-908). */
+size_t uk_cuda_reduce_workspace_size(int64_t rows, int64_t cols);
+int uk_cuda_reduce_f32(const float* X, float* Y, int64_t rows, int64_t cols,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- rmsnorm ---------------------------------------------------------------
+ * Y[l][c] = X[l][c] * (1 / sqrt(sum_c X[l][c]^2 / C + eps)) * W[c].
+ * The reference hard-codes eps = 1e-6 (src/codegen_hip.cpp:2162, :2175);
+ * pass 1e-6f for the KML contract.  Replaces uk_rmsnorm (:2154-2164). */
+int uk_cuda_rmsnorm_f32(const float* X, const float* W, float* Y, int64_t L,
+                        int64_t C, float eps, void* stream);
+
+/* ---- softmax ---------------------------------------------------------------
+ * Y[l][c] = exp(X[l][c] - max_l) / sum_c exp(X[l][c] - max_l).
+ * Replaces uk_softmax (src/codegen_hip.cpp:1985-1996). */
+int uk_cuda_softmax_f32(const float* X, float* Y, int64_t L, int64_t C, void* stream);
+
+/* ---- gemm f32 --------------------------------------------------------------
+ * C = A * B, fp32 FFMA (no TF32), fp32 accumulation.  Any M, N, K >= 0.
+ * Replaces uk_gemm (src/codegen_hip.cpp:1089-1120). */
+int uk_cuda_gemm_f32(const float* A, const float* B, float* C, int M, int N, int K,
+                     void* stream);
+
+/* ---- gemm f16 --------------------------------------------------------------
+ * C(f16) = A(f16) * B(f16) with fp32 accumulation on the tcgen05 tensor
+ * cores; A, B, C are IEEE binary16 bit patterns (uint16_t).  Row-major A[M][K],
+ * B[K][N], C[M][N] with leading dimensions lda >= K, ldb >= N, ldc >= N
+ * (in elements).  The tensor-core path needs K % 8 == 0, N % 8 == 0, the
+ * leading dimensions multiples of 8 and 16-byte aligned pointers; other
+ * shapes run a CUDA-core kernel with the same numerics.
+ * Replaces uk_gemm_h (src/codegen_hip.cpp:1777-1808). */
+int uk_cuda_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, int N,
+                     int K, void* stream);
+int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb,
+                        uint16_t* C, int64_t ldc, int M, int N, int K, void* stream);
+
+/* ---- conv2d ----------------------------------------------------------------
+ * layout UK_CONV_KML: the KML conv contract, one image, valid padding:
+ *   X[H][W][C], Wt[Oc][Kh][Kw][C], Y[Oc][Ho][Wo], Ho = H-Kh+1, Wo = W-Kw+1;
+ *   N must be 1 and pad 0 (src/reference.cpp:6-22, src/codegen_hip.cpp:337-411).
+ * layout UK_CONV_NCHW: X[N][C][H][W], Wt[Oc][C][Kh][Kw], Y[N][Oc][Ho][Wo],
+ *   zero padding `pad`, stride 1, Ho = H+2pad-Kh+1.
+ * scale (may be NULL): per-output-channel factor s[Oc] applied in the
+ * epilogue (the fused channelscale).  fp32 FFMA implicit GEMM. */
+#define UK_CONV_KML 0
+#define UK_CONV_NCHW 1
+int uk_cuda_conv2d_f32(const float* X, const float* Wt, float* Y, int N, int H, int W,
+                       int C, int Kh, int Kw, int Oc, int pad, const float* scale,
+                       int layout, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UNIKERN_CUDA_H */

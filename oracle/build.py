@@ -84,7 +84,25 @@ _EMIT = {
 
 # extern "C" forwarding written here (the cut-out functions take std::vector)
 _WRAPPERS = r'''
+static std::vector<float> g_B;
+static int g_K = 0, g_N = 0;
 extern "C" {
+// timing form: B is held once so that each call computes `rows` full rows of C
+void emit_gemm_set_B(const float* B, int K, int N) {
+  g_B.assign(B, B + (size_t)K * N);
+  g_K = K;
+  g_N = N;
+}
+void emit_gemm_f16_rows(const float* A, float* C, int rows) {
+  std::vector<float> a(A, A + (size_t)rows * g_K), c((size_t)rows * g_N);
+  ns_gemm_f16::cpu_ref(a, g_B, c, rows, g_N, g_K);
+  std::copy(c.begin(), c.end(), C);
+}
+void emit_gemm_rows(const float* A, float* C, int rows) {
+  std::vector<float> a(A, A + (size_t)rows * g_K), c((size_t)rows * g_N);
+  ns_gemm::cpu_ref(a, g_B, c, rows, g_N, g_K);
+  std::copy(c.begin(), c.end(), C);
+}
 float emit_initA(int i) { return ns_gemm::initA(i); }
 float emit_initB(int i) { return ns_gemm::initB(i); }
 float emit_initX(int i) { return ns_softmax::initX(i); }

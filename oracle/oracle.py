@@ -102,6 +102,9 @@ def emit():
             getattr(l, n).argtypes = [I]
         l.emit_gemm_cpu_ref.argtypes = [f32p, f32p, f32p, I, I, I]
         l.emit_gemm_f16_cpu_ref.argtypes = [f32p, f32p, f32p, I, I, I]
+        l.emit_gemm_set_B.argtypes = [f32p, I, I]
+        l.emit_gemm_f16_rows.argtypes = [f32p, f32p, I]
+        l.emit_gemm_rows.argtypes = [f32p, f32p, I]
         l.emit_conv.argtypes = [f32p, f32p, f32p] + [I] * 6
         l.emit_reduce.restype = C.c_float
         l.emit_reduce.argtypes = [f32p, C.c_longlong]

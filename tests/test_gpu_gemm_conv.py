@@ -1,0 +1,124 @@
+"""GPU parity of the GEMMs (f32 FFMA, f16 tensor-core) and the conv through
+the C ABI, against the CPU oracle (oracle/, pinned to the reference)."""
+import numpy as np
+import pytest
+
+import unikern_b200.abi as abi
+from oracle import oracle as O
+from uk_testutil import F16_TOL, F32_TOL, SUM_TAU, dev, empty, host
+
+pytestmark = pytest.mark.gpu
+
+
+def gemm32(A, B):
+    Cm = empty((A.shape[0], B.shape[1]))
+    abi.gemm_f32(dev(A), dev(B), Cm)
+    return host(Cm)
+
+
+def gemm16(Ah, Bh):
+    Cm = empty((Ah.shape[0], Bh.shape[1]), "f16")
+    abi.gemm_f16(dev(Ah), dev(Bh), Cm)
+    return O.f16_to_f32(host(Cm))
+
+
+# ---- f32 ---------------------------------------------------------------------
+
+def test_gemm_f32_reference_verify_instance_exact():
+    # src/codegen_hip.cpp:1030 + :604-605: 256^3 sawtooth, every partial sum exact
+    A = O.sawtooth("A", 256 * 256).reshape(256, 256)
+    B = O.sawtooth("B", 256 * 256).reshape(256, 256)
+    assert np.array_equal(gemm32(A, B), O.gemm_f32(A, B, threads=8))
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (1024, 768, 1000), (33, 47, 29), (1, 1, 1), (130, 1, 257),
+                                   (3, 515, 64), (2048, 2048, 256)])
+def test_gemm_f32_vs_f64(M, N, K):
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    ref = O.gemm_f64(A, B, threads=8)
+    assert O.rel_err(gemm32(A, B), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+
+
+def test_gemm_f32_k0_writes_zeros():
+    Cm = empty((3, 5))
+    Cm.fill_(5.0)
+    abi.gemm_f32(empty((3, 0)), empty((0, 5)), Cm)
+    assert np.array_equal(host(Cm), np.zeros((3, 5), np.float32))
+
+
+# ---- f16 ---------------------------------------------------------------------
+
+def test_gemm_f16_reference_verify_instance():
+    # src/codegen_hip.cpp:1851-1862: sawtooth quantised to half, 256^3
+    A = O.f32_to_f16(O.sawtooth("A", 256 * 256).reshape(256, 256))
+    B = O.f32_to_f16(O.sawtooth("B", 256 * 256).reshape(256, 256))
+    ref32 = O.gemm_f16(A, B, threads=8)
+    got = gemm16(A, B)
+    # the f32 sums are exact, so the only error is the final f16 rounding
+    assert np.array_equal(got, O.f16_to_f32(O.f32_to_f16(ref32)))
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (256, 1024, 768), (1024, 256, 4096), (384, 640, 192),
+                                   (32, 14336, 4096), (1, 4096, 4096), (33, 47, 29), (130, 72, 40)])
+def test_gemm_f16_vs_f64(M, N, K):
+    rng = np.random.default_rng(M + 5 * N + 11 * K)
+    A = O.f32_to_f16(rng.normal(0, 0.02, (M, K)).astype(np.float32) * 25)
+    B = O.f32_to_f16(rng.normal(0, 0.02, (K, N)).astype(np.float32) * 25)
+    ref = O.gemm_f16_f64(A, B, threads=8)
+    assert O.rel_err(gemm16(A, B), ref, SUM_TAU * O.rms(ref)) <= F16_TOL
+
+
+# ---- conv --------------------------------------------------------------------
+
+def test_conv_kml_reference_verify_instance_exact():
+    # src/codegen_hip.cpp:647-654: 32x32x8 input, 3x3, 16 outputs, sawtooth inits
+    H, W, Cc, Kh, Kw, Oc = 32, 32, 8, 3, 3, 16
+    x = O.sawtooth("A", H * W * Cc)
+    w = O.sawtooth("B", Oc * Kh * Kw * Cc)
+    y = empty((Oc * (H - 2) * (W - 2),))
+    abi.conv2d(dev(x), dev(w), y, 1, H, W, Cc, Kh, Kw, Oc, 0, None, abi.UK_CONV_KML)
+    assert np.array_equal(host(y), O.conv_f32(x, w, H, W, Cc, Kh, Kw, Oc))
+
+
+@pytest.mark.parametrize("H,W,Cc,Kh,Kw,Oc", [(58, 58, 32, 3, 3, 64), (9, 7, 3, 2, 3, 5), (16, 16, 5, 1, 1, 130)])
+def test_conv_kml_vs_f64(H, W, Cc, Kh, Kw, Oc):
+    rng = np.random.default_rng(H * W + Cc)
+    x = rng.uniform(0, 1, H * W * Cc).astype(np.float32)
+    w = rng.normal(0, 0.1, Oc * Kh * Kw * Cc).astype(np.float32)
+    y = empty((Oc * (H - Kh + 1) * (W - Kw + 1),))
+    abi.conv2d(dev(x), dev(w), y, 1, H, W, Cc, Kh, Kw, Oc, 0, None, abi.UK_CONV_KML)
+    ref = O.conv_f64(x, w, H, W, Cc, Kh, Kw, Oc, threads=8)
+    assert O.rel_err(host(y), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+
+
+@pytest.mark.parametrize("N,Cc,H,W,Oc,K,pad,scaled", [(2, 16, 13, 13, 24, 3, 1, True), (1, 256, 14, 14, 256, 3, 1, True),
+                                                      (3, 3, 10, 11, 7, 3, 0, False), (2, 8, 9, 9, 16, 1, 0, True),
+                                                      (1, 4, 6, 6, 3, 5, 2, False)])
+def test_conv_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):
+    rng = np.random.default_rng(N * 100 + Cc + H)
+    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / (K * K * Cc)), (Oc, Cc, K, K)).astype(np.float32)
+    s = rng.uniform(0.5, 1.5, Oc).astype(np.float32) if scaled else None
+    Ho, Wo = H + 2 * pad - K + 1, W + 2 * pad - K + 1
+    y = empty((N, Oc, Ho, Wo))
+    abi.conv2d(dev(x), dev(w), y, N, H, W, Cc, K, K, Oc, pad, dev(s) if scaled else None, abi.UK_CONV_NCHW)
+    ref = O.conv_nchw(x, w, s, pad)
+    assert O.rel_err(host(y), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+
+
+def test_conv_nchw_baseline_shape_sampled_images():
+    # the BASELINE configuration (N=32, 256->256, 56x56, 3x3, pad 1, scale):
+    # full-size run on the GPU, two images checked in full against f64
+    N, Cc, H, W, Oc = 32, 256, 56, 56, 256
+    rng = np.random.default_rng(2024)
+    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / (9 * 256)), (Oc, Cc, 3, 3)).astype(np.float32)
+    s = rng.uniform(0.5, 1.5, Oc).astype(np.float32)
+    y = empty((N, Oc, H, W))
+    abi.conv2d(dev(x), dev(w), y, N, H, W, Cc, 3, 3, Oc, 1, dev(s), abi.UK_CONV_NCHW)
+    got = host(y)
+    for n in (0, 31):
+        ref = O.conv_nchw(x[n:n + 1], w, s, 1)
+        assert O.rel_err(got[n:n + 1], ref, SUM_TAU * O.rms(ref)) <= F32_TOL

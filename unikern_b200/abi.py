@@ -1,0 +1,116 @@
+"""ctypes binding of include/unikern_cuda.h (the reference-side binding a
+Python caller would add; the C++ caller links the library directly).
+
+Wrappers take torch CUDA tensors only to obtain device pointers and the
+current stream; every computation happens in libunikern_cuda.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+_LIB = None
+_PATH = Path(__file__).resolve().parent / "_lib" / "libunikern_cuda.so"
+
+vp, i64, i32, f32, sz = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_size_t
+
+# name -> (restype, argtypes); must match include/unikern_cuda.h
+PROTOTYPES = {
+    "uk_cuda_last_error": (C.c_char_p, []),
+    "uk_cuda_abi_version": (i32, []),
+    "uk_cuda_device_supported": (i32, []),
+    "uk_cuda_channelscale_f32": (i32, [vp, vp, vp, i64, i64, vp]),
+    "uk_cuda_reduce_workspace_size": (sz, [i64, i64]),
+    "uk_cuda_reduce_f32": (i32, [vp, vp, i64, i64, vp, sz, vp]),
+    "uk_cuda_rmsnorm_f32": (i32, [vp, vp, vp, i64, i64, f32, vp]),
+    "uk_cuda_softmax_f32": (i32, [vp, vp, i64, i64, vp]),
+    "uk_cuda_gemm_f32": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+    "uk_cuda_gemm_f16": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+    "uk_cuda_gemm_f16_ld": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, i32, vp]),
+    "uk_cuda_conv2d_f32": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp]),
+}
+
+UK_CONV_KML, UK_CONV_NCHW = 0, 1
+
+
+class UkError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__("unikern_cuda error %d: %s" % (code, msg))
+        self.code = code
+
+
+def lib():
+    """Load libunikern_cuda.so (raises if it was not built)."""
+    global _LIB
+    if _LIB is None:
+        if not _PATH.exists():
+            raise ImportError("libunikern_cuda.so not built: run `python -m unikern_b200.build` "
+                              "(there is no CPU fallback)")
+        l = C.CDLL(str(_PATH))
+        for name, (res, args) in PROTOTYPES.items():
+            fn = getattr(l, name)
+            fn.restype, fn.argtypes = res, args
+        _LIB = l
+    return _LIB
+
+
+def check(rc: int):
+    if rc != 0:
+        raise UkError(rc, lib().uk_cuda_last_error().decode())
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+# ---- torch-tensor wrappers (shapes follow the C ABI) -------------------------
+
+def channelscale(X, S, Y, stream=None):
+    L, Cc = X.shape
+    check(lib().uk_cuda_channelscale_f32(_p(X), _p(S), _p(Y), L, Cc, _stream(stream)))
+
+
+def reduce_workspace_size(rows, cols):
+    return lib().uk_cuda_reduce_workspace_size(rows, cols)
+
+
+def reduce(X, Y, workspace=None, stream=None):
+    rows, cols = X.shape
+    ws = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(lib().uk_cuda_reduce_f32(_p(X), _p(Y), rows, cols, _p(workspace), ws, _stream(stream)))
+
+
+def rmsnorm(X, W, Y, eps=1e-6, stream=None):
+    L, Cc = X.shape
+    check(lib().uk_cuda_rmsnorm_f32(_p(X), _p(W), _p(Y), L, Cc, eps, _stream(stream)))
+
+
+def softmax(X, Y, stream=None):
+    L, Cc = X.shape
+    check(lib().uk_cuda_softmax_f32(_p(X), _p(Y), L, Cc, _stream(stream)))
+
+
+def gemm_f32(A, B, Cm, stream=None):
+    M, K = A.shape
+    N = B.shape[1]
+    check(lib().uk_cuda_gemm_f32(_p(A), _p(B), _p(Cm), M, N, K, _stream(stream)))
+
+
+def gemm_f16(A, B, Cm, stream=None):
+    """A, B, C: torch.float16 (or int16/uint16 bit patterns) row-major, any strides
+    with unit inner stride."""
+    M, K = A.shape
+    N = B.shape[1]
+    check(lib().uk_cuda_gemm_f16_ld(_p(A), A.stride(0), _p(B), B.stride(0), _p(Cm), Cm.stride(0),
+                                    M, N, K, _stream(stream)))
+
+
+def conv2d(X, Wt, Y, N, H, W, Cc, Kh, Kw, Oc, pad=0, scale=None, layout=UK_CONV_NCHW, stream=None):
+    check(lib().uk_cuda_conv2d_f32(_p(X), _p(Wt), _p(Y), N, H, W, Cc, Kh, Kw, Oc, pad, _p(scale), layout,
+                                   _stream(stream)))

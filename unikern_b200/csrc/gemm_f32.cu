@@ -1,0 +1,255 @@
+// gemm_f32.cu -- C = A * B in fp32 on the FFMA pipes (no TF32: the f32 KML
+// contract verifies at 1e-4 against an f64 yardstick, which TF32 inputs
+// would not meet).  Replaces uk_gemm (src/codegen_hip.cpp:1089-1120).
+//
+// Register-blocked SIMT GEMM: a CTA computes a BM x BN tile, each thread a
+// TM x TN micro-tile split into 4-wide groups so shared-memory reads are
+// 128-bit; the next K-slab is prefetched into registers while the current
+// one is multiplied, with two shared-memory buffers (one barrier per slab).
+// Each output accumulates k in ascending order with FFMA.
+#include <cuda_fp16.h>
+
+#include "uk_common.cuh"
+
+namespace {
+
+// 4 consecutive elements -> fp32 (VEC: one 16-byte float4 or 8-byte half4 load)
+__device__ __forceinline__ void ld4(float (&d)[4], const float* p) {
+  const float4 t = __ldg(reinterpret_cast<const float4*>(p));
+  d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+}
+__device__ __forceinline__ void ld4(float (&d)[4], const __half* p) {
+  const uint2 t = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&t.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&t.y));
+  d[0] = a.x; d[1] = a.y; d[2] = b.x; d[3] = b.y;
+}
+__device__ __forceinline__ float ld1(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float ld1(const __half* p) { return __half2float(__ldg(p)); }
+__device__ __forceinline__ void st1(float* p, float v) { *p = v; }
+__device__ __forceinline__ void st1(__half* p, float v) { *p = __float2half_rn(v); }
+__device__ __forceinline__ void st4(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void st4(__half* p, const float* v) {
+  __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+  uint2 t;
+  t.x = *reinterpret_cast<uint32_t*>(&a);
+  t.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = t;
+}
+
+template <int BM, int BN, int BK, int TM, int TN, bool VEC>
+struct SgemmCfg {
+  static constexpr int NTX = BN / TN;
+  static constexpr int NTY = BM / TM;
+  static constexpr int NT = NTX * NTY;
+  static constexpr int A_VECS = BM * BK / 4;  // float4 slots of the A slab
+  static constexpr int B_VECS = BK * BN / 4;
+  static constexpr int A_PER = (A_VECS + NT - 1) / NT;
+  static constexpr int B_PER = (B_VECS + NT - 1) / NT;
+  static constexpr int APAD = BM + 4;
+  static_assert(TM % 4 == 0 && TN % 4 == 0, "micro-tile must be 4-aligned");
+  static_assert(BK % 4 == 0, "BK must be a multiple of 4");
+};
+
+template <int BM, int BN, int BK, int TM, int TN, bool VEC, typename T>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+    k_sgemm(const T* __restrict__ A, const T* __restrict__ B, T* __restrict__ C, int M, int N, int K,
+            int64_t lda, int64_t ldb, int64_t ldc) {
+  using Cfg = SgemmCfg<BM, BN, BK, TM, TN, VEC>;
+  constexpr int NT = Cfg::NT, NTX = Cfg::NTX, NTY = Cfg::NTY;
+  __shared__ __align__(16) float As[2][BK][Cfg::APAD];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+
+  const int tid = threadIdx.x;
+  const int tx = tid % NTX, ty = tid / NTX;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+
+  float ra[Cfg::A_PER][4], rb[Cfg::B_PER][4];
+
+  // global -> registers for the slab starting at k0 (zero outside the matrix)
+  auto load_slab = [&](int k0) {
+#pragma unroll
+    for (int p = 0; p < Cfg::A_PER; ++p) {
+      const int i = tid + p * NT;
+      if (i < Cfg::A_VECS) {
+        const int m = i / (BK / 4), kq = (i % (BK / 4)) * 4;
+        const int gm = m0 + m, gk = k0 + kq;
+        if (VEC) {
+          if (gm < M && gk < K) {
+            ld4(ra[p], A + (size_t)gm * lda + gk);
+          } else {
+            ra[p][0] = ra[p][1] = ra[p][2] = ra[p][3] = 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            ra[p][j] = (gm < M && gk + j < K) ? ld1(A + (size_t)gm * lda + gk + j) : 0.f;
+        }
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < Cfg::B_PER; ++p) {
+      const int i = tid + p * NT;
+      if (i < Cfg::B_VECS) {
+        const int k = i / (BN / 4), nq = (i % (BN / 4)) * 4;
+        const int gk = k0 + k, gn = n0 + nq;
+        if (VEC) {
+          if (gk < K && gn < N) {
+            ld4(rb[p], B + (size_t)gk * ldb + gn);
+          } else {
+            rb[p][0] = rb[p][1] = rb[p][2] = rb[p][3] = 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            rb[p][j] = (gk < K && gn + j < N) ? ld1(B + (size_t)gk * ldb + gn + j) : 0.f;
+        }
+      }
+    }
+  };
+  auto store_slab = [&](int buf) {
+#pragma unroll
+    for (int p = 0; p < Cfg::A_PER; ++p) {
+      const int i = tid + p * NT;
+      if (i < Cfg::A_VECS) {
+        const int m = i / (BK / 4), kq = (i % (BK / 4)) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) As[buf][kq + j][m] = ra[p][j];
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < Cfg::B_PER; ++p) {
+      const int i = tid + p * NT;
+      if (i < Cfg::B_VECS) {
+        const int k = i / (BN / 4), nq = (i % (BN / 4)) * 4;
+        *reinterpret_cast<float4*>(&Bs[buf][k][nq]) = make_float4(rb[p][0], rb[p][1], rb[p][2], rb[p][3]);
+      }
+    }
+  };
+
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+
+  const int nslab = (K + BK - 1) / BK;
+  if (nslab > 0) {
+    load_slab(0);
+    store_slab(0);
+  }
+  __syncthreads();
+  for (int s = 0; s < nslab; ++s) {
+    const int buf = s & 1;
+    if (s + 1 < nslab) load_slab((s + 1) * BK);
+#pragma unroll
+    for (int k = 0; k < BK; ++k) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int g = 0; g < TM / 4; ++g) {
+        const float4 t = *reinterpret_cast<const float4*>(&As[buf][k][g * NTY * 4 + ty * 4]);
+        a[g * 4 + 0] = t.x; a[g * 4 + 1] = t.y; a[g * 4 + 2] = t.z; a[g * 4 + 3] = t.w;
+      }
+#pragma unroll
+      for (int g = 0; g < TN / 4; ++g) {
+        const float4 t = *reinterpret_cast<const float4*>(&Bs[buf][k][g * NTX * 4 + tx * 4]);
+        b[g * 4 + 0] = t.x; b[g * 4 + 1] = t.y; b[g * 4 + 2] = t.z; b[g * 4 + 3] = t.w;
+      }
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (s + 1 < nslab) store_slab(buf ^ 1);
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int gi = 0; gi < TM / 4; ++gi)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int gm = m0 + gi * NTY * 4 + ty * 4 + i;
+      if (gm >= M) continue;
+#pragma unroll
+      for (int gj = 0; gj < TN / 4; ++gj) {
+        const int gn = n0 + gj * NTX * 4 + tx * 4;
+        T* c = C + (size_t)gm * ldc + gn;
+        const float* v = &acc[gi * 4 + i][gj * 4];
+        if (VEC && gn + 3 < N) {
+          st4(c, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (gn + j < N) st1(c + j, v[j]);
+        }
+      }
+    }
+}
+
+template <int BM, int BN, int BK, int TM, int TN, typename T>
+void launch(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
+            cudaStream_t st) {
+  constexpr int NT = (BM / TM) * (BN / TN);
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  if (vec) k_sgemm<BM, BN, BK, TM, TN, true, T><<<grid, NT, 0, st>>>(A, B, C, M, N, K, lda, ldb, ldc);
+  else k_sgemm<BM, BN, BK, TM, TN, false, T><<<grid, NT, 0, st>>>(A, B, C, M, N, K, lda, ldb, ldc);
+}
+
+template <typename T>
+__global__ void k_zero2d(T* C, int M, int N, int64_t ldc) {
+  const int64_t n = (int64_t)M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    st1(C + (i / N) * ldc + i % N, 0.f);
+}
+
+// tile choice: the largest tile that still gives every SM a CTA; small
+// problems fall to smaller tiles (512^3: 128 CTAs of 32x64)
+template <typename T>
+void simt_gemm(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
+               cudaStream_t st) {
+  const int64_t sms = uk::sm_count();
+  auto ctas = [&](int bm, int bn) { return (int64_t)((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
+  if (ctas(128, 128) >= sms)
+    launch<128, 128, 8, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  else if (ctas(64, 64) >= sms)
+    launch<64, 64, 8, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  else
+    launch<32, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+}
+
+}  // namespace
+
+namespace uk {
+// CUDA-core f16 GEMM (f16 in, fp32 FFMA accumulation, f16 out): the path for
+// shapes the tensor-core kernel does not take.
+int gemm_f16_simt(const __half* A, int64_t lda, const __half* B, int64_t ldb, __half* C, int64_t ldc, int M, int N,
+                  int K, cudaStream_t st) {
+  if (K == 0) {
+    k_zero2d<__half><<<1024, 256, 0, st>>>(C, M, N, ldc);
+    return check_launch("gemm_f16(zero)");
+  }
+  const bool vec = K % 4 == 0 && N % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 && ldc % 4 == 0 &&
+                   ((uintptr_t)A & 7) == 0 && ((uintptr_t)B & 7) == 0 && ((uintptr_t)C & 7) == 0;
+  simt_gemm<__half>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  return check_launch("gemm_f16(simt)");
+}
+}  // namespace uk
+
+extern "C" int uk_cuda_gemm_f32(const float* A, const float* B, float* C, int M, int N, int K, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return uk::fail(UK_EINVAL, "gemm_f32: negative dims %d %d %d", M, N, K);
+  if (M == 0 || N == 0) return UK_OK;
+  if (int rc = uk::check_device_ptr(C, "C")) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (K == 0) {
+    k_zero2d<float><<<1024, 256, 0, st>>>(C, M, N, N);
+    return uk::check_launch("gemm_f32(zero)");
+  }
+  if (int rc = uk::check_device_ptr(A, "A")) return rc;
+  if (int rc = uk::check_device_ptr(B, "B")) return rc;
+  if ((M + 31) / 32 > 65535) return uk::fail(UK_EINVAL, "gemm_f32: M=%d exceeds the grid limit", M);
+  const bool vec = K % 4 == 0 && N % 4 == 0 && uk::aligned16(A) && uk::aligned16(B) && uk::aligned16(C);
+  simt_gemm<float>(A, B, C, M, N, K, K, N, N, vec, st);
+  return uk::check_launch("gemm_f32");
+}
