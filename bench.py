@@ -447,13 +447,39 @@ def run_reference(args, world, rank):
     return 0
 
 
+def run_single(args, ctx, pk):
+    """One op alone at its BASELINE size (used for per-op numbers and profiling)."""
+    op = args.op
+    if op in ("reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar"):
+        r = bench_rowop(ctx, op, args.steps, args.warmup)
+        val, unit, bound = r["value"], "GB/s", "hbm"
+    elif op == "conv":
+        r = bench_conv(ctx, args.steps, args.warmup)
+        val, unit, bound = r["value"], "TFLOP/s", "fp32"
+    elif op == "gemm_f32":
+        r = bench_gemm_f32(ctx, args.steps, args.warmup)
+        val, unit, bound = r["value"], "TFLOP/s", "fp32"
+    else:
+        r = bench_decode(ctx, args.steps, args.warmup)
+        val, unit, bound = r["value"], "GB/s", "hbm"
+    if ctx.rank == 0:
+        print(json.dumps({"metric": METRIC, "op": op, "value": round(val, 3), "unit": unit, "n_gpus": ctx.world,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 5),
+                          "higher_is_better": True, "roofline": roofline(bound, val, pk)}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="all", choices=["all", "gemm_f16"])
+    ap.add_argument("--op", default="all",
+                    choices=["all", "gemm_f16", "reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar",
+                             "conv", "gemm_f32", "decode"],
+                    help="all = headline f16 GEMM + every other op; otherwise one op alone (profiling)")
+    ap.add_argument("--gemm-shape", default="8192,8192,8192", help="M,N,K of the f16 GEMM")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -476,9 +502,12 @@ def main():
     ctx = Ctx(world, rank, local_rank)
     pk = peaks()
 
+    if args.op not in ("all", "gemm_f16"):
+        return run_single(args, ctx, pk)
+    M, N, K = (int(v) for v in args.gemm_shape.split(","))
     sampler = ClockSampler(local_rank)
     sampler.start()
-    g = bench_gemm_f16(ctx, args.steps, args.warmup)
+    g = bench_gemm_f16(ctx, args.steps, args.warmup, M, N, K)
     clocks = sampler.stop()
 
     ops = {}
@@ -489,11 +518,11 @@ def main():
             ops[op] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
                        "roofline": roofline("hbm", r["value"], pk, traffic_for("rowop_" + op))}
         r = bench_conv(Ctx(1, 0, local_rank), max(3, s // 4), 3)
-        ops["conv_n32_256_56_3x3_pad1_scaled"] = {"TFLOP/s": round(r["value"] / 1e3, 2), "ms": round(r["ms"], 4),
-                                                 "roofline": roofline("fp32", r["value"] / 1e3, pk)}
+        ops["conv_n32_256_56_3x3_pad1_scaled"] = {"TFLOP/s": round(r["value"], 2), "ms": round(r["ms"], 4),
+                                                 "roofline": roofline("fp32", r["value"], pk)}
         r = bench_gemm_f32(Ctx(1, 0, local_rank), s, 3)
-        ops["gemm_f32_512"] = {"TFLOP/s": round(r["value"] / 1e3, 3), "ms": round(r["ms"], 5),
-                               "roofline": roofline("fp32", r["value"] / 1e3, pk)}
+        ops["gemm_f32_512"] = {"TFLOP/s": round(r["value"], 3), "ms": round(r["ms"], 5),
+                               "roofline": roofline("fp32", r["value"], pk)}
         r = bench_decode(Ctx(1, 0, local_rank), s, 3)
         ops["decode_chain_b32"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
                                    "roofline": roofline("hbm", r["value"], pk)}
@@ -501,19 +530,19 @@ def main():
             for op in ("reduce", "rmsnorm", "softmax"):
                 ops[op]["cpu_baseline"] = {k: v for k, v in cpu_rowop(op, 8192, 16384).items() if k != "seconds"}
 
-    tflops = g["value"] / 1e3
+    tflops = g["value"]
     line = {"metric": METRIC, "value": round(tflops, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(g["ms"], 5), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,0.02) fp16 on device)",
-            "config": {"workload": "f16 GEMM C=A*B, f32 accumulation, f16 out, M=N=K=8192 row-major "
-                                   "(BASELINE configs[3])", "M": 8192, "N": 8192, "K": 8192,
+            "config": {"workload": "f16 GEMM C=A*B, f32 accumulation, f16 out, M=%d N=%d K=%d row-major "
+                                   "(BASELINE configs[3])" % (M, N, K), "M": M, "N": N, "K": K,
                        "parallelism": g["parallelism"], "l2": "inputs (256 MiB) larger than L2"},
             "roofline": roofline("tensor", tflops, pk, traffic_for("gemm_f16_8192")),
             "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in g["e2e"].items()},
             "gpu_launches": g["launches"], "clocks": clocks}
-    line["e2e"]["value"] = round(g["e2e"]["value"] / 1e3, 3)
+    line["e2e"]["value"] = round(g["e2e"]["value"], 3)
     if rank == 0 and not args.no_cpu:
-        cb = cpu_gemm_f16(8192, 8192, 8192)
+        cb = cpu_gemm_f16(M, N, K)
         line["cpu_baseline"] = {k: (round(v, 6) if isinstance(v, float) else v) for k, v in cb.items()
                                 if k != "seconds"}
     if ops:

@@ -91,6 +91,14 @@ int uk_cuda_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, i
 int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb,
                         uint16_t* C, int64_t ldc, int M, int N, int K, void* stream);
 
+/* Fault word of the tensor-core pipelines: 0 when no bounded wait inside a
+ * kernel of this library expired since the last call, otherwise a bit mask
+ * (1 producer, 2 MMA issuer, 4 epilogue, 8 teardown, 16 self-test, 32 peer
+ * wait).  Synchronises with the device and clears the word.  A kernel whose
+ * wait expires unwinds and leaves its outputs undefined instead of hanging.
+ * No reference counterpart (the reference has no device-side waits). */
+unsigned uk_cuda_pipeline_fault(void);
+
 /* ---- conv2d ----------------------------------------------------------------
  * layout UK_CONV_KML: the KML conv contract, one image, valid padding:
  *   X[H][W][C], Wt[Oc][Kh][Kw][C], Y[Oc][Ho][Wo], Ho = H-Kh+1, Wo = W-Kw+1;

@@ -38,7 +38,10 @@ def test_gemm_f32_vs_f64(M, N, K):
     A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
     B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
     ref = O.gemm_f64(A, B, threads=8)
-    assert O.rel_err(gemm32(A, B), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+    tau = SUM_TAU * O.rms(ref)
+    assert O.rel_err(gemm32(A, B), ref, tau) <= F32_TOL
+    # the gate is one the reference's own fp32 loop passes
+    assert O.rel_err(O.gemm_f32(A, B, threads=8), ref, tau) <= F32_TOL
 
 
 def test_gemm_f32_k0_writes_zeros():

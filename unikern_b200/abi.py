@@ -28,6 +28,7 @@ PROTOTYPES = {
     "uk_cuda_gemm_f16": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "uk_cuda_gemm_f16_ld": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, i32, vp]),
     "uk_cuda_conv2d_f32": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp]),
+    "uk_cuda_pipeline_fault": (C.c_uint, []),
 }
 
 UK_CONV_KML, UK_CONV_NCHW = 0, 1

@@ -1,13 +1,321 @@
-// gemm_f16.cu -- C(f16) = A(f16) * B(f16), fp32 accumulation.
-// Replaces uk_gemm_h (src/codegen_hip.cpp:1777-1808).
+// gemm_f16.cu -- C(f16) = A(f16) * B(f16) with fp32 accumulation on the
+// 5th-generation tensor cores (tcgen05, accumulators in TMEM, operands staged
+// by TMA).  Replaces uk_gemm_h (src/codegen_hip.cpp:1777-1808), which ran the
+// product on SIMT FMA from fp32 copies in shared memory.
+//
+// Kernel structure (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: per 64-wide K block, one 128x64 box of A
+//               (K-major) and four 64x64 boxes of B (row-major B is the
+//               MN-major operand), 128-byte swizzle, into a 4-stage ring
+//   warp 1      TMEM owner (alloc/dealloc 512 columns) and MMA issuer: one
+//               thread issues tcgen05.mma M=128 N=256 K=16 (4 per K block)
+//               into one of two 256-column fp32 accumulators
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, convert to f16
+//               (round to nearest even), 16-byte stores; with the second
+//               accumulator the epilogue of tile i overlaps the MMAs of i+1
+// The epilogue can also write each tile to up to 7 more buffers (other GPUs'
+// copies of C reached over NVLink): that is the all-gather of the N-sharded
+// multi-GPU GEMM, fused into the store.
+// Tiles are visited in groups of 16 M-blocks so the A and B panels a wave of
+// 148 CTAs touches stay in L2.
+//
+// Every mbarrier wait is bounded (uk_mbar_wait); a timeout sets the fault word
+// read by uk_cuda_pipeline_fault() and the CTA unwinds.  No TMA multicast.
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>
 
+#include <mutex>
+
+#include "sm100_ptx.cuh"
 #include "uk_common.cuh"
 
 namespace uk {
+// device fault word of this translation unit (no relocatable device code, so
+// each TU that runs bounded waits owns one); read by uk_cuda_pipeline_fault
+__device__ unsigned int g_fault_word = 0;
 int gemm_f16_simt(const __half* A, int64_t lda, const __half* B, int64_t ldb, __half* C, int64_t ldc, int M, int N,
                   int K, cudaStream_t st);
+}  // namespace uk
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;      // 16 KiB
+constexpr int B_BOX_BYTES = BK * 64 * 2;  // 8 KiB: 64 K rows x 64 N columns
+constexpr int B_BYTES = BK * BN * 2;      // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 16;
+constexpr int MAX_OUT = 8;
+constexpr uint32_t IDESC = uk_idesc_f16(BM, BN, /*B MN-major*/ 1);
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait
+
+struct OutList {
+  uint16_t* c[MAX_OUT];  // c[0]: this GPU's C; c[1..]: peers' C (same layout)
+  int n;
+};
+
+struct SmemCtl {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t teardown;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + sizeof(SmemCtl) + 1024;
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = GROUP_M * num_n;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int r = t - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
 }
+
+__device__ __forceinline__ void raise_fault(SmemCtl* ctl, unsigned bit) {
+  atomicOr(&uk::g_fault_word, bit);
+  ctl->abort = 1;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    k_gemm_f16_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, OutList out,
+                  int M, int N, int K, int64_t ldc) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  SmemCtl* ctl = (SmemCtl*)(smem + (size_t)STAGES * STAGE_BYTES);
+  volatile int* abort = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      uk_mbar_init(&ctl->full[s], 1);
+      uk_mbar_init(&ctl->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      uk_mbar_init(&ctl->tfull[b], 1);
+      uk_mbar_init(&ctl->tempty[b], 4);
+    }
+    uk_mbar_init(&ctl->teardown, 1);
+    ctl->abort = 0;
+    uk_fence_mbar_init();
+    uk_tma_prefetch_desc(&tmA);
+    uk_tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    uk_tmem_alloc(&ctl->tmem_base, TMEM_COLS);
+    uk_tmem_relinquish();
+  }
+  uk_tc_fence_before();
+  __syncthreads();
+  uk_tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!uk_mbar_wait(&ctl->empty[s], ph ^ 1u, abort, WAIT_NS)) {
+            raise_fault(ctl, UK_FAULT_PRODUCER);
+            break;
+          }
+          uint8_t* sa = smem + (size_t)s * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          uk_mbar_expect_tx(&ctl->full[s], STAGE_BYTES);
+          uk_tma_load_2d(sa, &tmA, &ctl->full[s], kb * BK, mb * BM);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            uk_tma_load_2d(sb + j * B_BOX_BYTES, &tmB, &ctl->full[s], nb * BN + j * 64, kb * BK);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, tl = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x, ++tl) {
+        const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
+        if (!uk_mbar_wait(&ctl->tempty[buf], tph ^ 1u, abort, WAIT_NS)) {
+          raise_fault(ctl, UK_FAULT_MMA);
+          break;
+        }
+        uk_tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!uk_mbar_wait(&ctl->full[s], ph, abort, WAIT_NS)) {
+            raise_fault(ctl, UK_FAULT_MMA);
+            ok = false;
+            break;
+          }
+          uk_tc_fence_after();
+          const uint32_t sa = uk_smem_u32(smem + (size_t)s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // A: K-major, +32 bytes per 16 K inside the 128-byte swizzle atom
+            const uint64_t ad = uk_desc_sw128(sa + k * 32, 16, 1024);
+            // B: MN-major, 64-column chunks 8 KiB apart (LBO), 8-row K groups
+            // 1 KiB apart (SBO), +16 rows (2 KiB) per 16 K
+            const uint64_t bd = uk_desc_sw128(sb + k * 2048, B_BOX_BYTES, 1024);
+            uk_umma_f16(d, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          uk_umma_commit(&ctl->empty[s]);  // frees the stage when these MMAs finish
+        }
+        if (!ok) break;
+        uk_umma_commit(&ctl->tfull[buf]);  // accumulator ready for the epilogue
+      }
+      // all MMAs issued by this thread complete before TMEM is released
+      uk_umma_commit(&ctl->teardown);
+      if (!uk_mbar_wait(&ctl->teardown, 0, nullptr, WAIT_NS)) atomicOr(&uk::g_fault_word, UK_FAULT_TEARDOWN);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+    uint32_t tl = 0;
+    for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x, ++tl) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
+      if (!uk_mbar_wait(&ctl->tfull[buf], tph, abort, WAIT_NS)) {
+        raise_fault(ctl, UK_FAULT_EPILOGUE);
+        break;
+      }
+      uk_tc_fence_after();
+      const int gm = mb * BM + row;
+      const int n0 = nb * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        uk_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, v);
+        uk_tmem_ld_wait();
+        if (gm < M) {
+          uint4 pk[4];
+          uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            __half2 h = __floats2half2_rn(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            pw[i] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          const int gn = n0 + c * 32;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (gn + j * 8 < N) {
+              const size_t off = (size_t)gm * ldc + gn + j * 8;
+              for (int o = 0; o < out.n; ++o) *reinterpret_cast<uint4*>(out.c[o] + off) = pk[j];
+            }
+          }
+        }
+      }
+      uk_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) uk_mbar_arrive(&ctl->tempty[buf]);
+    }
+  }
+
+  uk_tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    uk_tc_fence_after();
+    uk_tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---- host side ----------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// 2-D f16 tensor map: `inner` contiguous elements per row, `outer` rows,
+// `ld` elements between rows; box = box_inner x box_outer, 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+             uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return uk::fail(UK_ECUDA, "gemm_f16: cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return uk::fail(UK_ECUDA, "gemm_f16: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return UK_OK;
+}
+
+bool tc_shape_ok(const void* A, int64_t lda, const void* B, int64_t ldb, const void* const* Cs, int nc, int64_t ldc,
+                 int N, int K) {
+  if (K % 8 != 0 || N % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0 || ldc % 8 != 0) return false;
+  if (!uk::aligned16(A) || !uk::aligned16(B)) return false;
+  for (int i = 0; i < nc; ++i)
+    if (!uk::aligned16(Cs[i])) return false;
+  return K > 0;
+}
+
+}  // namespace
+
+namespace uk {
+
+// C[0..nc) all receive the product; used directly by the multi-GPU path with
+// peer pointers (C[0] local).  Shapes must satisfy tc_shape_ok.
+int gemm_f16_tc(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, uint16_t* const* Cs, int nc,
+                int64_t ldc, int M, int N, int K, cudaStream_t st) {
+  if (nc < 1 || nc > MAX_OUT) return fail(UK_EINVAL, "gemm_f16: 1..%d outputs, got %d", MAX_OUT, nc);
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM)) return rc;
+  if (int rc = make_map(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK)) return rc;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_f16_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    if (e != cudaSuccess) return fail(UK_ECUDA, "gemm_f16: smem attribute: %s", cudaGetErrorString(e));
+    attr_done[dev] = true;
+  }
+  OutList out{};
+  for (int i = 0; i < nc; ++i) out.c[i] = Cs[i];
+  out.n = nc;
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  k_gemm_f16_tc<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, M, N, K, ldc);
+  return check_launch("gemm_f16(tcgen05)");
+}
+
+bool gemm_f16_tc_ok(const void* A, int64_t lda, const void* B, int64_t ldb, const void* const* Cs, int nc,
+                    int64_t ldc, int N, int K) {
+  return tc_shape_ok(A, lda, B, ldb, Cs, nc, ldc, N, K);
+}
+
+}  // namespace uk
 
 extern "C" int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, uint16_t* C,
                                    int64_t ldc, int M, int N, int K, void* stream) {
@@ -21,12 +329,25 @@ extern "C" int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_
     if (int rc = uk::check_device_ptr(A, "A")) return rc;
     if (int rc = uk::check_device_ptr(B, "B")) return rc;
   }
-  if ((M + 31) / 32 > 65535) return uk::fail(UK_EINVAL, "gemm_f16: M=%d exceeds the grid limit", M);
   cudaStream_t st = (cudaStream_t)stream;
+  const void* cs[1] = {C};
+  if (uk::gemm_f16_tc_ok(A, lda, B, ldb, cs, 1, ldc, N, K)) {
+    uint16_t* outs[1] = {C};
+    return uk::gemm_f16_tc(A, lda, B, ldb, outs, 1, ldc, M, N, K, st);
+  }
+  if ((M + 31) / 32 > 65535) return uk::fail(UK_EINVAL, "gemm_f16: M=%d exceeds the grid limit", M);
   return uk::gemm_f16_simt((const __half*)A, lda, (const __half*)B, ldb, (__half*)C, ldc, M, N, K, st);
 }
 
 extern "C" int uk_cuda_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, int N, int K,
                                 void* stream) {
   return uk_cuda_gemm_f16_ld(A, K, B, N, C, N, M, N, K, stream);
+}
+
+extern "C" unsigned uk_cuda_pipeline_fault(void) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, uk::g_fault_word, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  const unsigned zero = 0;
+  cudaMemcpyToSymbol(uk::g_fault_word, &zero, sizeof(zero));
+  return v;
 }

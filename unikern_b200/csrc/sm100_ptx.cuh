@@ -1,0 +1,167 @@
+// sm100_ptx.cuh -- thin inline-PTX wrappers for the Blackwell (sm_100a)
+// features the tensor-core kernels use: mbarriers, TMA tiled loads (no
+// multicast anywhere in this library), tcgen05 MMA / TMEM alloc / loads.
+//
+// Every wait is bounded: uk_mbar_wait gives up after `timeout_ns` of
+// %globaltimer (or as soon as another role of the CTA raised the abort flag)
+// and returns false; callers record the fault and unwind instead of spinning.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+// bits of the device fault word (uk_cuda_pipeline_fault)
+#define UK_FAULT_PRODUCER 0x1u
+#define UK_FAULT_MMA 0x2u
+#define UK_FAULT_EPILOGUE 0x4u
+#define UK_FAULT_TEARDOWN 0x8u
+#define UK_FAULT_SELFTEST 0x10u
+#define UK_FAULT_PEER 0x20u
+
+__device__ __forceinline__ uint32_t uk_smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t uk_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier ----------------------------------------------------------------
+__device__ __forceinline__ void uk_mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(uk_smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void uk_fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void uk_mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(uk_smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void uk_mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(uk_smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool uk_mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(uk_smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with parity `parity` to complete.  Returns false on
+// timeout or when *abort was raised by another role of the CTA.
+__device__ __forceinline__ bool uk_mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                             uint64_t timeout_ns) {
+  if (uk_mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = uk_globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (uk_mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (abort != nullptr && *abort) return false;
+      if (uk_globaltimer() - t0 > timeout_ns) return false;
+    }
+  }
+}
+
+// ---- TMA (tiled, 2-D, no multicast) -----------------------------------------
+__device__ __forceinline__ void uk_tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// x = innermost coordinate (elements; callers keep x * elem_size a multiple
+// of 16 bytes), y = row coordinate.
+__device__ __forceinline__ void uk_tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          uk_smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(uk_smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// ---- tcgen05 -----------------------------------------------------------------
+__device__ __forceinline__ void uk_tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(uk_smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void uk_tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void uk_tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void uk_tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void uk_tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (both operands f16),
+// issued by one thread.
+__device__ __forceinline__ void uk_umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// mbarrier arrive (count one) once every tcgen05 op issued so far by this
+// thread has completed
+__device__ __forceinline__ void uk_umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   uk_smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i gets lane (base + i)
+__device__ __forceinline__ void uk_tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void uk_tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a 128-byte-swizzled operand tile
+// (sm100 descriptor: start >> 4 at [0,14), LBO >> 4 at [16,30), SBO >> 4 at
+// [32,46), version 1 at bit 46, layout type 2 = SWIZZLE_128B at [61,64)).
+__device__ __forceinline__ uint64_t uk_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D f32, A and B f16, A K-major,
+// B K-major (b_mn_major = 0) or MN-major (1), shape M x N.
+__host__ __device__ constexpr uint32_t uk_idesc_f16(int M, int N, int b_mn_major) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | ((uint32_t)b_mn_major << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
