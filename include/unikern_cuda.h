@@ -60,6 +60,25 @@ size_t uk_cuda_reduce_workspace_size(int64_t rows, int64_t cols);
 int uk_cuda_reduce_f32(const float* X, float* Y, int64_t rows, int64_t cols,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* Reduce without a workspace: the same result as uk_cuda_reduce_f32 (same
+ * kernels, same plan), for callers that cannot allocate device memory -- a
+ * plugin inside a host application that owns every device allocation through
+ * its own pool or budget, or a caller that must not risk an allocation's
+ * implicit synchronisation or out-of-memory failure in the middle of a run --
+ * and so have no workspace to pass.  This call allocates nothing: the partial
+ * sums of the split-row plan go to a 32 KiB array (8192 floats) inside the
+ * library, which every GPU that loads the library holds until the process
+ * exits.  Limit: a shape whose plan needs more than 8192 partial sums is
+ * rejected with UK_EINVAL (on a 148-SM B200 the plan never needs more than
+ * about 1800, so every shape fits).  The first call on each device looks up
+ * the array's device address with that device current; make that first call
+ * before any stream capture.  All calls share the one array: calls that
+ * overlap on the GPU (different streams, or threads, on the same device)
+ * race and must be serialised, e.g. on one stream.  The array keeps the last
+ * call's contents; nothing in it has to start at zero.
+ * No counterpart in the reference (its reduce always allocates its partials). */
+int uk_cuda_reduce_f32_noalloc(const float* X, float* Y, int64_t rows, int64_t cols, void* stream);
+
 /* ---- rmsnorm ---------------------------------------------------------------
  * Y[l][c] = X[l][c] * (1 / sqrt(sum_c X[l][c]^2 / C + eps)) * W[c].
  * The reference hard-codes eps = 1e-6 (src/codegen_hip.cpp:2162, :2175);

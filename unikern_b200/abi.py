@@ -22,6 +22,7 @@ PROTOTYPES = {
     "uk_cuda_channelscale_f32": (i32, [vp, vp, vp, i64, i64, vp]),
     "uk_cuda_reduce_workspace_size": (sz, [i64, i64]),
     "uk_cuda_reduce_f32": (i32, [vp, vp, i64, i64, vp, sz, vp]),
+    "uk_cuda_reduce_f32_noalloc": (i32, [vp, vp, i64, i64, vp]),
     "uk_cuda_rmsnorm_f32": (i32, [vp, vp, vp, i64, i64, f32, vp]),
     "uk_cuda_softmax_f32": (i32, [vp, vp, i64, i64, vp]),
     "uk_cuda_gemm_f32": (i32, [vp, vp, vp, i32, i32, i32, vp]),

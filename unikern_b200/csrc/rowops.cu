@@ -11,6 +11,7 @@
 //     result bits are the same on every call (deterministic);
 //   * grids are sized from the SM count (148 on B200), not from a label.
 #include <cmath>
+#include <mutex>
 
 #include "uk_common.cuh"
 
@@ -326,6 +327,36 @@ ReducePlan plan_reduce(int64_t rows, int64_t cols) {
   return {3, splits, chunk};
 }
 
+// ---------------------------------------------------------------------------
+// Scratch for uk_cuda_reduce_f32_noalloc: the split-row partial sums live in
+// this file-scope array instead of a caller workspace.  Every GPU that loads
+// the library holds it (32 KiB) until the process exits.  In host code the
+// name g_reduce_scratch is only a stand-in for the symbol, never a device
+// address: the launch below passes the address cudaGetSymbolAddress returned.
+// ---------------------------------------------------------------------------
+constexpr int64_t kReduceScratchFloats = 8192;
+static __device__ __align__(256) float g_reduce_scratch[kReduceScratchFloats];
+
+// Device address of g_reduce_scratch on the current device, looked up once per
+// device (the first call on each device does it, with that device current).
+int reduce_scratch_address(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {nullptr};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return uk::fail(UK_ECUDA, "reduce_noalloc: no usable current device");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_reduce_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return uk::fail(UK_ECUDA, "reduce_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    addr[dev] = (float*)p;
+  }
+  *out = addr[dev];
+  return UK_OK;
+}
+
 int check_rows(int64_t L, int64_t C, const char* op) {
   if (L < 0 || C < 0) return uk::fail(UK_EINVAL, "%s: negative size L=%lld C=%lld", op, (long long)L, (long long)C);
   if (L > 2147483647LL) return uk::fail(UK_EINVAL, "%s: L=%lld exceeds 2^31-1 rows", op, (long long)L);
@@ -430,6 +461,47 @@ int uk_cuda_softmax_f32(const float* X, float* Y, int64_t L, int64_t C, void* st
   if (vec) dispatch_rowop<kOpSoftmax, 4>(X, nullptr, Y, L, C, 0.f, st);
   else dispatch_rowop<kOpSoftmax, 1>(X, nullptr, Y, L, C, 0.f, st);
   return uk::check_launch("softmax");
+}
+
+// Same result as uk_cuda_reduce_f32 (same kernels, same plan), without a
+// caller workspace: see the header for who needs this and its limits.
+int uk_cuda_reduce_f32_noalloc(const float* X, float* Y, int64_t rows, int64_t cols, void* stream) {
+  if (int rc = check_rows(rows, cols, "reduce_noalloc")) return rc;
+  if (rows == 0) return UK_OK;
+  if (int rc = uk::check_device_ptr(Y, "Y")) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const ReducePlan p = plan_reduce(rows, cols);
+  if (p.mode == 0) {
+    k_fill_zero<<<(unsigned)((rows + 255) / 256 < 4096 ? (rows + 255) / 256 : 4096), 256, 0, st>>>(Y, rows);
+    return uk::check_launch("reduce_noalloc(zero)");
+  }
+  if (int rc = uk::check_device_ptr(X, "X")) return rc;
+  const bool vec = cols % 4 == 0 && uk::aligned16(X);
+  if (p.mode == 1) {
+    if (vec) k_rowsum_cta<4><<<(unsigned)rows, 256, 0, st>>>(X, Y, cols);
+    else k_rowsum_cta<1><<<(unsigned)rows, 256, 0, st>>>(X, Y, cols);
+  } else if (p.mode == 2) {
+    const unsigned g = (unsigned)((rows + 7) / 8);
+    if (vec) k_rowsum_warp<4><<<g, 256, 0, st>>>(X, Y, rows, cols);
+    else k_rowsum_warp<1><<<g, 256, 0, st>>>(X, Y, rows, cols);
+  } else {
+    const int64_t need = rows * p.splits;
+    if (need > kReduceScratchFloats)
+      return uk::fail(UK_EINVAL,
+                      "reduce_noalloc: rows=%lld cols=%lld need %lld partial sums, the static scratch holds %lld; "
+                      "use uk_cuda_reduce_f32 with a workspace",
+                      (long long)rows, (long long)cols, (long long)need, (long long)kReduceScratchFloats);
+    if (rows > 65535) return uk::fail(UK_EINVAL, "reduce_noalloc: internal split plan with rows > 65535");
+    float* P = nullptr;
+    if (int rc = reduce_scratch_address(&P)) return rc;
+    // every partial the fold reads is written by the split pass of the same
+    // call, so nothing in the shared array has to be cleared first
+    dim3 g1((unsigned)p.splits, (unsigned)rows);
+    if (vec) k_rowsum_split<4><<<g1, 256, 0, st>>>(X, P, cols, p.splits, p.chunk);
+    else k_rowsum_split<1><<<g1, 256, 0, st>>>(X, P, cols, p.splits, p.chunk);
+    k_rowsum_fold<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, p.splits);
+  }
+  return uk::check_launch("reduce_noalloc");
 }
 
 }  // extern "C"
