@@ -282,8 +282,6 @@ def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
     import unikern_b200.abi as abi
     torch = ctx.torch
     world, rank = ctx.world, ctx.rank
-    if N % world != 0:
-        raise SystemExit("N=%d not divisible by %d ranks" % (N, world))
     A = gen(torch, (M, K), "normal", 1, torch.float16, 0.02)
     B = gen(torch, (K, N), "normal", 2, torch.float16, 0.02)
     Cm = torch.empty((M, N), dtype=torch.float16, device="cuda")
@@ -292,10 +290,11 @@ def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
             abi.gemm_f16(A, B, Cm)
         launches_per_step = 1
         parallelism = "single GPU"
+        Bs = B
     else:
         from unikern_b200 import shard
-        plan = shard.GemmAllGather(M, N, K, world, rank, ctx.torch)
-        Bs = B[:, rank * (N // world):(rank + 1) * (N // world)]
+        plan = shard.GemmAllGather(Cm, M, N, K)
+        Bs = plan.b_shard(B)
 
         def step():
             plan.run(A, Bs, Cm)
@@ -307,7 +306,7 @@ def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
            "parallelism": parallelism}
     # e2e through the C ABI with pinned host buffers (rank-local inputs)
     Ah = A.cpu().pin_memory()
-    Bh = (B if world == 1 else B[:, rank * (N // world):(rank + 1) * (N // world)].contiguous()).cpu().pin_memory()
+    Bh = Bs.contiguous().cpu().pin_memory()
     Ch = torch.empty((M, N), dtype=torch.float16).pin_memory()
     Bd = torch.empty_like(Bh, device="cuda")
 
@@ -320,6 +319,16 @@ def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
             plan.run(A, Bd, Cm)
         Ch.copy_(Cm, non_blocking=True)
     e2e_ms = ctx.time_steps(e2e_step, max(2, min(steps, 10)), 1)
+    if world > 1:
+        # every rank must hold the same full C: spot-check against a column
+        # block computed locally on this GPU
+        ref = torch.empty((M, 64), dtype=torch.float16, device="cuda")
+        j0 = ((rank + 1) % world) * (N // world)
+        abi.gemm_f16(A, B[:, j0:j0 + 64], ref)
+        step()
+        torch.cuda.synchronize()
+        res["allgather_max_abs_diff"] = float((Cm[:, j0:j0 + 64].float() - ref.float()).abs().max().item())
+        plan.close()
     res["e2e"] = {"value": flops / e2e_ms / 1e9, "unit": "TFLOP/s",
                   "h2d_bytes_per_step": Ah.numel() * 2 + Bh.numel() * 2, "d2h_bytes_per_step": Ch.numel() * 2,
                   "ms_per_step": e2e_ms}
@@ -511,7 +520,7 @@ def main():
     clocks = sampler.stop()
 
     ops = {}
-    if args.op == "all" and rank == 0:
+    if args.op == "all" and world == 1:
         s = max(5, min(args.steps, 20))
         for op in ("reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar"):
             r = bench_rowop(Ctx(1, 0, local_rank), op, s, 3)
@@ -541,7 +550,9 @@ def main():
             "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in g["e2e"].items()},
             "gpu_launches": g["launches"], "clocks": clocks}
     line["e2e"]["value"] = round(g["e2e"]["value"], 3)
-    if rank == 0 and not args.no_cpu:
+    if "allgather_max_abs_diff" in g:
+        line["config"]["allgather_check_max_abs_diff"] = g["allgather_max_abs_diff"]
+    if world == 1 and not args.no_cpu:
         cb = cpu_gemm_f16(M, N, K)
         line["cpu_baseline"] = {k: (round(v, 6) if isinstance(v, float) else v) for k, v in cb.items()
                                 if k != "seconds"}

@@ -110,6 +110,28 @@ int uk_cuda_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, i
 int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb,
                         uint16_t* C, int64_t ldc, int M, int N, int K, void* stream);
 
+/* ---- multi-GPU f16 GEMM (one process per GPU, NVLink peers) ----------------
+ * N-sharded GEMM with the all-gather fused into the store: computes columns
+ * [col_offset, col_offset + N_shard) of C = A * B from this rank's column
+ * slice of B (B_shard[K][N_shard], leading dimension ldb) and writes every
+ * output tile into all n_c (<= 8) copies of the full C[M][ldc]:
+ * C_list[0] on this GPU, C_list[1..] other GPUs' buffers opened with
+ * uk_cuda_ipc_import.  The caller orders ranks after the call (a stream-
+ * ordered barrier) before reading C.  Tensor-core shapes only (K, N_shard,
+ * lda, ldb, ldc, col_offset multiples of 8).  No reference counterpart (the
+ * reference is single-GPU); the column split and all-gather are the north
+ * star's multi-GPU plan. */
+int uk_cuda_gemm_f16_allgather(const uint16_t* A, int64_t lda, const uint16_t* B_shard, int64_t ldb,
+                               uint16_t* const* C_list, int n_c, int64_t ldc, int M, int N_shard, int K,
+                               int64_t col_offset, void* stream);
+/* CUDA IPC: export a device buffer (handle of uk_cuda_ipc_handle_size() bytes
+ * plus the offset of `ptr` inside its allocation), open a peer's export as a
+ * pointer on this device, close it.  No reference counterpart. */
+size_t uk_cuda_ipc_handle_size(void);
+int uk_cuda_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+int uk_cuda_ipc_import(const void* handle, uint64_t offset, void** ptr_out);
+int uk_cuda_ipc_close(void* ptr, uint64_t offset);
+
 /* Fault word of the tensor-core pipelines: 0 when no bounded wait inside a
  * kernel of this library expired since the last call, otherwise a bit mask
  * (1 producer, 2 MMA issuer, 4 epilogue, 8 teardown, 16 self-test, 32 peer

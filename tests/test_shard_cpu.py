@@ -1,0 +1,64 @@
+"""Host logic of the multi-GPU GEMM on CPU: the column split, the store
+order and the handle exchange, run as world-size-2 gloo process groups."""
+import os
+import socket
+
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from unikern_b200 import shard
+
+
+@pytest.mark.parametrize("N,world", [(8192, 1), (8192, 2), (8192, 8), (14336, 8), (1000, 3), (8, 4), (24, 5)])
+def test_column_split_partitions_exactly(N, world):
+    blocks = [shard.column_split(N, world, r) for r in range(world)]
+    assert blocks[0][0] == 0 and blocks[-1][1] == N
+    for (a0, a1), (b0, b1) in zip(blocks, blocks[1:]):
+        assert a1 == b0
+    for a0, a1 in blocks:
+        assert a0 % 8 == 0 and a1 >= a0
+        assert a1 % 8 == 0 or a1 == N
+    sizes = [b - a for a, b in blocks]
+    assert max(sizes) - min(sizes) <= 8
+
+
+def test_store_order_local_first_ring():
+    assert shard.store_order(4, 2) == [2, 3, 0, 1]
+    for w in range(1, 9):
+        for r in range(w):
+            o = shard.store_order(w, r)
+            assert o[0] == r and sorted(o) == list(range(w))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        got = shard.gather_objects((b"handle-%d" % rank, 16 * rank))
+        blocks = shard.gather_objects(shard.column_split(8192, world, rank))
+        q.put((rank, got, blocks))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_handle_exchange_gloo_world2():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, got, blocks in results:
+        assert got == [(b"handle-0", 0), (b"handle-1", 16)]
+        assert blocks == [(0, 4096), (4096, 8192)]

@@ -30,6 +30,11 @@ PROTOTYPES = {
     "uk_cuda_gemm_f16_ld": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, i32, vp]),
     "uk_cuda_conv2d_f32": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp]),
     "uk_cuda_pipeline_fault": (C.c_uint, []),
+    "uk_cuda_gemm_f16_allgather": (i32, [vp, i64, vp, i64, C.POINTER(vp), i32, i64, i32, i32, i32, i64, vp]),
+    "uk_cuda_ipc_handle_size": (sz, []),
+    "uk_cuda_ipc_export": (i32, [vp, vp, C.POINTER(C.c_uint64)]),
+    "uk_cuda_ipc_import": (i32, [vp, C.c_uint64, C.POINTER(vp)]),
+    "uk_cuda_ipc_close": (i32, [vp, C.c_uint64]),
 }
 
 UK_CONV_KML, UK_CONV_NCHW = 0, 1

@@ -20,7 +20,8 @@
 // 148 CTAs touches stay in L2.
 //
 // Every mbarrier wait is bounded (uk_mbar_wait); a timeout sets the fault word
-// read by uk_cuda_pipeline_fault() and the CTA unwinds.  No TMA multicast.
+// read by uk_cuda_pipeline_fault() and the CTA unwinds.  Every TMA load is a
+// plain single-CTA load of this GPU's own memory.
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
@@ -230,6 +231,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) uk_mbar_arrive(&ctl->tempty[buf]);
     }
+    // stores into other GPUs' buffers are made visible system-wide before
+    // this CTA retires (the host orders ranks after the kernel)
+    if (out.n > 1) __threadfence_system();
   }
 
   uk_tc_fence_before();
@@ -342,6 +346,44 @@ extern "C" int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_
 extern "C" int uk_cuda_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, int N, int K,
                                 void* stream) {
   return uk_cuda_gemm_f16_ld(A, K, B, N, C, N, M, N, K, stream);
+}
+
+// N-sharded GEMM with the all-gather fused into the epilogue: this rank
+// computes columns [col_offset, col_offset + N_shard) of C = A * B from its
+// column slice of B, and stores every tile into all n_c copies of C (C_list[0]
+// on this GPU, the others peers' buffers opened with uk_cuda_ipc_import).
+extern "C" int uk_cuda_gemm_f16_allgather(const uint16_t* A, int64_t lda, const uint16_t* B_shard, int64_t ldb,
+                                          uint16_t* const* C_list, int n_c, int64_t ldc, int M, int N_shard, int K,
+                                          int64_t col_offset, void* stream) {
+  if (M < 0 || N_shard < 0 || K <= 0) return uk::fail(UK_EINVAL, "gemm_f16_allgather: dims %d %d %d", M, N_shard, K);
+  if (C_list == nullptr || n_c < 1 || n_c > MAX_OUT)
+    return uk::fail(UK_EINVAL, "gemm_f16_allgather: 1..%d outputs, got %d", MAX_OUT, n_c);
+  if (col_offset < 0 || col_offset % 8 != 0 || col_offset + N_shard > ldc)
+    return uk::fail(UK_EINVAL, "gemm_f16_allgather: column offset %lld (multiple of 8, inside ldc=%lld)",
+                    (long long)col_offset, (long long)ldc);
+  if (lda < K || ldb < N_shard) return uk::fail(UK_EINVAL, "gemm_f16_allgather: leading dimensions");
+  if (M == 0 || N_shard == 0) return UK_OK;
+  if (int rc = uk::check_device_ptr(A, "A")) return rc;
+  if (int rc = uk::check_device_ptr(B_shard, "B_shard")) return rc;
+  if (int rc = uk::check_device_ptr(C_list[0], "C_list[0]")) return rc;
+  uint16_t* outs[MAX_OUT];
+  for (int i = 0; i < n_c; ++i) {
+    if (C_list[i] == nullptr) return uk::fail(UK_EINVAL, "gemm_f16_allgather: C_list[%d] is NULL", i);
+    if (i > 0) {
+      cudaPointerAttributes a{};
+      if (cudaPointerGetAttributes(&a, C_list[i]) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+        cudaGetLastError();
+        return uk::fail(UK_ERESIDENCY, "gemm_f16_allgather: C_list[%d] is not device memory", i);
+      }
+    }
+    outs[i] = C_list[i] + col_offset;
+  }
+  const void* cs[MAX_OUT];
+  for (int i = 0; i < n_c; ++i) cs[i] = outs[i];
+  if (!uk::gemm_f16_tc_ok(A, lda, B_shard, ldb, cs, n_c, ldc, N_shard, K))
+    return uk::fail(UK_EINVAL, "gemm_f16_allgather: needs K, N_shard, lda, ldb, ldc multiples of 8 and 16-byte "
+                               "aligned pointers");
+  return uk::gemm_f16_tc(A, lda, B_shard, ldb, outs, n_c, ldc, M, N_shard, K, (cudaStream_t)stream);
 }
 
 extern "C" unsigned uk_cuda_pipeline_fault(void) {

@@ -1,6 +1,6 @@
 // sm100_ptx.cuh -- thin inline-PTX wrappers for the Blackwell (sm_100a)
-// features the tensor-core kernels use: mbarriers, TMA tiled loads (no
-// multicast anywhere in this library), tcgen05 MMA / TMEM alloc / loads.
+// features the tensor-core kernels use: mbarriers, TMA tiled loads (each a
+// plain single-CTA load), tcgen05 MMA / TMEM alloc / loads.
 //
 // Every wait is bounded: uk_mbar_wait gives up after `timeout_ns` of
 // %globaltimer (or as soon as another role of the CTA raised the abort flag)
@@ -73,7 +73,7 @@ __device__ __forceinline__ bool uk_mbar_wait(uint64_t* bar, uint32_t parity, vol
   }
 }
 
-// ---- TMA (tiled, 2-D, no multicast) -----------------------------------------
+// ---- TMA (tiled, 2-D, single-CTA destination) ------------------------------
 __device__ __forceinline__ void uk_tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
