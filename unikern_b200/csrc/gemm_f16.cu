@@ -67,7 +67,9 @@ struct SmemCtl {
   int abort;
 };
 
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + sizeof(SmemCtl) + 1024;
+// epilogue staging: per epilogue warp one 32-row x 64-column f16 block (4 KiB)
+constexpr int STG_BYTES = 32 * 64 * 2;
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 4 * STG_BYTES + sizeof(SmemCtl) + 1024;
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
@@ -89,7 +91,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   int M, int N, int K, int64_t ldc) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  SmemCtl* ctl = (SmemCtl*)(smem + (size_t)STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + (size_t)STAGES * STAGE_BYTES;
+  SmemCtl* ctl = (SmemCtl*)(staging + 4 * STG_BYTES);
   volatile int* abort = &ctl->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -190,8 +193,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    // TMEM -> registers (each lane one row) -> f16 -> swizzled staging block
+    // -> coalesced 128-byte row segments to every copy of C.  Staging chunk
+    // c (16 bytes) of row r sits at r*128 + ((c ^ (r & 7)) * 16), so both the
+    // row-wise writes and the column-wise reads are bank-conflict free.
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int row = q * 32 + lane;
+    uint8_t* stg = staging + (warp - 2) * STG_BYTES;
     uint32_t tl = 0;
     for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x, ++tl) {
       int mb, nb;
@@ -202,30 +209,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       uk_tc_fence_after();
-      const int gm = mb * BM + row;
+      const int row0 = mb * BM + q * 32;
       const int n0 = nb * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        uk_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, v);
+      for (int h = 0; h < BN / 64; ++h) {
+        uint32_t v0[32], v1[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * BN + h * 64;
+        uk_tmem_ld32(taddr, v0);
+        uk_tmem_ld32(taddr + 32, v1);
         uk_tmem_ld_wait();
-        if (gm < M) {
-          uint4 pk[4];
-          uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            __half2 h = __floats2half2_rn(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            pw[i] = *reinterpret_cast<uint32_t*>(&h);
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t* src = c < 4 ? &v0[(c & 3) * 8] : &v1[(c & 3) * 8];
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            __half2 h2 = __floats2half2_rn(__uint_as_float(src[2 * i]), __uint_as_float(src[2 * i + 1]));
+            w[i] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          const int gn = n0 + c * 32;
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        __syncwarp();
+        const int c = lane & 7;
+        const int gn = n0 + h * 64 + c * 8;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (gn + j * 8 < N) {
-              const size_t off = (size_t)gm * ldc + gn + j * 8;
-              for (int o = 0; o < out.n; ++o) *reinterpret_cast<uint4*>(out.c[o] + off) = pk[j];
-            }
+        for (int i = 0; i < 8; ++i) {
+          const int r = i * 4 + (lane >> 3);
+          const uint4 val = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) * 16));
+          const int gm = row0 + r;
+          if (gm < M && gn < N) {
+            const size_t off = (size_t)gm * ldc + gn;
+            for (int o = 0; o < out.n; ++o) *reinterpret_cast<uint4*>(out.c[o] + off) = val;
           }
         }
+        __syncwarp();
       }
       uk_tc_fence_before();
       __syncwarp();
