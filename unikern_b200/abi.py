@@ -9,8 +9,11 @@ from __future__ import annotations
 import ctypes as C
 from pathlib import Path
 
+import os
+
 _LIB = None
-_PATH = Path(__file__).resolve().parent / "_lib" / "libunikern_cuda.so"
+# UNIKERN_CUDA_LIB names another build of the same library (same ABI)
+_PATH = Path(os.environ.get("UNIKERN_CUDA_LIB") or Path(__file__).resolve().parent / "_lib" / "libunikern_cuda.so")
 
 vp, i64, i32, f32, sz = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_size_t
 

@@ -10,8 +10,10 @@
 //   warp 1      TMEM owner (alloc/dealloc 512 columns) and MMA issuer: one
 //               thread issues tcgen05.mma M=128 N=256 K=16 (4 per K block)
 //               into one of two 256-column fp32 accumulators
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, convert to f16
-//               (round to nearest even), 16-byte stores; with the second
+//   warps 2-5   epilogue, one warp per TMEM lane quadrant: tcgen05.ld
+//               32 lanes x 32 columns, convert
+//               to f16 (round to nearest even), stage in swizzled shared
+//               memory, store 128-byte row segments; with the second
 //               accumulator the epilogue of tile i overlaps the MMAs of i+1
 // The epilogue can also write each tile to up to 7 more buffers (other GPUs'
 // copies of C reached over NVLink): that is the all-gather of the N-sharded
@@ -45,7 +47,8 @@ constexpr int A_BYTES = BM * BK * 2;      // 16 KiB
 constexpr int B_BOX_BYTES = BK * 64 * 2;  // 8 KiB: 64 K rows x 64 N columns
 constexpr int B_BYTES = BK * BN * 2;      // 32 KiB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 4;  // one per TMEM lane quadrant (8 measured slower: more remote stores in flight per SM congest NVLink)
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
 constexpr int MAX_OUT = 8;
@@ -69,7 +72,8 @@ struct SmemCtl {
 
 // epilogue staging: per epilogue warp one 32-row x 64-column f16 block (4 KiB)
 constexpr int STG_BYTES = 32 * 64 * 2;
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 4 * STG_BYTES + sizeof(SmemCtl) + 1024;
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + EPI_WARPS * STG_BYTES + sizeof(SmemCtl) + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory per block on sm_100");
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
@@ -92,7 +96,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* staging = smem + (size_t)STAGES * STAGE_BYTES;
-  SmemCtl* ctl = (SmemCtl*)(staging + 4 * STG_BYTES);
+  SmemCtl* ctl = (SmemCtl*)(staging + EPI_WARPS * STG_BYTES);
   volatile int* abort = &ctl->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       uk_mbar_init(&ctl->tfull[b], 1);
-      uk_mbar_init(&ctl->tempty[b], 4);
+      uk_mbar_init(&ctl->tempty[b], EPI_WARPS);
     }
     uk_mbar_init(&ctl->teardown, 1);
     ctl->abort = 0;
@@ -192,12 +196,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2 .. 2 + EPI_WARPS) ----------------
     // TMEM -> registers (each lane one row) -> f16 -> swizzled staging block
     // -> coalesced 128-byte row segments to every copy of C.  Staging chunk
     // c (16 bytes) of row r sits at r*128 + ((c ^ (r & 7)) * 16), so both the
     // row-wise writes and the column-wise reads are bank-conflict free.
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;                       // TMEM lane quadrant this warp may access
+    constexpr int COLS = BN * 4 / EPI_WARPS;      // columns of the tile this warp drains
+    const int half = (warp - 2) >> 2;             // which COLS-wide part of the tile
     uint8_t* stg = staging + (warp - 2) * STG_BYTES;
     uint32_t tl = 0;
     for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x, ++tl) {
@@ -212,7 +218,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int row0 = mb * BM + q * 32;
       const int n0 = nb * BN;
 #pragma unroll 1
-      for (int h = 0; h < BN / 64; ++h) {
+      for (int h = half * (COLS / 64); h < (half + 1) * (COLS / 64); ++h) {
         uint32_t v0[32], v1[32];
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * BN + h * 64;
         uk_tmem_ld32(taddr, v0);

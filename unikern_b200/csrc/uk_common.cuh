@@ -13,7 +13,7 @@
 
 #include <string>
 
-#include "../../include/unikern_cuda.h"
+#include "unikern_cuda.h"
 
 namespace uk {
 
