@@ -44,6 +44,25 @@ int uk_cuda_abi_version(void);
 /* 1 when the current device is an sm_100 part this library can run on */
 int uk_cuda_device_supported(void);
 
+/* ---- launch plan -----------------------------------------------------------
+ * The tile this library launches for a KML op, given its KML dims (gemm M,N,K;
+ * conv H,W,C,Kh,Kw,Oc; reduce L; softmax/rmsnorm/channelscale L,C), on a part
+ * with `sms` multiprocessors (0 = the current device).  out4 = {tile_m,
+ * tile_n, k_block, stages}: outputs per CTA (rows x columns; for the row ops
+ * one row x the columns one register pass covers), the K depth of a pipeline
+ * step (0 for the row ops), and the pipeline stages (reduce: row splits;
+ * softmax/rmsnorm: 2 when the row streams from HBM twice).  Host only; with
+ * sms > 0 it needs no GPU.  Replaces emit_tile_for / the solver's tile choice
+ * (src/codegen_hip.cpp:58-68, src/solver.cpp:14-186): these are the tm/tn the
+ * runner records in the ledger row. */
+#define UK_OP_GEMM 0
+#define UK_OP_CONV 1
+#define UK_OP_REDUCE 2
+#define UK_OP_SOFTMAX 3
+#define UK_OP_RMSNORM 4
+#define UK_OP_CHANNELSCALE 5
+int uk_cuda_tile_plan(int op, int f16, const int64_t* dims, int sms, int* out4);
+
 /* ---- channelscale ----------------------------------------------------------
  * Y[i*C + c] = X[i*C + c] * S[c] for i < L, c < C.  Bit-exact to the reference.
  * Replaces uk_channelscale (src/codegen_hip.cpp:2329-2335). */
@@ -153,6 +172,35 @@ unsigned uk_cuda_pipeline_fault(void);
 int uk_cuda_conv2d_f32(const float* X, const float* Wt, float* Y, int N, int H, int W,
                        int C, int Kh, int Kw, int Oc, int pad, const float* scale,
                        int layout, void* stream);
+
+/* ---- KML runner (host side; the nvidia branch of `unikern run`) -----------
+ * uk_kml_describe: the KML contract for one declaration, no GPU needed.
+ *   Writes "key=value" lines to out: canonical= (canonical_form), signature=
+ *   (op_signature), ops= / bytes= (workload_of), tolerance= (the verify gate of
+ *   the dtype), gap= (empty when nvidia:cuda runs the tree), and with an HCS
+ *   also hcs_fingerprint=, ledger_key=, tile=, k_block=, stages=, c_ms=,
+ *   placement= (the solver, on `sms` multiprocessors; 0 = the HCS's
+ *   compute_units), then export= and the exported JSON.  A rejected
+ *   declaration returns UK_EINVAL with the reference's "rejected (N
+ *   violations): ..." text in out.
+ *   Replaces kml_import / canonical_form / op_signature / workload_of /
+ *   hcs_fingerprint / the ledger key (src/kml_front.cpp:75-251,
+ *   src/kml.cpp:60-177, src/hcs.cpp:52-115, src/main.cpp:217-219).
+ * uk_run_kml: import the HCS and the KML tree, look the ledger key up in the
+ *   TAB-separated file ledger (a hit reuses the recorded tile), solve on a
+ *   miss, run the tree on the current device (verify instance checked on the
+ *   GPU in fp64 against the dtype's gate, then e2e and kernel-only timing at
+ *   the declared dims), and commit a verified run when write_ledger != 0.
+ *   The transcript (LEDGER HIT, UNIKERN_RESULT backend=nvidia:cuda ..., RUN
+ *   ..., LEDGER COMMIT ...) goes to out.  Returns cmd_run's exit code: 0 ok,
+ *   1 run failed or verify FAIL, 2 bad input / unsupported tree, 3
+ *   infeasible, 5 residency violation.  ledger_path may be NULL (no ledger).
+ *   Replaces cmd_run's execute branch + run_ocl/run_hip (src/main.cpp:346-570,
+ *   src/runner_ocl.cpp); allocates its own device and pinned buffers (this is
+ *   the runner, not a hot call). */
+int uk_kml_describe(const char* kml_json, const char* hcs_json, int sms, char* out, size_t out_cap);
+int uk_run_kml(const char* hcs_json, const char* kml_json, const char* ledger_path, int write_ledger, char* out,
+               size_t out_cap);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,7 @@ def declared_symbols():
     for h in (ROOT / "include").glob("*.h"):
         text = h.read_text()
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-        names.update(re.findall(r"\b(uk_cuda_\w+)\s*\(", text))
+        names.update(re.findall(r"\b(uk_\w+)\s*\(", text))
     return sorted(names)
 
 

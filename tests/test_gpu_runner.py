@@ -1,0 +1,85 @@
+"""The nvidia:cuda runner on the GPU: `uk_run_kml` runs a KML declaration the
+way the reference's `unikern run` runs one on its own backends (verify
+instance, timing, UNIKERN_RESULT line, ledger commit; src/main.cpp:346-570,
+src/runner_ocl.cpp).
+
+The verify instances are the reference's own (sawtooth operands that keep
+every fp32 partial sum exact, src/codegen_hip.cpp:604-605, :2167, :2338):
+gemm/conv/reduce/channelscale must come back with max_rel = 0, as the
+reference's published runs do; softmax and rmsnorm within a few ulps.
+"""
+import pytest
+
+import unikern_b200.abi as abi
+
+pytestmark = pytest.mark.gpu
+HCS = (abi.SAMPLES / "hcs_nvidia_b200.json").read_text()
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda():
+    import torch
+    assert torch.cuda.is_available()
+    torch.cuda.set_device(0)
+
+
+CASES = [
+    ('{"op":"gemm","dtype":"fp32","dims":[512,512,512],"tile_m":64,"tile_n":128,"layout":"NT"}', 0.0),
+    ('{"op":"gemm","dtype":"fp16","dims":[512,512,512]}', 2 ** -11),   # one f16 rounding of an exact sum
+    ('{"op":"conv","dtype":"fp32","dims":[58,58,256,3,3,256]}', 0.0),
+    ('{"op":"reduce","dtype":"fp32","dims":[1048576]}', 0.0),
+    ('{"op":"softmax","dtype":"fp32","dims":[65536,256]}', 1e-6),
+    ('{"op":"rmsnorm","dtype":"fp32","dims":[4096,1000]}', 1e-6),
+    ('{"op":"channelscale","dtype":"fp32","dims":[65536,256]}', 0.0),
+]
+
+
+@pytest.mark.parametrize("kml,max_rel", CASES, ids=lambda v: v[:30] if isinstance(v, str) else "")
+def test_run_verifies_and_commits(tmp_path, kml, max_rel):
+    ledger = tmp_path / "ledger.jsonl"
+    rc, out = abi.run_kml(HCS, kml, str(ledger))
+    assert rc == 0, out
+    tok = abi.result_tokens(out)
+    assert tok["backend"] == "nvidia:cuda" and tok["verify"] == "PASS", out
+    assert float(tok["max_rel"]) <= max_rel, out
+    assert float(tok["kernel_ms"]) > 0 and float(tok["measured_ms"]) >= float(tok["kernel_ms"])
+    assert tok["mode"] == "resident" and tok["migrations"] == "0" and int(tok["checks"]) >= 4
+    assert int(tok["vram_total"]) > 100 * 2 ** 30
+    d = abi.kml_describe(kml, HCS)
+    rows = [r.split("\t") for r in ledger.read_text().splitlines()]
+    assert len(rows) == 1 and rows[0][0] == d["ledger_key"]
+    assert float(rows[0][2]) == pytest.approx(float(tok["measured_ms"]), rel=1e-5)
+    assert "x".join(rows[0][4:6]) == d["tile"]
+    assert "LEDGER COMMIT predicted_ms=" in out
+    # the second run hits the row and appends its own measurement
+    rc, out = abi.run_kml(HCS, kml, str(ledger))
+    assert rc == 0 and "LEDGER HIT" in out and len(ledger.read_text().splitlines()) == 2
+
+
+@pytest.mark.parametrize("kml", [
+    '{"op":"gemm","dtype":"fp16","dims":[8192,8192,8192]}',
+    '{"op":"reduce","dtype":"fp32","dims":[134217728]}',
+    '{"op":"softmax","dtype":"fp32","dims":[8192,16384]}',
+    '{"op":"rmsnorm","dtype":"fp32","dims":[8192,16384]}',
+], ids=["gemm_f16_8192", "reduce_2^27", "softmax_8192x16384", "rmsnorm_8192x16384"])
+def test_baseline_sizes_verify(kml):
+    rc, out = abi.run_kml(HCS, kml, None, write_ledger=False)
+    assert rc == 0 and "VERIFY PASS (no ledger write)" in out, out
+    tok = abi.result_tokens(out)
+    assert tok["verify"] == "PASS"
+    if "fp16" in kml:
+        assert tok["dtype"] == "fp16"
+
+
+def test_verify_mode_writes_no_ledger(tmp_path):
+    ledger = tmp_path / "ledger.jsonl"
+    rc, out = abi.run_kml(HCS, '{"op":"reduce","dtype":"fp32","dims":[4096]}', str(ledger), write_ledger=False)
+    assert rc == 0 and "VERIFY PASS" in out
+    assert not ledger.exists()
+
+
+def test_oversized_payload_is_refused_not_streamed(tmp_path):
+    # 3 x 65536^2 fp32 = 48 GiB per operand: far beyond 0.85 x HBM
+    rc, out = abi.run_kml(HCS, '{"op":"gemm","dtype":"fp32","dims":[131072,131072,131072]}', str(tmp_path / "l"))
+    assert rc == 1 and "UNIKERN_ERROR what=stream_refused" in out
+    assert not (tmp_path / "l").exists()

@@ -38,9 +38,14 @@ PROTOTYPES = {
     "uk_cuda_ipc_export": (i32, [vp, vp, C.POINTER(C.c_uint64)]),
     "uk_cuda_ipc_import": (i32, [vp, C.c_uint64, C.POINTER(vp)]),
     "uk_cuda_ipc_close": (i32, [vp, C.c_uint64]),
+    "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
+    "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
+    "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
 }
 
 UK_CONV_KML, UK_CONV_NCHW = 0, 1
+UK_OP = {"gemm": 0, "conv": 1, "reduce": 2, "softmax": 3, "rmsnorm": 4, "channelscale": 5}
+SAMPLES = Path(__file__).resolve().parent / "samples"
 
 
 class UkError(RuntimeError):
@@ -124,3 +129,45 @@ def gemm_f16(A, B, Cm, stream=None):
 def conv2d(X, Wt, Y, N, H, W, Cc, Kh, Kw, Oc, pad=0, scale=None, layout=UK_CONV_NCHW, stream=None):
     check(lib().uk_cuda_conv2d_f32(_p(X), _p(Wt), _p(Y), N, H, W, Cc, Kh, Kw, Oc, pad, _p(scale), layout,
                                    _stream(stream)))
+
+
+# ---- KML runner (host side) -----------------------------------------------------
+
+def tile_plan(op: str, dims, f16: bool = False, sms: int = 0):
+    """(tile_m, tile_n, k_block, stages) the library launches for a KML op."""
+    d = (C.c_int64 * 6)(*(list(dims) + [0] * (6 - len(dims))))
+    out = (C.c_int * 4)()
+    check(lib().uk_cuda_tile_plan(UK_OP[op], int(f16), d, sms, out))
+    return tuple(out)
+
+
+def kml_describe(kml_json: str, hcs_json: str | None = None, sms: int = 0):
+    """The KML contract of one declaration as a dict (raises UkError with the
+    reference's rejection text for an invalid declaration)."""
+    buf = C.create_string_buffer(1 << 16)
+    rc = lib().uk_kml_describe(kml_json.encode(), hcs_json.encode() if hcs_json else None, sms, buf, len(buf))
+    text = buf.value.decode()
+    if rc != 0:
+        raise UkError(rc, text)
+    head, _, export = text.partition("export=")
+    d = dict(line.split("=", 1) for line in head.splitlines() if "=" in line)
+    d["export"] = export
+    return d
+
+
+def run_kml(hcs_json: str, kml_json: str, ledger: str | None = None, write_ledger: bool = True):
+    """The nvidia branch of `unikern run` (write_ledger) / `verify`: returns
+    (exit code, transcript)."""
+    buf = C.create_string_buffer(1 << 16)
+    rc = lib().uk_run_kml(hcs_json.encode(), kml_json.encode(), ledger.encode() if ledger else None,
+                          int(write_ledger), buf, len(buf))
+    return rc, buf.value.decode()
+
+
+def result_tokens(transcript: str):
+    """key=value tokens of the UNIKERN_RESULT line (parsed by name, as the
+    reference's runner does)."""
+    for line in transcript.splitlines():
+        if line.startswith("UNIKERN_RESULT"):
+            return dict(t.split("=", 1) for t in line.split()[1:] if "=" in t)
+    return None

@@ -14,6 +14,7 @@
 // Output pixel p = n*Ho*Wo + q is stored at (n*Oc + oc)*Ho*Wo + q, which is
 // NCHW for the batch form and [Oc][Ho][Wo] for the KML form.
 #include "uk_common.cuh"
+#include "uk_plan.cuh"
 
 namespace {
 
@@ -190,11 +191,10 @@ void launch(const ConvArgs& a, cudaStream_t st) {
 
 template <int LAYOUT>
 void dispatch(const ConvArgs& a, cudaStream_t st) {
-  const int64_t sms = uk::sm_count();
-  auto ctas = [&](int bm, int bn) { return ((a.npix + bn - 1) / bn) * (int64_t)((a.Oc + bm - 1) / bm); };
-  if (ctas(128, 128) >= sms && a.Oc > 64)
+  const uk::Tile t = uk::conv_tile(a.npix, a.Oc, uk::sm_count());
+  if (t.bm == 128)
     launch<128, 128, 8, 8, 8, LAYOUT>(a, st);
-  else if (ctas(64, 64) >= sms || a.Oc <= 32)
+  else if (t.bm == 64)
     launch<64, 64, 8, 4, 4, LAYOUT>(a, st);
   else
     launch<32, 64, 16, 4, 4, LAYOUT>(a, st);

@@ -31,6 +31,7 @@
 
 #include "sm100_ptx.cuh"
 #include "uk_common.cuh"
+#include "uk_plan.cuh"
 
 namespace uk {
 // device fault word of this translation unit (no relocatable device code, so
@@ -43,6 +44,9 @@ int gemm_f16_simt(const __half* A, int64_t lda, const __half* B, int64_t ldb, __
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+static_assert(BM == uk::kGemmF16Tile.bm && BN == uk::kGemmF16Tile.bn && BK == uk::kGemmF16Tile.bk &&
+                  STAGES == uk::kGemmF16Tile.stages,
+              "the plan query must report the tile this kernel is built for");
 constexpr int A_BYTES = BM * BK * 2;      // 16 KiB
 constexpr int B_BOX_BYTES = BK * 64 * 2;  // 8 KiB: 64 K rows x 64 N columns
 constexpr int B_BYTES = BK * BN * 2;      // 32 KiB

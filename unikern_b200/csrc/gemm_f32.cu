@@ -10,6 +10,7 @@
 #include <cuda_fp16.h>
 
 #include "uk_common.cuh"
+#include "uk_plan.cuh"
 
 namespace {
 
@@ -204,16 +205,15 @@ __global__ void k_zero2d(T* C, int M, int N, int64_t ldc) {
     st1(C + (i / N) * ldc + i % N, 0.f);
 }
 
-// tile choice: the largest tile that still gives every SM a CTA; small
-// problems fall to smaller tiles (512^3: 128 CTAs of 32x64)
+// tile choice (uk::sgemm_tile): the largest tile that still gives every SM a
+// CTA; small problems fall to smaller tiles (512^3: 128 CTAs of 32x64)
 template <typename T>
 void simt_gemm(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
                cudaStream_t st) {
-  const int64_t sms = uk::sm_count();
-  auto ctas = [&](int bm, int bn) { return (int64_t)((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
-  if (ctas(128, 128) >= sms)
+  const uk::Tile t = uk::sgemm_tile(M, N, uk::sm_count());
+  if (t.bm == 128)
     launch<128, 128, 8, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
-  else if (ctas(64, 64) >= sms)
+  else if (t.bm == 64)
     launch<64, 64, 8, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   else
     launch<32, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);

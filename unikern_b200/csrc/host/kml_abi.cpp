@@ -1,0 +1,81 @@
+// kml_abi.cpp -- C entry points of the host runner (declared in
+// include/unikern_cuda.h): the KML contract queries (no GPU needed) and the
+// nvidia branch of the reference's `run`/`verify` flow.
+#include <cstring>
+#include <sstream>
+#include <string>
+
+#include "kml.hpp"
+#include "runner_cuda.hpp"
+#include "unikern_cuda.h"
+
+namespace {
+
+// copy `s` into out[cap] (always NUL-terminated); UK_EINVAL when it does not fit
+int put(const std::string& s, char* out, size_t cap) {
+  if (out == nullptr || cap == 0) return UK_EINVAL;
+  const size_t n = s.size() < cap - 1 ? s.size() : cap - 1;
+  std::memcpy(out, s.data(), n);
+  out[n] = '\0';
+  return s.size() < cap ? UK_OK : UK_EINVAL;
+}
+
+}  // namespace
+
+extern "C" {
+
+int uk_kml_describe(const char* kml_json, const char* hcs_json, int sms, char* out, size_t out_cap) {
+  if (kml_json == nullptr) {
+    put("kml_json is NULL", out, out_cap);
+    return UK_EINVAL;
+  }
+  std::string err;
+  const auto tree = ukb::kml_import(kml_json, &err);
+  if (!tree) {
+    put(err, out, out_cap);
+    return UK_EINVAL;
+  }
+  std::ostringstream os;
+  const ukb::Workload w = ukb::workload_of(*tree);
+  os << "canonical=" << ukb::canonical_form(*tree) << "\n"
+     << "signature=" << ukb::op_signature(*tree) << "\n"
+     << "ops=" << w.ops << "\n"
+     << "bytes=" << w.bytes << "\n"
+     << "tolerance=" << ukb::tolerance_for(tree->dtype) << "\n";
+  ukb::BackendNvidia be;
+  os << "gap=" << be.capability_gap(*tree) << "\n";
+  if (hcs_json != nullptr) {
+    const auto hcs = ukb::hcs_import(hcs_json, &err);
+    if (!hcs) {
+      put("HCS " + err, out, out_cap);
+      return UK_EINVAL;
+    }
+    os << "hcs_fingerprint=" << ukb::hcs_fingerprint(*hcs) << "\n"
+       << "ledger_key=" << ukb::ledger_key(*hcs, *tree) << "\n";
+    if (be.capability_gap(*tree).empty()) {
+      const ukb::Solution s = ukb::solve_b200(*hcs, *tree, sms > 0 ? sms : (hcs->compute_units > 0 ? hcs->compute_units : 148));
+      os.precision(17);
+      os << "tile=" << s.best.tile_m << "x" << s.best.tile_n << "\n"
+         << "k_block=" << s.best.k_block << "\n"
+         << "stages=" << s.best.stages << "\n"
+         << "c_ms=" << s.c_ms << "\n"
+         << "placement=" << s.placement_record << "\n";
+    }
+  }
+  os << "export=" << ukb::kml_export(*tree);
+  return put(os.str(), out, out_cap);
+}
+
+int uk_run_kml(const char* hcs_json, const char* kml_json, const char* ledger_path, int write_ledger, char* out,
+               size_t out_cap) {
+  if (hcs_json == nullptr || kml_json == nullptr) {
+    put("hcs_json and kml_json are required", out, out_cap);
+    return 2;
+  }
+  std::string transcript;
+  const int rc = ukb::run_kml(hcs_json, kml_json, ledger_path ? ledger_path : "", write_ledger != 0, &transcript);
+  if (out != nullptr && out_cap > 0) put(transcript, out, out_cap);
+  return rc;
+}
+
+}  // extern "C"

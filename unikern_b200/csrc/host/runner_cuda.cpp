@@ -1,0 +1,623 @@
+// runner_cuda.cpp -- the nvidia:cuda backend of the KML runner (see
+// runner_cuda.hpp for the reference interface each part keeps).
+//
+// run_cuda executes a KML tree in process through the library's own C ABI:
+//   1. verify instance: the reference's exact sawtooth operands at its verify
+//      shapes (gemm 256^3, conv 32x32x8 -> 16 with 3x3, reduce 2^20 x 2^-6,
+//      the row ops at the full declared shape), checked on the GPU by the fp64
+//      checker kernels against the dtype's gate (2^-5 fp32, 2^-4 fp16);
+//   2. timing at the declared dims: e2e passes (H2D of the inputs from pinned
+//      host memory, the launch, D2H of the output) and kernel-only launches,
+//      CUDA events on one stream; warm/iters as the reference (2/10, or 1/1
+//      when the payload exceeds 2 GiB; the fp16 gemm and the row ops warm once);
+//   3. the UNIKERN_RESULT line with the reference's tokens.
+// Resident only: a payload above 0.85 x the device's own reported memory is
+// refused (supports_streaming() is false), never silently streamed.
+#include "runner_cuda.hpp"
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <fstream>
+#include <iomanip>
+#include <limits>
+#include <sstream>
+#include <vector>
+
+#include "runner_dev.h"
+#include "unikern_cuda.h"
+
+namespace ukb {
+
+namespace {
+
+int uk_op_of(OpKind k) {
+  switch (k) {
+    case OpKind::Gemm: return UK_OP_GEMM;
+    case OpKind::Conv: return UK_OP_CONV;
+    case OpKind::Reduction: return UK_OP_REDUCE;
+    case OpKind::Softmax: return UK_OP_SOFTMAX;
+    case OpKind::RmsNorm: return UK_OP_RMSNORM;
+    case OpKind::ChannelScale: return UK_OP_CHANNELSCALE;
+  }
+  return -1;
+}
+
+std::string perf_string(const KmlTree& t) {
+  std::string s;
+  for (int i = 0; i < kml_arity(t.op); ++i) s += (i ? "x" : "") + std::to_string(t.dims[i]);
+  return s;
+}
+
+// bytes the declared tree keeps resident on the device while it is timed
+int64_t payload_bytes(const KmlTree& t, size_t reduce_ws) {
+  const int64_t* d = nullptr;
+  int64_t v[6];
+  for (int i = 0; i < 6; ++i) v[i] = t.dims[i];
+  d = v;
+  const int64_t es = dtype_bytes(t.dtype);
+  switch (t.op) {
+    case OpKind::Gemm: return (d[0] * d[2] + d[2] * d[1] + d[0] * d[1]) * es;
+    case OpKind::Conv:
+      return (d[0] * d[1] * d[2] + d[5] * d[3] * d[4] * d[2] + d[5] * (d[0] - d[3] + 1) * (d[1] - d[4] + 1)) * 4;
+    case OpKind::Reduction: return d[0] * 4 + (int64_t)reduce_ws + 4;
+    case OpKind::Softmax: return 2 * d[0] * d[1] * 4;
+    case OpKind::RmsNorm:
+    case OpKind::ChannelScale: return (2 * d[0] * d[1] + d[1]) * 4;
+  }
+  return 0;
+}
+
+// device allocations of one run, residency-probed like the reference's
+// uk_mmalloc (each allocation is one check; a non-device type is a migration)
+struct DevArena {
+  std::vector<void*> dev, host;
+  int checks = 0, migrations = 0;
+  std::string err;
+  ~DevArena() {
+    for (void* p : dev) cudaFree(p);
+    for (void* p : host) cudaFreeHost(p);
+  }
+  void* alloc(size_t bytes, const char* what) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) {
+      cudaGetLastError();
+      err = std::string("cudaMalloc ") + what + " (" + std::to_string(bytes) + " B) failed";
+      return nullptr;
+    }
+    dev.push_back(p);
+    cudaPointerAttributes a{};
+    ++checks;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      ++migrations;
+    }
+    return p;
+  }
+  void* pinned(size_t bytes, const char* what) {
+    void* p = nullptr;
+    if (cudaMallocHost(&p, bytes ? bytes : 16) != cudaSuccess) {
+      cudaGetLastError();
+      err = std::string("cudaMallocHost ") + what + " (" + std::to_string(bytes) + " B) failed";
+      return nullptr;
+    }
+    host.push_back(p);
+    return p;
+  }
+};
+
+// one op invocation through the C ABI
+struct OpCall {
+  OpKind op = OpKind::Gemm;
+  bool f16 = false;
+  int64_t d[6] = {0, 0, 0, 0, 0, 0};
+  void* in0 = nullptr;   // A / X
+  void* in1 = nullptr;   // B / Wt / W / S (null for softmax, reduce)
+  void* out = nullptr;   // C / Y
+  void* ws = nullptr;    // reduce workspace
+  size_t ws_bytes = 0;
+  int launch(cudaStream_t st) const {
+    switch (op) {
+      case OpKind::Gemm:
+        return f16 ? uk_cuda_gemm_f16((const uint16_t*)in0, (const uint16_t*)in1, (uint16_t*)out, (int)d[0],
+                                      (int)d[1], (int)d[2], st)
+                   : uk_cuda_gemm_f32((const float*)in0, (const float*)in1, (float*)out, (int)d[0], (int)d[1],
+                                      (int)d[2], st);
+      case OpKind::Conv:
+        return uk_cuda_conv2d_f32((const float*)in0, (const float*)in1, (float*)out, 1, (int)d[0], (int)d[1],
+                                  (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML, st);
+      case OpKind::Reduction:
+        return uk_cuda_reduce_f32((const float*)in0, (float*)out, 1, d[0], ws, ws_bytes, st);
+      case OpKind::Softmax:
+        return uk_cuda_softmax_f32((const float*)in0, (float*)out, d[0], d[1], st);
+      case OpKind::RmsNorm:
+        // the KML contract's eps (src/codegen_hip.cpp:2162, :2175)
+        return uk_cuda_rmsnorm_f32((const float*)in0, (const float*)in1, (float*)out, d[0], d[1], 1e-6f, st);
+      case OpKind::ChannelScale:
+        return uk_cuda_channelscale_f32((const float*)in0, (const float*)in1, (float*)out, d[0], d[1], st);
+    }
+    return UK_EINVAL;
+  }
+  // element counts of in0 / in1 / out
+  int64_t n_in0() const {
+    switch (op) {
+      case OpKind::Gemm: return d[0] * d[2];
+      case OpKind::Conv: return d[0] * d[1] * d[2];
+      case OpKind::Reduction: return d[0];
+      default: return d[0] * d[1];
+    }
+  }
+  int64_t n_in1() const {
+    switch (op) {
+      case OpKind::Gemm: return d[2] * d[1];
+      case OpKind::Conv: return d[5] * d[3] * d[4] * d[2];
+      case OpKind::RmsNorm:
+      case OpKind::ChannelScale: return d[1];
+      default: return 0;
+    }
+  }
+  int64_t n_out() const {
+    switch (op) {
+      case OpKind::Gemm: return d[0] * d[1];
+      case OpKind::Conv: return d[5] * (d[0] - d[3] + 1) * (d[1] - d[4] + 1);
+      case OpKind::Reduction: return 1;
+      default: return d[0] * d[1];
+    }
+  }
+  size_t es() const { return f16 ? 2 : 4; }
+};
+
+// allocate and fill the operands of `c` with the reference's initialisers
+bool stage_operands(OpCall* c, DevArena* ar, cudaStream_t st, std::string* err) {
+  c->in0 = ar->alloc(c->n_in0() * c->es(), "in0");
+  if (c->n_in1() > 0) c->in1 = ar->alloc(c->n_in1() * c->es(), "in1");
+  c->out = ar->alloc(c->n_out() * c->es(), "out");
+  if (c->op == OpKind::Reduction) {
+    c->ws_bytes = uk_cuda_reduce_workspace_size(1, c->d[0]);
+    if (c->ws_bytes) c->ws = ar->alloc(c->ws_bytes, "workspace");
+  }
+  if (!ar->err.empty()) {
+    *err = ar->err;
+    return false;
+  }
+  const int k0 = c->op == OpKind::Reduction ? UKR_SAW_CONST : UKR_SAW_A;
+  const int k1 = (c->op == OpKind::RmsNorm || c->op == OpKind::ChannelScale) ? UKR_SAW_W : UKR_SAW_B;
+  if (ukr_saw_fill(c->in0, c->n_in0(), k0, c->f16, st) != UK_OK ||
+      (c->in1 && ukr_saw_fill(c->in1, c->n_in1(), k1, c->f16, st) != UK_OK)) {
+    *err = uk_cuda_last_error();
+    return false;
+  }
+  return true;
+}
+
+bool cuda_ok(cudaError_t e, const char* what, std::string* err) {
+  if (e == cudaSuccess) return true;
+  *err = std::string(what) + ": " + cudaGetErrorString(e);
+  return false;
+}
+
+}  // namespace
+
+// ---- backend descriptor --------------------------------------------------------
+
+bool BackendNvidia::available() const {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return false;
+  }
+  return uk_cuda_device_supported() != 0;
+}
+
+std::string BackendNvidia::capability_gap(const KmlTree& t) const {
+  if (t.layout != "NT") return "layout=" + t.layout + " (only NT is implemented)";
+  if (t.dtype == DType::I8) return std::string("dtype=int8 for op=") + op_name(t.op) + " (nvidia:cuda runs fp32 ops and the fp16 gemm)";
+  if (t.dtype == DType::F16 && t.op != OpKind::Gemm)
+    return std::string("dtype=fp16 for op=") + op_name(t.op) + " (nvidia:cuda runs fp16 only for gemm)";
+  if (!t.children.empty()) return "children (a composite tree executes per op; declare each op on its own)";
+  if (t.op == OpKind::Conv && (t.dims[3] > t.dims[0] || t.dims[4] > t.dims[1]))
+    return "conv filter larger than the input";
+  return "";
+}
+
+std::string BackendNvidia::generate(const Solution& s, const Hcs& h, const KmlTree& t) const {
+  std::ostringstream os;
+  os << "// nvidia:cuda: precompiled sm_100a kernels of libunikern_cuda.so (no source is generated)\n"
+     << "// tree " << canonical_form(t) << "\n// device " << h.device << "\n// tile " << s.best.tile_m << "x"
+     << s.best.tile_n << " k_block=" << s.best.k_block << " stages=" << s.best.stages << "\n";
+  return os.str();
+}
+
+// ---- solver ------------------------------------------------------------------
+
+Solution solve_b200(const Hcs& h, const KmlTree& t, int sms) {
+  Solution s;
+  int64_t dims[6];
+  for (int i = 0; i < 6; ++i) dims[i] = t.dims[i];
+  int tile[4] = {0, 0, 0, 0};
+  if (uk_cuda_tile_plan(uk_op_of(t.op), t.dtype == DType::F16, dims, sms, tile) != UK_OK) return s;
+  s.best = {tile[0], tile[1], tile[2], tile[3]};
+  s.feasible_count = 1;
+  // predicted time: compute or device memory, whichever binds, scaled by the
+  // SMs a tile grid leaves idle; plus the host link copies that the measured
+  // (end-to-end) time includes
+  const Workload w = workload_of(t);
+  const double flops = h.flops_gflops * 1e9;
+  const double dev_bw = h.tier_bw(h.unified_memory ? "unified" : "vram") * 1e9;
+  double comp = flops > 0 ? double(w.ops) / flops * 1e3 : 1e18;
+  const double mem = dev_bw > 0 ? double(w.bytes) / dev_bw * 1e3 : 1e18;
+  if (t.op == OpKind::Gemm || t.op == OpKind::Conv) {
+    const int64_t rows = t.op == OpKind::Gemm ? dims[0] : dims[5];
+    const int64_t cols = t.op == OpKind::Gemm ? dims[1] : (dims[0] - dims[3] + 1) * (dims[1] - dims[4] + 1);
+    const int64_t ctas = ((rows + tile[0] - 1) / tile[0]) * ((cols + tile[1] - 1) / tile[1]);
+    const int64_t units = h.compute_units > 0 ? h.compute_units : 148;
+    if (ctas < units) comp *= double(units) / double(ctas > 0 ? ctas : 1);
+  }
+  const double copy = h.unified_memory || h.link_bw_gbps <= 0 ? 0.0 : double(w.bytes) / (h.link_bw_gbps * 1e9) * 1e3;
+  s.c_ms = std::max(comp, mem) + copy;
+  std::ostringstream pr;
+  pr << "placement: resident on " << h.device << " (sm_100a) tile=" << tile[0] << "x" << tile[1]
+     << " k_block=" << tile[2] << " stages=" << tile[3] << " path=pinned-copy";
+  s.placement_record = pr.str();
+  return s;
+}
+
+// ---- ledger --------------------------------------------------------------------
+
+namespace {
+const char kSep = '\t';
+const char* kViolation = "#VIOLATION";
+
+std::vector<std::string> split_tabs(const std::string& line) {
+  std::vector<std::string> f;
+  size_t pos = 0;
+  while (true) {
+    const size_t tab = line.find(kSep, pos);
+    f.push_back(line.substr(pos, tab == std::string::npos ? std::string::npos : tab - pos));
+    if (tab == std::string::npos) break;
+    pos = tab + 1;
+  }
+  return f;
+}
+}  // namespace
+
+std::optional<Solution> FileLedger::lookup(const std::string& key) const {
+  std::ifstream in(path_);
+  std::string line;
+  while (std::getline(in, line)) {
+    const std::vector<std::string> f = split_tabs(line);
+    if (f.size() < 4 || f[0] != key) continue;
+    Solution s;
+    try {
+      s.c_ms = std::stod(f[1]);
+      if (f.size() >= 7) {  // key c_ms measured kernel tm tn placement
+        s.best.tile_m = std::stoi(f[4]);
+        s.best.tile_n = std::stoi(f[5]);
+        s.placement_record = f[6];
+      } else if (f.size() >= 6) {  // key c_ms measured tm tn placement
+        s.best.tile_m = std::stoi(f[3]);
+        s.best.tile_n = std::stoi(f[4]);
+        s.placement_record = f[5];
+      } else {
+        s.placement_record = f[3];
+      }
+    } catch (...) {
+      continue;  // a corrupt row is skipped, never surfaced as a solution
+    }
+    s.from_ledger = true;
+    s.feasible_count = 1;
+    return s;
+  }
+  return std::nullopt;
+}
+
+void FileLedger::commit(const std::string& key, const Solution& s, double measured_ms, double kernel_ms) const {
+  std::ofstream out(path_, std::ios::app);
+  out.precision(std::numeric_limits<double>::max_digits10);
+  out << key << kSep << s.c_ms << kSep << measured_ms << kSep << kernel_ms << kSep << s.best.tile_m << kSep
+      << s.best.tile_n << kSep << s.placement_record << "\n";
+}
+
+void FileLedger::record_violation(const std::string& key, double rate, double threshold, int migrations, int checks,
+                                  unsigned long long vram_free) const {
+  std::ofstream out(path_, std::ios::app);
+  out.precision(std::numeric_limits<double>::max_digits10);
+  out << kViolation << kSep << key << kSep << rate << kSep << threshold << kSep << migrations << kSep << checks
+      << kSep << vram_free << "\n";
+}
+
+int FileLedger::size() const {
+  std::ifstream in(path_);
+  std::string line;
+  int n = 0;
+  while (std::getline(in, line))
+    if (!line.empty() && line.rfind(kViolation, 0) != 0) ++n;
+  return n;
+}
+
+// ---- run_cuda ------------------------------------------------------------------
+
+RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, const std::string& workdir) {
+  (void)sol;
+  (void)hcs;
+  (void)workdir;  // nothing is generated or compiled, so nothing is written
+  RunOutcome r;
+  std::ostringstream log;
+  auto finish = [&]() {
+    r.log = log.str();
+    return r;
+  };
+  BackendNvidia be;
+  if (!be.available()) {
+    log << "nvidia:cuda: no CUDA device of compute capability 10.0 (B200) is visible\n";
+    r.exit_code = 4;
+    return finish();
+  }
+  const std::string gap = be.capability_gap(tree);
+  if (!gap.empty()) {
+    log << "UNSUPPORTED: " << gap << "\n";
+    r.exit_code = 2;
+    return finish();
+  }
+  r.built = true;  // the precompiled sm_100a kernels load on this device
+  size_t fr = 0, tot = 0;
+  cudaMemGetInfo(&fr, &tot);
+  r.vram_free = fr;
+  r.vram_total = tot;
+
+  OpCall timed;
+  timed.op = tree.op;
+  timed.f16 = tree.dtype == DType::F16;
+  for (int i = 0; i < 6; ++i) timed.d[i] = tree.dims[i];
+  const size_t ws = tree.op == OpKind::Reduction ? uk_cuda_reduce_workspace_size(1, tree.dims[0]) : 0;
+  const int64_t payload = payload_bytes(tree, ws);
+  const double payload_mb = double(payload) / (1024.0 * 1024.0);
+  if (double(payload) > 0.85 * double(tot)) {
+    std::ostringstream e;
+    e << "UNIKERN_ERROR what=stream_refused payload_mb=" << std::fixed << std::setprecision(6) << payload_mb
+      << " vram_total=" << tot << " (nvidia:cuda is resident-only: the payload exceeds 0.85 * the device's "
+      << "reported memory and streaming is not implemented; nothing ran)";
+    r.result_line = e.str();
+    log << r.result_line << "\n";
+    r.exit_code = 4;
+    return finish();
+  }
+  const bool big = payload > (int64_t(2) << 30);
+  const bool warm_once = timed.f16 || tree.op == OpKind::Softmax || tree.op == OpKind::RmsNorm ||
+                         tree.op == OpKind::ChannelScale;
+  const int warm = big || warm_once ? 1 : 2, iters = big ? 1 : 10;
+
+  cudaStream_t st = nullptr;
+  std::string err;
+  if (!cuda_ok(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate", &err)) {
+    log << err << "\n";
+    r.exit_code = 4;
+    return finish();
+  }
+  DevArena ar;
+  int rc = UK_OK;
+  bool ok = true;
+
+  // ---- 1. verify instance ----
+  {
+    OpCall v = timed;
+    if (tree.op == OpKind::Gemm) {
+      v.d[0] = v.d[1] = v.d[2] = 256;
+    } else if (tree.op == OpKind::Conv) {
+      const int64_t vd[6] = {32, 32, 8, 3, 3, 16};
+      for (int i = 0; i < 6; ++i) v.d[i] = vd[i];
+    } else if (tree.op == OpKind::Reduction) {
+      v.d[0] = int64_t(1) << 20;
+    }
+    double* worst = static_cast<double*>(ar.alloc(sizeof(double), "max_rel"));
+    ok = worst && stage_operands(&v, &ar, st, &err) &&
+         cuda_ok(cudaMemsetAsync(worst, 0, sizeof(double), st), "memset max_rel", &err);
+    if (ok && (rc = v.launch(st)) != UK_OK) {
+      err = uk_cuda_last_error();
+      ok = false;
+    }
+    if (ok) {
+      switch (tree.op) {
+        case OpKind::Gemm:
+          rc = ukr_check_gemm(v.in0, v.in1, v.out, (int)v.d[0], (int)v.d[1], (int)v.d[2], v.f16, worst, st);
+          break;
+        case OpKind::Conv:
+          rc = ukr_check_conv((const float*)v.in0, (const float*)v.in1, (const float*)v.out, (int)v.d[0],
+                              (int)v.d[1], (int)v.d[2], (int)v.d[3], (int)v.d[4], (int)v.d[5], worst, st);
+          break;
+        case OpKind::Reduction:
+          rc = ukr_check_rows(UKR_OP_REDUCE, (const float*)v.in0, nullptr, (const float*)v.out, 1, v.d[0], 0.0,
+                              worst, st);
+          break;
+        case OpKind::Softmax:
+          rc = ukr_check_rows(UKR_OP_SOFTMAX, (const float*)v.in0, nullptr, (const float*)v.out, v.d[0], v.d[1],
+                              0.0, worst, st);
+          break;
+        case OpKind::RmsNorm:
+          rc = ukr_check_rows(UKR_OP_RMSNORM, (const float*)v.in0, (const float*)v.in1, (const float*)v.out,
+                              v.d[0], v.d[1], (double)1e-6f, worst, st);
+          break;
+        case OpKind::ChannelScale:
+          rc = ukr_check_rows(UKR_OP_CHANNELSCALE, (const float*)v.in0, (const float*)v.in1, (const float*)v.out,
+                              v.d[0], v.d[1], 0.0, worst, st);
+          break;
+      }
+      if (rc != UK_OK) {
+        err = uk_cuda_last_error();
+        ok = false;
+      }
+    }
+    double host_worst = 0;
+    ok = ok && cuda_ok(cudaMemcpyAsync(&host_worst, worst, sizeof(double), cudaMemcpyDeviceToHost, st),
+                       "read max_rel", &err) &&
+         cuda_ok(cudaStreamSynchronize(st), "verify", &err);
+    if (ok) {
+      r.max_rel = host_worst;
+      r.verified = host_worst <= tolerance_for(tree.dtype);
+    }
+    // the verify buffers are released before the timed payload is allocated
+    for (void* p : ar.dev) cudaFree(p);
+    ar.dev.clear();
+  }
+
+  // ---- 2. timing at the declared dims ----
+  if (ok) ok = stage_operands(&timed, &ar, st, &err);
+  void *h0 = nullptr, *h1 = nullptr, *hout = nullptr;
+  const size_t b0 = timed.n_in0() * timed.es(), b1 = timed.n_in1() * timed.es(), bo = timed.n_out() * timed.es();
+  if (ok) {
+    h0 = ar.pinned(b0, "in0");
+    h1 = b1 ? ar.pinned(b1, "in1") : nullptr;
+    hout = ar.pinned(bo, "out");
+    if (!ar.err.empty()) {
+      err = ar.err;
+      ok = false;
+    }
+  }
+  // the host copies hold the same sawtooth values as the device operands
+  ok = ok && cuda_ok(cudaMemcpyAsync(h0, timed.in0, b0, cudaMemcpyDeviceToHost, st), "stage in0", &err) &&
+       (!b1 || cuda_ok(cudaMemcpyAsync(h1, timed.in1, b1, cudaMemcpyDeviceToHost, st), "stage in1", &err)) &&
+       cuda_ok(cudaStreamSynchronize(st), "stage", &err);
+  auto pass = [&]() -> bool {
+    if (!cuda_ok(cudaMemcpyAsync(timed.in0, h0, b0, cudaMemcpyHostToDevice, st), "H2D in0", &err)) return false;
+    if (b1 && !cuda_ok(cudaMemcpyAsync(timed.in1, h1, b1, cudaMemcpyHostToDevice, st), "H2D in1", &err)) return false;
+    if (timed.launch(st) != UK_OK) {
+      err = uk_cuda_last_error();
+      return false;
+    }
+    return cuda_ok(cudaMemcpyAsync(hout, timed.out, bo, cudaMemcpyDeviceToHost, st), "D2H out", &err);
+  };
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (ok) ok = cuda_ok(cudaEventCreate(&e0), "event", &err) && cuda_ok(cudaEventCreate(&e1), "event", &err);
+  for (int i = 0; ok && i < warm; ++i) ok = pass();
+  if (ok) ok = cuda_ok(cudaStreamSynchronize(st), "warm", &err);
+  double total = 0;
+  for (int i = 0; ok && i < iters; ++i) {
+    float ms = 0;
+    ok = cuda_ok(cudaEventRecord(e0, st), "record", &err) && pass() &&
+         cuda_ok(cudaEventRecord(e1, st), "record", &err) && cuda_ok(cudaEventSynchronize(e1), "sync", &err) &&
+         cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
+    total += ms;
+  }
+  if (ok) {
+    r.measured_ms = total / iters;
+    float ms = 0;
+    ok = cuda_ok(cudaEventRecord(e0, st), "record", &err);
+    for (int i = 0; ok && i < iters; ++i)
+      if (timed.launch(st) != UK_OK) {
+        err = uk_cuda_last_error();
+        ok = false;
+      }
+    ok = ok && cuda_ok(cudaEventRecord(e1, st), "record", &err) && cuda_ok(cudaEventSynchronize(e1), "sync", &err) &&
+         cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
+    r.kernel_ms = double(ms) / iters;
+  }
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  const unsigned fault = uk_cuda_pipeline_fault();
+  if (ok && fault != 0) {
+    err = "a bounded wait inside a tensor-core pipeline expired (fault word " + std::to_string(fault) + ")";
+    ok = false;
+  }
+  cudaStreamSynchronize(st);
+  cudaStreamDestroy(st);
+  r.checks = ar.checks;
+  r.migrations = ar.migrations;
+  if (!ok) {
+    log << "nvidia:cuda run failed: " << err << "\n";
+    r.verified = false;
+    r.exit_code = r.migrations > 0 ? 5 : 4;
+    return finish();
+  }
+  r.ran = true;
+  r.exit_code = r.verified ? 0 : 1;
+  std::ostringstream res;
+  res << "UNIKERN_RESULT backend=nvidia:cuda verify=" << (r.verified ? "PASS" : "FAIL") << " max_rel=" << std::scientific
+      << std::setprecision(6) << r.max_rel << std::fixed << std::setprecision(6) << " measured_ms=" << r.measured_ms
+      << " kernel_ms=" << r.kernel_ms << " mode=resident payload_mb=" << payload_mb << " perf=" << perf_string(tree)
+      << (timed.f16 ? " dtype=fp16" : "") << " migrations=" << r.migrations << " checks=" << r.checks
+      << " vram_free=" << r.vram_free << " vram_total=" << r.vram_total;
+  r.result_line = res.str();
+  log << r.result_line << "\n";
+  return finish();
+}
+
+// ---- cmd_run's nvidia branch -------------------------------------------------
+
+int run_kml(const std::string& hcs_json, const std::string& kml_json, const std::string& ledger_path,
+            bool write_ledger, std::string* transcript) {
+  std::ostringstream out;
+  auto done = [&](int rc) {
+    if (transcript) *transcript = out.str();
+    return rc;
+  };
+  std::string err;
+  const std::optional<Hcs> hcs = hcs_import(hcs_json, &err);
+  if (!hcs) {
+    out << "HCS " << err << "\n";
+    return done(2);
+  }
+  const std::optional<KmlTree> tree = kml_import(kml_json, &err);
+  if (!tree) {
+    out << "KML " << err << "\n";
+    return done(2);
+  }
+  BackendNvidia be;
+  const std::string gap = be.capability_gap(*tree);
+  if (!gap.empty()) {
+    out << "UNSUPPORTED: " << gap << " - run/verify execute nothing and write no ledger row for this tree. [backend="
+        << be.name() << "]\n";
+    return done(2);
+  }
+  const std::string key = ledger_key(*hcs, *tree);
+  FileLedger ledger(ledger_path);
+  Solution sol;
+  if (auto rec = ledger_path.empty() ? std::nullopt : ledger.lookup(key)) {
+    sol = *rec;
+    out << "LEDGER HIT  c_cached_ms=" << sol.c_ms << "  tile=" << sol.best.tile_m << "x" << sol.best.tile_n
+        << "  (from ledger)\n"
+        << sol.placement_record << "\n";
+  } else {
+    int sms = 0;
+    if (!be.available()) sms = hcs->compute_units > 0 ? hcs->compute_units : 148;
+    sol = solve_b200(*hcs, *tree, sms);
+    if (sol.feasible_count == 0) {
+      out << "INFEASIBLE: no tile for " << canonical_form(*tree) << "\n";
+      return done(3);
+    }
+  }
+  RunOutcome r = run_cuda(sol, *hcs, *tree, "");
+  out << r.log;
+  out << "RUN " << be.name() << " built=" << (r.built ? "yes" : "no") << " ran=" << (r.ran ? "yes" : "no")
+      << " verified=" << (r.verified ? "PASS" : "FAIL") << " max_rel=" << r.max_rel
+      << " measured_ms=" << r.measured_ms;
+  if (r.migrations >= 0) out << " migrations=" << r.migrations;
+  if (r.checks >= 0) out << " checks=" << r.checks;
+  out << "\n";
+  if (r.migrations > 0 || r.exit_code == 5) {
+    const double rate = r.checks > 0 ? double(r.migrations) / r.checks : 1.0;
+    out << "UNIKERN_VIOLATION what=migration_rate rate=" << rate << " threshold=0 migrations=" << r.migrations
+        << " checks=" << r.checks << " exit=" << r.exit_code << " vram_free=" << r.vram_free
+        << " vram_total=" << r.vram_total << " committed=no\n";
+    if (write_ledger && !ledger_path.empty())
+      ledger.record_violation(key, rate, 0.0, r.migrations, r.checks, r.vram_free);
+    // a re-solve would need a streamed plan, which this backend refuses
+    out << "RESOLVE STOP: nvidia:cuda is resident-only; violation recorded, nothing committed.\n";
+    return done(5);
+  }
+  if (!r.built || !r.ran || !r.verified) {
+    out << "RUN FAILED; solution NOT committed to ledger\n";
+    return done(r.exit_code == 2 ? 2 : 1);
+  }
+  if (!write_ledger || ledger_path.empty()) {
+    out << "VERIFY PASS (no ledger write)\n";
+    return done(0);
+  }
+  ledger.commit(key, sol, r.measured_ms, r.kernel_ms);
+  const double eps_abs = std::fabs(r.measured_ms - sol.c_ms);
+  out << "LEDGER COMMIT predicted_ms=" << sol.c_ms << " measured_ms=" << r.measured_ms << " epsilon_abs=" << eps_abs
+      << " epsilon_rel=" << eps_abs / std::max(sol.c_ms, 1e-9) << "\n";
+  return done(0);
+}
+
+}  // namespace ukb

@@ -1,0 +1,34 @@
+// runner_dev.h -- device helpers of the KML runner (csrc/verify.cu): the
+// reference's sawtooth initialisers as fill kernels and fp64 checker kernels
+// that accumulate the worst per-element relative error into one device double.
+#pragma once
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// initialiser kinds (src/codegen_hip.cpp:604-605, :2167, :2338 of UNIKERN)
+#define UKR_SAW_A 0     // ((i % 17) - 8) * 2^-4   (initA, initX)
+#define UKR_SAW_B 1     // ((i % 13) - 6) * 2^-4   (initB)
+#define UKR_SAW_W 2     // 1 + ((i % 7) - 3) * 2^-4 (initW, initS)
+#define UKR_SAW_CONST 3 // 2^-6 everywhere (the reduce verify instance)
+
+#define UKR_OP_REDUCE 0
+#define UKR_OP_SOFTMAX 1
+#define UKR_OP_RMSNORM 2
+#define UKR_OP_CHANNELSCALE 3
+
+int ukr_saw_fill(void* p, int64_t n, int kind, int f16, void* stream);
+int ukr_check_gemm(const void* A, const void* B, const void* C, int M, int N, int K, int f16, double* worst,
+                   void* stream);
+int ukr_check_conv(const float* X, const float* Wt, const float* Y, int H, int W, int C, int Kh, int Kw, int Oc,
+                   double* worst, void* stream);
+// row ops: REDUCE compares Y[r] with the row sum; the others compare Y[r][c]
+int ukr_check_rows(int op, const float* X, const float* W, const float* Y, int64_t L, int64_t C, double eps,
+                   double* worst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif

@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "uk_common.cuh"
+#include "uk_plan.cuh"
 
 namespace {
 
@@ -287,45 +288,31 @@ void launch_rowop(const float* X, const float* G, float* Y, int64_t L, int64_t C
   k_rowop<OP, THREADS, VPT, W><<<(unsigned)L, THREADS, 0, st>>>(X, G, Y, C, eps);
 }
 
-// pick (THREADS, VPT): the fewest threads that keep <= 8 vectors per thread
+// (THREADS, VPT) from uk::rowop_plan; rows too long for registers stream
 template <int OP, int W>
 bool dispatch_rowop(const float* X, const float* G, float* Y, int64_t L, int64_t C, float eps, cudaStream_t st) {
-  const int64_t nv = C / W;
-#define UK_TRY(T, V)                                        \
-  if (nv <= (int64_t)(T) * (V)) {                           \
-    launch_rowop<OP, T, V, W>(X, G, Y, L, C, eps, st);      \
-    return true;                                            \
+  int t = 0, v = 0;
+  if (uk::rowop_plan(C, W, &t, &v)) {
+#define UK_CASE(T, V)                                     \
+  if (t == (T) && v == (V)) {                             \
+    launch_rowop<OP, T, V, W>(X, G, Y, L, C, eps, st);    \
+    return true;                                          \
   }
-  if constexpr (W == 4) {
-    UK_TRY(32, 1) UK_TRY(32, 2) UK_TRY(64, 2) UK_TRY(128, 2) UK_TRY(128, 4)
-    UK_TRY(256, 4) UK_TRY(256, 8) UK_TRY(512, 8) UK_TRY(512, 16)
-  } else {
-    UK_TRY(32, 1) UK_TRY(64, 2) UK_TRY(128, 4) UK_TRY(256, 4) UK_TRY(256, 8)
+    if constexpr (W == 4) {
+      UK_CASE(32, 1) UK_CASE(32, 2) UK_CASE(64, 2) UK_CASE(128, 2) UK_CASE(128, 4)
+      UK_CASE(256, 4) UK_CASE(256, 8) UK_CASE(512, 8) UK_CASE(512, 16)
+    } else {
+      UK_CASE(32, 1) UK_CASE(64, 2) UK_CASE(128, 4) UK_CASE(256, 4) UK_CASE(256, 8)
+    }
+#undef UK_CASE
   }
-#undef UK_TRY
   k_rowop_stream<OP, W><<<(unsigned)L, 512, 0, st>>>(X, G, Y, C, eps);
   return true;
 }
 
-// reduce plan: shared by the workspace query and the launch
-struct ReducePlan {
-  int mode;  // 0 zero-fill, 1 CTA per row, 2 warp per row, 3 split rows
-  int64_t splits, chunk;
-};
+using uk::ReducePlan;
 
-ReducePlan plan_reduce(int64_t rows, int64_t cols) {
-  if (cols == 0) return {0, 0, 0};
-  const int64_t target = (int64_t)uk::sm_count() * 8;
-  if (rows >= target / 2 || cols < 16384) return {cols >= 1024 ? 1 : 2, 1, cols};
-  int64_t splits = (target + rows - 1) / rows;
-  const int64_t cap = cols / 4096;
-  if (splits > cap) splits = cap;
-  if (splits <= 1) return {1, 1, cols};
-  int64_t chunk = (cols + splits - 1) / splits;
-  chunk = (chunk + 3) / 4 * 4;
-  splits = (cols + chunk - 1) / chunk;
-  return {3, splits, chunk};
-}
+ReducePlan plan_reduce(int64_t rows, int64_t cols) { return uk::plan_reduce(rows, cols, uk::sm_count()); }
 
 // ---------------------------------------------------------------------------
 // Scratch for uk_cuda_reduce_f32_noalloc: the split-row partial sums live in

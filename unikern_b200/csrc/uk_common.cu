@@ -4,6 +4,7 @@
 #include <mutex>
 
 #include "uk_common.cuh"
+#include "uk_plan.cuh"
 
 namespace uk {
 
@@ -73,6 +74,51 @@ int uk_cuda_device_supported(void) {
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   return major == 10 && minor == 0;
+}
+
+int uk_cuda_tile_plan(int op, int f16, const int64_t* dims, int sms, int* out4) {
+  if (dims == nullptr || out4 == nullptr) return uk::fail(UK_EINVAL, "tile_plan: NULL dims or out4");
+  if (sms < 0) return uk::fail(UK_EINVAL, "tile_plan: sms < 0");
+  const int64_t n_sm = sms > 0 ? sms : uk::sm_count();
+  uk::Tile t{0, 0, 0, 0};
+  switch (op) {
+    case UK_OP_GEMM:  // dims M, N, K
+      if (f16 && dims[2] % 8 == 0 && dims[1] % 8 == 0) t = uk::kGemmF16Tile;
+      else t = uk::sgemm_tile(dims[0], dims[1], n_sm);
+      break;
+    case UK_OP_CONV: {  // KML dims H, W, C, Kh, Kw, Oc (one image, valid)
+      const int64_t npix = (dims[0] - dims[3] + 1) * (dims[1] - dims[4] + 1);
+      t = uk::conv_tile(npix, dims[5], n_sm);
+      break;
+    }
+    case UK_OP_REDUCE: {  // dims L: one row of L columns
+      const uk::ReducePlan p = uk::plan_reduce(1, dims[0], n_sm);
+      t = {1, (int)(p.mode == 3 ? p.chunk : dims[0]), 0, (int)(p.mode == 3 ? p.splits : 1)};
+      break;
+    }
+    case UK_OP_SOFTMAX:
+    case UK_OP_RMSNORM: {  // dims L, C: one CTA per row, row in registers
+      int th = 0, v = 0;
+      const int w = dims[1] % 4 == 0 ? 4 : 1;
+      if (uk::rowop_plan(dims[1], w, &th, &v)) t = {1, th * v * w, 0, 1};
+      else t = {1, 512 * w, 0, 2};  // two-pass streaming kernel
+      break;
+    }
+    case UK_OP_CHANNELSCALE: {  // dims L, C: 256 threads over (C/W) x rows, 4 rows each
+      const int w = dims[1] % 4 == 0 ? 4 : 1;
+      const int64_t ncv = (dims[1] + w - 1) / w;
+      const int tx = (int)(ncv < 256 ? ((ncv + 31) / 32) * 32 : 256);
+      t = {(256 / tx) * 4, tx * w, 0, 1};
+      break;
+    }
+    default:
+      return uk::fail(UK_EINVAL, "tile_plan: unknown op %d", op);
+  }
+  out4[0] = t.bm;
+  out4[1] = t.bn;
+  out4[2] = t.bk;
+  out4[3] = t.stages;
+  return UK_OK;
 }
 
 }  // extern "C"

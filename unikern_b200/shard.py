@@ -100,12 +100,20 @@ class GemmAllGather:
     def b_shard(self, B):
         return B[:, self.n0:self.n1]
 
-    def run(self, A, B_shard, C_full, stream=None):
-        import torch.distributed as dist
+    def launch(self, A, B_shard, stream=None):
+        """This rank's GEMM: its column block, stored into every rank's C."""
         abi.check(abi.lib().uk_cuda_gemm_f16_allgather(
             A.data_ptr(), A.stride(0), B_shard.data_ptr(), B_shard.stride(0), self.c_list, self.world, self.ldc,
             self.M, self.n1 - self.n0, self.K, self.n0, abi._stream(stream)))
+
+    def barrier(self):
+        """Stream-ordered: after it, every rank's stores into this rank's C are done."""
+        import torch.distributed as dist
         dist.all_reduce(self.flag, group=self.group)
+
+    def run(self, A, B_shard, C_full, stream=None):
+        self.launch(A, B_shard, stream)
+        self.barrier()
 
     def close(self):
         self.peers.close()
