@@ -182,9 +182,10 @@ def cpu_gemm_f16(M, N, K, budget_s=10.0, rows=None):
         Af = O.f16_to_f32(Ah)
         out = np.zeros((nrows, N), np.float32)
 
-        def work(i):
-            e.emit_gemm_f16_rows(Af[i:i + 1].copy(), out[i:i + 1], 1)
-        dt = run_threads(work, nrows) if nrows <= nt else None
+        def work(t):  # thread t takes rows t, t + nt, ...
+            for i in range(t, nrows, nt):
+                e.emit_gemm_f16_rows(Af[i:i + 1].copy(), out[i:i + 1], 1)
+        dt = run_threads(work, min(nt, nrows))
     else:
         t0 = time.perf_counter()
         O.gemm_f16(np.vstack([Ah, np.zeros((0, K), np.uint16)]), Bh, rows=(0, nrows), threads=nt)
@@ -199,7 +200,7 @@ def cpu_rowop(op, L, C, budget_rows=None):
     import numpy as np
     from oracle import oracle as O
     nt = cpu_threads()
-    rows = budget_rows or max(nt * 16, 256)
+    rows = budget_rows or L  # the whole workload: it takes well under a minute on the host
     rng = np.random.default_rng(6)
     X = rng.normal(0, 1, (rows, C)).astype(np.float32)
     W = rng.normal(1, 0.1, C).astype(np.float32)
@@ -236,7 +237,7 @@ def cpu_rowop(op, L, C, budget_rows=None):
     dt = run_threads(work, nt)
     nbytes = rows * C * 4 * (1 if op == "reduce" else 2)
     return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": nt, "kind": kind,
-            "sample": "%d of %d rows (C=%d), %.2f s%s" % (rows, L, C, dt,
+            "sample": "%d of %d rows (C=%d, one contiguous block of rows per thread), %.2f s%s" % (rows, L, C, dt,
                                                            "; eps fixed at 1e-6 in the reference" if op == "rmsnorm" else ""),
             "seconds": dt}
 
@@ -432,13 +433,21 @@ def bench_decode(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
     return {"ms": ms, "value": nbytes / ms / 1e6, "bytes_per_step": nbytes, "batch": Bt}
 
 
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture of `python bench.py --op <op> --steps 2 --warmup 3 --no-cpu` with
+# --metrics dram__bytes_read.sum,dram__bytes_write.sum (profiles/dram_traffic_per_kernel.md)
+NCU_TRAFFIC = {
+    "gemm_f16_8192x8192x8192_n1": 994161664 + 127519488,
+    "rowop_reduce": 536887296 + 3104256,
+    "rowop_rmsnorm": 536972800 + 480955136,
+    "rowop_softmax": 536904448 + 484363008,
+    "rowop_channelscale": 537094912 + 489366272,
+    "rowop_reduce_scalar": 536998144 + 3074048,
+}
+
+
 def traffic_for(kernel_key):
-    p = ROOT / "profiles" / "ncu_traffic.json"
-    if not p.exists():
-        return None
-    d = json.loads(p.read_text())
-    v = d.get(kernel_key)
-    return v.get("bytes_per_launch") if isinstance(v, dict) else None
+    return NCU_TRAFFIC.get(kernel_key)
 
 
 def roofline(bound, achieved, pk, traffic=None):
@@ -576,7 +585,7 @@ def main():
     if "allgather_max_abs_diff" in g:
         line["config"]["allgather_check_max_abs_diff"] = g["allgather_max_abs_diff"]
     if world == 1 and not args.no_cpu:
-        cb = cpu_gemm_f16(M, N, K)
+        cb = cpu_gemm_f16(M, N, K, rows=10 * cpu_threads())  # ~10 s of host work
         line["cpu_baseline"] = {k: (round(v, 6) if isinstance(v, float) else v) for k, v in cb.items()
                                 if k != "seconds"}
     if ops:

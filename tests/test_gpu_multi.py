@@ -1,5 +1,8 @@
-"""Multi-GPU parity: the N-sharded f16 GEMM with the all-gather fused into
-its epilogue, on 2 GPUs (skipped where fewer GPUs are visible)."""
+"""Multi-GPU parity on 2 GPUs (skipped where fewer GPUs are visible): the
+N-sharded f16 GEMM with the all-gather fused into its epilogue, and the
+batch-sharded conv with the NCCL all-gather of Y.  Each worker compares every
+rank's full output with a single-GPU run of the same inputs."""
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -9,14 +12,22 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_gemm_allgather_two_gpus_matches_single_gpu():
+def _torchrun(worker, port):
     import torch
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 GPUs, %d visible" % n)
-    worker = Path(__file__).with_name("multigpu_gemm_worker.py")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29517", str(worker)]
-    r = subprocess.run(cmd, capture_output=True, text=True, env={**__import__("os").environ, "NCCL_NVLS_ENABLE": "0"})
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=%d" % port,
+           str(Path(__file__).with_name(worker))]
+    r = subprocess.run(cmd, capture_output=True, text=True, env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
     print(r.stdout[-3000:], r.stderr[-3000:])
     assert r.returncode == 0
+
+
+def test_gemm_allgather_two_gpus_matches_single_gpu():
+    _torchrun("multigpu_gemm_worker.py", 29517)
+
+
+def test_conv_batch_shard_two_gpus_matches_single_gpu():
+    _torchrun("multigpu_conv_worker.py", 29518)

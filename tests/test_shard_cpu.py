@@ -62,3 +62,45 @@ def test_handle_exchange_gloo_world2():
     for rank, got, blocks in results:
         assert got == [(b"handle-0", 0), (b"handle-1", 16)]
         assert blocks == [(0, 4096), (4096, 8192)]
+
+
+@pytest.mark.parametrize("N,world", [(32, 1), (32, 2), (32, 8), (7, 3), (2, 4), (33, 8)])
+def test_batch_split_partitions_exactly(N, world):
+    blocks = [shard.batch_split(N, world, r) for r in range(world)]
+    assert blocks[0][0] == 0 and blocks[-1][1] == N
+    for (a0, a1), (b0, b1) in zip(blocks, blocks[1:]):
+        assert a1 == b0
+    sizes = [b - a for a, b in blocks]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def _conv_worker(rank, world, port, N, q):
+    import torch
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        plan = shard.ConvBatchShard(N, 4, 6, 6, 3, 3, 3, 1, None)
+        Y = torch.full((N, 3, 6, 6), float("nan"))
+        # stand-in for this rank's conv: its images carry their own index
+        for b in range(plan.b0, plan.b1):
+            Y[b] = b
+        plan.gather(Y)
+        q.put((rank, Y[:, 0, 0, 0].tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("N", [8, 5])  # equal blocks (in place) and unequal (staging)
+def test_conv_batch_gather_gloo_world2(N):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_conv_worker, args=(r, 2, port, N, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, col in results:
+        assert col == [float(b) for b in range(N)]

@@ -117,3 +117,79 @@ class GemmAllGather:
 
     def close(self):
         self.peers.close()
+
+
+def batch_split(N: int, world: int, rank: int):
+    """[b0, b1): the contiguous block of images owned by `rank` (as even as
+    possible; the first N % world ranks take one more)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad rank %d of %d" % (rank, world))
+    per, extra = divmod(N, world)
+    b0 = rank * per + min(rank, extra)
+    return b0, b0 + per + (1 if rank < extra else 0)
+
+
+class ConvBatchShard:
+    """conv2d (NCHW, stride 1, zero padding, fused per-channel scale) over
+    `world` GPUs: the batch is split into contiguous image blocks, weights and
+    scale are replicated, and the output is all-gathered so every rank holds
+    the full Y[N][Oc][Ho][Wo].  Images are independent, so the only exchange is
+    the gather (NCCL over NVLink): in place into Y when the blocks are equal,
+    through a padded staging buffer otherwise."""
+
+    def __init__(self, N, Cc, H, W, Oc, Kh, Kw, pad, group=None):
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.N, self.C, self.H, self.W, self.Oc, self.Kh, self.Kw, self.pad = N, Cc, H, W, Oc, Kh, Kw, pad
+        self.Ho, self.Wo = H + 2 * pad - Kh + 1, W + 2 * pad - Kw + 1
+        self.blocks = [batch_split(N, self.world, r) for r in range(self.world)]
+        self.b0, self.b1 = self.blocks[self.rank]
+        self.even = len({b1 - b0 for b0, b1 in self.blocks}) == 1
+        self._stage = None
+        self.launches_per_step = 1
+
+    def describe(self):
+        return "batch-sharded over %d GPUs (%d images each), NCCL all-gather of Y" % (self.world, self.b1 - self.b0)
+
+    def x_shard(self, X):
+        return X[self.b0:self.b1]
+
+    def launch(self, x_shard, Wt, Y, scale=None, stream=None):
+        """This rank's images into its block of Y."""
+        n = self.b1 - self.b0
+        if n:
+            abi.conv2d(x_shard, Wt, Y[self.b0:self.b1], n, self.H, self.W, self.C, self.Kh, self.Kw, self.Oc,
+                       self.pad, scale, abi.UK_CONV_NCHW, stream)
+
+    def gather(self, Y):
+        """Every rank's block into every rank's Y."""
+        import torch
+        import torch.distributed as dist
+        if self.world == 1:
+            return
+        def gather_into(out, mine):
+            # NCCL gathers in place (the input is this rank's slot of the
+            # output); gloo, used by the CPU tests, takes a list and a copy
+            if out.is_cuda:
+                dist.all_gather_into_tensor(out, mine, group=self.group)
+            else:
+                dist.all_gather(list(out.split(mine.shape[0])), mine.clone(), group=self.group)
+
+        if self.even:
+            gather_into(Y, Y[self.b0:self.b1])
+            return
+        mx = max(b1 - b0 for b0, b1 in self.blocks)
+        if self._stage is None:
+            self._stage = torch.empty((self.world * mx,) + tuple(Y.shape[1:]), dtype=Y.dtype, device=Y.device)
+        mine = self._stage[self.rank * mx:(self.rank + 1) * mx]
+        mine[: self.b1 - self.b0].copy_(Y[self.b0:self.b1])
+        gather_into(self._stage, mine)
+        for r, (b0, b1) in enumerate(self.blocks):
+            if r != self.rank and b1 > b0:
+                Y[b0:b1].copy_(self._stage[r * mx:r * mx + b1 - b0])
+
+    def run(self, x_shard, Wt, Y, scale=None, stream=None):
+        self.launch(x_shard, Wt, Y, scale, stream)
+        self.gather(Y)
