@@ -410,26 +410,25 @@ def bench_gemm_f32(ctx, steps, warmup, M=512, N=512, K=512):
 
 
 def bench_decode(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
-    """RMSNorm [B x 4096] -> f16 skinny GEMM [B x 4096] x [4096 x 14336] ->
-    softmax over [B*32 x 8192]; HBM-bound on the 112 MiB of weights."""
+    """Decode-layer chain: RMSNorm [B x 4096] fused into
+    the f16 skinny GEMM [B x 4096] x [4096 x 14336] (one kernel), then softmax
+    over [B*32 x 8192] scores.  HBM-bound: the 112 MiB of weights dominate."""
     import unikern_b200.abi as abi
     torch = ctx.torch
     x = gen(torch, (Bt, H), "normal", 13)
     g = gen(torch, (H,), "normal", 14, None, 0.1) + 1.0
-    xn = torch.empty((Bt, H), device="cuda")
-    xh = torch.empty((Bt, H), dtype=torch.float16, device="cuda")
     Wt = gen(torch, (H, F), "normal", 15, torch.float16, 0.02)
     out = torch.empty((Bt, F), dtype=torch.float16, device="cuda")
     sc = gen(torch, (Bt * heads, S), "normal", 16)
     pr = torch.empty_like(sc)
 
+    ws = abi.decode_workspace(Bt, H)
+
     def step():
-        abi.rmsnorm(x, g, xn, 1e-5)
-        xh.copy_(xn)
-        abi.gemm_f16(xh, Wt, out)
+        abi.decode_rmsnorm_gemm(x, g, Wt, out, 1e-5, ws)
         abi.softmax(sc, pr)
     ms = ctx.time_steps(step, steps, warmup)
-    nbytes = 2 * Bt * H * 4 + H * F * 2 + Bt * (H + F) * 2 + 2 * Bt * heads * S * 4
+    nbytes = Bt * H * 4 + H * 4 + H * F * 2 + Bt * F * 2 + 2 * Bt * heads * S * 4
     return {"ms": ms, "value": nbytes / ms / 1e6, "bytes_per_step": nbytes, "batch": Bt}
 
 

@@ -143,6 +143,27 @@ int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_t* B, int64
 int uk_cuda_gemm_f16_allgather(const uint16_t* A, int64_t lda, const uint16_t* B_shard, int64_t ldb,
                                uint16_t* const* C_list, int n_c, int64_t ldc, int M, int N_shard, int K,
                                int64_t col_offset, void* stream);
+/* ---- decode layer: RMSNorm -> skinny f16 GEMM ----------------------------
+ * For B <= 32 token rows X[B][K] (fp32, contiguous) and this rank's column
+ * block W[K][N_shard] (f16, leading dimension ldw) of the layer weight:
+ *   Y[b][col_offset + n] = f16( sum_k f16((X[b][k] * rms_b) * gamma[k]) * W[k][n] ),
+ *   rms_b = 1 / sqrt(sum_k X[b][k]^2 / K + eps),  fp32 accumulation,
+ * written into all n_y (<= 8) copies Y_list[i][B][ldy] (Y_list[0] on this GPU,
+ * the others peers' buffers from uk_cuda_ipc_import: the weight-column
+ * sharding of the decode layer with its all-gather fused into the store).
+ * The normalised f16 rows go to the caller's workspace of
+ * uk_cuda_decode_workspace_size(B, K) bytes.  Needs K a multiple of 8, ldw a
+ * multiple of 8, X, gamma, W and the workspace 16-byte aligned.
+ * Deterministic.  Two kernels (the norm, then tcgen05 tiles of W streamed by
+ * TMA, K split over a thread-block cluster when N_shard is narrow) overlapped
+ * by programmatic dependent launch.  Replaces the RMSNorm -> fp16 GEMM steps
+ * of the decode chain (uk_rmsnorm src/codegen_hip.cpp:2154-2164 and uk_gemm_h
+ * :1777-1808 run back to back). */
+size_t uk_cuda_decode_workspace_size(int B, int K);
+int uk_cuda_decode_rmsnorm_gemm_f16(const float* X, const float* gamma, float eps, const uint16_t* W, int64_t ldw,
+                                    uint16_t* const* Y_list, int n_y, int64_t ldy, int B, int N_shard, int K,
+                                    int64_t col_offset, void* workspace, size_t workspace_bytes, void* stream);
+
 /* CUDA IPC: export a device buffer (handle of uk_cuda_ipc_handle_size() bytes
  * plus the offset of `ptr` inside its allocation), open a peer's export as a
  * pointer on this device, close it.  No reference counterpart. */

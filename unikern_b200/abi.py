@@ -38,6 +38,9 @@ PROTOTYPES = {
     "uk_cuda_ipc_export": (i32, [vp, vp, C.POINTER(C.c_uint64)]),
     "uk_cuda_ipc_import": (i32, [vp, C.c_uint64, C.POINTER(vp)]),
     "uk_cuda_ipc_close": (i32, [vp, C.c_uint64]),
+    "uk_cuda_decode_workspace_size": (sz, [i32, i32]),
+    "uk_cuda_decode_rmsnorm_gemm_f16": (i32, [vp, vp, f32, vp, i64, C.POINTER(vp), i32, i64, i32, i32, i32, i64,
+                                               vp, sz, vp]),
     "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
@@ -129,6 +132,22 @@ def gemm_f16(A, B, Cm, stream=None):
 def conv2d(X, Wt, Y, N, H, W, Cc, Kh, Kw, Oc, pad=0, scale=None, layout=UK_CONV_NCHW, stream=None):
     check(lib().uk_cuda_conv2d_f32(_p(X), _p(Wt), _p(Y), N, H, W, Cc, Kh, Kw, Oc, pad, _p(scale), layout,
                                    _stream(stream)))
+
+
+def decode_workspace(B, K):
+    import torch
+    n = lib().uk_cuda_decode_workspace_size(B, K)
+    return torch.empty((max(n, 16) + 15) // 16 * 4, dtype=torch.float32, device="cuda")
+
+
+def decode_rmsnorm_gemm(X, gamma, W, Y, eps=1e-5, workspace=None, stream=None):
+    """Y[B][N] (f16) = f16(rmsnorm(X) * gamma) @ W (f16 [K][N])."""
+    B, K = X.shape
+    N = W.shape[1]
+    ws = workspace if workspace is not None else decode_workspace(B, K)
+    ys = (vp * 1)(Y.data_ptr())
+    check(lib().uk_cuda_decode_rmsnorm_gemm_f16(_p(X), _p(gamma), eps, _p(W), W.stride(0), ys, 1, Y.stride(0), B, N,
+                                                K, 0, _p(ws), ws.numel() * ws.element_size(), _stream(stream)))
 
 
 # ---- KML runner (host side) -----------------------------------------------------

@@ -1,0 +1,448 @@
+// decode.cu -- the decode-layer chain's GEMM with the RMSNorm in front of it:
+//
+//   Y(f16)[b][n] = sum_k f16((X[b][k] * rms_b) * gamma[k]) * W[k][n],
+//   rms_b = 1 / sqrt(sum_k X[b][k]^2 / K + eps),   fp32 accumulation,
+//
+// for a handful of token rows b < B <= 32 (decode) against a large f16
+// weight W[K][N] (Llama-3-8B: 4096 x 14336, 112 MiB).  The op is bound by
+// streaming W from HBM once; everything is arranged around that.
+//
+// Two kernels, overlapped by programmatic dependent launch:
+// * k_rms_f16: one CTA per token row forms rms_b and writes the normalised
+//   row as f16 into the caller's workspace Xn[B][K] (B*K*2 bytes).  It lets
+//   the GEMM launch at once, so the GEMM's first weight loads are in flight
+//   while the norm runs.
+// * k_skinny_gemm: tensor cores on the transposed product
+//   D[n][b] = W^T[n][k] * Xn^T[k][b]: a 128-column slice of W is the UMMA A
+//   operand (M = 128, MN-major, loaded straight from row-major W by TMA),
+//   the normalised tokens are the B operand (N = 32, K-major, rows >= B
+//   zero-filled by TMA), the accumulator is 128 TMEM lanes x 32 columns.  One
+//   thread streams W and Xn through an 8-stage ring (20 KiB per 64-deep k
+//   block), one thread issues the MMAs, so each SM keeps ~160 KiB of W in
+//   flight.  When N gives too few 128-column tiles to fill the GPU (a
+//   weight-column shard on 8 GPUs: 14 tiles), K is split over a
+//   thread-block cluster and the partial tiles are summed through
+//   distributed shared memory in a fixed rank order (deterministic).
+//   The f16 result can be stored into up to 8 copies of Y (other GPUs'
+//   buffers over NVLink): the weight-column sharding of the decode layer with
+//   its all-gather fused into the store.
+//
+// Every mbarrier wait is bounded (2 s); a timeout records a bit in this
+// file's fault word (read through uk_cuda_pipeline_fault) and every CTA still
+// passes every cluster barrier, so no peer is left waiting.  TMA loads are
+// plain single-CTA loads of this GPU's memory; nothing uses multicast.
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "sm100_ptx.cuh"
+#include "uk_common.cuh"
+
+namespace uk {
+__device__ unsigned int g_decode_fault = 0;
+}  // namespace uk
+
+namespace {
+
+constexpr int TM = 128;        // W columns per tile (UMMA M)
+constexpr int BP = 32;         // token rows, zero-padded (UMMA N)
+constexpr int BK = 64;         // K per k-block (one 128-byte swizzle row of f16)
+#ifndef UK_DECODE_STAGES
+#define UK_DECODE_STAGES 8
+#endif
+#ifndef UK_DECODE_MIN_CTAS
+#define UK_DECODE_MIN_CTAS 100
+#endif
+constexpr int STAGES = UK_DECODE_STAGES;
+constexpr int CL_MAX = 16;     // CTAs per cluster (K split)
+constexpr int THREADS = 128;   // 4 warps = the 4 TMEM lane quadrants
+constexpr int MAX_OUT = 8;
+constexpr int W_BOX = BK * 64 * 2;        // 8 KiB: 64 k rows x 64 W columns
+constexpr int W_BLOCK = 2 * W_BOX;        // 16 KiB per k-block
+constexpr int X_BLOCK = BP * BK * 2;      // 4 KiB per k-block
+constexpr int STAGE_BYTES = W_BLOCK + X_BLOCK;
+constexpr int RED_BYTES = TM * BP * 4;    // 16 KiB: this CTA's fp32 partial tile
+constexpr uint32_t IDESC = uk_idesc_f16_ab(TM, BP, /*A MN-major*/ 1, /*B K-major*/ 0);
+constexpr uint64_t WAIT_NS = 2000000000ull;
+
+struct YList {
+  uint16_t* y[MAX_OUT];  // y[0] on this GPU; y[1..] other GPUs' copies (same layout)
+  int n;
+};
+
+struct Ctl {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+  int acc_ok;
+};
+
+// the fp32 partial tile of a K-split cluster reuses the ring (all loads have
+// landed once the last MMA completed)
+static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "partial tile fits in the ring");
+constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(Ctl);
+static_assert(SMEM_BYTES <= 232448, "shared memory per block on sm_100");
+
+__device__ __forceinline__ void fault(Ctl* ctl, unsigned bit) {
+  atomicOr(&uk::g_decode_fault, bit);
+  ctl->abort = 1;
+}
+
+// ---- 1. RMSNorm into f16 ------------------------------------------------------
+constexpr int RMS_THREADS = 256;
+
+__global__ void __launch_bounds__(RMS_THREADS) k_rms_f16(const float* __restrict__ X, const float* __restrict__ gamma,
+                                                         float eps, __half* __restrict__ Xn, int K) {
+  uk_pdl_launch_dependents();  // the GEMM may start streaming W now
+  __shared__ float red[33];
+  const int b = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(X + (int64_t)b * K);
+  const float4* gr = reinterpret_cast<const float4*>(gamma);
+  float ss = 0.f;
+  for (int k4 = threadIdx.x; k4 < K / 4; k4 += RMS_THREADS) {
+    const float4 v = __ldg(xr + k4);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = uk_block_sum<RMS_THREADS>(ss, red);
+  const float r = 1.0f / sqrtf(ss / (float)K + eps);
+  uint2* out = reinterpret_cast<uint2*>(Xn + (int64_t)b * K);
+  for (int k4 = threadIdx.x; k4 < K / 4; k4 += RMS_THREADS) {
+    const float4 v = __ldg(xr + k4), g = __ldg(gr + k4);
+    __half2 h0 = __floats2half2_rn((v.x * r) * g.x, (v.y * r) * g.y);
+    __half2 h1 = __floats2half2_rn((v.z * r) * g.z, (v.w * r) * g.w);
+    out[k4] = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+  }
+}
+
+// ---- 2. skinny GEMM -------------------------------------------------------------
+__global__ void __launch_bounds__(THREADS)
+    k_skinny_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, YList out,
+                  int64_t ldy, int B, int N, int K, int64_t col_offset, int kb_per_cta) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* red = smem;
+  Ctl* ctl = (Ctl*)(smem + (size_t)STAGES * STAGE_BYTES);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t crank = uk_cluster_ctarank();
+  const uint32_t csize = gridDim.x;  // the cluster spans grid x (K split)
+  const int n0 = blockIdx.y * TM;
+  const int kb_total = (K + BK - 1) / BK;
+  const int kb0 = (int)crank * kb_per_cta;
+  const int nkb = max(0, min(kb_per_cta, kb_total - kb0));
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      uk_mbar_init(&ctl->full[s], 1);
+      uk_mbar_init(&ctl->empty[s], 1);
+    }
+    uk_mbar_init(&ctl->mma_done, 1);
+    ctl->abort = 0;
+    ctl->acc_ok = 0;
+    uk_fence_mbar_init();
+    uk_tma_prefetch_desc(&tmW);
+    uk_tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) {
+    uk_tmem_alloc(&ctl->tmem_base, 32);
+    uk_tmem_relinquish();
+  }
+  uk_tc_fence_before();
+  __syncthreads();
+  uk_tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (tid == 0) {
+    // ---- producer: W does not depend on the norm kernel, Xn does ----
+    const int pre = min(STAGES, nkb);
+    for (int i = 0; i < pre; ++i) {
+      uint8_t* st = smem + (size_t)i * STAGE_BYTES;
+      uk_mbar_expect_tx(&ctl->full[i], STAGE_BYTES);
+      uk_tma_load_2d(st, &tmW, &ctl->full[i], n0, (kb0 + i) * BK);
+      uk_tma_load_2d(st + W_BOX, &tmW, &ctl->full[i], n0 + 64, (kb0 + i) * BK);
+    }
+    uk_pdl_wait();  // Xn is complete and visible from here on
+    for (int i = 0; i < pre; ++i)
+      uk_tma_load_2d(smem + (size_t)i * STAGE_BYTES + W_BLOCK, &tmX, &ctl->full[i], (kb0 + i) * BK, 0);
+    for (int i = pre; i < nkb; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+      if (!uk_mbar_wait(&ctl->empty[s], ph ^ 1u, &ctl->abort, WAIT_NS)) {
+        fault(ctl, UK_FAULT_PRODUCER);
+        break;
+      }
+      uint8_t* st = smem + (size_t)s * STAGE_BYTES;
+      uk_mbar_expect_tx(&ctl->full[s], STAGE_BYTES);
+      uk_tma_load_2d(st, &tmW, &ctl->full[s], n0, (kb0 + i) * BK);
+      uk_tma_load_2d(st + W_BOX, &tmW, &ctl->full[s], n0 + 64, (kb0 + i) * BK);
+      uk_tma_load_2d(st + W_BLOCK, &tmX, &ctl->full[s], (kb0 + i) * BK, 0);
+    }
+  } else if (tid == 32) {
+    // ---- MMA issuer ----
+    bool ok = true;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+      if (!uk_mbar_wait(&ctl->full[s], ph, &ctl->abort, WAIT_NS)) {
+        fault(ctl, UK_FAULT_MMA);
+        ok = false;
+        break;
+      }
+      uk_tc_fence_after();
+      const uint32_t aw = uk_smem_u32(smem + (size_t)s * STAGE_BYTES);
+      const uint32_t ax = aw + W_BLOCK;
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) {
+        // W: MN-major, the two 64-column chunks 8 KiB apart (LBO), 8-row K
+        // groups 1 KiB apart (SBO), +16 rows (2 KiB) per 16 K
+        const uint64_t ad = uk_desc_sw128(aw + k * 2048, W_BOX, 1024);
+        // Xn: K-major, +32 bytes per 16 K inside the swizzle atom
+        const uint64_t bd = uk_desc_sw128(ax + k * 32, 16, 1024);
+        uk_umma_f16(tmem, ad, bd, IDESC, (i > 0 || k > 0) ? 1u : 0u);
+      }
+      uk_umma_commit(&ctl->empty[s]);  // frees the stage when these MMAs finish
+    }
+    if (nkb > 0) {
+      // arrives once every MMA issued above has finished (also after a
+      // timeout, so TMEM is never released under an MMA in flight)
+      uk_umma_commit(&ctl->mma_done);
+      if (!uk_mbar_wait(&ctl->mma_done, 0, nullptr, WAIT_NS)) fault(ctl, UK_FAULT_TEARDOWN);
+      else ctl->acc_ok = ok ? 1 : 0;
+    }
+  }
+  uk_tc_fence_before();
+  __syncthreads();
+  uk_tc_fence_after();
+
+  // ---- epilogue: lane m of the accumulator is W column n0 + m ----
+  const int m = warp * 32 + lane;
+  uint32_t v[32];
+  if (ctl->acc_ok) {
+    uk_tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), v);
+    uk_tmem_ld_wait();
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0u;
+  }
+  if (csize == 1) {
+    const int n = n0 + m;
+    if (n < N) {
+#pragma unroll
+      for (int b = 0; b < BP; ++b) {
+        if (b < B) {
+          const uint16_t h = __half_as_ushort(__float2half_rn(__uint_as_float(v[b])));
+          const int64_t off = (int64_t)b * ldy + col_offset + n;
+          for (int o = 0; o < out.n; ++o) out.y[o][off] = h;
+        }
+      }
+    }
+  } else {
+    // partial tile -> shared memory (16-byte chunk c of row m at
+    // m * 128 + ((c ^ (m & 7)) * 16)), then this CTA's slice of rows is summed
+    // over the cluster in rank order
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(red + m * 128 + ((c ^ (m & 7)) * 16)) =
+          make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    uk_cluster_sync();
+    const int rows = TM / (int)csize;
+    const int m_lo = (int)crank * rows;
+    for (int idx = tid; idx < rows * 8; idx += THREADS) {
+      const int mm = m_lo + idx % rows, c = idx / rows;
+      const uint32_t a = uk_smem_u32(red + mm * 128 + ((c ^ (mm & 7)) * 16));
+      float4 part[CL_MAX];
+#pragma unroll
+      for (int r = 0; r < CL_MAX; ++r)
+        if (r < (int)csize) part[r] = uk_ld_dsmem_f32x4(uk_mapa(a, (uint32_t)r));
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < CL_MAX; ++r)
+        if (r < (int)csize) {
+          s.x += part[r].x;
+          s.y += part[r].y;
+          s.z += part[r].z;
+          s.w += part[r].w;
+        }
+      const int n = n0 + mm;
+      const float sv[4] = {s.x, s.y, s.z, s.w};
+      if (n < N) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int b = c * 4 + j;
+          if (b < B) {
+            const uint16_t h = __half_as_ushort(__float2half_rn(sv[j]));
+            const int64_t off = (int64_t)b * ldy + col_offset + n;
+            for (int o = 0; o < out.n; ++o) out.y[o][off] = h;
+          }
+        }
+      }
+    }
+    uk_cluster_sync();  // no CTA leaves while a peer still reads its shared memory
+  }
+  if (out.n > 1) __threadfence_system();
+
+  uk_tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    uk_tc_fence_after();
+    uk_tmem_dealloc(tmem, 32);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+int make_map_f16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+                 uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return uk::fail(UK_ECUDA, "decode_rmsnorm_gemm: cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult cr = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return uk::fail(UK_ECUDA, "decode_rmsnorm_gemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
+  return UK_OK;
+}
+
+}  // namespace
+
+namespace uk {
+
+// fault bits of the decode kernels since the last call (clears them)
+unsigned decode_fault_take() {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_decode_fault, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  const unsigned zero = 0;
+  cudaMemcpyToSymbol(g_decode_fault, &zero, sizeof(zero));
+  return v;
+}
+
+}  // namespace uk
+
+extern "C" size_t uk_cuda_decode_workspace_size(int B, int K) {
+  if (B < 1 || K < 1) return 0;
+  return ((size_t)B * (size_t)K * 2 + 255) / 256 * 256;
+}
+
+extern "C" int uk_cuda_decode_rmsnorm_gemm_f16(const float* X, const float* gamma, float eps, const uint16_t* W,
+                                               int64_t ldw, uint16_t* const* Y_list, int n_y, int64_t ldy, int B,
+                                               int N_shard, int K, int64_t col_offset, void* workspace,
+                                               size_t workspace_bytes, void* stream) {
+  if (B < 1 || B > BP) return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: B=%d token rows (1..%d)", B, BP);
+  if (K <= 0 || K % 8 != 0) return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: K=%d must be a positive multiple of 8", K);
+  if (N_shard < 0 || ldw < N_shard || ldw % 8 != 0)
+    return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: N_shard=%d, ldw=%lld (ldw >= N_shard, multiple of 8)", N_shard,
+                    (long long)ldw);
+  if (col_offset < 0 || col_offset + N_shard > ldy)
+    return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: columns [%lld, %lld) outside ldy=%lld", (long long)col_offset,
+                    (long long)(col_offset + N_shard), (long long)ldy);
+  if (!(eps >= 0.f)) return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: eps must be >= 0");
+  if (Y_list == nullptr || n_y < 1 || n_y > MAX_OUT)
+    return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: 1..%d outputs, got %d", MAX_OUT, n_y);
+  const size_t need = uk_cuda_decode_workspace_size(B, K);
+  if (workspace == nullptr || workspace_bytes < need)
+    return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: needs a %zu-byte workspace (uk_cuda_decode_workspace_size)",
+                    need);
+  if (N_shard == 0) return UK_OK;
+  if (int rc = uk::check_device_ptr(X, "X")) return rc;
+  if (int rc = uk::check_device_ptr(gamma, "gamma")) return rc;
+  if (int rc = uk::check_device_ptr(W, "W")) return rc;
+  if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
+  if (int rc = uk::check_device_ptr(Y_list[0], "Y_list[0]")) return rc;
+  if (!uk::aligned16(X) || !uk::aligned16(gamma) || !uk::aligned16(W) || !uk::aligned16(workspace))
+    return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: X, gamma, W and the workspace must be 16-byte aligned");
+  YList out{};
+  for (int i = 0; i < n_y; ++i) {
+    if (Y_list[i] == nullptr) return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: Y_list[%d] is NULL", i);
+    if (i > 0) {
+      cudaPointerAttributes a{};
+      if (cudaPointerGetAttributes(&a, Y_list[i]) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+        cudaGetLastError();
+        return uk::fail(UK_ERESIDENCY, "decode_rmsnorm_gemm: Y_list[%d] is not device memory", i);
+      }
+    }
+    out.y[i] = Y_list[i];
+  }
+  out.n = n_y;
+
+  // K split: none while the 128-column tiles alone give ~100+ CTAs; otherwise
+  // the smallest power-of-two cluster that does (a weight-column shard)
+  const int kb_total = (K + BK - 1) / BK;
+  const int tiles = (N_shard + TM - 1) / TM;
+  if (tiles > 65535) return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: N_shard too large");
+  int csize = 1;
+  while (tiles * csize < UK_DECODE_MIN_CTAS && csize < CL_MAX && kb_total >= 2 * csize) csize *= 2;
+
+  CUtensorMap tmW, tmX;
+  if (int rc = make_map_f16(&tmW, W, (uint64_t)N_shard, (uint64_t)K, (uint64_t)ldw, 64, BK)) return rc;
+  if (int rc = make_map_f16(&tmX, workspace, (uint64_t)K, (uint64_t)B, (uint64_t)K, BK, BP)) return rc;
+
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(k_skinny_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(k_skinny_gemm, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      return uk::check_launch("decode_rmsnorm_gemm: function attributes");
+    attr_done[dev] = true;
+  }
+  const cudaStream_t st = (cudaStream_t)stream;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  // a cluster the GPU cannot co-schedule is halved until it can (the answer
+  // per device and cluster size is asked once: 1 yes, -1 no)
+  static signed char cluster_fits[64][5] = {};
+  for (;; csize /= 2) {
+    cfg.gridDim = dim3((unsigned)csize, (unsigned)tiles, 1);
+    attr[0].val.clusterDim.x = (unsigned)csize;
+    if (csize == 1) break;
+    int lg = 0;
+    while ((1 << lg) < csize) ++lg;
+    signed char* fit = (dev >= 0 && dev < 64) ? &cluster_fits[dev][lg] : nullptr;
+    if (fit == nullptr || *fit == 0) {
+      int nclusters = 0;
+      const bool ok = cudaOccupancyMaxActiveClusters(&nclusters, k_skinny_gemm, &cfg) == cudaSuccess && nclusters > 0;
+      cudaGetLastError();
+      if (fit) *fit = ok ? 1 : -1;
+      if (ok) break;
+    } else if (*fit > 0) {
+      break;
+    }
+  }
+  const int kb_per_cta = (kb_total + csize - 1) / csize;
+
+  k_rms_f16<<<B, RMS_THREADS, 0, st>>>(X, gamma, eps, (__half*)workspace, K);
+  if (int rc = uk::check_launch("decode_rmsnorm_gemm(norm)")) return rc;
+
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, k_skinny_gemm, tmW, tmX, out, ldy, B, N_shard, K, col_offset, kb_per_cta);
+  if (e != cudaSuccess) return uk::fail(UK_ECUDA, "decode_rmsnorm_gemm: launch: %s", cudaGetErrorString(e));
+  return uk::check_launch("decode_rmsnorm_gemm");
+}

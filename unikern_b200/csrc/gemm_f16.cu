@@ -413,10 +413,14 @@ extern "C" int uk_cuda_gemm_f16_allgather(const uint16_t* A, int64_t lda, const 
   return uk::gemm_f16_tc(A, lda, B_shard, ldb, outs, n_c, ldc, M, N_shard, K, (cudaStream_t)stream);
 }
 
+namespace uk {
+unsigned decode_fault_take();  // decode.cu
+}
+
 extern "C" unsigned uk_cuda_pipeline_fault(void) {
   unsigned v = 0;
   if (cudaMemcpyFromSymbol(&v, uk::g_fault_word, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
   const unsigned zero = 0;
   cudaMemcpyToSymbol(uk::g_fault_word, &zero, sizeof(zero));
-  return v;
+  return v | uk::decode_fault_take();
 }

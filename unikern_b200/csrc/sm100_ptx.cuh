@@ -165,3 +165,71 @@ __host__ __device__ constexpr uint32_t uk_idesc_f16(int M, int N, int b_mn_major
   return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | ((uint32_t)b_mn_major << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
+
+// Instruction descriptor, kind::f16, with both majors chosen: A K-major (0)
+// or MN-major (1) at bit 15, B likewise at bit 16.
+__host__ __device__ constexpr uint32_t uk_idesc_f16_ab(int M, int N, int a_mn_major, int b_mn_major) {
+  return (1u << 4) | ((uint32_t)a_mn_major << 15) | ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// 32 lanes x 16 consecutive 32-bit columns: thread i gets lane (base + i)
+__device__ __forceinline__ void uk_tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// generic-proxy shared-memory writes become visible to the async proxy
+// (tensor core operand reads) of this CTA
+__device__ __forceinline__ void uk_fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- thread-block clusters ---------------------------------------------------
+__device__ __forceinline__ uint32_t uk_cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of every CTA in the cluster arrives (release) and waits
+// (acquire).  All threads of each CTA must reach every such barrier.
+__device__ __forceinline__ void uk_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t uk_mapa(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float uk_ld_dsmem_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float4 uk_ld_dsmem_f32x4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
+// ---- programmatic dependent launch ------------------------------------------
+// the next kernel in the stream (launched with programmatic serialization)
+// may start its prologue now
+__device__ __forceinline__ void uk_pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// block until the preceding kernel in the stream has completed and its
+// memory is visible (a no-op without a programmatic dependency)
+__device__ __forceinline__ void uk_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
