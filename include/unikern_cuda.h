@@ -194,6 +194,22 @@ int uk_cuda_conv2d_f32(const float* X, const float* Wt, float* Y, int N, int H, 
                        int C, int Kh, int Kw, int Oc, int pad, const float* scale,
                        int layout, void* stream);
 
+/* The same convolution on the tcgen05 tensor cores, at fp32 accuracy: the
+ * operands are split into tf32 (hi, lo) pairs and each step accumulates
+ * lo*hi + hi*lo + hi*hi in fp32 (within a few ulps of the output scale of
+ * an fp32 FFMA result; the fp32 gate, 1e-4 against fp64, holds).  The split
+ * operands (and, for NCHW, the input transposed to NHWC) live in a caller
+ * workspace of uk_cuda_conv2d_workspace_size(...) bytes (16-byte aligned).
+ * Takes the tensor cores when C is a multiple of 32; other shapes run the
+ * FFMA kernel of uk_cuda_conv2d_f32 (the size query then returns 0 and the
+ * workspace may be NULL).  Replaces uk_conv<OCB>/uk_conv_g
+ * (src/codegen_hip.cpp:337-411) at the sizes where the tensor cores pay. */
+size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc,
+                                     int pad, int layout);
+int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W,
+                          int C, int Kh, int Kw, int Oc, int pad, const float* scale,
+                          int layout, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- KML runner (host side; the nvidia branch of `unikern run`) -----------
  * uk_kml_describe: the KML contract for one declaration, no GPU needed.
  *   Writes "key=value" lines to out: canonical= (canonical_form), signature=

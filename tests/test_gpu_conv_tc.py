@@ -1,0 +1,105 @@
+"""The tensor-core convolution (uk_cuda_conv2d_f32_ws: split-tf32 operands on
+tcgen05) against the fp64 oracle of the reference's cpu_conv
+(src/reference.cpp:6-22, restated in oracle/uk_oracle.c), with the same fp32
+gate as the FFMA kernel: rel_err <= 1e-4 with the output-scale floor.
+
+Shapes cover both layouts, channel counts that are multiples of 32 (the
+tensor-core path), output widths above the 64-pixel tile, more than 256
+output channels (two channel tiles), 1x1 and 3x3 filters, padding 0 and 1,
+and the full BASELINE configuration.  Shapes the tensor cores do not take
+(C not a multiple of 32) must run the FFMA kernel and give its bits.
+"""
+import numpy as np
+import pytest
+
+import unikern_b200.abi as abi
+from oracle import oracle as O
+from uk_testutil import F32_TOL, SUM_TAU, dev, empty, host
+
+pytestmark = pytest.mark.gpu
+
+
+def run_nchw(x, w, s, pad, tc=True):
+    N, Cc, H, W = x.shape
+    Oc, _, Kh, Kw = w.shape
+    y = empty((N, Oc, H + 2 * pad - Kh + 1, W + 2 * pad - Kw + 1))
+    fn = abi.conv2d_tc if tc else abi.conv2d
+    fn(dev(x), dev(w), y, N, H, W, Cc, Kh, Kw, Oc, pad, dev(s) if s is not None else None, abi.UK_CONV_NCHW)
+    return host(y)
+
+
+@pytest.mark.parametrize("N,Cc,H,W,Oc,K,pad,scaled", [
+    (2, 32, 9, 9, 16, 3, 1, True),
+    (3, 64, 13, 70, 300, 3, 1, True),     # two w tiles, two channel tiles
+    (1, 256, 14, 14, 256, 3, 1, True),
+    (2, 96, 7, 5, 40, 1, 0, False),        # 1x1
+    (1, 32, 6, 66, 8, 3, 0, True),         # valid padding, ragged tiles
+    (1, 64, 20, 20, 64, 5, 2, False),      # 5x5, pad 2
+])
+def test_conv_tc_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):
+    rng = np.random.default_rng(N * 1000 + Cc * 10 + H)
+    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / (K * K * Cc)), (Oc, Cc, K, K)).astype(np.float32)
+    s = rng.uniform(0.5, 1.5, Oc).astype(np.float32) if scaled else None
+    assert abi.lib().uk_cuda_conv2d_workspace_size(N, H, W, Cc, K, K, Oc, pad, abi.UK_CONV_NCHW) > 0
+    got = run_nchw(x, w, s, pad)
+    ref = O.conv_nchw(x, w, s, pad)
+    assert O.rel_err(got, ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+    assert abi.lib().uk_cuda_pipeline_fault() == 0
+    # and against the FFMA kernel of the same op
+    ffma = run_nchw(x, w, s, pad, tc=False)
+    assert O.rel_err(got, ffma.astype(np.float64), SUM_TAU * O.rms(ref)) <= F32_TOL
+
+
+def test_conv_tc_kml_layout_vs_f64():
+    # the KML conv contract at its BASELINE declaration: [58, 58, 256, 3, 3, 256]
+    H, W, Cc, Kh, Kw, Oc = 58, 58, 256, 3, 3, 256
+    rng = np.random.default_rng(58)
+    x = rng.uniform(0, 1, H * W * Cc).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / (9 * Cc)), Oc * Kh * Kw * Cc).astype(np.float32)
+    y = empty((Oc * (H - 2) * (W - 2),))
+    abi.conv2d_tc(dev(x), dev(w), y, 1, H, W, Cc, Kh, Kw, Oc, 0, None, abi.UK_CONV_KML)
+    ref = O.conv_f64(x, w, H, W, Cc, Kh, Kw, Oc, threads=8)
+    assert O.rel_err(host(y), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+
+
+def test_conv_tc_sawtooth_instance_exact():
+    # the reference's exact operands (multiples of 2^-4): every product and
+    # partial sum is exact, so the split path must reproduce fp32 bit for bit
+    H, W, Cc, Kh, Kw, Oc = 34, 34, 32, 3, 3, 16
+    x = O.sawtooth("A", H * W * Cc)
+    w = O.sawtooth("B", Oc * Kh * Kw * Cc)
+    y = empty((Oc * (H - 2) * (W - 2),))
+    abi.conv2d_tc(dev(x), dev(w), y, 1, H, W, Cc, Kh, Kw, Oc, 0, None, abi.UK_CONV_KML)
+    assert np.array_equal(host(y), O.conv_f32(x, w, H, W, Cc, Kh, Kw, Oc))
+
+
+def test_conv_tc_other_shapes_take_the_ffma_kernel():
+    N, Cc, H, W, Oc = 2, 8, 9, 9, 16
+    assert abi.lib().uk_cuda_conv2d_workspace_size(N, H, W, Cc, 3, 3, Oc, 1, abi.UK_CONV_NCHW) == 0
+    rng = np.random.default_rng(3)
+    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
+    w = rng.normal(0, 0.2, (Oc, Cc, 3, 3)).astype(np.float32)
+    assert np.array_equal(run_nchw(x, w, None, 1), run_nchw(x, w, None, 1, tc=False))
+
+
+def test_conv_tc_missing_workspace_is_refused():
+    x, w, y = empty((1, 32, 8, 8)), empty((8, 32, 3, 3)), empty((1, 8, 8, 8))
+    rc = abi.lib().uk_cuda_conv2d_f32_ws(x.data_ptr(), w.data_ptr(), y.data_ptr(), 1, 8, 8, 32, 3, 3, 8, 1, None,
+                                         abi.UK_CONV_NCHW, None, 0, None)
+    assert rc == 2 and "workspace" in abi.lib().uk_cuda_last_error().decode()
+
+
+def test_conv_tc_baseline_shape_sampled_images():
+    # N=32, 256->256, 56x56, 3x3, pad 1, channel scale;
+    # the full batch on the GPU, two images checked in full against fp64
+    N, Cc, H, W, Oc = 32, 256, 56, 56, 256
+    rng = np.random.default_rng(2024)
+    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / (9 * 256)), (Oc, Cc, 3, 3)).astype(np.float32)
+    s = rng.uniform(0.5, 1.5, Oc).astype(np.float32)
+    got = run_nchw(x, w, s, 1)
+    for n in (0, 31):
+        ref = O.conv_nchw(x[n:n + 1], w, s, 1)
+        assert O.rel_err(got[n:n + 1], ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+    assert abi.lib().uk_cuda_pipeline_fault() == 0

@@ -32,6 +32,8 @@ PROTOTYPES = {
     "uk_cuda_gemm_f16": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "uk_cuda_gemm_f16_ld": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, i32, vp]),
     "uk_cuda_conv2d_f32": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp]),
+    "uk_cuda_conv2d_workspace_size": (sz, [i32] * 9),
+    "uk_cuda_conv2d_f32_ws": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp, sz, vp]),
     "uk_cuda_pipeline_fault": (C.c_uint, []),
     "uk_cuda_gemm_f16_allgather": (i32, [vp, i64, vp, i64, C.POINTER(vp), i32, i64, i32, i32, i32, i64, vp]),
     "uk_cuda_ipc_handle_size": (sz, []),
@@ -148,6 +150,22 @@ def decode_rmsnorm_gemm(X, gamma, W, Y, eps=1e-5, workspace=None, stream=None):
     ys = (vp * 1)(Y.data_ptr())
     check(lib().uk_cuda_decode_rmsnorm_gemm_f16(_p(X), _p(gamma), eps, _p(W), W.stride(0), ys, 1, Y.stride(0), B, N,
                                                 K, 0, _p(ws), ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def conv2d_workspace(N, H, W, Cc, Kh, Kw, Oc, pad=0, layout=UK_CONV_NCHW):
+    import torch
+    n = lib().uk_cuda_conv2d_workspace_size(N, H, W, Cc, Kh, Kw, Oc, pad, layout)
+    return torch.empty(((n + 15) // 16) * 4, dtype=torch.float32, device="cuda") if n else None
+
+
+def conv2d_tc(X, Wt, Y, N, H, W, Cc, Kh, Kw, Oc, pad=0, scale=None, layout=UK_CONV_NCHW, workspace=None,
+              stream=None):
+    """The tensor-core (split-tf32) convolution; allocates its workspace
+    through torch when none is passed."""
+    ws = workspace if workspace is not None else conv2d_workspace(N, H, W, Cc, Kh, Kw, Oc, pad, layout)
+    nbytes = ws.numel() * ws.element_size() if ws is not None else 0
+    check(lib().uk_cuda_conv2d_f32_ws(_p(X), _p(Wt), _p(Y), N, H, W, Cc, Kh, Kw, Oc, pad, _p(scale), layout,
+                                      _p(ws), nbytes, _stream(stream)))
 
 
 # ---- KML runner (host side) -----------------------------------------------------

@@ -202,8 +202,20 @@ void dispatch(const ConvArgs& a, cudaStream_t st) {
 
 }  // namespace
 
+namespace uk {
+int conv2d_ffma(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh, int Kw, int Oc,
+                int pad, const float* scale, int layout, cudaStream_t st);
+}
+
 extern "C" int uk_cuda_conv2d_f32(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh,
                                   int Kw, int Oc, int pad, const float* scale, int layout, void* stream) {
+  return uk::conv2d_ffma(X, Wt, Y, N, H, W, C, Kh, Kw, Oc, pad, scale, layout, (cudaStream_t)stream);
+}
+
+// the FFMA implicit GEMM (also the path of uk_cuda_conv2d_f32_ws for shapes
+// the tensor-core kernel does not take)
+int uk::conv2d_ffma(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh, int Kw, int Oc,
+                    int pad, const float* scale, int layout, cudaStream_t st) {
   if (layout != UK_CONV_KML && layout != UK_CONV_NCHW)
     return uk::fail(UK_EINVAL, "conv2d: unknown layout %d", layout);
   if (N < 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0 || pad < 0)
@@ -227,7 +239,6 @@ extern "C" int uk_cuda_conv2d_f32(const float* X, const float* Wt, float* Y, int
   if (int rc = uk::check_device_ptr(Y, "Y")) return rc;
   if (scale)
     if (int rc = uk::check_device_ptr(scale, "scale")) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
   // the weight loader uses 16-byte loads when K % 4 == 0: refuse a misaligned
   // base instead of faulting
   if (!uk::aligned16(Wt) && a.K % 4 == 0) return uk::fail(UK_EINVAL, "conv2d: Wt must be 16-byte aligned");

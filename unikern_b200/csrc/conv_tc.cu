@@ -1,0 +1,466 @@
+// conv_tc.cu -- 2-D convolution (stride 1, zero padding, fused per-output-
+// channel scale) as an implicit GEMM on the tcgen05 tensor cores, at fp32
+// accuracy through split-tf32 operands ("3xTF32").
+//
+// GEMM view: rows = output pixels of one image (a 2 x 64 patch of (ho, wo)
+// per tile, UMMA M = 128), columns = output channels (UMMA N = 256), inner
+// dimension k = (kh, kw, c) in 32-channel steps.  The input lives in the
+// workspace as NHWC, so for one filter tap (kh, kw) and 32 channels the A
+// tile is a single 4-D TMA box [32 c][64 w][2 h][1 n] at (c0, wo0 + kw - pad,
+// ho0 + kh - pad, n): each pixel's 32 channels are one 128-byte swizzled row
+// (the K-major UMMA layout) and the zero padding is TMA's out-of-bounds fill
+// (only the channel coordinate, always a multiple of 32, is innermost).  The
+// weights are [Oc][kh][kw][c] in the workspace: the B tile is one 2-D box
+// [32 k][256 oc].
+//
+// Accuracy: an fp32 value x is carried as hi = tf32(x) plus lo = tf32(x - hi)
+// (the pre-pass stores both), and each k-step issues lo*hi + hi*lo + hi*hi
+// into the fp32 accumulator (the lo*lo term is below fp32 resolution).  The
+// result matches an fp32 FFMA convolution to a few ulps of the output scale:
+// the fp32 gate (1e-4 relative to an fp64 reference) holds with margin.
+//
+// Structure (the f16 GEMM's): a persistent CTA per SM, 192 threads; warp 0
+// issues the TMA loads into a 2-stage ring (96 KiB per stage: A hi/lo, B
+// hi/lo), warp 1 owns 512 TMEM columns (two 256-column accumulators) and one
+// thread issues the MMAs, warps 2-5 drain the accumulator of the previous tile
+// (tcgen05.ld, scale, coalesced stores to NCHW) while the next tile's MMAs
+// run.  Every mbarrier wait is bounded (2 s); a timeout sets this file's fault
+// word (uk_cuda_pipeline_fault) and the CTA unwinds.  Plain single-CTA TMA
+// loads of this GPU's memory only; nothing uses multicast.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "sm100_ptx.cuh"
+#include "uk_common.cuh"
+
+namespace uk {
+__device__ unsigned int g_conv_fault = 0;
+int conv2d_ffma(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh, int Kw, int Oc,
+                int pad, const float* scale, int layout, cudaStream_t st);
+}  // namespace uk
+
+namespace {
+
+constexpr int BH = 2, BW = 64, BM = BH * BW;  // output pixels per tile
+constexpr int BN = 256;                        // output channels per tile
+constexpr int BK = 32;                         // channels per k-step (128-byte rows)
+constexpr int STAGES = 2;
+constexpr int A_BYTES = BM * BK * 4;  // 16 KiB
+constexpr int B_BYTES = BN * BK * 4;  // 32 KiB
+constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+constexpr int EPI_WARPS = 4;
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr uint32_t IDESC = uk_idesc_tf32(BM, BN, 0, 0);
+constexpr uint64_t WAIT_NS = 2000000000ull;
+
+struct SmemCtl {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t teardown;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(SmemCtl);
+static_assert(SMEM_BYTES <= 232448, "shared memory per block on sm_100");
+
+struct ConvTc {
+  float* y;
+  const float* scale;
+  int N, Ho, Wo, Oc, C, Kh, Kw, pad;
+  int tiles_w, tiles_h, tiles_oc, num_tiles;
+};
+
+__device__ __forceinline__ void tile_coords(const ConvTc& p, int t, int& n, int& ho0, int& wo0, int& oc0) {
+  const int oct = t % p.tiles_oc;
+  t /= p.tiles_oc;
+  const int wt = t % p.tiles_w;
+  t /= p.tiles_w;
+  const int ht = t % p.tiles_h;
+  n = t / p.tiles_h;
+  ho0 = ht * BH;
+  wo0 = wt * BW;
+  oc0 = oct * BN;
+}
+
+__device__ __forceinline__ void raise_fault(SmemCtl* ctl, unsigned bit) {
+  atomicOr(&uk::g_conv_fault, bit);
+  ctl->abort = 1;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    k_conv_tc(const __grid_constant__ CUtensorMap tmXh, const __grid_constant__ CUtensorMap tmXl,
+              const __grid_constant__ CUtensorMap tmWh, const __grid_constant__ CUtensorMap tmWl, const ConvTc p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  SmemCtl* ctl = (SmemCtl*)(smem + (size_t)STAGES * STAGE_BYTES);
+  volatile int* abort = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int csteps = p.C / BK;
+  const int ksteps = p.Kh * p.Kw * csteps;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      uk_mbar_init(&ctl->full[s], 1);
+      uk_mbar_init(&ctl->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      uk_mbar_init(&ctl->tfull[b], 1);
+      uk_mbar_init(&ctl->tempty[b], EPI_WARPS);
+    }
+    uk_mbar_init(&ctl->teardown, 1);
+    ctl->abort = 0;
+    uk_fence_mbar_init();
+    uk_tma_prefetch_desc(&tmXh);
+    uk_tma_prefetch_desc(&tmXl);
+    uk_tma_prefetch_desc(&tmWh);
+    uk_tma_prefetch_desc(&tmWl);
+  }
+  if (warp == 1) {
+    uk_tmem_alloc(&ctl->tmem_base, TMEM_COLS);
+    uk_tmem_relinquish();
+  }
+  uk_tc_fence_before();
+  __syncthreads();
+  uk_tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort; t += gridDim.x) {
+        int n, ho0, wo0, oc0;
+        tile_coords(p, t, n, ho0, wo0, oc0);
+        bool ok = true;
+        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!uk_mbar_wait(&ctl->empty[s], ph ^ 1u, abort, WAIT_NS)) {
+            raise_fault(ctl, UK_FAULT_PRODUCER);
+            ok = false;
+            break;
+          }
+          const int tap = ks / csteps, c0 = (ks - tap * csteps) * BK;
+          const int kh = tap / p.Kw, kw = tap - kh * p.Kw;
+          uint8_t* st = smem + (size_t)s * STAGE_BYTES;
+          uk_mbar_expect_tx(&ctl->full[s], STAGE_BYTES);
+          uk_tma_load_4d(st, &tmXh, &ctl->full[s], c0, wo0 + kw - p.pad, ho0 + kh - p.pad, n);
+          uk_tma_load_4d(st + A_BYTES, &tmXl, &ctl->full[s], c0, wo0 + kw - p.pad, ho0 + kh - p.pad, n);
+          const int kcol = tap * p.C + c0;
+          uk_tma_load_2d(st + 2 * A_BYTES, &tmWh, &ctl->full[s], kcol, oc0);
+          uk_tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmWl, &ctl->full[s], kcol, oc0);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, tl = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort; t += gridDim.x, ++tl) {
+        const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
+        if (!uk_mbar_wait(&ctl->tempty[buf], tph ^ 1u, abort, WAIT_NS)) {
+          raise_fault(ctl, UK_FAULT_MMA);
+          break;
+        }
+        uk_tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        bool ok = true;
+        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!uk_mbar_wait(&ctl->full[s], ph, abort, WAIT_NS)) {
+            raise_fault(ctl, UK_FAULT_MMA);
+            ok = false;
+            break;
+          }
+          uk_tc_fence_after();
+          const uint32_t ah = uk_smem_u32(smem + (size_t)s * STAGE_BYTES);
+          const uint32_t al = ah + A_BYTES, bh = ah + 2 * A_BYTES, bl = bh + B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            // K-major, 128-byte swizzle: +32 bytes per 8 tf32 inside the atom,
+            // 8-row groups 1 KiB apart
+            const uint64_t dah = uk_desc_sw128(ah + kk * 32, 16, 1024);
+            const uint64_t dal = uk_desc_sw128(al + kk * 32, 16, 1024);
+            const uint64_t dbh = uk_desc_sw128(bh + kk * 32, 16, 1024);
+            const uint64_t dbl = uk_desc_sw128(bl + kk * 32, 16, 1024);
+            uk_umma_tf32(d, dal, dbh, IDESC, (ks > 0 || kk > 0) ? 1u : 0u);  // small terms first
+            uk_umma_tf32(d, dah, dbl, IDESC, 1u);
+            uk_umma_tf32(d, dah, dbh, IDESC, 1u);
+          }
+          uk_umma_commit(&ctl->empty[s]);
+        }
+        if (!ok) break;
+        uk_umma_commit(&ctl->tfull[buf]);
+      }
+      uk_umma_commit(&ctl->teardown);
+      if (!uk_mbar_wait(&ctl->teardown, 0, nullptr, WAIT_NS)) atomicOr(&uk::g_conv_fault, UK_FAULT_TEARDOWN);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2 .. 5) ----------------
+    // lane = tile row m = pixel (m / 64, m % 64) of the 2 x 64 patch; the 32
+    // lanes of a warp are 32 consecutive wo of one output row, so every
+    // column (output channel) is one coalesced 128-byte store
+    const int q = warp & 3;
+    const int m = q * 32 + lane;
+    uint32_t tl = 0;
+    for (int t = blockIdx.x; t < p.num_tiles && !*abort; t += gridDim.x, ++tl) {
+      int n, ho0, wo0, oc0;
+      tile_coords(p, t, n, ho0, wo0, oc0);
+      const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
+      if (!uk_mbar_wait(&ctl->tfull[buf], tph, abort, WAIT_NS)) {
+        raise_fault(ctl, UK_FAULT_EPILOGUE);
+        break;
+      }
+      uk_tc_fence_after();
+      const int ho = ho0 + m / BW, wo = wo0 + m % BW;
+      const bool valid = ho < p.Ho && wo < p.Wo;
+      float* ybase = p.y + (((int64_t)n * p.Oc + oc0) * p.Ho + ho) * p.Wo + wo;
+      const int64_t ocs = (int64_t)p.Ho * p.Wo;
+#pragma unroll 1
+      for (int j = 0; j < BN / 32; ++j) {
+        uint32_t v[32];
+        uk_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + j * 32, v);
+        uk_tmem_ld_wait();
+        const int ocj = oc0 + j * 32;
+        const float sc_lane = (p.scale != nullptr && ocj + lane < p.Oc) ? __ldg(p.scale + ocj + lane) : 1.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float sc = __shfl_sync(0xffffffffu, sc_lane, i);
+          if (valid && ocj + i < p.Oc) ybase[(int64_t)(j * 32 + i) * ocs] = __uint_as_float(v[i]) * sc;
+        }
+      }
+      uk_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) uk_mbar_arrive(&ctl->tempty[buf]);
+    }
+  }
+
+  uk_tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    uk_tc_fence_after();
+    uk_tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---- pre-pass: fp32 -> (hi, lo) tf32 pairs, NCHW -> NHWC ------------------------
+__device__ __forceinline__ void split(float v, float& hi, float& lo) {
+  hi = uk_tf32_rna(v);
+  lo = uk_tf32_rna(v - hi);
+}
+
+// X[n][c][h][w] -> Xh/Xl[n][h][w][c] through a 32 x 32 shared-memory tile
+__global__ void k_split_nchw_nhwc(const float* __restrict__ X, float* __restrict__ Xh, float* __restrict__ Xl, int C,
+                                  int H, int W) {
+  __shared__ float tile[32][33];
+  const int tiles_w = (W + 31) / 32;
+  const int64_t nh = blockIdx.x / tiles_w;
+  const int w0 = (int)(blockIdx.x % tiles_w) * 32, c0 = blockIdx.y * 32;
+  const int n = (int)(nh / H), h = (int)(nh % H);
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int c = c0 + r, w = w0 + threadIdx.x;
+    tile[r][threadIdx.x] = (c < C && w < W) ? __ldcs(X + (((int64_t)n * C + c) * H + h) * W + w) : 0.f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int w = w0 + r, c = c0 + threadIdx.x;
+    if (w < W && c < C) {
+      float hi, lo;
+      split(tile[threadIdx.x][r], hi, lo);
+      const int64_t o = (((int64_t)n * H + h) * W + w) * C + c;
+      Xh[o] = hi;
+      Xl[o] = lo;
+    }
+  }
+}
+
+// elementwise split (the KML input is already HWC)
+__global__ void k_split_flat(const float* __restrict__ X, float* __restrict__ Xh, float* __restrict__ Xl, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float hi, lo;
+    split(__ldcs(X + i), hi, lo);
+    Xh[i] = hi;
+    Xl[i] = lo;
+  }
+}
+
+// weights -> [Oc][kh][kw][c] hi/lo (NCHW weights are [Oc][c][kh][kw])
+__global__ void k_split_weights(const float* __restrict__ Wt, float* __restrict__ Wh, float* __restrict__ Wl, int Oc,
+                                int C, int Kh, int Kw, int nchw) {
+  const int64_t K = (int64_t)C * Kh * Kw, total = (int64_t)Oc * K;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t oc = i / K;
+    const int k = (int)(i - oc * K);
+    int64_t src = i;
+    if (nchw) {
+      const int tap = k / C, c = k - tap * C, kh = tap / Kw, kw = tap - kh * Kw;
+      src = ((oc * C + c) * Kh + kh) * Kw + kw;
+    }
+    float hi, lo;
+    split(__ldg(Wt + src), hi, lo);
+    Wh[i] = hi;
+    Wl[i] = lo;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  });
+  return fn;
+}
+
+int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+           const cuuint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return uk::fail(UK_ECUDA, "conv2d: cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return uk::fail(UK_ECUDA, "conv2d: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return UK_OK;
+}
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+bool tc_applies(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad, int layout) {
+  (void)Oc;
+  if (C < BK || C % BK != 0) return false;
+  const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
+  if (Ho <= 0 || Wo <= 0 || N <= 0) return false;
+  if (layout == UK_CONV_KML && (N != 1 || pad != 0)) return false;
+  return true;
+}
+
+}  // namespace
+
+namespace uk {
+
+unsigned conv_fault_take() {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_conv_fault, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  const unsigned zero = 0;
+  cudaMemcpyToSymbol(g_conv_fault, &zero, sizeof(zero));
+  return v;
+}
+
+}  // namespace uk
+
+extern "C" size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad,
+                                                int layout) {
+  if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout)) return 0;
+  const size_t xs = align256((size_t)N * H * W * C * 4), ws = align256((size_t)Oc * Kh * Kw * C * 4);
+  return 2 * xs + 2 * ws;
+}
+
+extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh,
+                                     int Kw, int Oc, int pad, const float* scale, int layout, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (layout != UK_CONV_KML && layout != UK_CONV_NCHW)
+    return uk::fail(UK_EINVAL, "conv2d: unknown layout %d", layout);
+  if (N < 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0 || pad < 0)
+    return uk::fail(UK_EINVAL, "conv2d: invalid dims N=%d H=%d W=%d C=%d Kh=%d Kw=%d Oc=%d pad=%d", N, H, W, C, Kh,
+                    Kw, Oc, pad);
+  if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout))
+    return uk::conv2d_ffma(X, Wt, Y, N, H, W, C, Kh, Kw, Oc, pad, scale, layout, st);
+  const size_t need = uk_cuda_conv2d_workspace_size(N, H, W, C, Kh, Kw, Oc, pad, layout);
+  if (workspace == nullptr || workspace_bytes < need)
+    return uk::fail(UK_EINVAL, "conv2d: needs a %zu-byte workspace (uk_cuda_conv2d_workspace_size), got %zu", need,
+                    workspace ? workspace_bytes : (size_t)0);
+  if ((int64_t)N * H * W * C > ((int64_t)1 << 40)) return uk::fail(UK_EINVAL, "conv2d: input too large");
+  if (int rc = uk::check_device_ptr(X, "X")) return rc;
+  if (int rc = uk::check_device_ptr(Wt, "Wt")) return rc;
+  if (int rc = uk::check_device_ptr(Y, "Y")) return rc;
+  if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
+  if (scale)
+    if (int rc = uk::check_device_ptr(scale, "scale")) return rc;
+  if (!uk::aligned16(workspace)) return uk::fail(UK_EINVAL, "conv2d: the workspace must be 16-byte aligned");
+
+  const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
+  const size_t xs = align256((size_t)N * H * W * C * 4), wsz = align256((size_t)Oc * Kh * Kw * C * 4);
+  float* Xh = (float*)workspace;
+  float* Xl = (float*)((uint8_t*)workspace + xs);
+  float* Wh = (float*)((uint8_t*)workspace + 2 * xs);
+  float* Wl = (float*)((uint8_t*)workspace + 2 * xs + wsz);
+
+  // pre-pass: operands as tf32 (hi, lo) pairs, input as NHWC
+  if (N == 0) return UK_OK;
+  if (layout == UK_CONV_NCHW) {
+    const int64_t gx = (int64_t)((W + 31) / 32) * N * H;
+    if (gx > 2147483647LL || C / 32 > 65535) return uk::fail(UK_EINVAL, "conv2d: input too large for the pre-pass");
+    const dim3 g((unsigned)gx, (unsigned)(C / 32), 1);
+    k_split_nchw_nhwc<<<g, dim3(32, 8), 0, st>>>(X, Xh, Xl, C, H, W);
+  } else {
+    const int64_t n = (int64_t)H * W * C;
+    k_split_flat<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 16), 256, 0, st>>>(X, Xh,
+                                                                                                            Xl, n);
+  }
+  {
+    const int64_t n = (int64_t)Oc * Kh * Kw * C;
+    k_split_weights<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 8), 256, 0, st>>>(
+        Wt, Wh, Wl, Oc, C, Kh, Kw, layout == UK_CONV_NCHW ? 1 : 0);
+  }
+  if (int rc = uk::check_launch("conv2d(split)")) return rc;
+
+  // tensor maps: input [N][H][W][C] as 4-D (C innermost), weights [Oc][K]
+  CUtensorMap txh, txl, twh, twl;
+  const cuuint64_t xdims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
+  const cuuint64_t xstr[3] = {(cuuint64_t)C * 4, (cuuint64_t)W * C * 4, (cuuint64_t)H * W * C * 4};
+  const cuuint32_t xbox[4] = {BK, BW, BH, 1};
+  const int64_t K = (int64_t)Kh * Kw * C;
+  const cuuint64_t wdims[2] = {(cuuint64_t)K, (cuuint64_t)Oc};
+  const cuuint64_t wstr[1] = {(cuuint64_t)K * 4};
+  const cuuint32_t wbox[2] = {BK, BN};
+  if (int rc = encode(&txh, Xh, 4, xdims, xstr, xbox)) return rc;
+  if (int rc = encode(&txl, Xl, 4, xdims, xstr, xbox)) return rc;
+  if (int rc = encode(&twh, Wh, 2, wdims, wstr, wbox)) return rc;
+  if (int rc = encode(&twl, Wl, 2, wdims, wstr, wbox)) return rc;
+
+  ConvTc p{};
+  p.y = Y;
+  p.scale = scale;
+  p.N = N;
+  p.Ho = Ho;
+  p.Wo = Wo;
+  p.Oc = Oc;
+  p.C = C;
+  p.Kh = Kh;
+  p.Kw = Kw;
+  p.pad = pad;
+  p.tiles_w = (Wo + BW - 1) / BW;
+  p.tiles_h = (Ho + BH - 1) / BH;
+  p.tiles_oc = (Oc + BN - 1) / BN;
+  const int64_t tiles = (int64_t)N * p.tiles_h * p.tiles_w * p.tiles_oc;
+  if (tiles > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d: too many tiles");
+  p.num_tiles = (int)tiles;
+
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    if (e != cudaSuccess) return uk::fail(UK_ECUDA, "conv2d: smem attribute: %s", cudaGetErrorString(e));
+    attr_done[dev] = true;
+  }
+  const int grid = p.num_tiles < uk::sm_count() ? p.num_tiles : uk::sm_count();
+  k_conv_tc<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(txh, txl, twh, twl, p);
+  return uk::check_launch("conv2d(tcgen05)");
+}

@@ -415,6 +415,7 @@ extern "C" int uk_cuda_gemm_f16_allgather(const uint16_t* A, int64_t lda, const 
 
 namespace uk {
 unsigned decode_fault_take();  // decode.cu
+unsigned conv_fault_take();    // conv_tc.cu
 }
 
 extern "C" unsigned uk_cuda_pipeline_fault(void) {
@@ -422,5 +423,5 @@ extern "C" unsigned uk_cuda_pipeline_fault(void) {
   if (cudaMemcpyFromSymbol(&v, uk::g_fault_word, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
   const unsigned zero = 0;
   cudaMemcpyToSymbol(uk::g_fault_word, &zero, sizeof(zero));
-  return v | uk::decode_fault_take();
+  return v | uk::decode_fault_take() | uk::conv_fault_take();
 }

@@ -233,3 +233,42 @@ __device__ __forceinline__ void uk_pdl_launch_dependents() {
 // block until the preceding kernel in the stream has completed and its
 // memory is visible (a no-op without a programmatic dependency)
 __device__ __forceinline__ void uk_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---- tf32 ----------------------------------------------------------------------
+// D[tmem] (+)= A * B, kind::tf32 (both operands tf32: fp32 bit patterns whose
+// low 13 mantissa bits the tensor core ignores), K = 8 per instruction.
+__device__ __forceinline__ void uk_umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor, kind::tf32: D f32 (bits 4-5 = 1), A and B TF32
+// (format 2 at bits 7-9 and 10-12), majors at bits 15 / 16, shape M x N.
+__host__ __device__ constexpr uint32_t uk_idesc_tf32(int M, int N, int a_mn_major, int b_mn_major) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn_major << 15) | ((uint32_t)b_mn_major << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// round to tf32, ties away from zero; the low 13 mantissa bits come back zero
+__device__ __forceinline__ float uk_tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r & 0xFFFFE000u);
+}
+
+// ---- TMA (tiled, 4-D, single-CTA destination) ------------------------------
+// c0 = innermost coordinate (elements; callers keep c0 * elem_size a multiple
+// of 16 bytes); the outer coordinates may be negative (zero fill).
+__device__ __forceinline__ void uk_tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                               int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(uk_smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(uk_smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
