@@ -433,6 +433,47 @@ def bench_decode(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
     return {"ms": ms, "value": nbytes / ms / 1e6, "bytes_per_step": nbytes, "batch": Bt}
 
 
+def bench_conv_sharded(ctx, steps, warmup, N=32, Cc=256, H=56, W=56, Oc=256, pad=1):
+    """BASELINE configs[2] over the ranks: images split by batch, tensor-core
+    conv per rank, NCCL all-gather of Y (every rank ends with the full Y)."""
+    from unikern_b200 import shard
+    torch = ctx.torch
+    plan = shard.ConvBatchShard(N, Cc, H, W, Oc, 3, 3, pad)
+    x = gen(torch, (N, Cc, H, W), "uniform", 8)[plan.b0:plan.b1].contiguous()
+    w = gen(torch, (Oc, Cc, 3, 3), "normal", 9, None, (2.0 / (9 * Cc)) ** 0.5)
+    s = gen(torch, (Oc,), "uniform", 10, None, lo=0.5, hi=1.5)
+    y = torch.empty((N, Oc, H, W), device="cuda")
+    ms = ctx.time_steps(lambda: plan.run(x, w, y, s), steps, warmup)
+    flops = 2.0 * N * H * W * Cc * 9 * Oc
+    return {"ms": ms, "value": flops / ms / 1e9, "parallelism": plan.describe()}
+
+
+def bench_decode_sharded(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
+    """BASELINE configs[4] over the ranks: weight columns sharded with the
+    all-gather fused into the GEMM's store; the softmax rows split over the
+    ranks (independent rows, no exchange)."""
+    import unikern_b200.abi as abi
+    from unikern_b200 import shard
+    torch = ctx.torch
+    x = gen(torch, (Bt, H), "normal", 13)
+    g = gen(torch, (H,), "normal", 14, None, 0.1) + 1.0
+    out = torch.empty((Bt, F), dtype=torch.float16, device="cuda")
+    plan = shard.DecodeColumnShard(out, Bt, F, H)
+    Ws = gen(torch, (H, F), "normal", 15, torch.float16, 0.02)[:, plan.n0:plan.n1].contiguous()
+    r0, r1 = shard.batch_split(Bt * heads, ctx.world, ctx.rank)
+    sc = gen(torch, (r1 - r0, S), "normal", 16)
+    pr = torch.empty_like(sc)
+
+    def step():
+        plan.launch(x, g, Ws)
+        abi.softmax(sc, pr)
+        plan.barrier()
+    ms = ctx.time_steps(step, steps, warmup)
+    nbytes = Bt * H * 4 + H * 4 + H * F * 2 + Bt * F * 2 + 2 * Bt * heads * S * 4
+    plan.close()
+    return {"ms": ms, "value": nbytes / ms / 1e6, "parallelism": plan.describe()}
+
+
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
 # capture of `python bench.py --op <op> --steps 2 --warmup 3 --no-cpu` with
 # --metrics dram__bytes_read.sum,dram__bytes_write.sum (profiles/dram_traffic_per_kernel.md)
@@ -576,6 +617,14 @@ def main():
         if not args.no_cpu:
             for op in ("reduce", "rmsnorm", "softmax"):
                 ops[op]["cpu_baseline"] = {k: v for k, v in cpu_rowop(op, 8192, 16384).items() if k != "seconds"}
+
+    if args.op == "all" and world > 1:
+        r = bench_conv_sharded(ctx, max(3, min(args.steps, 10)), 3)
+        ops["conv_n32_batch_sharded"] = {"TFLOP/s": round(r["value"], 2), "ms": round(r["ms"], 4),
+                                         "parallelism": r["parallelism"], "scaling": "strong"}
+        r = bench_decode_sharded(ctx, max(5, min(args.steps, 20)), 3)
+        ops["decode_chain_b32_column_sharded"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
+                                                  "parallelism": r["parallelism"], "scaling": "strong"}
 
     tflops = g["value"]
     line = {"metric": METRIC, "value": round(tflops, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,

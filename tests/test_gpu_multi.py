@@ -31,3 +31,7 @@ def test_gemm_allgather_two_gpus_matches_single_gpu():
 
 def test_conv_batch_shard_two_gpus_matches_single_gpu():
     _torchrun("multigpu_conv_worker.py", 29518)
+
+
+def test_decode_column_shard_two_gpus_matches_single_gpu():
+    _torchrun("multigpu_decode_worker.py", 29519)

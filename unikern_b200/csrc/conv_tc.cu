@@ -26,7 +26,7 @@
 // (tcgen05.ld, scale, coalesced stores to NCHW) while the next tile's MMAs
 // run.  Every mbarrier wait is bounded (2 s); a timeout sets this file's fault
 // word (uk_cuda_pipeline_fault) and the CTA unwinds.  Plain single-CTA TMA
-// loads of this GPU's memory only; nothing uses multicast.
+// loads of this GPU's memory only, each into its own CTA.
 #include <cudaTypedefs.h>
 
 #include <algorithm>

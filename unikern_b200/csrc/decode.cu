@@ -30,7 +30,7 @@
 // Every mbarrier wait is bounded (2 s); a timeout records a bit in this
 // file's fault word (read through uk_cuda_pipeline_fault) and every CTA still
 // passes every cluster barrier, so no peer is left waiting.  TMA loads are
-// plain single-CTA loads of this GPU's memory; nothing uses multicast.
+// plain single-CTA loads of this GPU's memory, each into its own CTA.
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 

@@ -51,7 +51,7 @@ std::string perf_string(const KmlTree& t) {
 }
 
 // bytes the declared tree keeps resident on the device while it is timed
-int64_t payload_bytes(const KmlTree& t, size_t reduce_ws) {
+int64_t payload_bytes(const KmlTree& t, size_t op_ws) {  // op_ws: the reduce / conv workspace
   const int64_t* d = nullptr;
   int64_t v[6];
   for (int i = 0; i < 6; ++i) v[i] = t.dims[i];
@@ -60,8 +60,9 @@ int64_t payload_bytes(const KmlTree& t, size_t reduce_ws) {
   switch (t.op) {
     case OpKind::Gemm: return (d[0] * d[2] + d[2] * d[1] + d[0] * d[1]) * es;
     case OpKind::Conv:
-      return (d[0] * d[1] * d[2] + d[5] * d[3] * d[4] * d[2] + d[5] * (d[0] - d[3] + 1) * (d[1] - d[4] + 1)) * 4;
-    case OpKind::Reduction: return d[0] * 4 + (int64_t)reduce_ws + 4;
+      return (d[0] * d[1] * d[2] + d[5] * d[3] * d[4] * d[2] + d[5] * (d[0] - d[3] + 1) * (d[1] - d[4] + 1)) * 4 +
+             (int64_t)op_ws;
+    case OpKind::Reduction: return d[0] * 4 + (int64_t)op_ws + 4;
     case OpKind::Softmax: return 2 * d[0] * d[1] * 4;
     case OpKind::RmsNorm:
     case OpKind::ChannelScale: return (2 * d[0] * d[1] + d[1]) * 4;
@@ -115,7 +116,7 @@ struct OpCall {
   void* in0 = nullptr;   // A / X
   void* in1 = nullptr;   // B / Wt / W / S (null for softmax, reduce)
   void* out = nullptr;   // C / Y
-  void* ws = nullptr;    // reduce workspace
+  void* ws = nullptr;    // reduce / conv workspace
   size_t ws_bytes = 0;
   int launch(cudaStream_t st) const {
     switch (op) {
@@ -124,9 +125,10 @@ struct OpCall {
                                       (int)d[1], (int)d[2], st)
                    : uk_cuda_gemm_f32((const float*)in0, (const float*)in1, (float*)out, (int)d[0], (int)d[1],
                                       (int)d[2], st);
-      case OpKind::Conv:
-        return uk_cuda_conv2d_f32((const float*)in0, (const float*)in1, (float*)out, 1, (int)d[0], (int)d[1],
-                                  (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML, st);
+      case OpKind::Conv:  // tensor cores when C % 32 == 0 (workspace sized for it), else FFMA
+        return uk_cuda_conv2d_f32_ws((const float*)in0, (const float*)in1, (float*)out, 1, (int)d[0], (int)d[1],
+                                     (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML, ws,
+                                     ws_bytes, st);
       case OpKind::Reduction:
         return uk_cuda_reduce_f32((const float*)in0, (float*)out, 1, d[0], ws, ws_bytes, st);
       case OpKind::Softmax:
@@ -173,10 +175,11 @@ bool stage_operands(OpCall* c, DevArena* ar, cudaStream_t st, std::string* err) 
   c->in0 = ar->alloc(c->n_in0() * c->es(), "in0");
   if (c->n_in1() > 0) c->in1 = ar->alloc(c->n_in1() * c->es(), "in1");
   c->out = ar->alloc(c->n_out() * c->es(), "out");
-  if (c->op == OpKind::Reduction) {
-    c->ws_bytes = uk_cuda_reduce_workspace_size(1, c->d[0]);
-    if (c->ws_bytes) c->ws = ar->alloc(c->ws_bytes, "workspace");
-  }
+  if (c->op == OpKind::Reduction) c->ws_bytes = uk_cuda_reduce_workspace_size(1, c->d[0]);
+  if (c->op == OpKind::Conv)
+    c->ws_bytes = uk_cuda_conv2d_workspace_size(1, (int)c->d[0], (int)c->d[1], (int)c->d[2], (int)c->d[3],
+                                                (int)c->d[4], (int)c->d[5], 0, UK_CONV_KML);
+  if (c->ws_bytes) c->ws = ar->alloc(c->ws_bytes, "workspace");
   if (!ar->err.empty()) {
     *err = ar->err;
     return false;
@@ -370,7 +373,11 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
   timed.op = tree.op;
   timed.f16 = tree.dtype == DType::F16;
   for (int i = 0; i < 6; ++i) timed.d[i] = tree.dims[i];
-  const size_t ws = tree.op == OpKind::Reduction ? uk_cuda_reduce_workspace_size(1, tree.dims[0]) : 0;
+  const size_t ws = tree.op == OpKind::Reduction ? uk_cuda_reduce_workspace_size(1, tree.dims[0])
+                    : tree.op == OpKind::Conv
+                        ? uk_cuda_conv2d_workspace_size(1, tree.dims[0], tree.dims[1], tree.dims[2], tree.dims[3],
+                                                        tree.dims[4], tree.dims[5], 0, UK_CONV_KML)
+                        : 0;
   const int64_t payload = payload_bytes(tree, ws);
   const double payload_mb = double(payload) / (1024.0 * 1024.0);
   if (double(payload) > 0.85 * double(tot)) {

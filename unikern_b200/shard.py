@@ -148,7 +148,11 @@ class ConvBatchShard:
         self.b0, self.b1 = self.blocks[self.rank]
         self.even = len({b1 - b0 for b0, b1 in self.blocks}) == 1
         self._stage = None
-        self.launches_per_step = 1
+        # the tensor-core kernel's workspace for this rank's images (None when
+        # the shape runs the FFMA kernel)
+        self.ws = abi.conv2d_workspace(max(1, self.b1 - self.b0), H, W, Cc, Kh, Kw, Oc, pad, abi.UK_CONV_NCHW) \
+            if self.b1 > self.b0 else None
+        self.launches_per_step = 3  # the hi/lo pre-passes and the conv
 
     def describe(self):
         return "batch-sharded over %d GPUs (%d images each), NCCL all-gather of Y" % (self.world, self.b1 - self.b0)
@@ -160,8 +164,8 @@ class ConvBatchShard:
         """This rank's images into its block of Y."""
         n = self.b1 - self.b0
         if n:
-            abi.conv2d(x_shard, Wt, Y[self.b0:self.b1], n, self.H, self.W, self.C, self.Kh, self.Kw, self.Oc,
-                       self.pad, scale, abi.UK_CONV_NCHW, stream)
+            abi.conv2d_tc(x_shard, Wt, Y[self.b0:self.b1], n, self.H, self.W, self.C, self.Kh, self.Kw, self.Oc,
+                          self.pad, scale, abi.UK_CONV_NCHW, self.ws, stream)
 
     def gather(self, Y):
         """Every rank's block into every rank's Y."""
@@ -193,3 +197,53 @@ class ConvBatchShard:
     def run(self, x_shard, Wt, Y, scale=None, stream=None):
         self.launch(x_shard, Wt, Y, scale, stream)
         self.gather(Y)
+
+
+class DecodeColumnShard:
+    """The decode layer's RMSNorm -> f16 GEMM over `world` GPUs: the weight's
+    columns are split (W[:, n0:n1] on each rank, 14336 / 8 = 1792 for
+    Llama-3-8B), the token rows and gamma are replicated, and every rank's
+    kernel stores its column block of Y into all ranks' Y (peer stores over
+    NVLink), so the all-gather is fused into the GEMM's store."""
+
+    def __init__(self, Y_full, B: int, N: int, K: int, group=None):
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > MAX_RANKS:
+            raise ValueError("the fused all-gather stores to at most %d GPUs" % MAX_RANKS)
+        self.B, self.N, self.K = B, N, K
+        self.n0, self.n1 = column_split(N, self.world, self.rank)
+        self.peers = PeerBuffers(Y_full, group)
+        order = store_order(self.world, self.rank)
+        self.y_list = (C.c_void_p * self.world)(*[self.peers.ptrs[r] for r in order])
+        self.ldy = Y_full.stride(0)
+        self.ws = abi.decode_workspace(B, K)
+        import torch
+        self.flag = torch.zeros(1, device="cuda")
+        self.launches_per_step = 2  # the norm kernel and the GEMM
+
+    def describe(self):
+        return "weight columns sharded over %d GPUs (%d each), all-gather fused into the store" % (
+            self.world, self.n1 - self.n0)
+
+    def w_shard(self, W):
+        return W[:, self.n0:self.n1]
+
+    def launch(self, X, gamma, W_shard, eps=1e-5, stream=None):
+        abi.check(abi.lib().uk_cuda_decode_rmsnorm_gemm_f16(
+            X.data_ptr(), gamma.data_ptr(), eps, W_shard.data_ptr(), W_shard.stride(0), self.y_list, self.world,
+            self.ldy, self.B, self.n1 - self.n0, self.K, self.n0, self.ws.data_ptr(),
+            self.ws.numel() * self.ws.element_size(), abi._stream(stream)))
+
+    def barrier(self):
+        import torch.distributed as dist
+        dist.all_reduce(self.flag, group=self.group)
+
+    def run(self, X, gamma, W_shard, eps=1e-5, stream=None):
+        self.launch(X, gamma, W_shard, eps, stream)
+        self.barrier()
+
+    def close(self):
+        self.peers.close()
