@@ -284,6 +284,70 @@ __global__ void k_split_nchw_nhwc(const float* __restrict__ X, float* __restrict
   }
 }
 
+// One CTA per input row (n, h): the C x W plane of that row is staged in
+// shared memory ([w][c], padded to C + 1 so the column-wise writes are
+// conflict free), then written out as the contiguous NHWC row (W * C floats)
+// with 16-byte stores, hi and lo.  Used when the plane fits in shared memory.
+constexpr int ROW_THREADS = 512;
+
+__global__ void __launch_bounds__(ROW_THREADS) k_split_row_nhwc(const float* __restrict__ X, float* __restrict__ Xh,
+                                                                 float* __restrict__ Xl, int C, int H, int W) {
+  extern __shared__ float plane[];  // [W][C + 1]
+  const int64_t nh = blockIdx.x;
+  const int n = (int)(nh / H), h = (int)(nh % H);
+  const int cp = C + 1;
+  const float* src = X + ((int64_t)n * C * H + h) * W;  // + c * H * W + w
+  const int64_t cw = (int64_t)C * W;
+  if (W % 4 == 0) {
+    // 16-byte loads, eight per thread issued before any is consumed
+    constexpr int UNR = 8;
+    const int w4n = W / 4;
+    const int64_t n4 = cw / 4;
+    for (int64_t base = threadIdx.x; base < n4; base += (int64_t)ROW_THREADS * UNR) {
+      float4 v[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int64_t i = base + (int64_t)u * ROW_THREADS;
+        if (i < n4) {
+          const int c = (int)(i / w4n), w4 = (int)(i - (int64_t)c * w4n);
+          v[u] = __ldcs(reinterpret_cast<const float4*>(src + (int64_t)c * H * W) + w4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int64_t i = base + (int64_t)u * ROW_THREADS;
+        if (i < n4) {
+          const int c = (int)(i / w4n), w = 4 * (int)(i - (int64_t)c * w4n);
+          plane[w * cp + c] = v[u].x;
+          plane[(w + 1) * cp + c] = v[u].y;
+          plane[(w + 2) * cp + c] = v[u].z;
+          plane[(w + 3) * cp + c] = v[u].w;
+        }
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < cw; i += ROW_THREADS) {
+      const int c = (int)(i / W), w = (int)(i - (int64_t)c * W);
+      plane[w * cp + c] = __ldcs(src + (int64_t)c * H * W + w);
+    }
+  }
+  __syncthreads();
+  float4* dh = reinterpret_cast<float4*>(Xh + nh * cw);
+  float4* dl = reinterpret_cast<float4*>(Xl + nh * cw);
+  for (int64_t i = threadIdx.x; i < cw / 4; i += ROW_THREADS) {
+    const int64_t e = i * 4;
+    const int w = (int)(e / C), c = (int)(e - (int64_t)w * C);
+    const float* p = plane + w * cp + c;
+    float h0, h1, h2, h3, l0, l1, l2, l3;
+    split(p[0], h0, l0);
+    split(p[1], h1, l1);
+    split(p[2], h2, l2);
+    split(p[3], h3, l3);
+    dh[i] = make_float4(h0, h1, h2, h3);
+    dl[i] = make_float4(l0, l1, l2, l3);
+  }
+}
+
 // elementwise split (the KML input is already HWC)
 __global__ void k_split_flat(const float* __restrict__ X, float* __restrict__ Xh, float* __restrict__ Xl, int64_t n) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -403,7 +467,21 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
 
   // pre-pass: operands as tf32 (hi, lo) pairs, input as NHWC
   if (N == 0) return UK_OK;
-  if (layout == UK_CONV_NCHW) {
+  const size_t plane_bytes = (size_t)W * (C + 1) * 4;
+  // the row-staged pre-pass needs 16-byte aligned rows of X for its vector loads
+  if (layout == UK_CONV_NCHW && plane_bytes <= 100 * 1024 && (W % 4 != 0 || uk::aligned16(X))) {
+    static bool plane_attr[64] = {false};
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d >= 0 && d < 64 && !plane_attr[d]) {
+      if (cudaFuncSetAttribute(k_split_row_nhwc, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) !=
+          cudaSuccess)
+        return uk::check_launch("conv2d: pre-pass attribute");
+      plane_attr[d] = true;
+    }
+    if ((int64_t)N * H > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d: N*H too large");
+    k_split_row_nhwc<<<(unsigned)((int64_t)N * H), ROW_THREADS, plane_bytes, st>>>(X, Xh, Xl, C, H, W);
+  } else if (layout == UK_CONV_NCHW) {
     const int64_t gx = (int64_t)((W + 31) / 32) * N * H;
     if (gx > 2147483647LL || C / 32 > 65535) return uk::fail(UK_EINVAL, "conv2d: input too large for the pre-pass");
     const dim3 g((unsigned)gx, (unsigned)(C / 32), 1);
