@@ -81,7 +81,8 @@ def test_capability_gaps(kml, gap):
 
 # the plans the kernels launch, on a 148-SM B200 (the ledger's tm / tn)
 @pytest.mark.parametrize("op,dims,f16,want", [
-    ("gemm", (8192, 8192, 8192), True, (128, 256, 64, 4)),     # tcgen05 tile
+    ("gemm", (8192, 8192, 8192), True, (256, 256, 64, 6)),     # tcgen05 SM-pair tile
+    ("gemm", (128, 4096, 4096), True, (128, 256, 64, 4)),      # one 128-row block: single-SM tile
     ("gemm", (8192, 8192, 8190), True, (128, 128, 8, 2)),      # K % 8: CUDA-core path
     ("gemm", (512, 512, 512), False, (32, 64, 16, 2)),         # 128 CTAs of 32x64
     ("gemm", (4096, 4096, 4096), False, (128, 128, 8, 2)),
@@ -98,10 +99,10 @@ def test_tile_plan(op, dims, f16, want):
 
 def test_solver_reports_the_plan_and_a_roofline_cost():
     d = abi.kml_describe('{"op":"gemm","dtype":"fp16","dims":[8192,8192,8192]}', B200_HCS, 148)
-    assert d["tile"] == "128x256" and d["k_block"] == "64" and d["stages"] == "4"
+    assert d["tile"] == "256x256" and d["k_block"] == "64" and d["stages"] == "6"
     # 1.0995e12 flop at 2.25 PFLOP/s + 384 MiB over a 55 GB/s link
     assert float(d["c_ms"]) == pytest.approx(2 * 8192 ** 3 / 2.25e15 * 1e3 + 402653184 / 55e9 * 1e3, rel=1e-12)
-    assert "tile=128x256" in d["placement"]
+    assert "tile=256x256" in d["placement"]
 
 
 def test_run_without_a_device_commits_nothing(tmp_path):

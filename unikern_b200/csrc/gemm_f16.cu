@@ -27,6 +27,7 @@
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "sm100_ptx.cuh"
@@ -318,9 +319,25 @@ namespace uk {
 
 // C[0..nc) all receive the product; used directly by the multi-GPU path with
 // peer pointers (C[0] local).  Shapes must satisfy tc_shape_ok.
+int gemm_f16_tc_2sm(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, uint16_t* const* Cs, int nc,
+                    int64_t ldc, int M, int N, int K, cudaStream_t st);  // gemm_f16_2sm.cu
+
+// Kernel choice: the SM-pair kernel (256 x 256 tiles over two SMs) once M has
+// two 128-row blocks; UNIKERN_GEMM_F16_PAIR=0 in the environment selects the
+// single-SM kernel instead (for comparisons).
+static bool use_pair_kernel(int M) {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("UNIKERN_GEMM_F16_PAIR");
+    env = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return env == 1 && M > 128;
+}
+
 int gemm_f16_tc(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, uint16_t* const* Cs, int nc,
                 int64_t ldc, int M, int N, int K, cudaStream_t st) {
   if (nc < 1 || nc > MAX_OUT) return fail(UK_EINVAL, "gemm_f16: 1..%d outputs, got %d", MAX_OUT, nc);
+  if (use_pair_kernel(M)) return gemm_f16_tc_2sm(A, lda, B, ldb, Cs, nc, ldc, M, N, K, st);
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM)) return rc;
   if (int rc = make_map(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK)) return rc;
@@ -416,6 +433,7 @@ extern "C" int uk_cuda_gemm_f16_allgather(const uint16_t* A, int64_t lda, const 
 namespace uk {
 unsigned decode_fault_take();  // decode.cu
 unsigned conv_fault_take();    // conv_tc.cu
+unsigned fault_take_2sm();     // gemm_f16_2sm.cu
 }
 
 extern "C" unsigned uk_cuda_pipeline_fault(void) {
@@ -423,5 +441,5 @@ extern "C" unsigned uk_cuda_pipeline_fault(void) {
   if (cudaMemcpyFromSymbol(&v, uk::g_fault_word, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
   const unsigned zero = 0;
   cudaMemcpyToSymbol(uk::g_fault_word, &zero, sizeof(zero));
-  return v | uk::decode_fault_take() | uk::conv_fault_take();
+  return v | uk::decode_fault_take() | uk::conv_fault_take() | uk::fault_take_2sm();
 }

@@ -272,3 +272,83 @@ __device__ __forceinline__ void uk_tma_load_4d(void* dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(uk_smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+
+// ---- 2-SM (cta_group::2) forms: a CTA pair of a cluster shares one MMA --------
+__device__ __forceinline__ void uk_tmem_alloc_cg2(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(uk_smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void uk_tmem_relinquish_cg2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void uk_tmem_dealloc_cg2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A * B with M = 256 split over the pair: each CTA
+// supplies its 128 rows of A and half of B's N columns from the same shared
+// memory offsets; issued by one thread of the even (leader) CTA
+__device__ __forceinline__ void uk_umma_f16_cg2(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// arrive (count one) on the mbarrier at this shared-memory offset in every CTA
+// of `cta_mask` once all prior tcgen05 ops of this thread have completed
+__device__ __forceinline__ void uk_umma_commit_cg2(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                   "r"(uk_smem_u32(bar)),
+               "h"(cta_mask)
+               : "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on an
+// mbarrier of the pair's leader CTA (bar_cluster: a shared::cluster address)
+__device__ __forceinline__ void uk_tma_load_2d_cg2(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                   int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(uk_smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+// arrive (count one, release at cluster scope) on an mbarrier of another CTA
+__device__ __forceinline__ void uk_mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// uk_mbar_wait with cluster-scope acquire: for barriers that other CTAs of the
+// cluster (or their tensor-core commits) arrive on
+__device__ __forceinline__ bool uk_mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(uk_smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool uk_mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                     uint64_t timeout_ns) {
+  if (uk_mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = uk_globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (uk_mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (abort != nullptr && *abort) return false;
+      if (uk_globaltimer() - t0 > timeout_ns) return false;
+    }
+  }
+}

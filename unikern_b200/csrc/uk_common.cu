@@ -83,7 +83,7 @@ int uk_cuda_tile_plan(int op, int f16, const int64_t* dims, int sms, int* out4) 
   uk::Tile t{0, 0, 0, 0};
   switch (op) {
     case UK_OP_GEMM:  // dims M, N, K
-      if (f16 && dims[2] % 8 == 0 && dims[1] % 8 == 0) t = uk::kGemmF16Tile;
+      if (f16 && dims[2] % 8 == 0 && dims[1] % 8 == 0) t = dims[0] > 128 ? uk::kGemmF16PairTile : uk::kGemmF16Tile;
       else t = uk::sgemm_tile(dims[0], dims[1], n_sm);
       break;
     case UK_OP_CONV: {  // KML dims H, W, C, Kh, Kw, Oc (one image, valid)

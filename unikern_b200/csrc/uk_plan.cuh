@@ -19,7 +19,10 @@ struct Tile {
 };
 
 // f16 tensor-core GEMM: 128 x 256 UMMA tile, 64-deep K blocks, 4-stage ring
+// (single SM); and the SM-pair kernel's 256 x 256 tile (128 rows per SM,
+// 6-stage ring), which runs whenever M > 128
 constexpr Tile kGemmF16Tile = {128, 256, 64, 4};
+constexpr Tile kGemmF16PairTile = {256, 256, 64, 6};
 
 // f32 FFMA GEMM (and the CUDA-core f16 path): the largest tile that still
 // gives every SM a CTA; double-buffered shared memory (2 stages)
