@@ -327,19 +327,22 @@ def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
     res = {"ms": ms, "value": flops / ms / 1e9, "flops_per_step": flops, "launches": launches_per_step * steps,
            "parallelism": parallelism, "kernel_ms": kernel_ms,
            "kernel_tflops": flops_per_launch / kernel_ms / 1e9}
-    # e2e through the C ABI with pinned host buffers (rank-local inputs)
+    # e2e through the C ABI with pinned host buffers (rank-local inputs): on
+    # one GPU the pipelined host-to-host entry point (uploads of A row blocks,
+    # their GEMMs and the downloads of C blocks overlapped); on N GPUs each
+    # rank uploads A and its B block, runs the sharded GEMM and downloads C
     Ah = A.cpu().pin_memory()
     Bh = Bs.contiguous().cpu().pin_memory()
     Ch = torch.empty((M, N), dtype=torch.float16).pin_memory()
     Bd = torch.empty_like(Bh, device="cuda")
 
     def e2e_step():
+        if world == 1:
+            abi.gemm_f16_host(Ah, Bh, Ch, A, Bd, Cm)
+            return
         A.copy_(Ah, non_blocking=True)
         Bd.copy_(Bh, non_blocking=True)
-        if world == 1:
-            abi.gemm_f16(A, Bd, Cm)
-        else:
-            plan.run(A, Bd, Cm)
+        plan.run(A, Bd, Cm)
         Ch.copy_(Cm, non_blocking=True)
     e2e_ms = ctx.time_steps(e2e_step, max(2, min(steps, 10)), 1)
     if world > 1:
@@ -478,7 +481,7 @@ def bench_decode_sharded(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S
 # capture of `python bench.py --op <op> --steps 2 --warmup 3 --no-cpu` with
 # --metrics dram__bytes_read.sum,dram__bytes_write.sum (profiles/dram_traffic_per_kernel.md)
 NCU_TRAFFIC = {
-    "gemm_f16_8192x8192x8192_n1": 994161664 + 127519488,
+    "gemm_f16_8192x8192x8192_n1": 1255296768 + 126162944,  # k_gemm_f16_tc2 (profiles/launches_gemm_f16_8192.md)
     "rowop_reduce": 536887296 + 3104256,
     "rowop_rmsnorm": 536972800 + 480955136,
     "rowop_softmax": 536904448 + 484363008,

@@ -129,6 +129,20 @@ int uk_cuda_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, i
 int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb,
                         uint16_t* C, int64_t ldc, int M, int N, int K, void* stream);
 
+/* The same GEMM from and to HOST memory: hA[M][K], hB[K][N] in, hC[M][N] out
+ * (page-locked host memory; anything else is refused with UK_EINVAL), through
+ * the caller's device buffers dA, dB, dC of the same shapes.  The copies are
+ * pipelined against the GEMM over `chunks` row blocks of A and C (0 = 8):
+ * B uploads first, then each block of A; a block's GEMM starts when its rows
+ * have landed, and its rows of C download while later blocks compute.  The
+ * call is asynchronous on `stream` and complete, C included, when `stream`
+ * is.  Two copy streams and their events are created per device on first use
+ * and kept; calls on one device from different host threads must not
+ * overlap.  This is the reference's end-to-end measurement (upload, run,
+ * download: src/codegen_hip.cpp:692-744) with the phases overlapped. */
+int uk_cuda_gemm_f16_host(const uint16_t* hA, const uint16_t* hB, uint16_t* hC, uint16_t* dA,
+                          uint16_t* dB, uint16_t* dC, int M, int N, int K, int chunks, void* stream);
+
 /* ---- multi-GPU f16 GEMM (one process per GPU, NVLink peers) ----------------
  * N-sharded GEMM with the all-gather fused into the store: computes columns
  * [col_offset, col_offset + N_shard) of C = A * B from this rank's column

@@ -43,6 +43,7 @@ PROTOTYPES = {
     "uk_cuda_decode_workspace_size": (sz, [i32, i32]),
     "uk_cuda_decode_rmsnorm_gemm_f16": (i32, [vp, vp, f32, vp, i64, C.POINTER(vp), i32, i64, i32, i32, i32, i64,
                                                vp, sz, vp]),
+    "uk_cuda_gemm_f16_host": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
@@ -150,6 +151,15 @@ def decode_rmsnorm_gemm(X, gamma, W, Y, eps=1e-5, workspace=None, stream=None):
     ys = (vp * 1)(Y.data_ptr())
     check(lib().uk_cuda_decode_rmsnorm_gemm_f16(_p(X), _p(gamma), eps, _p(W), W.stride(0), ys, 1, Y.stride(0), B, N,
                                                 K, 0, _p(ws), ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def gemm_f16_host(Ah, Bh, Ch, Ad, Bd, Cd, chunks=0, stream=None):
+    """C = A * B from pinned host tensors through device buffers, with the
+    copies pipelined against the GEMM (row blocks of A and C)."""
+    M, K = Ah.shape
+    N = Bh.shape[1]
+    check(lib().uk_cuda_gemm_f16_host(_p(Ah), _p(Bh), _p(Ch), _p(Ad), _p(Bd), _p(Cd), M, N, K, chunks,
+                                      _stream(stream)))
 
 
 def conv2d_workspace(N, H, W, Cc, Kh, Kw, Oc, pad=0, layout=UK_CONV_NCHW):
