@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "sm100_ptx.cuh"
@@ -253,6 +254,214 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ---- the same convolution on SM pairs (tcgen05 cta_group::2) -------------------
+// A pair of CTAs (a 2-CTA cluster) shares a 256-pixel x 256-channel tile: the
+// leader holds output rows ho0, ho0+1 and the peer ho0+2, ho0+3 (a 2 x 64
+// patch each, its A operand), and each holds 128 of the 256 channels of the
+// weights (its half of the B operand).  The leader issues M = 256 MMAs over
+// both CTAs' shared memory; each CTA's TMEM receives its 128 pixels.  Every
+// SM loads 64 KiB per k-step instead of 96 (its half of B), so the ring is 3
+// stages deep.  Loads count on the leader's full barrier; the leader commits
+// MMA completion to both CTAs' barriers; the epilogues arrive remotely on the
+// leader's tile-empty barrier (the f16 GEMM's pair pipeline).
+constexpr int P_BH = 4;                       // output rows per pair tile
+constexpr int P_STAGES = 3;
+constexpr int P_BNC = BN / 2;                 // channels of B per CTA
+constexpr int P_B_BYTES = P_BNC * BK * 4;     // 16 KiB
+constexpr int P_STAGE_BYTES = 2 * A_BYTES + 2 * P_B_BYTES;  // 64 KiB
+constexpr uint32_t P_IDESC = uk_idesc_tf32(2 * BM, BN, 0, 0);
+constexpr uint16_t P_PAIR = 0x3;
+struct SmemCtlP {
+  uint64_t full[P_STAGES];
+  uint64_t empty[P_STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t teardown;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t P_SMEM_BYTES = 1024 + (size_t)P_STAGES * P_STAGE_BYTES + sizeof(SmemCtlP);
+static_assert(P_SMEM_BYTES <= 232448, "shared memory per block on sm_100");
+
+__device__ __forceinline__ void pair_tile_coords(const ConvTc& p, int t, int& n, int& ho0, int& wo0, int& oc0) {
+  const int oct = t % p.tiles_oc;
+  t /= p.tiles_oc;
+  const int wt = t % p.tiles_w;
+  t /= p.tiles_w;
+  const int ht = t % p.tiles_h;  // tiles_h counts 4-row pair tiles here
+  n = t / p.tiles_h;
+  ho0 = ht * P_BH;
+  wo0 = wt * BW;
+  oc0 = oct * BN;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    k_conv_tc2(const __grid_constant__ CUtensorMap tmXh, const __grid_constant__ CUtensorMap tmXl,
+               const __grid_constant__ CUtensorMap tmWh, const __grid_constant__ CUtensorMap tmWl, const ConvTc p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  SmemCtlP* ctl = (SmemCtlP*)(smem + (size_t)P_STAGES * P_STAGE_BYTES);
+  volatile int* abort = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = uk_cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int csteps = p.C / BK;
+  const int ksteps = p.Kh * p.Kw * csteps;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      uk_mbar_init(&ctl->full[s], 1);
+      uk_mbar_init(&ctl->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      uk_mbar_init(&ctl->tfull[b], 1);
+      uk_mbar_init(&ctl->tempty[b], 2 * EPI_WARPS);
+    }
+    uk_mbar_init(&ctl->teardown, 1);
+    ctl->abort = 0;
+    uk_fence_mbar_init();
+    uk_tma_prefetch_desc(&tmXh);
+    uk_tma_prefetch_desc(&tmXl);
+    uk_tma_prefetch_desc(&tmWh);
+    uk_tma_prefetch_desc(&tmWl);
+  }
+  if (warp == 1) {
+    uk_tmem_alloc_cg2(&ctl->tmem_base, TMEM_COLS);
+    uk_tmem_relinquish_cg2();
+  }
+  uk_tc_fence_before();
+  __syncthreads();
+  uk_cluster_sync();
+  uk_tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = pair; t < p.num_tiles && !*abort; t += npairs) {
+        int n, ho0, wo0, oc0;
+        pair_tile_coords(p, t, n, ho0, wo0, oc0);
+        const int hr = ho0 + (int)crank * BH;  // this CTA's first output row
+        bool ok = true;
+        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1u;
+          if (!uk_mbar_wait_cluster(&ctl->empty[s], ph ^ 1u, abort, WAIT_NS)) {
+            atomicOr(&uk::g_conv_fault, UK_FAULT_PRODUCER);
+            ctl->abort = 1;
+            ok = false;
+            break;
+          }
+          const int tap = ks / csteps, c0 = (ks - tap * csteps) * BK;
+          const int kh = tap / p.Kw, kw = tap - kh * p.Kw;
+          uint8_t* st = smem + (size_t)s * P_STAGE_BYTES;
+          const uint32_t bar = uk_mapa(uk_smem_u32(&ctl->full[s]), 0);
+          if (crank == 0) uk_mbar_expect_tx(&ctl->full[s], 2 * P_STAGE_BYTES);
+          uk_tma_load_4d_cg2(st, &tmXh, bar, c0, wo0 + kw - p.pad, hr + kh - p.pad, n);
+          uk_tma_load_4d_cg2(st + A_BYTES, &tmXl, bar, c0, wo0 + kw - p.pad, hr + kh - p.pad, n);
+          const int kcol = tap * p.C + c0;
+          uk_tma_load_2d_cg2(st + 2 * A_BYTES, &tmWh, bar, kcol, oc0 + (int)crank * P_BNC);
+          uk_tma_load_2d_cg2(st + 2 * A_BYTES + P_B_BYTES, &tmWl, bar, kcol, oc0 + (int)crank * P_BNC);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (crank == 0 && lane == 0) {
+      uint32_t it = 0, tl = 0;
+      for (int t = pair; t < p.num_tiles && !*abort; t += npairs, ++tl) {
+        const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
+        if (!uk_mbar_wait_cluster(&ctl->tempty[buf], tph ^ 1u, abort, WAIT_NS)) {
+          atomicOr(&uk::g_conv_fault, UK_FAULT_MMA);
+          ctl->abort = 1;
+          break;
+        }
+        uk_tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        bool ok = true;
+        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1u;
+          if (!uk_mbar_wait_cluster(&ctl->full[s], ph, abort, WAIT_NS)) {
+            atomicOr(&uk::g_conv_fault, UK_FAULT_MMA);
+            ctl->abort = 1;
+            ok = false;
+            break;
+          }
+          uk_tc_fence_after();
+          const uint32_t ah = uk_smem_u32(smem + (size_t)s * P_STAGE_BYTES);
+          const uint32_t al = ah + A_BYTES, bh = ah + 2 * A_BYTES, bl = bh + P_B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint64_t dah = uk_desc_sw128(ah + kk * 32, 16, 1024);
+            const uint64_t dal = uk_desc_sw128(al + kk * 32, 16, 1024);
+            const uint64_t dbh = uk_desc_sw128(bh + kk * 32, 16, 1024);
+            const uint64_t dbl = uk_desc_sw128(bl + kk * 32, 16, 1024);
+            uk_umma_tf32_cg2(d, dal, dbh, P_IDESC, (ks > 0 || kk > 0) ? 1u : 0u);
+            uk_umma_tf32_cg2(d, dah, dbl, P_IDESC, 1u);
+            uk_umma_tf32_cg2(d, dah, dbh, P_IDESC, 1u);
+          }
+          uk_umma_commit_cg2(&ctl->empty[s], P_PAIR);
+        }
+        if (!ok) break;
+        uk_umma_commit_cg2(&ctl->tfull[buf], P_PAIR);
+      }
+      uk_umma_commit_cg2(&ctl->teardown, P_PAIR);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int m = q * 32 + lane;
+    const uint32_t tempty_leader[2] = {uk_mapa(uk_smem_u32(&ctl->tempty[0]), 0),
+                                       uk_mapa(uk_smem_u32(&ctl->tempty[1]), 0)};
+    uint32_t tl = 0;
+    for (int t = pair; t < p.num_tiles && !*abort; t += npairs, ++tl) {
+      int n, ho0, wo0, oc0;
+      pair_tile_coords(p, t, n, ho0, wo0, oc0);
+      const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
+      if (!uk_mbar_wait_cluster(&ctl->tfull[buf], tph, abort, WAIT_NS)) {
+        atomicOr(&uk::g_conv_fault, UK_FAULT_EPILOGUE);
+        ctl->abort = 1;
+        break;
+      }
+      uk_tc_fence_after();
+      const int ho = ho0 + (int)crank * BH + m / BW, wo = wo0 + m % BW;
+      const bool valid = ho < p.Ho && wo < p.Wo;
+      float* ybase = p.y + (((int64_t)n * p.Oc + oc0) * p.Ho + ho) * p.Wo + wo;
+      const int64_t ocs = (int64_t)p.Ho * p.Wo;
+#pragma unroll 1
+      for (int j = 0; j < BN / 32; ++j) {
+        uint32_t v[32];
+        uk_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + j * 32, v);
+        uk_tmem_ld_wait();
+        const int ocj = oc0 + j * 32;
+        const float sc_lane = (p.scale != nullptr && ocj + lane < p.Oc) ? __ldg(p.scale + ocj + lane) : 1.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float sc = __shfl_sync(0xffffffffu, sc_lane, i);
+          if (valid && ocj + i < p.Oc) ybase[(int64_t)(j * 32 + i) * ocs] = __uint_as_float(v[i]) * sc;
+        }
+      }
+      uk_tc_fence_before();
+      __syncwarp();
+      if (lane == 0) uk_mbar_arrive_cluster(tempty_leader[buf]);
+    }
+  }
+
+  if (warp == 1 && lane == 0) {
+    if (!uk_mbar_wait_cluster(&ctl->teardown, 0, nullptr, WAIT_NS)) atomicOr(&uk::g_conv_fault, UK_FAULT_TEARDOWN);
+  }
+  uk_tc_fence_before();
+  __syncthreads();
+  uk_cluster_sync();
+  if (warp == 1) {
+    uk_tc_fence_after();
+    uk_tmem_dealloc_cg2(tmem, TMEM_COLS);
+  }
+}
+
 // ---- pre-pass: fp32 -> (hi, lo) tf32 pairs, NCHW -> NHWC ------------------------
 __device__ __forceinline__ void split(float v, float& hi, float& lo) {
   hi = uk_tf32_rna(v);
@@ -404,6 +613,16 @@ int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, c
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
+// the SM-pair kernel unless UNIKERN_CONV_PAIR=0 (for comparisons)
+bool use_pair_kernel() {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("UNIKERN_CONV_PAIR");
+    env = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return env == 1;
+}
+
 bool tc_applies(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad, int layout) {
   (void)Oc;
   if (C < BK || C % BK != 0) return false;
@@ -506,7 +725,8 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   const int64_t K = (int64_t)Kh * Kw * C;
   const cuuint64_t wdims[2] = {(cuuint64_t)K, (cuuint64_t)Oc};
   const cuuint64_t wstr[1] = {(cuuint64_t)K * 4};
-  const cuuint32_t wbox[2] = {BK, BN};
+  const bool pair = use_pair_kernel();
+  const cuuint32_t wbox[2] = {BK, (cuuint32_t)(pair ? P_BNC : BN)};
   if (int rc = encode(&txh, Xh, 4, xdims, xstr, xbox)) return rc;
   if (int rc = encode(&txl, Xl, 4, xdims, xstr, xbox)) return rc;
   if (int rc = encode(&twh, Wh, 2, wdims, wstr, wbox)) return rc;
@@ -524,7 +744,7 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   p.Kw = Kw;
   p.pad = pad;
   p.tiles_w = (Wo + BW - 1) / BW;
-  p.tiles_h = (Ho + BH - 1) / BH;
+  p.tiles_h = pair ? (Ho + P_BH - 1) / P_BH : (Ho + BH - 1) / BH;
   p.tiles_oc = (Oc + BN - 1) / BN;
   const int64_t tiles = (int64_t)N * p.tiles_h * p.tiles_w * p.tiles_oc;
   if (tiles > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d: too many tiles");
@@ -534,11 +754,31 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-    if (e != cudaSuccess) return uk::fail(UK_ECUDA, "conv2d: smem attribute: %s", cudaGetErrorString(e));
+    if (cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(k_conv_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM_BYTES) !=
+            cudaSuccess)
+      return uk::check_launch("conv2d: smem attribute");
     attr_done[dev] = true;
   }
-  const int grid = p.num_tiles < uk::sm_count() ? p.num_tiles : uk::sm_count();
-  k_conv_tc<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(txh, txl, twh, twl, p);
-  return uk::check_launch("conv2d(tcgen05)");
+  if (!pair) {
+    const int grid = p.num_tiles < uk::sm_count() ? p.num_tiles : uk::sm_count();
+    k_conv_tc<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(txh, txl, twh, twl, p);
+    return uk::check_launch("conv2d(tcgen05)");
+  }
+  const int pairs = p.num_tiles < uk::sm_count() / 2 ? p.num_tiles : uk::sm_count() / 2;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_tc2, txh, txl, twh, twl, p);
+  if (e != cudaSuccess) return uk::fail(UK_ECUDA, "conv2d(pair): launch: %s", cudaGetErrorString(e));
+  return uk::check_launch("conv2d(tcgen05 pair)");
 }
