@@ -427,13 +427,37 @@ def bench_decode(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
     pr = torch.empty_like(sc)
 
     ws = abi.decode_workspace(Bt, H)
+    side = torch.cuda.Stream()
 
-    def step():
+    def chain():
+        # the softmax does not depend on the GEMM: it runs on a forked stream,
+        # so the graph holds two branches and the softmax's CTAs use the SMs
+        # the GEMM leaves free (112 of 148 stream the weight)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            abi.softmax(sc, pr)
         abi.decode_rmsnorm_gemm(x, g, Wt, out, 1e-5, ws)
-        abi.softmax(sc, pr)
-    ms = ctx.time_steps(step, steps, warmup)
+        torch.cuda.current_stream().wait_stream(side)
+    # a decode step is a handful of short launches: it runs as one CUDA graph
+    # (captured once, replayed every step) so host launch overhead stays out
+    graph = capture(ctx, chain)
+    ms = ctx.time_steps(graph.replay, steps, warmup)
     nbytes = Bt * H * 4 + H * 4 + H * F * 2 + Bt * F * 2 + 2 * Bt * heads * S * 4
-    return {"ms": ms, "value": nbytes / ms / 1e6, "bytes_per_step": nbytes, "batch": Bt}
+    return {"ms": ms, "value": nbytes / ms / 1e6, "bytes_per_step": nbytes, "batch": Bt, "graph": True}
+
+
+def capture(ctx, fn):
+    """fn's launches as a CUDA graph on the bench stream (after two eager
+    warm-up calls that set up per-device state)."""
+    torch = ctx.torch
+    fn()
+    fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):  # captured on a side stream, replayed on the bench stream
+        fn()
+    torch.cuda.synchronize()
+    return graph
 
 
 def bench_conv_sharded(ctx, steps, warmup, N=32, Cc=256, H=56, W=56, Oc=256, pad=1):
@@ -467,14 +491,27 @@ def bench_decode_sharded(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S
     sc = gen(torch, (r1 - r0, S), "normal", 16)
     pr = torch.empty_like(sc)
 
-    def step():
+    side = torch.cuda.Stream()
+
+    def chain():
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            abi.softmax(sc, pr)
         plan.launch(x, g, Ws)
-        abi.softmax(sc, pr)
+        torch.cuda.current_stream().wait_stream(side)
+
+    # the kernels run as one CUDA graph per step (softmax on a parallel
+    # branch); the cross-rank barrier (an NCCL all-reduce) stays outside it
+    graph = capture(ctx, chain)
+
+    def step():
+        graph.replay()
         plan.barrier()
     ms = ctx.time_steps(step, steps, warmup)
     nbytes = Bt * H * 4 + H * 4 + H * F * 2 + Bt * F * 2 + 2 * Bt * heads * S * 4
+    del graph
     plan.close()
-    return {"ms": ms, "value": nbytes / ms / 1e6, "parallelism": plan.describe()}
+    return {"ms": ms, "value": nbytes / ms / 1e6, "parallelism": plan.describe(), "graph": True}
 
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
