@@ -266,6 +266,95 @@ def cpu_conv(N, Cc, H, W, Oc, pad):
             "sample": "%d images of %d (one per thread), %.2f s" % (nt, N, dt), "seconds": dt}
 
 
+def cpu_gemm_f32(M=512, N=512, K=512):
+    """The whole f32 GEMM with the reference's cpu_ref
+    loop (src/codegen_hip.cpp:1124-1132), rows split over the host threads."""
+    import numpy as np
+    from oracle import oracle as O
+    nt = cpu_threads()
+    rng = np.random.default_rng(11)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    out = np.zeros((M, N), np.float32)
+    e = O.emit()
+    per = (M + nt - 1) // nt
+    if e is not None:
+        e.emit_gemm_set_B(B, K, N)
+
+        def work(i):
+            a, b = i * per, min(M, (i + 1) * per)
+            if a < b:
+                e.emit_gemm_rows(np.ascontiguousarray(A[a:b]), out[a:b], b - a)
+        dt = run_threads(work, nt)
+    else:
+        t0 = time.perf_counter()
+        O.gemm_f32(A, B, threads=nt)
+        dt = time.perf_counter() - t0
+    return {"value": 2.0 * M * N * K / dt / 1e12, "unit": "TFLOP/s", "cores": nt,
+            "kind": "reference" if e is not None else "port",
+            "sample": "the whole %dx%dx%d GEMM, rows split over %d threads, %.3f s" % (M, N, K, nt, dt), "seconds": dt}
+
+
+def cpu_reduce_scalar(L=134217728):
+    """The KML reduce (one vector of L floats to a scalar) with the reference's
+    cpu_reduce_blocked (src/reference.cpp:36-48): one pass, one thread, as the
+    reference runs it."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(17)
+    X = rng.normal(0, 1, L).astype(np.float32)
+    r = O.ref()
+    t0 = time.perf_counter()
+    if r is not None:
+        r.ref_cpu_reduce_blocked(X, L, 1024)
+    else:
+        O.reduce_blocked_f32(X, 1024)
+    dt = time.perf_counter() - t0
+    return {"value": L * 4 / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "reference" if r is not None else "port",
+            "sample": "the whole vector (L = %d), %.3f s" % (L, dt), "seconds": dt}
+
+
+def cpu_decode(Bt=32, H=4096, F=14336, heads=32, S=8192):
+    """The decode chain on the host with the reference's CPU paths: cpu_rmsnorm
+    (eps fixed at 1e-6 in the reference), the half-quantised f16 cpu_ref over
+    the 32 token rows, cpu_softmax over the 1024 score rows; threads over rows."""
+    import numpy as np
+    from oracle import oracle as O
+    e = O.emit()
+    nt = cpu_threads()
+    rng = np.random.default_rng(18)
+    x = rng.normal(0, 1, (Bt, H)).astype(np.float32)
+    g = rng.normal(1, 0.1, H).astype(np.float32)
+    W = O.f16_to_f32(O.f32_to_f16(rng.normal(0, 0.02, (H, F)).astype(np.float32)))
+    sc = rng.normal(0, 1, (Bt * heads, S)).astype(np.float32)
+    xn = np.zeros_like(x)
+    y = np.zeros((Bt, F), np.float32)
+    pr = np.zeros_like(sc)
+    if e is None:
+        return None
+    e.emit_gemm_set_B(W, H, F)
+    sp = (Bt * heads + nt - 1) // nt
+
+    def work(i):
+        if i < Bt:
+            e.emit_gemm_f16_rows(np.ascontiguousarray(xn[i:i + 1]), y[i:i + 1], 1)
+        a, b = i * sp, min(Bt * heads, (i + 1) * sp)
+        if a < b:
+            e.emit_softmax(np.ascontiguousarray(sc[a:b]), pr[a:b], b - a, S)
+    t0 = time.perf_counter()
+    e.emit_rmsnorm(x, g, xn, Bt, H)
+    run_threads(work, max(nt, 1))
+    dt = time.perf_counter() - t0
+    nbytes = Bt * H * 4 + H * 4 + H * F * 2 + Bt * F * 2 + 2 * Bt * heads * S * 4
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": nt, "kind": "reference",
+            "sample": "the whole chain (B = %d), %.3f s" % (Bt, dt), "seconds": dt}
+
+
+def strip(d):
+    return None if d is None else {k: (round(v, 6) if isinstance(v, float) else v) for k, v in d.items()
+                                   if k != "seconds"}
+
+
 # ---------------------------------------------------------------------------
 # GPU workloads
 # ---------------------------------------------------------------------------
@@ -655,8 +744,13 @@ def main():
         ops["decode_chain_b32"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
                                    "roofline": roofline("hbm", r["value"], pk)}
         if not args.no_cpu:
-            for op in ("reduce", "rmsnorm", "softmax"):
-                ops[op]["cpu_baseline"] = {k: v for k, v in cpu_rowop(op, 8192, 16384).items() if k != "seconds"}
+            # the reference's CPU path for every op, timed on this host in this run
+            for op in ("reduce", "rmsnorm", "softmax", "channelscale"):
+                ops[op]["cpu_baseline"] = strip(cpu_rowop(op, 8192, 16384))
+            ops["reduce_scalar"]["cpu_baseline"] = strip(cpu_reduce_scalar())
+            ops["conv_n32_256_56_3x3_pad1_scaled"]["cpu_baseline"] = strip(cpu_conv(32, 256, 56, 56, 256, 1))
+            ops["gemm_f32_512"]["cpu_baseline"] = strip(cpu_gemm_f32())
+            ops["decode_chain_b32"]["cpu_baseline"] = strip(cpu_decode())
 
     if args.op == "all" and world > 1:
         r = bench_conv_sharded(ctx, max(3, min(args.steps, 10)), 3)
