@@ -7,8 +7,16 @@
 // 128-bit; the next K-slab is prefetched into registers while the current
 // one is multiplied, with two shared-memory buffers (one barrier per slab).
 // Each output accumulates k in ascending order with FFMA.
+//
+// Small problems (512^3: 128 tiles of 32 x 64 on 148 SMs) would leave each SM
+// one CTA of four warps walking all of K, too little work in flight to hide
+// latency.  There K is split over a thread-block cluster of KS CTAs (grid z):
+// each CTA accumulates its K range in ascending order, the partial tiles meet
+// in distributed shared memory, and each CTA sums its slice of rows over the
+// cluster in rank order -- deterministic, no workspace.
 #include <cuda_fp16.h>
 
+#include "sm100_ptx.cuh"
 #include "uk_common.cuh"
 #include "uk_plan.cuh"
 
@@ -54,7 +62,7 @@ struct SgemmCfg {
   static_assert(BK % 4 == 0, "BK must be a multiple of 4");
 };
 
-template <int BM, int BN, int BK, int TM, int TN, bool VEC, typename T>
+template <int BM, int BN, int BK, int TM, int TN, bool VEC, typename T, int KS = 1>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     k_sgemm(const T* __restrict__ A, const T* __restrict__ B, T* __restrict__ C, int M, int N, int K,
             int64_t lda, int64_t ldb, int64_t ldc) {
@@ -66,6 +74,13 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
   const int tid = threadIdx.x;
   const int tx = tid % NTX, ty = tid / NTX;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  // this CTA's K range: all of K, or its share of a K-split cluster (grid z)
+  int kbeg = 0, kend = K;
+  if constexpr (KS > 1) {
+    const int kc = ((K + KS - 1) / KS + BK - 1) / BK * BK;
+    kbeg = min(K, (int)blockIdx.z * kc);
+    kend = min(K, kbeg + kc);
+  }
 
   float ra[Cfg::A_PER][4], rb[Cfg::B_PER][4];
 
@@ -78,7 +93,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         const int m = i / (BK / 4), kq = (i % (BK / 4)) * 4;
         const int gm = m0 + m, gk = k0 + kq;
         if (VEC) {
-          if (gm < M && gk < K) {
+          if (gm < M && gk < kend) {
             ld4(ra[p], A + (size_t)gm * lda + gk);
           } else {
             ra[p][0] = ra[p][1] = ra[p][2] = ra[p][3] = 0.f;
@@ -86,7 +101,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         } else {
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            ra[p][j] = (gm < M && gk + j < K) ? ld1(A + (size_t)gm * lda + gk + j) : 0.f;
+            ra[p][j] = (gm < M && gk + j < kend) ? ld1(A + (size_t)gm * lda + gk + j) : 0.f;
         }
       }
     }
@@ -97,7 +112,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         const int k = i / (BN / 4), nq = (i % (BN / 4)) * 4;
         const int gk = k0 + k, gn = n0 + nq;
         if (VEC) {
-          if (gk < K && gn < N) {
+          if (gk < kend && gn < N) {
             ld4(rb[p], B + (size_t)gk * ldb + gn);
           } else {
             rb[p][0] = rb[p][1] = rb[p][2] = rb[p][3] = 0.f;
@@ -105,7 +120,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         } else {
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            rb[p][j] = (gk < K && gn + j < N) ? ld1(B + (size_t)gk * ldb + gn + j) : 0.f;
+            rb[p][j] = (gk < kend && gn + j < N) ? ld1(B + (size_t)gk * ldb + gn + j) : 0.f;
         }
       }
     }
@@ -136,15 +151,15 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
 #pragma unroll
     for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
 
-  const int nslab = (K + BK - 1) / BK;
+  const int nslab = (kend - kbeg + BK - 1) / BK;
   if (nslab > 0) {
-    load_slab(0);
+    load_slab(kbeg);
     store_slab(0);
   }
   __syncthreads();
   for (int s = 0; s < nslab; ++s) {
     const int buf = s & 1;
-    if (s + 1 < nslab) load_slab((s + 1) * BK);
+    if (s + 1 < nslab) load_slab(kbeg + (s + 1) * BK);
 #pragma unroll
     for (int k = 0; k < BK; ++k) {
       float a[TM], b[TN];
@@ -165,6 +180,56 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     }
     if (s + 1 < nslab) store_slab(buf ^ 1);
     __syncthreads();
+  }
+
+  if constexpr (KS > 1) {
+    // the partial tile into shared memory (the slab buffers are free after the
+    // loop's last barrier), then this CTA's BM / KS rows summed over the
+    // cluster in rank order
+    static_assert(BM * BN <= 2 * BK * Cfg::APAD + 2 * BK * BN, "partial tile fits in the slab buffers");
+    static_assert(BM % KS == 0 && BN % 4 == 0, "row slices of the partial tile");
+    float* red = &As[0][0][0];
+#pragma unroll
+    for (int gi = 0; gi < TM / 4; ++gi)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int gj = 0; gj < TN / 4; ++gj) {
+          const int lm = gi * NTY * 4 + ty * 4 + i, ln = gj * NTX * 4 + tx * 4;
+          const float* v = &acc[gi * 4 + i][gj * 4];
+          *reinterpret_cast<float4*>(red + lm * BN + ln) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    uk_cluster_sync();
+    constexpr int ROWS = BM / KS;
+    const int r0 = (int)blockIdx.z * ROWS;
+    for (int idx = tid; idx < ROWS * BN / 4; idx += NT) {
+      const int lm = r0 + idx / (BN / 4), ln = (idx % (BN / 4)) * 4;
+      const uint32_t a = uk_smem_u32(red + lm * BN + ln);
+      float4 part[KS];
+#pragma unroll
+      for (int r = 0; r < KS; ++r) part[r] = uk_ld_dsmem_f32x4(uk_mapa(a, (uint32_t)r));
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < KS; ++r) {
+        v[0] += part[r].x;
+        v[1] += part[r].y;
+        v[2] += part[r].z;
+        v[3] += part[r].w;
+      }
+      const int gm = m0 + lm, gn = n0 + ln;
+      if (gm < M) {
+        T* c = C + (size_t)gm * ldc + gn;
+        if (VEC && gn + 3 < N) {
+          st4(c, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (gn + j < N) st1(c + j, v[j]);
+        }
+      }
+    }
+    uk_cluster_sync();  // no CTA leaves while a peer still reads its partial tile
+    return;
   }
 
 #pragma unroll
@@ -205,18 +270,49 @@ __global__ void k_zero2d(T* C, int M, int N, int64_t ldc) {
     st1(C + (i / N) * ldc + i % N, 0.f);
 }
 
+// the 32 x 64 tile with K split over a KS-CTA cluster (grid z)
+#ifndef UK_SGEMM_SPLIT_BK
+#define UK_SGEMM_SPLIT_BK 16
+#endif
+template <int KS, typename T>
+void launch_split(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
+                  cudaStream_t st) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)((N + 63) / 64), (unsigned)((M + 31) / 32), KS);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = KS;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  constexpr int BK = UK_SGEMM_SPLIT_BK;
+  if (vec) cudaLaunchKernelEx(&cfg, k_sgemm<32, 64, BK, 4, 4, true, T, KS>, A, B, C, M, N, K, lda, ldb, ldc);
+  else cudaLaunchKernelEx(&cfg, k_sgemm<32, 64, BK, 4, 4, false, T, KS>, A, B, C, M, N, K, lda, ldb, ldc);
+}
+
 // tile choice (uk::sgemm_tile): the largest tile that still gives every SM a
-// CTA; small problems fall to smaller tiles (512^3: 128 CTAs of 32x64)
+// CTA; small problems fall to smaller tiles (512^3: 128 CTAs of 32x64), and
+// when even those leave the GPU short of work, K is split over a cluster
+// (uk::sgemm_ksplit: 512^3 -> 4 CTAs per tile, 512 CTAs)
 template <typename T>
 void simt_gemm(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
                cudaStream_t st) {
-  const uk::Tile t = uk::sgemm_tile(M, N, uk::sm_count());
-  if (t.bm == 128)
+  const int64_t sms = uk::sm_count();
+  const uk::Tile t = uk::sgemm_tile(M, N, sms);
+  if (t.bm == 128) {
     launch<128, 128, 8, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
-  else if (t.bm == 64)
+  } else if (t.bm == 64) {
     launch<64, 64, 8, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
-  else
-    launch<32, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  } else {
+    const int ks = uk::sgemm_ksplit(M, N, K, sms);
+    if (ks == 8) launch_split<8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    else if (ks == 4) launch_split<4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    else if (ks == 2) launch_split<2>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    else launch<32, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  }
 }
 
 }  // namespace

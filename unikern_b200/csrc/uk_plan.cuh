@@ -33,6 +33,18 @@ inline Tile sgemm_tile(int64_t M, int64_t N, int64_t sms) {
   return {32, 64, 16, 2};
 }
 
+// K split of the smallest f32 tile (32 x 64): CTAs per tile (a cluster along
+// K) so that up to UK_SGEMM_SPLIT_CAP CTAs per SM run, each keeping >= 64 of K
+#ifndef UK_SGEMM_SPLIT_CAP
+#define UK_SGEMM_SPLIT_CAP 4
+#endif
+inline int sgemm_ksplit(int64_t M, int64_t N, int64_t K, int64_t sms) {
+  const int64_t ctas = ((M + 31) / 32) * ((N + 63) / 64);
+  int ks = 1;
+  while (ks < 8 && ctas * ks * 2 <= UK_SGEMM_SPLIT_CAP * sms && K / (ks * 2) >= 64) ks *= 2;
+  return ks;
+}
+
 // implicit-GEMM conv: rows = output channels, columns = output pixels
 inline Tile conv_tile(int64_t npix, int64_t Oc, int64_t sms) {
   auto ctas = [&](int bm, int bn) { return ((npix + bn - 1) / bn) * ((Oc + bm - 1) / bm); };
