@@ -640,6 +640,30 @@ def roofline(bound, achieved, pk, traffic=None):
             "peak_source": src, "traffic": traffic, "scope": "one launch of the kernel on one GPU"}
 
 
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (900 nominal)
+
+
+def fused_roofline(g, M, N, K, world, pk):
+    """Roofline of the N-sharded GEMM with the all-gather fused into its store:
+    the target time per launch is the slower of its flops at the measured
+    bf16 peak and the bytes it must push over NVLink (its C block to every
+    peer: M * N/world * 2 B * (world - 1)) at the measured 770 GB/s per
+    direction; frac = target / measured kernel time."""
+    peak = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
+    flops = 2.0 * M * (N / world) * K
+    link_bytes = M * (N / world) * 2.0 * (world - 1)
+    t_tensor = flops / (peak * 1e12) * 1e3
+    t_link = link_bytes / (NVLINK_GBS * 1e9) * 1e3
+    target = max(t_tensor, t_link)
+    return {"bound": "tensor" if t_tensor >= t_link else "nvlink", "achieved": round(g["kernel_tflops"], 2),
+            "peak": peak, "unit": "TFLOP/s", "frac": round(target / g["kernel_ms"], 4),
+            "peak_source": "%s bf16 burst; NVLink %.0f GB/s per direction (measured peer copy)" % (pk["source"],
+                                                                                                 NVLINK_GBS),
+            "target_ms": round(target, 5), "tensor_ms": round(t_tensor, 5), "nvlink_ms": round(t_link, 5),
+            "nvlink_bytes_per_launch": link_bytes, "kernel_ms": round(g["kernel_ms"], 5), "traffic": None,
+            "scope": "one launch of this rank's fused GEMM + all-gather kernel"}
+
+
 def run_reference(args, world, rank):
     """Reference arm: the reference's CPU implementation of the headline op."""
     if rank != 0:
@@ -771,7 +795,8 @@ def main():
                                    "(BASELINE configs[3])" % (M, N, K), "M": M, "N": N, "K": K,
                        "parallelism": g["parallelism"], "l2": "inputs (256 MiB) larger than L2"},
             "roofline": roofline("tensor", g["kernel_tflops"], pk,
-                                 traffic_for("gemm_f16_%dx%dx%d_n%d" % (M, N, K, world))),
+                                 traffic_for("gemm_f16_%dx%dx%d_n%d" % (M, N, K, world))) if world == 1 else
+            fused_roofline(g, M, N, K, world, pk),
             "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in g["e2e"].items()},
             "gpu_launches": g["launches"], "clocks": clocks}
     line["e2e"]["value"] = round(g["e2e"]["value"], 3)
