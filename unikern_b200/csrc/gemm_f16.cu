@@ -323,21 +323,25 @@ int gemm_f16_tc_2sm(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t l
                     int64_t ldc, int M, int N, int K, cudaStream_t st);  // gemm_f16_2sm.cu
 
 // Kernel choice: the SM-pair kernel (256 x 256 tiles over two SMs) once M has
-// two 128-row blocks; UNIKERN_GEMM_F16_PAIR=0 in the environment selects the
-// single-SM kernel instead (for comparisons).
-static bool use_pair_kernel(int M) {
+// two 128-row blocks and the tiles go to at most two copies of C.  With more
+// copies (the all-gather over 4-8 GPUs) each tile's epilogue is bound by
+// NVLink stores, and a pair must wait for the slower of its two epilogues
+// before its next tile: measured on 8 GPUs, the single-SM kernel is faster
+// there (0.186 vs 0.284 ms per step).  UNIKERN_GEMM_F16_PAIR=0 selects the
+// single-SM kernel everywhere (for comparisons).
+static bool use_pair_kernel(int M, int nc) {
   static int env = -1;
   if (env < 0) {
     const char* e = getenv("UNIKERN_GEMM_F16_PAIR");
     env = (e != nullptr && e[0] == '0') ? 0 : 1;
   }
-  return env == 1 && M > 128;
+  return env == 1 && M > 128 && nc <= 2;
 }
 
 int gemm_f16_tc(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, uint16_t* const* Cs, int nc,
                 int64_t ldc, int M, int N, int K, cudaStream_t st) {
   if (nc < 1 || nc > MAX_OUT) return fail(UK_EINVAL, "gemm_f16: 1..%d outputs, got %d", MAX_OUT, nc);
-  if (use_pair_kernel(M)) return gemm_f16_tc_2sm(A, lda, B, ldb, Cs, nc, ldc, M, N, K, st);
+  if (use_pair_kernel(M, nc)) return gemm_f16_tc_2sm(A, lda, B, ldb, Cs, nc, ldc, M, N, K, st);
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM)) return rc;
   if (int rc = make_map(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK)) return rc;
