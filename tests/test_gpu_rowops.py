@@ -13,7 +13,8 @@ pytestmark = pytest.mark.gpu
 
 # ---- channelscale: bit-exact (one fp32 multiply per element) ----------------
 
-@pytest.mark.parametrize("L,C", [(64, 256), (65536, 256), (7, 33), (1, 1), (3, 4099), (1000, 4)])
+@pytest.mark.parametrize("L,C", [(64, 256), (65536, 256), (7, 33), (1, 1), (3, 4099), (1000, 4),
+                                 (8192, 16384), (5, 2048), (3, 32768), (2, 40000), (9, 6000)])
 def test_channelscale_bit_exact(L, C):
     rng = np.random.default_rng(L * 7 + C)
     X = rng.normal(0, 1, (L, C)).astype(np.float32)

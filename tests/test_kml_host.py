@@ -92,6 +92,7 @@ def test_capability_gaps(kml, gap):
     ("softmax", (8192, 16384), False, (1, 16384, 0, 1)),
     ("rmsnorm", (8, 100000), False, (1, 2048, 0, 2)),          # streams twice
     ("channelscale", (65536, 256), False, (16, 256, 0, 1)),
+    ("channelscale", (8192, 16384), False, (1, 16384, 0, 1)),   # long rows: one CTA per row
 ])
 def test_tile_plan(op, dims, f16, want):
     assert abi.tile_plan(op, dims, f16, sms=148) == want

@@ -20,6 +20,7 @@ namespace {
 
 constexpr int kOpRms = 0;
 constexpr int kOpSoftmax = 1;
+constexpr int kOpScale = 2;  // channelscale: y = x * s[c], no row statistic
 
 // ---------------------------------------------------------------------------
 // channelscale: Y[i*C + c] = X[i*C + c] * S[c].  threadIdx.x walks column
@@ -157,7 +158,21 @@ __global__ void __launch_bounds__(THREADS) k_rowop(const float* __restrict__ X, 
       for (int w = 0; w < W; ++w) v[k][w] = OP == kOpSoftmax ? -INFINITY : 0.f;
     }
   }
-  if constexpr (OP == kOpRms) {
+  if constexpr (OP == kOpScale) {
+    (void)red;
+    (void)eps;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int64_t j = threadIdx.x + (int64_t)k * THREADS;
+      if (j < nv) {
+        float g[W];
+        uk_ld_g<W>(g, G + j * W);
+#pragma unroll
+        for (int w = 0; w < W; ++w) v[k][w] = v[k][w] * g[w];
+        uk_st_cs<W>(y + j * W, v[k]);
+      }
+    }
+  } else if constexpr (OP == kOpRms) {
     float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
@@ -306,8 +321,11 @@ bool dispatch_rowop(const float* X, const float* G, float* Y, int64_t L, int64_t
     }
 #undef UK_CASE
   }
-  k_rowop_stream<OP, W><<<(unsigned)L, 512, 0, st>>>(X, G, Y, C, eps);
-  return true;
+  if constexpr (OP != kOpScale) {  // the scale op only takes rows that fit in registers
+    k_rowop_stream<OP, W><<<(unsigned)L, 512, 0, st>>>(X, G, Y, C, eps);
+    return true;
+  }
+  return false;
 }
 
 using uk::ReducePlan;
@@ -363,6 +381,13 @@ int uk_cuda_channelscale_f32(const float* X, const float* S, float* Y, int64_t L
   if (int rc = uk::check_device_ptr(Y, "Y")) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   const bool vec = C % 4 == 0 && uk::aligned16(X) && uk::aligned16(S) && uk::aligned16(Y);
+  int th = 0, vp = 0;
+  if (vec && C >= 2048 && L <= 2147483647LL && uk::rowop_plan(C, 4, &th, &vp)) {
+    // long rows: one CTA per row streams it contiguously (the row ops' kernel
+    // with the scale in place of the statistic)
+    dispatch_rowop<kOpScale, 4>(X, S, Y, L, C, 0.f, st);
+    return uk::check_launch("channelscale");
+  }
   const int W = vec ? 4 : 1;
   const int64_t ncv = (C + W - 1) / W;
   int tx = (int)(ncv < 256 ? ((ncv + 31) / 32) * 32 : 256);

@@ -104,8 +104,14 @@ int uk_cuda_tile_plan(int op, int f16, const int64_t* dims, int sms, int* out4) 
       else t = {1, 512 * w, 0, 2};  // two-pass streaming kernel
       break;
     }
-    case UK_OP_CHANNELSCALE: {  // dims L, C: 256 threads over (C/W) x rows, 4 rows each
+    case UK_OP_CHANNELSCALE: {  // dims L, C
       const int w = dims[1] % 4 == 0 ? 4 : 1;
+      int th = 0, v = 0;
+      if (w == 4 && dims[1] >= 2048 && uk::rowop_plan(dims[1], 4, &th, &v)) {
+        t = {1, th * v * 4, 0, 1};  // long rows: one CTA per row
+        break;
+      }
+      // 256 threads over (C/W) column vectors x rows, 4 rows each
       const int64_t ncv = (dims[1] + w - 1) / w;
       const int tx = (int)(ncv < 256 ? ((ncv + 31) / 32) * 32 : 256);
       t = {(256 / tx) * 4, tx * w, 0, 1};
