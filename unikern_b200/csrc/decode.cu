@@ -92,7 +92,11 @@ __device__ __forceinline__ void fault(Ctl* ctl, unsigned bit) {
 }
 
 // ---- 1. RMSNorm into f16 ------------------------------------------------------
-constexpr int RMS_THREADS = 256;
+// One CTA of 1024 threads per token row.  Rows up to 16384 columns stay in
+// registers (at most four 16-byte vectors per thread): one read of X, a
+// fixed-order block sum, the scaled f16 row out.  Longer rows take two passes.
+constexpr int RMS_THREADS = 1024;
+constexpr int RMS_VPT = 4;
 
 __global__ void __launch_bounds__(RMS_THREADS) k_rms_f16(const float* __restrict__ X, const float* __restrict__ gamma,
                                                          float eps, __half* __restrict__ Xn, int K) {
@@ -101,15 +105,38 @@ __global__ void __launch_bounds__(RMS_THREADS) k_rms_f16(const float* __restrict
   const int b = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(X + (int64_t)b * K);
   const float4* gr = reinterpret_cast<const float4*>(gamma);
+  uint2* out = reinterpret_cast<uint2*>(Xn + (int64_t)b * K);
+  const int n4 = K / 4;
   float ss = 0.f;
-  for (int k4 = threadIdx.x; k4 < K / 4; k4 += RMS_THREADS) {
+  if (n4 <= RMS_VPT * RMS_THREADS) {
+    float4 v[RMS_VPT];
+#pragma unroll
+    for (int u = 0; u < RMS_VPT; ++u) {
+      const int k4 = threadIdx.x + u * RMS_THREADS;
+      v[u] = k4 < n4 ? __ldg(xr + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+    }
+    ss = uk_block_sum<RMS_THREADS>(ss, red);
+    const float r = 1.0f / sqrtf(ss / (float)K + eps);
+#pragma unroll
+    for (int u = 0; u < RMS_VPT; ++u) {
+      const int k4 = threadIdx.x + u * RMS_THREADS;
+      if (k4 < n4) {
+        const float4 g = __ldg(gr + k4);
+        __half2 h0 = __floats2half2_rn((v[u].x * r) * g.x, (v[u].y * r) * g.y);
+        __half2 h1 = __floats2half2_rn((v[u].z * r) * g.z, (v[u].w * r) * g.w);
+        out[k4] = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+      }
+    }
+    return;
+  }
+  for (int k4 = threadIdx.x; k4 < n4; k4 += RMS_THREADS) {
     const float4 v = __ldg(xr + k4);
     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   ss = uk_block_sum<RMS_THREADS>(ss, red);
   const float r = 1.0f / sqrtf(ss / (float)K + eps);
-  uint2* out = reinterpret_cast<uint2*>(Xn + (int64_t)b * K);
-  for (int k4 = threadIdx.x; k4 < K / 4; k4 += RMS_THREADS) {
+  for (int k4 = threadIdx.x; k4 < n4; k4 += RMS_THREADS) {
     const float4 v = __ldg(xr + k4), g = __ldg(gr + k4);
     __half2 h0 = __floats2half2_rn((v.x * r) * g.x, (v.y * r) * g.y);
     __half2 h1 = __floats2half2_rn((v.z * r) * g.z, (v.w * r) * g.w);

@@ -60,16 +60,20 @@ __global__ void __launch_bounds__(256) k_channelscale(const float* __restrict__ 
 // ---------------------------------------------------------------------------
 // reduce
 // ---------------------------------------------------------------------------
-template <int W>
+// U loads of W floats in flight per thread; U partial sums combined in a
+// fixed order, so the result does not depend on timing
+template <int W, int U = 4>
 __device__ __forceinline__ float sum_span(const float* __restrict__ x, int64_t nv, int tid, int nthr) {
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) acc[u] = 0.f;
   int64_t v = tid;
-  for (; v + 3 * (int64_t)nthr < nv; v += 4 * (int64_t)nthr) {
-    float d[4][W];
+  for (; v + (U - 1) * (int64_t)nthr < nv; v += U * (int64_t)nthr) {
+    float d[U][W];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) uk_ld_cs<W>(d[u], x + (v + u * (int64_t)nthr) * W);
+    for (int u = 0; u < U; ++u) uk_ld_cs<W>(d[u], x + (v + u * (int64_t)nthr) * W);
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < U; ++u)
 #pragma unroll
       for (int w = 0; w < W; ++w) acc[u] += d[u][w];
   }
@@ -79,7 +83,11 @@ __device__ __forceinline__ float sum_span(const float* __restrict__ x, int64_t n
 #pragma unroll
     for (int w = 0; w < W; ++w) acc[0] += d[w];
   }
-  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+#pragma unroll
+  for (int h = U / 2; h > 0; h /= 2)
+#pragma unroll
+    for (int u = 0; u < h; ++u) acc[u] += acc[u + h];
+  return acc[0];
 }
 
 // one 256-thread CTA per row
