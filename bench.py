@@ -552,6 +552,42 @@ def capture(ctx, fn):
     return graph
 
 
+def bench_rowop_f16(ctx, op, steps, warmup, L=8192, C=16384):
+    """The fp16 row ops (f16 rows in and out, fp32 arithmetic) at the BASELINE row shape."""
+    import unikern_b200.abi as abi
+    torch = ctx.torch
+    X = gen(torch, (L, C), "normal", 3, torch.float16, 2.0 if op == "softmax" else 1.0)
+    W = (gen(torch, (C,), "normal", 4, None, 0.1) + 1.0).half()
+    Y = torch.empty_like(X)
+    if op == "softmax":
+        step = lambda: abi.softmax_f16(X, Y)  # noqa: E731
+        nbytes = 2 * L * C * 2
+    elif op == "rmsnorm":
+        step = lambda: abi.rmsnorm_f16(X, W, Y, 1e-5)  # noqa: E731
+        nbytes = 2 * L * C * 2 + C * 2
+    else:
+        step = lambda: abi.channelscale_f16(X, W, Y)  # noqa: E731
+        nbytes = 2 * L * C * 2 + C * 2
+    ms = ctx.time_steps(step, steps, warmup)
+    return {"ms": ms, "value": nbytes / ms / 1e6}
+
+
+def bench_conv_f16(ctx, steps, warmup, N=32, Cc=256, H=56, W=56, Oc=256, pad=1):
+    """The BASELINE conv shape in fp16 (kind::f16 MMAs on SM pairs)."""
+    import unikern_b200.abi as abi
+    torch = ctx.torch
+    x = gen(torch, (N, Cc, H, W), "uniform", 8).half()
+    w = gen(torch, (Oc, Cc, 3, 3), "normal", 9, None, (2.0 / (9 * Cc)) ** 0.5).half()
+    s = gen(torch, (Oc,), "uniform", 10, None, lo=0.5, hi=1.5).half()
+    y = torch.empty((N, Oc, H, W), dtype=torch.float16, device="cuda")
+    n = abi.lib().uk_cuda_conv2d_f16_workspace_size(N, H, W, Cc, 3, 3, Oc, pad, abi.UK_CONV_NCHW)
+    ws = torch.empty(((n + 15) // 16) * 4, dtype=torch.float32, device="cuda")
+    step = lambda: abi.conv2d_f16(x, w, y, N, H, W, Cc, 3, 3, Oc, pad, s, abi.UK_CONV_NCHW, ws)  # noqa: E731
+    ms = ctx.time_steps(step, steps, warmup)
+    flops = 2.0 * N * H * W * Cc * 9 * Oc
+    return {"ms": ms, "value": flops / ms / 1e9}
+
+
 def bench_conv_sharded(ctx, steps, warmup, N=32, Cc=256, H=56, W=56, Oc=256, pad=1):
     """BASELINE configs[2] over the ranks: images split by batch, tensor-core
     conv per rank, NCCL all-gather of Y (every rank ends with the full Y)."""
@@ -698,6 +734,12 @@ def run_single(args, ctx, pk):
     elif op == "conv":
         r = bench_conv(ctx, args.steps, args.warmup)
         val, unit, bound = r["value"], "TFLOP/s", "tensor_3xtf32"
+    elif op in ("softmax_f16", "rmsnorm_f16", "channelscale_f16"):
+        r = bench_rowop_f16(ctx, op[:-4], args.steps, args.warmup)
+        val, unit, bound = r["value"], "GB/s", "hbm"
+    elif op == "conv_f16":
+        r = bench_conv_f16(ctx, args.steps, args.warmup)
+        val, unit, bound = r["value"], "TFLOP/s", "tensor"
     elif op == "gemm_f32":
         r = bench_gemm_f32(ctx, args.steps, args.warmup)
         val, unit, bound = r["value"], "TFLOP/s", "fp32"
@@ -719,7 +761,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--op", default="all",
                     choices=["all", "gemm_f16", "reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar",
-                             "conv", "gemm_f32", "decode"],
+                             "conv", "gemm_f32", "decode", "softmax_f16", "rmsnorm_f16", "channelscale_f16",
+                             "conv_f16"],
                     help="all = headline f16 GEMM + every other op; otherwise one op alone (profiling)")
     ap.add_argument("--gemm-shape", default="8192,8192,8192", help="M,N,K of the f16 GEMM")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
@@ -770,6 +813,14 @@ def main():
         r = bench_decode(Ctx(1, 0, local_rank), s, 3)
         ops["decode_chain_b32"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
                                    "roofline": roofline("hbm", r["value"], pk)}
+        # fp16 variants (beyond the reference's dtype interval)
+        for op in ("softmax", "rmsnorm", "channelscale"):
+            r = bench_rowop_f16(Ctx(1, 0, local_rank), op, s, 3)
+            ops[op + "_f16"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
+                                "roofline": roofline("hbm", r["value"], pk)}
+        r = bench_conv_f16(Ctx(1, 0, local_rank), max(3, s // 2), 3)
+        ops["conv_f16_n32_256_56_3x3_pad1_scaled"] = {"TFLOP/s": round(r["value"], 2), "ms": round(r["ms"], 4),
+                                                     "roofline": roofline("tensor", r["value"], pk)}
         if not args.no_cpu:
             # the reference's CPU path for every op, timed on this host in this run
             for op in ("reduce", "rmsnorm", "softmax", "channelscale"):

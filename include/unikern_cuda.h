@@ -110,6 +110,19 @@ int uk_cuda_rmsnorm_f32(const float* X, const float* W, float* Y, int64_t L,
  * Replaces uk_softmax (src/codegen_hip.cpp:1985-1996). */
 int uk_cuda_softmax_f32(const float* X, float* Y, int64_t L, int64_t C, void* stream);
 
+/* ---- fp16 row ops ------------------------------------------------------------
+ * softmax / RMSNorm / channelscale on IEEE binary16 rows (uint16_t bit
+ * patterns in and out, fp32 arithmetic, one rounding to f16 per output), with
+ * the formulas and operation order of the fp32 entry points above.  W (the
+ * RMSNorm weight) and S (the channel scale) are f16 too.  Deterministic.
+ * The reference refuses fp16 for these ops (src/codegen_hip.cpp:81-89); these
+ * widen the dtype interval with the same algorithms. */
+int uk_cuda_softmax_f16(const uint16_t* X, uint16_t* Y, int64_t L, int64_t C, void* stream);
+int uk_cuda_rmsnorm_f16(const uint16_t* X, const uint16_t* W, uint16_t* Y, int64_t L, int64_t C, float eps,
+                        void* stream);
+int uk_cuda_channelscale_f16(const uint16_t* X, const uint16_t* S, uint16_t* Y, int64_t L, int64_t C,
+                             void* stream);
+
 /* ---- gemm f32 --------------------------------------------------------------
  * C = A * B, fp32 FFMA (no TF32), fp32 accumulation.  Any M, N, K >= 0.
  * Replaces uk_gemm (src/codegen_hip.cpp:1089-1120). */
@@ -220,6 +233,20 @@ int uk_cuda_conv2d_f32(const float* X, const float* Wt, float* Y, int N, int H, 
  * (src/codegen_hip.cpp:337-411) at the sizes where the tensor cores pay. */
 size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc,
                                      int pad, int layout);
+
+/* fp16 convolution on the tcgen05 tensor cores (kind::f16 MMAs over SM
+ * pairs): X, Wt, scale and Y are IEEE binary16 (uint16_t bit patterns) in the
+ * layouts of uk_cuda_conv2d_f32; fp32 accumulation, the scale applied in
+ * fp32, one rounding to f16.  Needs C a multiple of 64.  The KML layout (HWC
+ * input, [Oc][Kh][Kw][C] weights) is read in place and needs no workspace;
+ * NCHW takes a workspace of uk_cuda_conv2d_f16_workspace_size(...) bytes for
+ * the NHWC copy of X and the permuted weights.  The reference refuses fp16
+ * conv (src/codegen_hip.cpp:81-89); this widens the dtype interval. */
+size_t uk_cuda_conv2d_f16_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc,
+                                         int pad, int layout);
+int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_t* Y, int N, int H, int W,
+                       int C, int Kh, int Kw, int Oc, int pad, const uint16_t* scale, int layout,
+                       void* workspace, size_t workspace_bytes, void* stream);
 int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W,
                           int C, int Kh, int Kw, int Oc, int pad, const float* scale,
                           int layout, void* workspace, size_t workspace_bytes, void* stream);

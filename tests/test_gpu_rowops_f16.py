@@ -1,0 +1,67 @@
+"""fp16 softmax / RMSNorm / channelscale (f16 rows, fp32 arithmetic) against
+the fp64 oracle on the same half inputs (oracle/uk_oracle.c restates the
+reference's cpu_softmax / cpu_rmsnorm / cpu_channelscale,
+src/codegen_hip.cpp:1999-2009, :2168-2178, :2339-2344).
+
+Gate: one f16 rounding of the fp32 result, rel_err <= 1e-3 with the floor
+tau = 2^-14 (the smallest normal f16: below it f16 keeps an absolute step of
+2^-24).  channelscale rounds one fp32 product, so it must equal the oracle's
+fp32 product rounded to f16 bit for bit.
+"""
+import numpy as np
+import pytest
+
+import unikern_b200.abi as abi
+from oracle import oracle as O
+from uk_testutil import dev, empty, host
+
+pytestmark = pytest.mark.gpu
+F16_OUT_TOL = 1e-3
+TAU = 2.0 ** -14
+
+SHAPES = [(64, 256), (7, 33), (1, 1), (3, 4104), (8192, 4096), (2, 40000), (5, 65536), (33, 1000)]
+
+
+def half(a):
+    return O.f32_to_f16(np.asarray(a, np.float32))
+
+
+@pytest.mark.parametrize("L,C", SHAPES)
+def test_softmax_f16(L, C):
+    rng = np.random.default_rng(L + C)
+    Xh = half(rng.normal(0, 2, (L, C)))
+    Y = empty((L, C), "f16")
+    abi.softmax_f16(dev(Xh), Y)
+    ref = O.softmax_f64(O.f16_to_f32(Xh))
+    assert O.rel_err(O.f16_to_f32(host(Y)), ref, TAU) <= F16_OUT_TOL
+
+
+@pytest.mark.parametrize("L,C", SHAPES)
+def test_rmsnorm_f16(L, C):
+    rng = np.random.default_rng(L * 3 + C)
+    Xh = half(rng.normal(0, 1, (L, C)))
+    Wh = half(rng.normal(1, 0.1, C))
+    Y = empty((L, C), "f16")
+    abi.rmsnorm_f16(dev(Xh), dev(Wh), Y, 1e-5)
+    ref = O.rmsnorm_f64(O.f16_to_f32(Xh), O.f16_to_f32(Wh), 1e-5)
+    assert O.rel_err(O.f16_to_f32(host(Y)), ref, TAU) <= F16_OUT_TOL
+
+
+@pytest.mark.parametrize("L,C", SHAPES)
+def test_channelscale_f16_bit_exact(L, C):
+    rng = np.random.default_rng(L * 5 + C)
+    Xh = half(rng.normal(0, 1, (L, C)))
+    Sh = half(rng.uniform(0.5, 1.5, C))
+    Y = empty((L, C), "f16")
+    abi.channelscale_f16(dev(Xh), dev(Sh), Y)
+    want = half(O.channelscale_f32(O.f16_to_f32(Xh), O.f16_to_f32(Sh)))
+    assert np.array_equal(host(Y), want)
+
+
+def test_f16_row_ops_deterministic():
+    rng = np.random.default_rng(9)
+    Xh = dev(half(rng.normal(0, 2, (512, 16384))))
+    Y1, Y2 = empty((512, 16384), "f16"), empty((512, 16384), "f16")
+    abi.softmax_f16(Xh, Y1)
+    abi.softmax_f16(Xh, Y2)
+    assert np.array_equal(host(Y1), host(Y2))

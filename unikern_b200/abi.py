@@ -44,6 +44,11 @@ PROTOTYPES = {
     "uk_cuda_decode_rmsnorm_gemm_f16": (i32, [vp, vp, f32, vp, i64, C.POINTER(vp), i32, i64, i32, i32, i32, i64,
                                                vp, sz, vp]),
     "uk_cuda_gemm_f16_host": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+    "uk_cuda_softmax_f16": (i32, [vp, vp, i64, i64, vp]),
+    "uk_cuda_rmsnorm_f16": (i32, [vp, vp, vp, i64, i64, f32, vp]),
+    "uk_cuda_channelscale_f16": (i32, [vp, vp, vp, i64, i64, vp]),
+    "uk_cuda_conv2d_f16_workspace_size": (sz, [i32] * 9),
+    "uk_cuda_conv2d_f16": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp, sz, vp]),
     "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
@@ -117,6 +122,21 @@ def softmax(X, Y, stream=None):
     check(lib().uk_cuda_softmax_f32(_p(X), _p(Y), L, Cc, _stream(stream)))
 
 
+def softmax_f16(X, Y, stream=None):
+    L, Cc = X.shape
+    check(lib().uk_cuda_softmax_f16(_p(X), _p(Y), L, Cc, _stream(stream)))
+
+
+def rmsnorm_f16(X, W, Y, eps=1e-6, stream=None):
+    L, Cc = X.shape
+    check(lib().uk_cuda_rmsnorm_f16(_p(X), _p(W), _p(Y), L, Cc, eps, _stream(stream)))
+
+
+def channelscale_f16(X, S, Y, stream=None):
+    L, Cc = X.shape
+    check(lib().uk_cuda_channelscale_f16(_p(X), _p(S), _p(Y), L, Cc, _stream(stream)))
+
+
 def gemm_f32(A, B, Cm, stream=None):
     M, K = A.shape
     N = B.shape[1]
@@ -176,6 +196,19 @@ def conv2d_tc(X, Wt, Y, N, H, W, Cc, Kh, Kw, Oc, pad=0, scale=None, layout=UK_CO
     nbytes = ws.numel() * ws.element_size() if ws is not None else 0
     check(lib().uk_cuda_conv2d_f32_ws(_p(X), _p(Wt), _p(Y), N, H, W, Cc, Kh, Kw, Oc, pad, _p(scale), layout,
                                       _p(ws), nbytes, _stream(stream)))
+
+
+def conv2d_f16(X, Wt, Y, N, H, W, Cc, Kh, Kw, Oc, pad=0, scale=None, layout=UK_CONV_NCHW, workspace=None,
+               stream=None):
+    """fp16 convolution on the tensor cores (f16 tensors in and out)."""
+    import torch
+    n = lib().uk_cuda_conv2d_f16_workspace_size(N, H, W, Cc, Kh, Kw, Oc, pad, layout)
+    ws = workspace
+    if ws is None and n:
+        ws = torch.empty(((n + 15) // 16) * 4, dtype=torch.float32, device="cuda")
+    nbytes = ws.numel() * ws.element_size() if ws is not None else 0
+    check(lib().uk_cuda_conv2d_f16(_p(X), _p(Wt), _p(Y), N, H, W, Cc, Kh, Kw, Oc, pad, _p(scale), layout,
+                                   _p(ws), nbytes, _stream(stream)))
 
 
 # ---- KML runner (host side) -----------------------------------------------------

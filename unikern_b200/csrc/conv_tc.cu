@@ -27,6 +27,7 @@
 // run.  Every mbarrier wait is bounded (2 s); a timeout sets this file's fault
 // word (uk_cuda_pipeline_fault) and the CTA unwinds.  Plain single-CTA TMA
 // loads of this GPU's memory only, each into its own CTA.
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -71,8 +72,8 @@ constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(SmemC
 static_assert(SMEM_BYTES <= 232448, "shared memory per block on sm_100");
 
 struct ConvTc {
-  float* y;
-  const float* scale;
+  void* y;            // float (fp32 conv) or __half (fp16 conv)
+  const void* scale;  // same type as y
   int N, Ho, Wo, Oc, C, Kh, Kw, pad;
   int tiles_w, tiles_h, tiles_oc, num_tiles;
 };
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uk_tc_fence_after();
       const int ho = ho0 + m / BW, wo = wo0 + m % BW;
       const bool valid = ho < p.Ho && wo < p.Wo;
-      float* ybase = p.y + (((int64_t)n * p.Oc + oc0) * p.Ho + ho) * p.Wo + wo;
+      float* ybase = (float*)p.y + (((int64_t)n * p.Oc + oc0) * p.Ho + ho) * p.Wo + wo;
       const int64_t ocs = (int64_t)p.Ho * p.Wo;
 #pragma unroll 1
       for (int j = 0; j < BN / 32; ++j) {
@@ -233,7 +234,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uk_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + j * 32, v);
         uk_tmem_ld_wait();
         const int ocj = oc0 + j * 32;
-        const float sc_lane = (p.scale != nullptr && ocj + lane < p.Oc) ? __ldg(p.scale + ocj + lane) : 1.f;
+        const float sc_lane =
+            (p.scale != nullptr && ocj + lane < p.Oc) ? __ldg((const float*)p.scale + ocj + lane) : 1.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float sc = __shfl_sync(0xffffffffu, sc_lane, i);
@@ -259,21 +261,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // leader holds output rows ho0, ho0+1 and the peer ho0+2, ho0+3 (a 2 x 64
 // patch each, its A operand), and each holds 128 of the 256 channels of the
 // weights (its half of the B operand).  The leader issues M = 256 MMAs over
-// both CTAs' shared memory; each CTA's TMEM receives its 128 pixels.  Every
-// SM loads 64 KiB per k-step instead of 96 (its half of B), so the ring is 3
-// stages deep.  Loads count on the leader's full barrier; the leader commits
-// MMA completion to both CTAs' barriers; the epilogues arrive remotely on the
-// leader's tile-empty barrier (the f16 GEMM's pair pipeline).
+// both CTAs' shared memory; each CTA's TMEM receives its 128 pixels.  Loads
+// count on the leader's full barrier; the leader commits MMA completion to
+// both CTAs' barriers; the epilogues arrive remotely on the leader's
+// tile-empty barrier (the f16 GEMM's pair pipeline).
+//
+// One kernel, two operand formats (each k-step is one 128-byte row per pixel
+// and per output channel):
+//   PairF32  fp32 data as tf32 (hi, lo) tiles, 32 channels per k-step, three
+//            kind::tf32 MMAs (lo*hi, hi*lo, hi*hi) per 8-deep slice; 64 KiB
+//            per stage per SM, 3 stages; fp32 output
+//   PairF16  fp16 data, 64 channels per k-step, one kind::f16 MMA per 16-deep
+//            slice; 32 KiB per stage per SM, 6 stages; fp16 output (fp32
+//            accumulation and scale, one rounding)
 constexpr int P_BH = 4;                       // output rows per pair tile
-constexpr int P_STAGES = 3;
 constexpr int P_BNC = BN / 2;                 // channels of B per CTA
-constexpr int P_B_BYTES = P_BNC * BK * 4;     // 16 KiB
-constexpr int P_STAGE_BYTES = 2 * A_BYTES + 2 * P_B_BYTES;  // 64 KiB
-constexpr uint32_t P_IDESC = uk_idesc_tf32(2 * BM, BN, 0, 0);
+constexpr int P_TILE_BYTES = 128 * 128;       // 128 rows x 128 bytes (A, or this CTA's half of B)
 constexpr uint16_t P_PAIR = 0x3;
-struct SmemCtlP {
-  uint64_t full[P_STAGES];
-  uint64_t empty[P_STAGES];
+
+struct PairF32 {
+  using Out = float;
+  static constexpr int BKE = 32, TILES = 2, STAGES = 3;
+  static constexpr uint32_t IDESC = uk_idesc_tf32(2 * BM, BN, 0, 0);
+};
+struct PairF16 {
+  using Out = __half;
+  static constexpr int BKE = 64, TILES = 1, STAGES = 6;
+  static constexpr uint32_t IDESC = uk_idesc_f16_ab(2 * BM, BN, 0, 0);
+};
+
+template <class Tr>
+struct PairCtl {
+  uint64_t full[Tr::STAGES];
+  uint64_t empty[Tr::STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t teardown;
@@ -281,8 +301,16 @@ struct SmemCtlP {
   int abort;
 };
 
-constexpr size_t P_SMEM_BYTES = 1024 + (size_t)P_STAGES * P_STAGE_BYTES + sizeof(SmemCtlP);
-static_assert(P_SMEM_BYTES <= 232448, "shared memory per block on sm_100");
+template <class Tr>
+constexpr int pair_stage_bytes() {
+  return 2 * Tr::TILES * P_TILE_BYTES;  // A tiles then B tiles
+}
+template <class Tr>
+constexpr size_t pair_smem_bytes() {
+  return 1024 + (size_t)Tr::STAGES * pair_stage_bytes<Tr>() + sizeof(PairCtl<Tr>);
+}
+static_assert(pair_smem_bytes<PairF32>() <= 232448 && pair_smem_bytes<PairF16>() <= 232448,
+              "shared memory per block on sm_100");
 
 __device__ __forceinline__ void pair_tile_coords(const ConvTc& p, int t, int& n, int& ho0, int& wo0, int& oc0) {
   const int oct = t % p.tiles_oc;
@@ -296,22 +324,34 @@ __device__ __forceinline__ void pair_tile_coords(const ConvTc& p, int t, int& n,
   oc0 = oct * BN;
 }
 
+__device__ __forceinline__ float out_scale(const float* s, int i) { return __ldg(s + i); }
+__device__ __forceinline__ float out_scale(const __half* s, int i) { return __half2float(__ldg(s + i)); }
+__device__ __forceinline__ void out_store(float* y, float v) { *y = v; }
+__device__ __forceinline__ void out_store(__half* y, float v) { *y = __float2half_rn(v); }
+
+// tmX0/tmW0: the input / weights (fp32 hi, or fp16); tmX1/tmW1: the lo tiles
+// (fp32 only).  p.y / p.scale are of the traits' output type.
+template <class Tr>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    k_conv_tc2(const __grid_constant__ CUtensorMap tmXh, const __grid_constant__ CUtensorMap tmXl,
-               const __grid_constant__ CUtensorMap tmWh, const __grid_constant__ CUtensorMap tmWl, const ConvTc p) {
+    k_conv_pair(const __grid_constant__ CUtensorMap tmX0, const __grid_constant__ CUtensorMap tmX1,
+                const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1, const ConvTc p) {
+  using Out = typename Tr::Out;
+  constexpr int STAGES = Tr::STAGES, STAGE_BYTES = pair_stage_bytes<Tr>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  SmemCtlP* ctl = (SmemCtlP*)(smem + (size_t)P_STAGES * P_STAGE_BYTES);
+  PairCtl<Tr>* ctl = (PairCtl<Tr>*)(smem + (size_t)STAGES * STAGE_BYTES);
   volatile int* abort = &ctl->abort;
+  Out* Y = (Out*)p.y;
+  const Out* scale = (const Out*)p.scale;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t crank = uk_cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int csteps = p.C / BK;
+  const int csteps = p.C / Tr::BKE;
   const int ksteps = p.Kh * p.Kw * csteps;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       uk_mbar_init(&ctl->full[s], 1);
       uk_mbar_init(&ctl->empty[s], 1);
     }
@@ -322,10 +362,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uk_mbar_init(&ctl->teardown, 1);
     ctl->abort = 0;
     uk_fence_mbar_init();
-    uk_tma_prefetch_desc(&tmXh);
-    uk_tma_prefetch_desc(&tmXl);
-    uk_tma_prefetch_desc(&tmWh);
-    uk_tma_prefetch_desc(&tmWl);
+    uk_tma_prefetch_desc(&tmX0);
+    uk_tma_prefetch_desc(&tmW0);
+    if (Tr::TILES == 2) {
+      uk_tma_prefetch_desc(&tmX1);
+      uk_tma_prefetch_desc(&tmW1);
+    }
   }
   if (warp == 1) {
     uk_tmem_alloc_cg2(&ctl->tmem_base, TMEM_COLS);
@@ -346,24 +388,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int hr = ho0 + (int)crank * BH;  // this CTA's first output row
         bool ok = true;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          const int s = it % P_STAGES;
-          const uint32_t ph = (it / P_STAGES) & 1u;
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
           if (!uk_mbar_wait_cluster(&ctl->empty[s], ph ^ 1u, abort, WAIT_NS)) {
             atomicOr(&uk::g_conv_fault, UK_FAULT_PRODUCER);
             ctl->abort = 1;
             ok = false;
             break;
           }
-          const int tap = ks / csteps, c0 = (ks - tap * csteps) * BK;
+          const int tap = ks / csteps, c0 = (ks - tap * csteps) * Tr::BKE;
           const int kh = tap / p.Kw, kw = tap - kh * p.Kw;
-          uint8_t* st = smem + (size_t)s * P_STAGE_BYTES;
+          uint8_t* st = smem + (size_t)s * STAGE_BYTES;
           const uint32_t bar = uk_mapa(uk_smem_u32(&ctl->full[s]), 0);
-          if (crank == 0) uk_mbar_expect_tx(&ctl->full[s], 2 * P_STAGE_BYTES);
-          uk_tma_load_4d_cg2(st, &tmXh, bar, c0, wo0 + kw - p.pad, hr + kh - p.pad, n);
-          uk_tma_load_4d_cg2(st + A_BYTES, &tmXl, bar, c0, wo0 + kw - p.pad, hr + kh - p.pad, n);
+          if (crank == 0) uk_mbar_expect_tx(&ctl->full[s], 2 * STAGE_BYTES);
           const int kcol = tap * p.C + c0;
-          uk_tma_load_2d_cg2(st + 2 * A_BYTES, &tmWh, bar, kcol, oc0 + (int)crank * P_BNC);
-          uk_tma_load_2d_cg2(st + 2 * A_BYTES + P_B_BYTES, &tmWl, bar, kcol, oc0 + (int)crank * P_BNC);
+          uk_tma_load_4d_cg2(st, &tmX0, bar, c0, wo0 + kw - p.pad, hr + kh - p.pad, n);
+          uk_tma_load_2d_cg2(st + Tr::TILES * P_TILE_BYTES, &tmW0, bar, kcol, oc0 + (int)crank * P_BNC);
+          if (Tr::TILES == 2) {
+            uk_tma_load_4d_cg2(st + P_TILE_BYTES, &tmX1, bar, c0, wo0 + kw - p.pad, hr + kh - p.pad, n);
+            uk_tma_load_2d_cg2(st + 3 * P_TILE_BYTES, &tmW1, bar, kcol, oc0 + (int)crank * P_BNC);
+          }
         }
         if (!ok) break;
       }
@@ -382,8 +426,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t d = tmem + buf * BN;
         bool ok = true;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          const int s = it % P_STAGES;
-          const uint32_t ph = (it / P_STAGES) & 1u;
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
           if (!uk_mbar_wait_cluster(&ctl->full[s], ph, abort, WAIT_NS)) {
             atomicOr(&uk::g_conv_fault, UK_FAULT_MMA);
             ctl->abort = 1;
@@ -391,17 +435,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           uk_tc_fence_after();
-          const uint32_t ah = uk_smem_u32(smem + (size_t)s * P_STAGE_BYTES);
-          const uint32_t al = ah + A_BYTES, bh = ah + 2 * A_BYTES, bl = bh + P_B_BYTES;
+          const uint32_t a0 = uk_smem_u32(smem + (size_t)s * STAGE_BYTES);
+          const uint32_t b0 = a0 + Tr::TILES * P_TILE_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint64_t dah = uk_desc_sw128(ah + kk * 32, 16, 1024);
-            const uint64_t dal = uk_desc_sw128(al + kk * 32, 16, 1024);
-            const uint64_t dbh = uk_desc_sw128(bh + kk * 32, 16, 1024);
-            const uint64_t dbl = uk_desc_sw128(bl + kk * 32, 16, 1024);
-            uk_umma_tf32_cg2(d, dal, dbh, P_IDESC, (ks > 0 || kk > 0) ? 1u : 0u);
-            uk_umma_tf32_cg2(d, dah, dbl, P_IDESC, 1u);
-            uk_umma_tf32_cg2(d, dah, dbh, P_IDESC, 1u);
+          for (int kk = 0; kk < 4; ++kk) {
+            // K-major, 128-byte swizzle: +32 bytes per MMA slice (8 tf32 or
+            // 16 f16) inside the atom, 8-row groups 1 KiB apart
+            const uint64_t da = uk_desc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t db = uk_desc_sw128(b0 + kk * 32, 16, 1024);
+            const uint32_t acc = (ks > 0 || kk > 0) ? 1u : 0u;
+            if constexpr (Tr::TILES == 2) {
+              const uint64_t dal = uk_desc_sw128(a0 + P_TILE_BYTES + kk * 32, 16, 1024);
+              const uint64_t dbl = uk_desc_sw128(b0 + P_TILE_BYTES + kk * 32, 16, 1024);
+              uk_umma_tf32_cg2(d, dal, db, Tr::IDESC, acc);  // small terms first
+              uk_umma_tf32_cg2(d, da, dbl, Tr::IDESC, 1u);
+              uk_umma_tf32_cg2(d, da, db, Tr::IDESC, 1u);
+            } else {
+              uk_umma_f16_cg2(d, da, db, Tr::IDESC, acc);
+            }
           }
           uk_umma_commit_cg2(&ctl->empty[s], P_PAIR);
         }
@@ -429,7 +480,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uk_tc_fence_after();
       const int ho = ho0 + (int)crank * BH + m / BW, wo = wo0 + m % BW;
       const bool valid = ho < p.Ho && wo < p.Wo;
-      float* ybase = p.y + (((int64_t)n * p.Oc + oc0) * p.Ho + ho) * p.Wo + wo;
+      Out* ybase = Y + (((int64_t)n * p.Oc + oc0) * p.Ho + ho) * p.Wo + wo;
       const int64_t ocs = (int64_t)p.Ho * p.Wo;
 #pragma unroll 1
       for (int j = 0; j < BN / 32; ++j) {
@@ -437,11 +488,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uk_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + j * 32, v);
         uk_tmem_ld_wait();
         const int ocj = oc0 + j * 32;
-        const float sc_lane = (p.scale != nullptr && ocj + lane < p.Oc) ? __ldg(p.scale + ocj + lane) : 1.f;
+        const float sc_lane = (scale != nullptr && ocj + lane < p.Oc) ? out_scale(scale, ocj + lane) : 1.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float sc = __shfl_sync(0xffffffffu, sc_lane, i);
-          if (valid && ocj + i < p.Oc) ybase[(int64_t)(j * 32 + i) * ocs] = __uint_as_float(v[i]) * sc;
+          if (valid && ocj + i < p.Oc) out_store(ybase + (int64_t)(j * 32 + i) * ocs, __uint_as_float(v[i]) * sc);
         }
       }
       uk_tc_fence_before();
@@ -755,8 +806,8 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     if (cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(k_conv_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM_BYTES) !=
-            cudaSuccess)
+        cudaFuncSetAttribute(k_conv_pair<PairF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)pair_smem_bytes<PairF32>()) != cudaSuccess)
       return uk::check_launch("conv2d: smem attribute");
     attr_done[dev] = true;
   }
@@ -769,7 +820,7 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  cfg.dynamicSmemBytes = pair_smem_bytes<PairF32>();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -778,7 +829,183 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_tc2, txh, txl, twh, twl, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_pair<PairF32>, txh, txl, twh, twl, p);
   if (e != cudaSuccess) return uk::fail(UK_ECUDA, "conv2d(pair): launch: %s", cudaGetErrorString(e));
   return uk::check_launch("conv2d(tcgen05 pair)");
+}
+
+// ---- fp16 convolution -------------------------------------------------------------
+namespace {
+
+// X[n][c][h][w] (f16) -> Xt[n][h][w][c] (f16): one CTA per input row, the C x W
+// plane staged in shared memory (as fp32, exact), contiguous 16-byte stores
+__global__ void __launch_bounds__(ROW_THREADS) k_row_nhwc_h(const __half* __restrict__ X, __half* __restrict__ Xt,
+                                                             int C, int H, int W) {
+  extern __shared__ float plane_h[];  // [W][C + 1]
+  const int64_t nh = blockIdx.x;
+  const int n = (int)(nh / H), h = (int)(nh % H);
+  const int cp = C + 1;
+  const __half* src = X + ((int64_t)n * C * H + h) * W;
+  const int64_t cw = (int64_t)C * W;
+  for (int64_t i = threadIdx.x; i < cw; i += ROW_THREADS) {
+    const int c = (int)(i / W), w = (int)(i - (int64_t)c * W);
+    plane_h[w * cp + c] = __half2float(__ldcs(src + (int64_t)c * H * W + w));
+  }
+  __syncthreads();
+  uint4* dst = reinterpret_cast<uint4*>(Xt + nh * cw);
+  for (int64_t i = threadIdx.x; i < cw / 8; i += ROW_THREADS) {
+    const int64_t e = i * 8;
+    const int w = (int)(e / C), c = (int)(e - (int64_t)w * C);
+    const float* q = plane_h + w * cp + c;
+    uint32_t u[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half2 hh = __floats2half2_rn(q[2 * j], q[2 * j + 1]);
+      u[j] = *reinterpret_cast<uint32_t*>(&hh);
+    }
+    dst[i] = make_uint4(u[0], u[1], u[2], u[3]);
+  }
+}
+
+// weights [Oc][C][Kh][Kw] -> [Oc][kh][kw][c] (f16)
+__global__ void k_permute_weights_h(const __half* __restrict__ Wt, __half* __restrict__ Wp, int Oc, int C, int Kh,
+                                    int Kw) {
+  const int64_t K = (int64_t)C * Kh * Kw, total = (int64_t)Oc * K;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t oc = i / K;
+    const int k = (int)(i - oc * K);
+    const int tap = k / C, c = k - tap * C, kh = tap / Kw, kw = tap - kh * Kw;
+    Wp[i] = Wt[((oc * C + c) * Kh + kh) * Kw + kw];
+  }
+}
+
+int encode_h(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+             const cuuint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return uk::fail(UK_ECUDA, "conv2d_f16: cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return uk::fail(UK_ECUDA, "conv2d_f16: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return UK_OK;
+}
+
+}  // namespace
+
+extern "C" size_t uk_cuda_conv2d_f16_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad,
+                                                    int layout) {
+  (void)pad;
+  if (layout != UK_CONV_NCHW || N <= 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0) return 0;
+  return align256((size_t)N * H * W * C * 2) + align256((size_t)Oc * Kh * Kw * C * 2);
+}
+
+extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_t* Y, int N, int H, int W, int C,
+                                  int Kh, int Kw, int Oc, int pad, const uint16_t* scale, int layout, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (layout != UK_CONV_KML && layout != UK_CONV_NCHW)
+    return uk::fail(UK_EINVAL, "conv2d_f16: unknown layout %d", layout);
+  if (N < 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0 || pad < 0)
+    return uk::fail(UK_EINVAL, "conv2d_f16: invalid dims N=%d H=%d W=%d C=%d Kh=%d Kw=%d Oc=%d pad=%d", N, H, W, C,
+                    Kh, Kw, Oc, pad);
+  if (C % 64 != 0)
+    return uk::fail(UK_EINVAL, "conv2d_f16: C=%d must be a multiple of 64 (one 128-byte row of channels per step)", C);
+  if (layout == UK_CONV_KML && (N != 1 || pad != 0))
+    return uk::fail(UK_EINVAL, "conv2d_f16: the KML layout is one image with valid padding (N=1, pad=0)");
+  const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
+  if (Ho <= 0 || Wo <= 0) return uk::fail(UK_EINVAL, "conv2d_f16: the filter is larger than the padded input");
+  if (N == 0) return UK_OK;
+  if (int rc = uk::check_device_ptr(X, "X")) return rc;
+  if (int rc = uk::check_device_ptr(Wt, "Wt")) return rc;
+  if (int rc = uk::check_device_ptr(Y, "Y")) return rc;
+  if (scale)
+    if (int rc = uk::check_device_ptr(scale, "scale")) return rc;
+  const uint16_t* Xn = X;   // NHWC input
+  const uint16_t* Wk = Wt;  // [Oc][kh][kw][c] weights
+  if (layout == UK_CONV_NCHW) {
+    const size_t need = uk_cuda_conv2d_f16_workspace_size(N, H, W, C, Kh, Kw, Oc, pad, layout);
+    if (workspace == nullptr || workspace_bytes < need)
+      return uk::fail(UK_EINVAL, "conv2d_f16: needs a %zu-byte workspace (uk_cuda_conv2d_f16_workspace_size), got %zu",
+                      need, workspace ? workspace_bytes : (size_t)0);
+    if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
+    if (!uk::aligned16(workspace)) return uk::fail(UK_EINVAL, "conv2d_f16: the workspace must be 16-byte aligned");
+    const size_t plane = (size_t)W * (C + 1) * 4;
+    if (plane > 200 * 1024) return uk::fail(UK_EINVAL, "conv2d_f16: W*C too large for the layout pre-pass");
+    uint16_t* Xt = (uint16_t*)workspace;
+    uint16_t* Wp = (uint16_t*)((uint8_t*)workspace + align256((size_t)N * H * W * C * 2));
+    static bool attr[64] = {false};
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d >= 0 && d < 64 && !attr[d]) {
+      if (cudaFuncSetAttribute(k_row_nhwc_h, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+        return uk::check_launch("conv2d_f16: pre-pass attribute");
+      attr[d] = true;
+    }
+    if ((int64_t)N * H > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d_f16: N*H too large");
+    k_row_nhwc_h<<<(unsigned)((int64_t)N * H), ROW_THREADS, plane, st>>>((const __half*)X, (__half*)Xt, C, H, W);
+    const int64_t nw = (int64_t)Oc * Kh * Kw * C;
+    k_permute_weights_h<<<(unsigned)std::min<int64_t>((nw + 255) / 256, (int64_t)uk::sm_count() * 8), 256, 0, st>>>(
+        (const __half*)Wt, (__half*)Wp, Oc, C, Kh, Kw);
+    if (int rc = uk::check_launch("conv2d_f16(pre-pass)")) return rc;
+    Xn = Xt;
+    Wk = Wp;
+  } else if (!uk::aligned16(X) || !uk::aligned16(Wt)) {
+    return uk::fail(UK_EINVAL, "conv2d_f16: X and Wt must be 16-byte aligned");
+  }
+
+  CUtensorMap tx, tw;
+  const cuuint64_t xdims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
+  const cuuint64_t xstr[3] = {(cuuint64_t)C * 2, (cuuint64_t)W * C * 2, (cuuint64_t)H * W * C * 2};
+  const cuuint32_t xbox[4] = {(cuuint32_t)PairF16::BKE, BW, BH, 1};
+  const int64_t K = (int64_t)Kh * Kw * C;
+  const cuuint64_t wdims[2] = {(cuuint64_t)K, (cuuint64_t)Oc};
+  const cuuint64_t wstr[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t wbox[2] = {(cuuint32_t)PairF16::BKE, (cuuint32_t)P_BNC};
+  if (int rc = encode_h(&tx, Xn, 4, xdims, xstr, xbox)) return rc;
+  if (int rc = encode_h(&tw, Wk, 2, wdims, wstr, wbox)) return rc;
+
+  ConvTc p{};
+  p.y = Y;
+  p.scale = scale;
+  p.N = N;
+  p.Ho = Ho;
+  p.Wo = Wo;
+  p.Oc = Oc;
+  p.C = C;
+  p.Kh = Kh;
+  p.Kw = Kw;
+  p.pad = pad;
+  p.tiles_w = (Wo + BW - 1) / BW;
+  p.tiles_h = (Ho + P_BH - 1) / P_BH;
+  p.tiles_oc = (Oc + BN - 1) / BN;
+  const int64_t tiles = (int64_t)N * p.tiles_h * p.tiles_w * p.tiles_oc;
+  if (tiles > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d_f16: too many tiles");
+  p.num_tiles = (int)tiles;
+
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(k_conv_pair<PairF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)pair_smem_bytes<PairF16>()) != cudaSuccess)
+      return uk::check_launch("conv2d_f16: smem attribute");
+    attr_done[dev] = true;
+  }
+  const int pairs = p.num_tiles < uk::sm_count() / 2 ? p.num_tiles : uk::sm_count() / 2;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = pair_smem_bytes<PairF16>();
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_pair<PairF16>, tx, tx, tw, tw, p);
+  if (e != cudaSuccess) return uk::fail(UK_ECUDA, "conv2d_f16: launch: %s", cudaGetErrorString(e));
+  return uk::check_launch("conv2d_f16(tcgen05 pair)");
 }
