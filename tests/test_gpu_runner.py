@@ -31,6 +31,12 @@ CASES = [
     ('{"op":"softmax","dtype":"fp32","dims":[65536,256]}', 1e-6),
     ('{"op":"rmsnorm","dtype":"fp32","dims":[4096,1000]}', 1e-6),
     ('{"op":"channelscale","dtype":"fp32","dims":[65536,256]}', 0.0),
+    # the fp16 widening (refused by the reference): one f16 rounding of the
+    # fp32 result, channelscale exact on the sawtooth operands
+    ('{"op":"softmax","dtype":"fp16","dims":[65536,256]}', 2 ** -10),
+    ('{"op":"rmsnorm","dtype":"fp16","dims":[4096,1000]}', 2 ** -10),
+    ('{"op":"channelscale","dtype":"fp16","dims":[65536,256]}', 0.0),
+    ('{"op":"conv","dtype":"fp16","dims":[58,58,256,3,3,256]}', 2 ** -10),
 ]
 
 

@@ -69,7 +69,8 @@ def test_b200_hcs_parses_and_fingerprints_stably():
 
 
 @pytest.mark.parametrize("kml,gap", [
-    ('{"op":"softmax","dtype":"fp16","dims":[4,4]}', "dtype=fp16 for op=softmax"),
+    ('{"op":"reduce","dtype":"fp16","dims":[4]}', "dtype=fp16 for op=reduce"),
+    ('{"op":"conv","dtype":"fp16","dims":[32,32,8,3,3,16]}', "needs C a multiple of 64"),
     ('{"op":"gemm","dtype":"int8","dims":[4,4,4]}', "dtype=int8"),
     ('{"op":"gemm","dtype":"fp32","dims":[4,4,4],"children":[{"op":"reduce","dtype":"fp32","dims":[8]}]}',
      "children"),
@@ -136,5 +137,14 @@ def test_bad_inputs_return_2():
     assert rc == 2 and out.startswith("HCS missing required fields:")
     rc, out = abi.run_kml(B200_HCS, '{"op":"gemm","dtype":"fp32","dims":[4,4]}')
     assert rc == 2 and "rejected (1 violations)" in out
-    rc, out = abi.run_kml(B200_HCS, '{"op":"rmsnorm","dtype":"fp16","dims":[4,4]}')
+    rc, out = abi.run_kml(B200_HCS, '{"op":"reduce","dtype":"fp16","dims":[4]}')
     assert rc == 2 and out.startswith("UNSUPPORTED: dtype=fp16")
+
+
+@pytest.mark.parametrize("kml", ['{"op":"softmax","dtype":"fp16","dims":[4,4]}',
+                                 '{"op":"rmsnorm","dtype":"fp16","dims":[4,4]}',
+                                 '{"op":"channelscale","dtype":"fp16","dims":[4,4]}',
+                                 '{"op":"conv","dtype":"fp16","dims":[58,58,256,3,3,256]}'])
+def test_fp16_widening_is_supported(kml):
+    # the reference refuses these (src/codegen_hip.cpp:81-89); nvidia:cuda runs them
+    assert abi.kml_describe(kml)["gap"] == ""

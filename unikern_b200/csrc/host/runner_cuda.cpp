@@ -60,12 +60,12 @@ int64_t payload_bytes(const KmlTree& t, size_t op_ws) {  // op_ws: the reduce / 
   switch (t.op) {
     case OpKind::Gemm: return (d[0] * d[2] + d[2] * d[1] + d[0] * d[1]) * es;
     case OpKind::Conv:
-      return (d[0] * d[1] * d[2] + d[5] * d[3] * d[4] * d[2] + d[5] * (d[0] - d[3] + 1) * (d[1] - d[4] + 1)) * 4 +
+      return (d[0] * d[1] * d[2] + d[5] * d[3] * d[4] * d[2] + d[5] * (d[0] - d[3] + 1) * (d[1] - d[4] + 1)) * es +
              (int64_t)op_ws;
     case OpKind::Reduction: return d[0] * 4 + (int64_t)op_ws + 4;
-    case OpKind::Softmax: return 2 * d[0] * d[1] * 4;
+    case OpKind::Softmax: return 2 * d[0] * d[1] * es;
     case OpKind::RmsNorm:
-    case OpKind::ChannelScale: return (2 * d[0] * d[1] + d[1]) * 4;
+    case OpKind::ChannelScale: return (2 * d[0] * d[1] + d[1]) * es;
   }
   return 0;
 }
@@ -125,19 +125,29 @@ struct OpCall {
                                       (int)d[1], (int)d[2], st)
                    : uk_cuda_gemm_f32((const float*)in0, (const float*)in1, (float*)out, (int)d[0], (int)d[1],
                                       (int)d[2], st);
-      case OpKind::Conv:  // tensor cores when C % 32 == 0 (workspace sized for it), else FFMA
+      case OpKind::Conv:
+        if (f16)  // fp16: kind::f16 tensor cores, the KML input read in place
+          return uk_cuda_conv2d_f16((const uint16_t*)in0, (const uint16_t*)in1, (uint16_t*)out, 1, (int)d[0],
+                                    (int)d[1], (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML,
+                                    nullptr, 0, st);
+        // fp32: tensor cores when C % 32 == 0 (workspace sized for it), else FFMA
         return uk_cuda_conv2d_f32_ws((const float*)in0, (const float*)in1, (float*)out, 1, (int)d[0], (int)d[1],
                                      (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML, ws,
                                      ws_bytes, st);
       case OpKind::Reduction:
         return uk_cuda_reduce_f32((const float*)in0, (float*)out, 1, d[0], ws, ws_bytes, st);
       case OpKind::Softmax:
-        return uk_cuda_softmax_f32((const float*)in0, (float*)out, d[0], d[1], st);
+        return f16 ? uk_cuda_softmax_f16((const uint16_t*)in0, (uint16_t*)out, d[0], d[1], st)
+                   : uk_cuda_softmax_f32((const float*)in0, (float*)out, d[0], d[1], st);
       case OpKind::RmsNorm:
         // the KML contract's eps (src/codegen_hip.cpp:2162, :2175)
-        return uk_cuda_rmsnorm_f32((const float*)in0, (const float*)in1, (float*)out, d[0], d[1], 1e-6f, st);
+        return f16 ? uk_cuda_rmsnorm_f16((const uint16_t*)in0, (const uint16_t*)in1, (uint16_t*)out, d[0], d[1],
+                                         1e-6f, st)
+                   : uk_cuda_rmsnorm_f32((const float*)in0, (const float*)in1, (float*)out, d[0], d[1], 1e-6f, st);
       case OpKind::ChannelScale:
-        return uk_cuda_channelscale_f32((const float*)in0, (const float*)in1, (float*)out, d[0], d[1], st);
+        return f16 ? uk_cuda_channelscale_f16((const uint16_t*)in0, (const uint16_t*)in1, (uint16_t*)out, d[0], d[1],
+                                              st)
+                   : uk_cuda_channelscale_f32((const float*)in0, (const float*)in1, (float*)out, d[0], d[1], st);
     }
     return UK_EINVAL;
   }
@@ -176,7 +186,7 @@ bool stage_operands(OpCall* c, DevArena* ar, cudaStream_t st, std::string* err) 
   if (c->n_in1() > 0) c->in1 = ar->alloc(c->n_in1() * c->es(), "in1");
   c->out = ar->alloc(c->n_out() * c->es(), "out");
   if (c->op == OpKind::Reduction) c->ws_bytes = uk_cuda_reduce_workspace_size(1, c->d[0]);
-  if (c->op == OpKind::Conv)
+  if (c->op == OpKind::Conv && !c->f16)
     c->ws_bytes = uk_cuda_conv2d_workspace_size(1, (int)c->d[0], (int)c->d[1], (int)c->d[2], (int)c->d[3],
                                                 (int)c->d[4], (int)c->d[5], 0, UK_CONV_KML);
   if (c->ws_bytes) c->ws = ar->alloc(c->ws_bytes, "workspace");
@@ -216,8 +226,10 @@ bool BackendNvidia::available() const {
 std::string BackendNvidia::capability_gap(const KmlTree& t) const {
   if (t.layout != "NT") return "layout=" + t.layout + " (only NT is implemented)";
   if (t.dtype == DType::I8) return std::string("dtype=int8 for op=") + op_name(t.op) + " (nvidia:cuda runs fp32 ops and the fp16 gemm)";
-  if (t.dtype == DType::F16 && t.op != OpKind::Gemm)
-    return std::string("dtype=fp16 for op=") + op_name(t.op) + " (nvidia:cuda runs fp16 only for gemm)";
+  if (t.dtype == DType::F16 && t.op == OpKind::Reduction)
+    return "dtype=fp16 for op=reduce (nvidia:cuda runs fp16 gemm, conv, softmax, rmsnorm and channelscale)";
+  if (t.dtype == DType::F16 && t.op == OpKind::Conv && t.dims[2] % 64 != 0)
+    return "dtype=fp16 conv with C=" + std::to_string(t.dims[2]) + " (the fp16 conv needs C a multiple of 64)";
   if (!t.children.empty()) return "children (a composite tree executes per op; declare each op on its own)";
   if (t.op == OpKind::Conv && (t.dims[3] > t.dims[0] || t.dims[4] > t.dims[1]))
     return "conv filter larger than the input";
@@ -374,7 +386,7 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
   timed.f16 = tree.dtype == DType::F16;
   for (int i = 0; i < 6; ++i) timed.d[i] = tree.dims[i];
   const size_t ws = tree.op == OpKind::Reduction ? uk_cuda_reduce_workspace_size(1, tree.dims[0])
-                    : tree.op == OpKind::Conv
+                    : tree.op == OpKind::Conv && tree.dtype == DType::F32
                         ? uk_cuda_conv2d_workspace_size(1, tree.dims[0], tree.dims[1], tree.dims[2], tree.dims[3],
                                                         tree.dims[4], tree.dims[5], 0, UK_CONV_KML)
                         : 0;
@@ -412,7 +424,9 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
     if (tree.op == OpKind::Gemm) {
       v.d[0] = v.d[1] = v.d[2] = 256;
     } else if (tree.op == OpKind::Conv) {
-      const int64_t vd[6] = {32, 32, 8, 3, 3, 16};
+      // the reference's instance (32 x 32 x 8 -> 16, 3 x 3); the fp16 conv
+      // takes 64-channel steps, so its instance has 64 input channels
+      const int64_t vd[6] = {32, 32, timed.f16 ? 64 : 8, 3, 3, 16};
       for (int i = 0; i < 6; ++i) v.d[i] = vd[i];
     } else if (tree.op == OpKind::Reduction) {
       v.d[0] = int64_t(1) << 20;
@@ -430,24 +444,20 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
           rc = ukr_check_gemm(v.in0, v.in1, v.out, (int)v.d[0], (int)v.d[1], (int)v.d[2], v.f16, worst, st);
           break;
         case OpKind::Conv:
-          rc = ukr_check_conv((const float*)v.in0, (const float*)v.in1, (const float*)v.out, (int)v.d[0],
-                              (int)v.d[1], (int)v.d[2], (int)v.d[3], (int)v.d[4], (int)v.d[5], worst, st);
+          rc = ukr_check_conv(v.in0, v.in1, v.out, (int)v.d[0], (int)v.d[1], (int)v.d[2], (int)v.d[3],
+                              (int)v.d[4], (int)v.d[5], v.f16, worst, st);
           break;
         case OpKind::Reduction:
-          rc = ukr_check_rows(UKR_OP_REDUCE, (const float*)v.in0, nullptr, (const float*)v.out, 1, v.d[0], 0.0,
-                              worst, st);
+          rc = ukr_check_rows(UKR_OP_REDUCE, v.in0, nullptr, v.out, 1, v.d[0], 0.0, 0, worst, st);
           break;
         case OpKind::Softmax:
-          rc = ukr_check_rows(UKR_OP_SOFTMAX, (const float*)v.in0, nullptr, (const float*)v.out, v.d[0], v.d[1],
-                              0.0, worst, st);
+          rc = ukr_check_rows(UKR_OP_SOFTMAX, v.in0, nullptr, v.out, v.d[0], v.d[1], 0.0, v.f16, worst, st);
           break;
         case OpKind::RmsNorm:
-          rc = ukr_check_rows(UKR_OP_RMSNORM, (const float*)v.in0, (const float*)v.in1, (const float*)v.out,
-                              v.d[0], v.d[1], (double)1e-6f, worst, st);
+          rc = ukr_check_rows(UKR_OP_RMSNORM, v.in0, v.in1, v.out, v.d[0], v.d[1], (double)1e-6f, v.f16, worst, st);
           break;
         case OpKind::ChannelScale:
-          rc = ukr_check_rows(UKR_OP_CHANNELSCALE, (const float*)v.in0, (const float*)v.in1, (const float*)v.out,
-                              v.d[0], v.d[1], 0.0, worst, st);
+          rc = ukr_check_rows(UKR_OP_CHANNELSCALE, v.in0, v.in1, v.out, v.d[0], v.d[1], 0.0, v.f16, worst, st);
           break;
       }
       if (rc != UK_OK) {

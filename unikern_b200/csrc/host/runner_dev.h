@@ -23,10 +23,11 @@ extern "C" {
 int ukr_saw_fill(void* p, int64_t n, int kind, int f16, void* stream);
 int ukr_check_gemm(const void* A, const void* B, const void* C, int M, int N, int K, int f16, double* worst,
                    void* stream);
-int ukr_check_conv(const float* X, const float* Wt, const float* Y, int H, int W, int C, int Kh, int Kw, int Oc,
-                   double* worst, void* stream);
+// f16 != 0: the operands and the result are IEEE binary16, else fp32
+int ukr_check_conv(const void* X, const void* Wt, const void* Y, int H, int W, int C, int Kh, int Kw, int Oc,
+                   int f16, double* worst, void* stream);
 // row ops: REDUCE compares Y[r] with the row sum; the others compare Y[r][c]
-int ukr_check_rows(int op, const float* X, const float* W, const float* Y, int64_t L, int64_t C, double eps,
+int ukr_check_rows(int op, const void* X, const void* W, const void* Y, int64_t L, int64_t C, double eps, int f16,
                    double* worst, void* stream);
 
 #ifdef __cplusplus

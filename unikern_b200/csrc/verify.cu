@@ -67,9 +67,13 @@ __global__ void k_check_gemm(const T* A, const T* B, const T* C, int M, int N, i
   publish(worst, rel);
 }
 
-// KML conv: X[H][W][C], Wt[Oc][Kh][Kw][C] -> Y[Oc][Ho][Wo], valid
-__global__ void k_check_conv(const float* X, const float* Wt, const float* Y, int H, int W, int C, int Kh, int Kw,
-                             int Oc, double* worst) {
+__device__ __forceinline__ double val(const float* p, int64_t i) { return (double)p[i]; }
+__device__ __forceinline__ double val(const __half* p, int64_t i) { return (double)__half2float(p[i]); }
+
+// KML conv: X[H][W][C], Wt[Oc][Kh][Kw][C] -> Y[Oc][Ho][Wo], valid (fp32 or f16 data)
+template <typename T>
+__global__ void k_check_conv(const T* X, const T* Wt, const T* Y, int H, int W, int C, int Kh, int Kw, int Oc,
+                             double* worst) {
   const int Ho = H - Kh + 1, Wo = W - Kw + 1;
   const int64_t n = (int64_t)Oc * Ho * Wo;
   double rel = 0.0;
@@ -79,32 +83,32 @@ __global__ void k_check_conv(const float* X, const float* Wt, const float* Y, in
     for (int kh = 0; kh < Kh; ++kh)
       for (int kw = 0; kw < Kw; ++kw)
         for (int c = 0; c < C; ++c)
-          s += (double)X[((int64_t)(ho + kh) * W + (wo + kw)) * C + c] *
-               (double)Wt[(((int64_t)oc * Kh + kh) * Kw + kw) * C + c];
-    rel = fmax(rel, rel_of((double)Y[t], s));
+          s += val(X, ((int64_t)(ho + kh) * W + (wo + kw)) * C + c) * val(Wt, (((int64_t)oc * Kh + kh) * Kw + kw) * C + c);
+    rel = fmax(rel, rel_of(val(Y, t), s));
   }
   publish(worst, rel);
 }
 
 // one warp per row: the row statistic in fp64, then every element checked
-__global__ void k_check_rows(int op, const float* X, const float* W, const float* Y, int64_t L, int64_t C, double eps,
+template <typename T>
+__global__ void k_check_rows(int op, const T* X, const T* W, const T* Y, int64_t L, int64_t C, double eps,
                              double* worst) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   double rel = 0.0;  // this lane's worst over all its rows
   for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < L; r += warps) {
-    const float* x = X + r * C;
-    const float* y = Y + r * C;
+    const T* x = X + r * C;
+    const T* y = Y + r * C;
     if (op == UKR_OP_REDUCE) {
       double s = 0.0;
-      for (int64_t c = lane; c < C; c += 32) s += (double)x[c];
+      for (int64_t c = lane; c < C; c += 32) s += val(x, c);
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) rel = fmax(rel, rel_of((double)Y[r], s));
+      if (lane == 0) rel = fmax(rel, rel_of(val(Y, r), s));
       continue;
     }
     double a = op == UKR_OP_SOFTMAX ? -INFINITY : 0.0;
     for (int64_t c = lane; c < C; c += 32) {
-      const double v = (double)x[c];
+      const double v = val(x, c);
       if (op == UKR_OP_SOFTMAX) a = fmax(a, v);
       else if (op == UKR_OP_RMSNORM) a += v * v;
     }
@@ -114,16 +118,16 @@ __global__ void k_check_rows(int op, const float* X, const float* W, const float
     }
     double sum = 0.0;
     if (op == UKR_OP_SOFTMAX) {
-      for (int64_t c = lane; c < C; c += 32) sum += exp((double)x[c] - a);
+      for (int64_t c = lane; c < C; c += 32) sum += exp(val(x, c) - a);
       for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     }
     const double rms = op == UKR_OP_RMSNORM ? 1.0 / sqrt(a / (double)C + eps) : 0.0;
     for (int64_t c = lane; c < C; c += 32) {
       double ref;
-      if (op == UKR_OP_SOFTMAX) ref = exp((double)x[c] - a) / sum;
-      else if (op == UKR_OP_RMSNORM) ref = (double)x[c] * rms * (double)W[c];
-      else ref = (double)x[c] * (double)W[c];  // channelscale
-      rel = fmax(rel, rel_of((double)y[c], ref));
+      if (op == UKR_OP_SOFTMAX) ref = exp(val(x, c) - a) / sum;
+      else if (op == UKR_OP_RMSNORM) ref = val(x, c) * rms * val(W, c);
+      else ref = val(x, c) * val(W, c);  // channelscale
+      rel = fmax(rel, rel_of(val(y, c), ref));
     }
   }
   publish(worst, rel);
@@ -162,20 +166,30 @@ int ukr_check_gemm(const void* A, const void* B, const void* C, int M, int N, in
   return uk::check_launch("check gemm");
 }
 
-int ukr_check_conv(const float* X, const float* Wt, const float* Y, int H, int W, int C, int Kh, int Kw, int Oc,
-                   double* worst, void* stream) {
+int ukr_check_conv(const void* X, const void* Wt, const void* Y, int H, int W, int C, int Kh, int Kw, int Oc,
+                   int f16, double* worst, void* stream) {
   const int64_t n = (int64_t)Oc * (H - Kh + 1) * (W - Kw + 1);
   if (n <= 0) return UK_OK;
-  k_check_conv<<<grid_for(n, 128), 128, 0, static_cast<cudaStream_t>(stream)>>>(X, Wt, Y, H, W, C, Kh, Kw, Oc,
-                                                                                 worst);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (f16)
+    k_check_conv<__half><<<grid_for(n, 128), 128, 0, s>>>((const __half*)X, (const __half*)Wt, (const __half*)Y, H,
+                                                          W, C, Kh, Kw, Oc, worst);
+  else
+    k_check_conv<float><<<grid_for(n, 128), 128, 0, s>>>((const float*)X, (const float*)Wt, (const float*)Y, H, W,
+                                                         C, Kh, Kw, Oc, worst);
   return uk::check_launch("check conv");
 }
 
-int ukr_check_rows(int op, const float* X, const float* W, const float* Y, int64_t L, int64_t C, double eps,
+int ukr_check_rows(int op, const void* X, const void* W, const void* Y, int64_t L, int64_t C, double eps, int f16,
                    double* worst, void* stream) {
   if (L <= 0) return UK_OK;
-  k_check_rows<<<grid_for(L * 32, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(op, X, W, Y, L, C, eps,
-                                                                                      worst);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (f16)
+    k_check_rows<__half><<<grid_for(L * 32, 256), 256, 0, s>>>(op, (const __half*)X, (const __half*)W,
+                                                               (const __half*)Y, L, C, eps, worst);
+  else
+    k_check_rows<float><<<grid_for(L * 32, 256), 256, 0, s>>>(op, (const float*)X, (const float*)W,
+                                                              (const float*)Y, L, C, eps, worst);
   return uk::check_launch("check rows");
 }
 
