@@ -156,6 +156,19 @@ int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_t* B, int64
 int uk_cuda_gemm_f16_host(const uint16_t* hA, const uint16_t* hB, uint16_t* hC, uint16_t* dA,
                           uint16_t* dB, uint16_t* dC, int M, int N, int K, int chunks, void* stream);
 
+/* GEMM larger than the device (the reference's streamed scenario B,
+ * src/codegen_hip.cpp:1143-1238): C = A * B from and to page-locked host
+ * memory with only B resident (dB, K*N elements) and A, C passing through a
+ * two-slot ring of block_rows-row blocks in `ring` (at least
+ * uk_cuda_gemm_streamed_ring_size(M, N, K, f16, block_rows) bytes of device
+ * memory).  Block i's upload, GEMM and download overlap blocks i+-1; a slot is
+ * reused only after its previous block's GEMM and download finished.  f16 != 0:
+ * binary16 data on the tensor cores; 0: fp32 on the FFMA kernel.  Asynchronous
+ * on `stream`; shares the copy streams of uk_cuda_gemm_f16_host. */
+size_t uk_cuda_gemm_streamed_ring_size(int M, int N, int K, int f16, int block_rows);
+int uk_cuda_gemm_streamed(const void* hA, const void* hB, void* hC, void* dB, void* ring, size_t ring_bytes,
+                          int M, int N, int K, int f16, int block_rows, void* stream);
+
 /* ---- multi-GPU f16 GEMM (one process per GPU, NVLink peers) ----------------
  * N-sharded GEMM with the all-gather fused into the store: computes columns
  * [col_offset, col_offset + N_shard) of C = A * B from this rank's column

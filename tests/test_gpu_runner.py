@@ -84,8 +84,47 @@ def test_verify_mode_writes_no_ledger(tmp_path):
     assert not ledger.exists()
 
 
-def test_oversized_payload_is_refused_not_streamed(tmp_path):
-    # 3 x 65536^2 fp32 = 48 GiB per operand: far beyond 0.85 x HBM
-    rc, out = abi.run_kml(HCS, '{"op":"gemm","dtype":"fp32","dims":[131072,131072,131072]}', str(tmp_path / "l"))
+def test_oversized_payload_is_refused_when_b_does_not_fit(tmp_path):
+    # B alone is 262144^2 fp32 = 256 GiB: beyond 0.85 x HBM, so not even the
+    # streamed GEMM (B resident) can run it
+    rc, out = abi.run_kml(HCS, '{"op":"gemm","dtype":"fp32","dims":[1024,262144,262144]}', str(tmp_path / "l"))
     assert rc == 1 and "UNIKERN_ERROR what=stream_refused" in out
     assert not (tmp_path / "l").exists()
+
+
+def small_vram_hcs(mib):
+    import json
+    h = json.loads(HCS)
+    for t in h["tiers"]:
+        if t["name"] == "vram":
+            t["bytes"] = mib << 20
+    return json.dumps(h)
+
+
+@pytest.mark.parametrize("kml,rows,max_rel", [
+    ('{"op":"gemm","dtype":"fp16","dims":[4096,1024,1024]}', 1280, 2 ** -11),
+    ('{"op":"gemm","dtype":"fp32","dims":[2048,1024,1024]}', 512, 0.0),
+], ids=["fp16_4096x1024x1024", "fp32_2048x1024x1024"])
+def test_payload_beyond_the_device_tier_streams(tmp_path, kml, rows, max_rel):
+    # a 16 MiB device tier models a device the operands do not fit: the GEMM
+    # runs streamed (scenario B), verifies through the ring and commits
+    hcs = small_vram_hcs(16)
+    d = abi.kml_describe(kml, hcs)
+    assert "placement: streamed" in d["placement"] and f"{rows}-row blocks" in d["placement"]
+    ledger = tmp_path / "ledger.jsonl"
+    rc, out = abi.run_kml(hcs, kml, str(ledger))
+    assert rc == 0, out
+    tok = abi.result_tokens(out)
+    assert tok["verify"] == "PASS" and float(tok["max_rel"]) <= max_rel, out
+    assert tok["mode"] == "streamed" and tok["stream_path"] == "pinned", out
+    assert float(tok["kernel_ms"]) > 0 and float(tok["measured_ms"]) > 0
+    assert float(tok["payload_mb"]) > 0.85 * 16
+    rows_ = [r.split("\t") for r in ledger.read_text().splitlines()]
+    assert len(rows_) == 1 and rows_[0][0] == d["ledger_key"] and "streamed" in rows_[0][-1]
+    assert abi.lib().uk_cuda_pipeline_fault() == 0
+
+
+def test_streamed_refused_for_non_gemm(tmp_path):
+    rc, out = abi.run_kml(small_vram_hcs(16), '{"op":"softmax","dtype":"fp32","dims":[8192,1024]}',
+                          str(tmp_path / "l"))
+    assert rc == 1 and "UNIKERN_ERROR what=stream_refused" in out

@@ -68,6 +68,30 @@ def test_b200_hcs_parses_and_fingerprints_stably():
     assert a["gap"] == ""
 
 
+def _hcs_with_vram(mib):
+    h = json.loads(B200_HCS)
+    for t in h["tiers"]:
+        if t["name"] == "vram":
+            t["bytes"] = mib << 20
+    return json.dumps(h)
+
+
+@pytest.mark.parametrize("kml,mib,want", [
+    ('{"op":"gemm","dtype":"fp16","dims":[4096,1024,1024]}', 16, "streamed"),   # 18 MiB > 0.85 x 16
+    ('{"op":"gemm","dtype":"fp16","dims":[1024,1024,1024]}', 16, "resident"),   # 6 MiB fits
+    ('{"op":"gemm","dtype":"fp32","dims":[1024,4096,1024]}', 16, "refused"),    # B alone is 16 MiB
+    ('{"op":"softmax","dtype":"fp32","dims":[8192,1024]}', 16, "refused"),     # only a gemm streams
+    ('{"op":"gemm","dtype":"fp16","dims":[8192,8192,8192]}', 183359, "resident"),
+])
+def test_placement_resident_streamed_or_refused(kml, mib, want):
+    # scenario B: a gemm beyond 0.85 x the device tier keeps B resident and
+    # streams A / C through a ring of row blocks (multiples of 256 rows)
+    d = abi.kml_describe(kml, _hcs_with_vram(mib))
+    assert d["placement"].startswith("placement: " + want), d["placement"]
+    if want == "streamed":
+        assert "1280-row blocks" in d["placement"]
+
+
 @pytest.mark.parametrize("kml,gap", [
     ('{"op":"reduce","dtype":"fp16","dims":[4]}', "dtype=fp16 for op=reduce"),
     ('{"op":"conv","dtype":"fp16","dims":[32,32,8,3,3,16]}', "needs C a multiple of 64"),

@@ -49,6 +49,8 @@ PROTOTYPES = {
     "uk_cuda_channelscale_f16": (i32, [vp, vp, vp, i64, i64, vp]),
     "uk_cuda_conv2d_f16_workspace_size": (sz, [i32] * 9),
     "uk_cuda_conv2d_f16": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp, sz, vp]),
+    "uk_cuda_gemm_streamed_ring_size": (sz, [i32, i32, i32, i32, i32]),
+    "uk_cuda_gemm_streamed": (i32, [vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, vp]),
     "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
@@ -180,6 +182,17 @@ def gemm_f16_host(Ah, Bh, Ch, Ad, Bd, Cd, chunks=0, stream=None):
     N = Bh.shape[1]
     check(lib().uk_cuda_gemm_f16_host(_p(Ah), _p(Bh), _p(Ch), _p(Ad), _p(Bd), _p(Cd), M, N, K, chunks,
                                       _stream(stream)))
+
+
+def gemm_streamed(Ah, Bh, Ch, Bd, ring, block_rows, stream=None):
+    """C = A * B (host tensors, f16 or fp32) with only B resident and A / C
+    streamed through a two-slot device ring of block_rows-row blocks."""
+    import torch
+    M, K = Ah.shape
+    N = Bh.shape[1]
+    f16 = int(Ah.dtype == torch.float16)
+    check(lib().uk_cuda_gemm_streamed(_p(Ah), _p(Bh), _p(Ch), _p(Bd), _p(ring), ring.numel() * ring.element_size(),
+                                      M, N, K, f16, block_rows, _stream(stream)))
 
 
 def conv2d_workspace(N, H, W, Cc, Kh, Kw, Oc, pad=0, layout=UK_CONV_NCHW):

@@ -23,6 +23,7 @@
 #include <iomanip>
 #include <limits>
 #include <sstream>
+#include <unistd.h>
 #include <vector>
 
 #include "runner_dev.h"
@@ -244,6 +245,24 @@ std::string BackendNvidia::generate(const Solution& s, const Hcs& h, const KmlTr
   return os.str();
 }
 
+// ---- scenario B ----------------------------------------------------------------
+
+// A GEMM whose operands exceed 0.85 x the device budget runs streamed (the
+// reference's scenario B, src/codegen_hip.cpp:1485-1500): B stays resident
+// and A, C pass through a two-slot ring of row blocks.  Returns the block
+// rows (a multiple of 256 where the budget allows, else of 32), or 0 when
+// the payload fits (resident), the op is not a GEMM, or B plus the smallest
+// ring does not fit the budget.
+int64_t stream_block_rows(const KmlTree& t, int64_t payload, double budget_bytes) {
+  if (double(payload) <= 0.85 * budget_bytes || t.op != OpKind::Gemm) return 0;
+  const int64_t M = t.dims[0], N = t.dims[1], K = t.dims[2], es = dtype_bytes(t.dtype);
+  const double left = 0.85 * budget_bytes - double(K) * double(N) * double(es) - 1024.0;
+  int64_t rows = left > 0 ? (int64_t)(left / (2.0 * double(K + N) * double(es))) : 0;
+  rows = rows >= 256 ? rows / 256 * 256 : rows / 32 * 32;
+  if (rows < 32) return 0;
+  return rows < M ? rows : M;
+}
+
 // ---- solver ------------------------------------------------------------------
 
 Solution solve_b200(const Hcs& h, const KmlTree& t, int sms) {
@@ -270,10 +289,24 @@ Solution solve_b200(const Hcs& h, const KmlTree& t, int sms) {
     if (ctas < units) comp *= double(units) / double(ctas > 0 ? ctas : 1);
   }
   const double copy = h.unified_memory || h.link_bw_gbps <= 0 ? 0.0 : double(w.bytes) / (h.link_bw_gbps * 1e9) * 1e3;
-  s.c_ms = std::max(comp, mem) + copy;
+  const int64_t payload = payload_bytes(t, 0);
+  const int64_t rows = stream_block_rows(t, payload, double(h.device_capacity()));
   std::ostringstream pr;
-  pr << "placement: resident on " << h.device << " (sm_100a) tile=" << tile[0] << "x" << tile[1]
-     << " k_block=" << tile[2] << " stages=" << tile[3] << " path=pinned-copy";
+  if (rows == 0 && h.device_capacity() > 0 && double(payload) > 0.85 * double(h.device_capacity())) {
+    s.c_ms = std::max(comp, mem) + copy;
+    pr << "placement: refused on " << h.device << " (the payload exceeds 0.85 x the device tier and only a gemm "
+       << "whose B fits streams) path=none";
+  } else if (rows > 0) {
+    // streamed: the ring overlaps the copies with the block GEMMs
+    s.c_ms = std::max(std::max(comp, mem), copy);
+    pr << "placement: streamed on " << h.device << " (sm_100a; B resident, A/C in a two-slot ring of " << rows
+       << "-row blocks) tile=" << tile[0] << "x" << tile[1] << " k_block=" << tile[2] << " stages=" << tile[3]
+       << " path=pinned-copy";
+  } else {
+    s.c_ms = std::max(comp, mem) + copy;
+    pr << "placement: resident on " << h.device << " (sm_100a) tile=" << tile[0] << "x" << tile[1]
+       << " k_block=" << tile[2] << " stages=" << tile[3] << " path=pinned-copy";
+  }
   s.placement_record = pr.str();
   return s;
 }
@@ -392,15 +425,32 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
                         : 0;
   const int64_t payload = payload_bytes(tree, ws);
   const double payload_mb = double(payload) / (1024.0 * 1024.0);
-  if (double(payload) > 0.85 * double(tot)) {
-    std::ostringstream e;
-    e << "UNIKERN_ERROR what=stream_refused payload_mb=" << std::fixed << std::setprecision(6) << payload_mb
-      << " vram_total=" << tot << " (nvidia:cuda is resident-only: the payload exceeds 0.85 * the device's "
-      << "reported memory and streaming is not implemented; nothing ran)";
-    r.result_line = e.str();
-    log << r.result_line << "\n";
-    r.exit_code = 4;
-    return finish();
+  // the device budget: the HCS's declared device tier, never more than the
+  // device reports (a smaller HCS tier models a smaller device)
+  const int64_t declared = hcs.device_capacity();
+  const double budget = double(declared > 0 && (uint64_t)declared < tot ? (uint64_t)declared : tot);
+  const int64_t stream_rows = stream_block_rows(tree, payload, budget);  // > 0: scenario B
+  if (double(payload) > 0.85 * budget) {
+    // the streamed operands live in page-locked host memory: at most half of
+    // the host's RAM (and of the HCS's host tier where it declares one)
+    const int64_t es = dtype_bytes(tree.dtype);
+    const double host_need =
+        double(tree.dims[0] * tree.dims[2] + tree.dims[2] * tree.dims[1] + tree.dims[0] * tree.dims[1]) * double(es);
+    double host_cap = double(sysconf(_SC_PHYS_PAGES)) * double(sysconf(_SC_PAGE_SIZE));
+    const int64_t ram = hcs.tier_bytes("ram");
+    if (ram > 0 && double(ram) < host_cap) host_cap = double(ram);
+    if (stream_rows == 0 || host_need > 0.5 * host_cap) {
+      std::ostringstream e;
+      e << "UNIKERN_ERROR what=stream_refused payload_mb=" << std::fixed << std::setprecision(6) << payload_mb
+        << " vram_total=" << tot << " ("
+        << (stream_rows == 0 ? "the payload exceeds 0.85 * the device budget and only a gemm whose B fits streams"
+                             : "the streamed operands exceed half of the host's memory")
+        << "; nothing ran)";
+      r.result_line = e.str();
+      log << r.result_line << "\n";
+      r.exit_code = 4;
+      return finish();
+    }
   }
   const bool big = payload > (int64_t(2) << 30);
   const bool warm_once = timed.f16 || tree.op == OpKind::Softmax || tree.op == OpKind::RmsNorm ||
@@ -434,7 +484,23 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
     double* worst = static_cast<double*>(ar.alloc(sizeof(double), "max_rel"));
     ok = worst && stage_operands(&v, &ar, st, &err) &&
          cuda_ok(cudaMemsetAsync(worst, 0, sizeof(double), st), "memset max_rel", &err);
-    if (ok && (rc = v.launch(st)) != UK_OK) {
+    if (ok && stream_rows > 0) {
+      // scenario B verifies the streamed path itself: the 256^3 instance
+      // through the ring in four 64-row blocks, from and to pinned memory
+      const size_t es = v.es(), nb = 256 * 256 * es;
+      const size_t rb = uk_cuda_gemm_streamed_ring_size(256, 256, 256, v.f16, 64);
+      void *hA = ar.pinned(nb, "A"), *hB = ar.pinned(nb, "B"), *hC = ar.pinned(nb, "C");
+      void* ring = ar.alloc(rb, "ring");
+      ok = ar.err.empty();
+      if (!ok) err = ar.err;
+      ok = ok && cuda_ok(cudaMemcpyAsync(hA, v.in0, nb, cudaMemcpyDeviceToHost, st), "stage A", &err) &&
+           cuda_ok(cudaMemcpyAsync(hB, v.in1, nb, cudaMemcpyDeviceToHost, st), "stage B", &err);
+      if (ok && uk_cuda_gemm_streamed(hA, hB, hC, v.in1, ring, rb, 256, 256, 256, v.f16, 64, st) != UK_OK) {
+        err = uk_cuda_last_error();
+        ok = false;
+      }
+      ok = ok && cuda_ok(cudaMemcpyAsync(v.out, hC, nb, cudaMemcpyHostToDevice, st), "return C", &err);
+    } else if (ok && (rc = v.launch(st)) != UK_OK) {
       err = uk_cuda_last_error();
       ok = false;
     }
@@ -478,59 +544,132 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
     ar.dev.clear();
   }
 
-  // ---- 2. timing at the declared dims ----
-  if (ok) ok = stage_operands(&timed, &ar, st, &err);
-  void *h0 = nullptr, *h1 = nullptr, *hout = nullptr;
-  const size_t b0 = timed.n_in0() * timed.es(), b1 = timed.n_in1() * timed.es(), bo = timed.n_out() * timed.es();
-  if (ok) {
-    h0 = ar.pinned(b0, "in0");
-    h1 = b1 ? ar.pinned(b1, "in1") : nullptr;
-    hout = ar.pinned(bo, "out");
+  // ---- 2a. scenario B: the GEMM streamed through a ring (B resident) ----
+  if (ok && stream_rows > 0) {
+    const int64_t M = tree.dims[0], N = tree.dims[1], K = tree.dims[2];
+    const size_t es = timed.es();
+    const size_t ring_bytes = uk_cuda_gemm_streamed_ring_size((int)M, (int)N, (int)K, timed.f16, (int)stream_rows);
+    void* dB = ar.alloc((size_t)K * N * es, "B");
+    void* ring = ar.alloc(ring_bytes, "ring");
+    void* hA = ar.pinned((size_t)M * K * es, "A");
+    void* hB = ar.pinned((size_t)K * N * es, "B");
+    void* hC = ar.pinned((size_t)M * N * es, "C");
     if (!ar.err.empty()) {
       err = ar.err;
       ok = false;
     }
-  }
-  // the host copies hold the same sawtooth values as the device operands
-  ok = ok && cuda_ok(cudaMemcpyAsync(h0, timed.in0, b0, cudaMemcpyDeviceToHost, st), "stage in0", &err) &&
-       (!b1 || cuda_ok(cudaMemcpyAsync(h1, timed.in1, b1, cudaMemcpyDeviceToHost, st), "stage in1", &err)) &&
-       cuda_ok(cudaStreamSynchronize(st), "stage", &err);
-  auto pass = [&]() -> bool {
-    if (!cuda_ok(cudaMemcpyAsync(timed.in0, h0, b0, cudaMemcpyHostToDevice, st), "H2D in0", &err)) return false;
-    if (b1 && !cuda_ok(cudaMemcpyAsync(timed.in1, h1, b1, cudaMemcpyHostToDevice, st), "H2D in1", &err)) return false;
-    if (timed.launch(st) != UK_OK) {
-      err = uk_cuda_last_error();
-      return false;
+    // the host operands get the sawtooth values, a ring-sized block at a time
+    ok = ok && ukr_saw_fill(dB, K * N, UKR_SAW_B, timed.f16, st) == UK_OK &&
+         cuda_ok(cudaMemcpyAsync(hB, dB, (size_t)K * N * es, cudaMemcpyDeviceToHost, st), "stage B", &err);
+    for (int64_t r0 = 0; ok && r0 < M; r0 += stream_rows) {
+      const int64_t nr = r0 + stream_rows < M ? stream_rows : M - r0;
+      ok = ukr_saw_fill_at(ring, nr * K, r0 * K, UKR_SAW_A, timed.f16, st) == UK_OK &&
+           cuda_ok(cudaMemcpyAsync((uint8_t*)hA + r0 * K * es, ring, nr * K * es, cudaMemcpyDeviceToHost, st),
+                   "stage A", &err) &&
+           cuda_ok(cudaStreamSynchronize(st), "stage", &err);
     }
-    return cuda_ok(cudaMemcpyAsync(hout, timed.out, bo, cudaMemcpyDeviceToHost, st), "D2H out", &err);
-  };
-  cudaEvent_t e0 = nullptr, e1 = nullptr;
-  if (ok) ok = cuda_ok(cudaEventCreate(&e0), "event", &err) && cuda_ok(cudaEventCreate(&e1), "event", &err);
-  for (int i = 0; ok && i < warm; ++i) ok = pass();
-  if (ok) ok = cuda_ok(cudaStreamSynchronize(st), "warm", &err);
-  double total = 0;
-  for (int i = 0; ok && i < iters; ++i) {
-    float ms = 0;
-    ok = cuda_ok(cudaEventRecord(e0, st), "record", &err) && pass() &&
-         cuda_ok(cudaEventRecord(e1, st), "record", &err) && cuda_ok(cudaEventSynchronize(e1), "sync", &err) &&
-         cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
-    total += ms;
-  }
-  if (ok) {
-    r.measured_ms = total / iters;
-    float ms = 0;
-    ok = cuda_ok(cudaEventRecord(e0, st), "record", &err);
-    for (int i = 0; ok && i < iters; ++i)
-      if (timed.launch(st) != UK_OK) {
+    auto pass = [&]() -> bool {
+      if (uk_cuda_gemm_streamed(hA, hB, hC, dB, ring, ring_bytes, (int)M, (int)N, (int)K, timed.f16,
+                                (int)stream_rows, st) != UK_OK) {
         err = uk_cuda_last_error();
+        return false;
+      }
+      return true;
+    };
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ok) ok = cuda_ok(cudaEventCreate(&e0), "event", &err) && cuda_ok(cudaEventCreate(&e1), "event", &err);
+    for (int i = 0; ok && i < warm; ++i) ok = pass();
+    double total = 0;
+    for (int i = 0; ok && i < iters; ++i) {
+      float ms = 0;
+      ok = cuda_ok(cudaEventRecord(e0, st), "record", &err) && pass() &&
+           cuda_ok(cudaEventRecord(e1, st), "record", &err) && cuda_ok(cudaEventSynchronize(e1), "sync", &err) &&
+           cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
+      total += ms;
+    }
+    if (ok) {
+      // kernel-only: the block GEMMs of one pass, run on the ring's first slot
+      r.measured_ms = total / iters;
+      const int64_t nblk = (M + stream_rows - 1) / stream_rows;
+      uint8_t* a0 = (uint8_t*)(((uintptr_t)ring + 255) & ~(uintptr_t)255);
+      const size_t a_slot = ((size_t)stream_rows * K * es + 255) / 256 * 256;
+      uint8_t* c0 = a0 + 2 * a_slot;
+      float ms = 0;
+      ok = cuda_ok(cudaEventRecord(e0, st), "record", &err);
+      for (int64_t b = 0; ok && b < nblk * iters; ++b) {
+        const int nr = (int)((b % nblk) == nblk - 1 ? M - (nblk - 1) * stream_rows : stream_rows);
+        const int rc = timed.f16 ? uk_cuda_gemm_f16((const uint16_t*)a0, (const uint16_t*)dB, (uint16_t*)c0, nr,
+                                                    (int)N, (int)K, st)
+                                 : uk_cuda_gemm_f32((const float*)a0, (const float*)dB, (float*)c0, nr, (int)N,
+                                                    (int)K, st);
+        if (rc != UK_OK) {
+          err = uk_cuda_last_error();
+          ok = false;
+        }
+      }
+      ok = ok && cuda_ok(cudaEventRecord(e1, st), "record", &err) &&
+           cuda_ok(cudaEventSynchronize(e1), "sync", &err) && cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
+      r.kernel_ms = double(ms) / iters;
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+  }
+
+  // ---- 2. timing at the declared dims (resident) ----
+  if (stream_rows == 0) {
+    ok = ok && stage_operands(&timed, &ar, st, &err);
+    void *h0 = nullptr, *h1 = nullptr, *hout = nullptr;
+    const size_t b0 = timed.n_in0() * timed.es(), b1 = timed.n_in1() * timed.es(), bo = timed.n_out() * timed.es();
+    if (ok) {
+      h0 = ar.pinned(b0, "in0");
+      h1 = b1 ? ar.pinned(b1, "in1") : nullptr;
+      hout = ar.pinned(bo, "out");
+      if (!ar.err.empty()) {
+        err = ar.err;
         ok = false;
       }
-    ok = ok && cuda_ok(cudaEventRecord(e1, st), "record", &err) && cuda_ok(cudaEventSynchronize(e1), "sync", &err) &&
-         cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
-    r.kernel_ms = double(ms) / iters;
+    }
+    // the host copies hold the same sawtooth values as the device operands
+    ok = ok && cuda_ok(cudaMemcpyAsync(h0, timed.in0, b0, cudaMemcpyDeviceToHost, st), "stage in0", &err) &&
+         (!b1 || cuda_ok(cudaMemcpyAsync(h1, timed.in1, b1, cudaMemcpyDeviceToHost, st), "stage in1", &err)) &&
+         cuda_ok(cudaStreamSynchronize(st), "stage", &err);
+    auto pass = [&]() -> bool {
+      if (!cuda_ok(cudaMemcpyAsync(timed.in0, h0, b0, cudaMemcpyHostToDevice, st), "H2D in0", &err)) return false;
+      if (b1 && !cuda_ok(cudaMemcpyAsync(timed.in1, h1, b1, cudaMemcpyHostToDevice, st), "H2D in1", &err)) return false;
+      if (timed.launch(st) != UK_OK) {
+        err = uk_cuda_last_error();
+        return false;
+      }
+      return cuda_ok(cudaMemcpyAsync(hout, timed.out, bo, cudaMemcpyDeviceToHost, st), "D2H out", &err);
+    };
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ok) ok = cuda_ok(cudaEventCreate(&e0), "event", &err) && cuda_ok(cudaEventCreate(&e1), "event", &err);
+    for (int i = 0; ok && i < warm; ++i) ok = pass();
+    if (ok) ok = cuda_ok(cudaStreamSynchronize(st), "warm", &err);
+    double total = 0;
+    for (int i = 0; ok && i < iters; ++i) {
+      float ms = 0;
+      ok = cuda_ok(cudaEventRecord(e0, st), "record", &err) && pass() &&
+           cuda_ok(cudaEventRecord(e1, st), "record", &err) && cuda_ok(cudaEventSynchronize(e1), "sync", &err) &&
+           cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
+      total += ms;
+    }
+    if (ok) {
+      r.measured_ms = total / iters;
+      float ms = 0;
+      ok = cuda_ok(cudaEventRecord(e0, st), "record", &err);
+      for (int i = 0; ok && i < iters; ++i)
+        if (timed.launch(st) != UK_OK) {
+          err = uk_cuda_last_error();
+          ok = false;
+        }
+      ok = ok && cuda_ok(cudaEventRecord(e1, st), "record", &err) && cuda_ok(cudaEventSynchronize(e1), "sync", &err) &&
+           cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
+      r.kernel_ms = double(ms) / iters;
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
   }
-  if (e0) cudaEventDestroy(e0);
-  if (e1) cudaEventDestroy(e1);
   const unsigned fault = uk_cuda_pipeline_fault();
   if (ok && fault != 0) {
     err = "a bounded wait inside a tensor-core pipeline expired (fault word " + std::to_string(fault) + ")";
@@ -547,11 +686,13 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
     return finish();
   }
   r.ran = true;
+  r.stream_path = "pinned";  // the only host data path: page-locked copies
   r.exit_code = r.verified ? 0 : 1;
   std::ostringstream res;
   res << "UNIKERN_RESULT backend=nvidia:cuda verify=" << (r.verified ? "PASS" : "FAIL") << " max_rel=" << std::scientific
       << std::setprecision(6) << r.max_rel << std::fixed << std::setprecision(6) << " measured_ms=" << r.measured_ms
-      << " kernel_ms=" << r.kernel_ms << " mode=resident payload_mb=" << payload_mb << " perf=" << perf_string(tree)
+      << " kernel_ms=" << r.kernel_ms << " mode=" << (stream_rows > 0 ? "streamed" : "resident")
+      << " stream_path=pinned payload_mb=" << payload_mb << " perf=" << perf_string(tree)
       << (timed.f16 ? " dtype=fp16" : "") << " migrations=" << r.migrations << " checks=" << r.checks
       << " vram_free=" << r.vram_free << " vram_total=" << r.vram_total;
   r.result_line = res.str();

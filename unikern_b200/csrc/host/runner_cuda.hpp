@@ -41,7 +41,7 @@ struct RunOutcome {
   int migrations = -1, checks = -1;
   unsigned long long vram_free = 0, vram_total = 0;
   int exit_code = 0;
-  std::string stream_path;  // never set: resident-only backend
+  std::string stream_path;  // the host data path of a run: "pinned" (page-locked copies) once it ran
   std::string result_line;  // the UNIKERN_RESULT line (or the UNIKERN_ERROR line)
   std::string log;
 };

@@ -21,6 +21,8 @@ extern "C" {
 #define UKR_OP_CHANNELSCALE 3
 
 int ukr_saw_fill(void* p, int64_t n, int kind, int f16, void* stream);
+// the initialiser's values for indices [offset, offset + n)
+int ukr_saw_fill_at(void* p, int64_t n, int64_t offset, int kind, int f16, void* stream);
 int ukr_check_gemm(const void* A, const void* B, const void* C, int M, int N, int K, int f16, double* worst,
                    void* stream);
 // f16 != 0: the operands and the result are IEEE binary16, else fp32

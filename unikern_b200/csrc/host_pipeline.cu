@@ -20,6 +20,8 @@
 
 #include "uk_common.cuh"
 
+extern "C" int uk_cuda_gemm_f32(const float* A, const float* B, float* C, int M, int N, int K, void* stream);
+
 namespace {
 
 constexpr int MAX_CHUNKS = 64;
@@ -120,5 +122,113 @@ extern "C" int uk_cuda_gemm_f16_host(const uint16_t* hA, const uint16_t* hB, uin
   // the caller's stream completes when the last block of C is home
   if (cudaEventRecord(p->done, p->out) != cudaSuccess || cudaStreamWaitEvent(st, p->done, 0) != cudaSuccess)
     return uk::check_launch("gemm_f16_host: join");
+  return UK_OK;
+}
+
+// ---- streamed GEMM (payload larger than the device) -------------------------
+// Only B is resident; A and C pass through a two-slot ring of row blocks in
+// the caller's device buffer.  Block i uses slot i % 2: its upload waits until
+// block i-2's GEMM has finished reading the slot's A rows, its GEMM waits
+// until block i-2's C rows have left the slot.  Device memory: K*N elements
+// for B plus 2 * block_rows * (K + N) for the ring.
+namespace {
+
+struct StreamPipe {
+  cudaEvent_t a_ready[2] = {}, gemm_done[2] = {}, c_home[2] = {};
+  bool ok = false;
+};
+StreamPipe g_spipe[MAX_DEV];
+
+int get_stream_pipe(StreamPipe** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEV)
+    return uk::fail(UK_ECUDA, "gemm_streamed: no current device");
+  std::lock_guard<std::mutex> lock(g_pipe_mu);
+  StreamPipe& p = g_spipe[dev];
+  if (!p.ok) {
+    bool ok = true;
+    for (int i = 0; ok && i < 2; ++i)
+      ok = cudaEventCreateWithFlags(&p.a_ready[i], cudaEventDisableTiming) == cudaSuccess &&
+           cudaEventCreateWithFlags(&p.gemm_done[i], cudaEventDisableTiming) == cudaSuccess &&
+           cudaEventCreateWithFlags(&p.c_home[i], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) return uk::check_launch("gemm_streamed: event creation");
+    p.ok = true;
+  }
+  *out = &p;
+  return UK_OK;
+}
+
+}  // namespace
+
+extern "C" size_t uk_cuda_gemm_streamed_ring_size(int M, int N, int K, int f16, int block_rows) {
+  if (M <= 0 || N <= 0 || K <= 0 || block_rows <= 0) return 0;
+  const int64_t rows = block_rows < M ? block_rows : M;
+  return (size_t)(2 * rows * ((int64_t)K + N) * (f16 ? 2 : 4) + 512);
+}
+
+extern "C" int uk_cuda_gemm_streamed(const void* hA, const void* hB, void* hC, void* dB, void* ring,
+                                     size_t ring_bytes, int M, int N, int K, int f16, int block_rows, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return uk::fail(UK_EINVAL, "gemm_streamed: negative dims %d %d %d", M, N, K);
+  if (block_rows <= 0) return uk::fail(UK_EINVAL, "gemm_streamed: block_rows must be positive");
+  if (M == 0 || N == 0) return UK_OK;
+  if (int rc = check_host(hA, "hA")) return rc;
+  if (int rc = check_host(hB, "hB")) return rc;
+  if (int rc = check_host(hC, "hC")) return rc;
+  if (int rc = uk::check_device_ptr(dB, "dB")) return rc;
+  if (int rc = uk::check_device_ptr(ring, "ring")) return rc;
+  const size_t need = uk_cuda_gemm_streamed_ring_size(M, N, K, f16, block_rows);
+  if (ring_bytes < need)
+    return uk::fail(UK_EINVAL, "gemm_streamed: the ring needs %zu bytes (uk_cuda_gemm_streamed_ring_size), got %zu",
+                    need, ring_bytes);
+  DevPipe* p = nullptr;
+  StreamPipe* q = nullptr;
+  if (int rc = get_pipe(&p)) return rc;
+  if (int rc = get_stream_pipe(&q)) return rc;
+  const cudaStream_t st = (cudaStream_t)stream;
+  const size_t es = f16 ? 2 : 4;
+  const int64_t rows = block_rows < M ? block_rows : M;
+  const int nblk = (int)((M + rows - 1) / rows);
+  // ring layout: A slot 0, A slot 1, C slot 0, C slot 1 (each 256-byte aligned)
+  auto align = [](size_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* base = (uint8_t*)(((uintptr_t)ring + 255) & ~(uintptr_t)255);
+  const size_t a_slot = align(rows * (size_t)K * es), c_slot = align(rows * (size_t)N * es);
+  uint8_t* a_buf[2] = {base, base + a_slot};
+  uint8_t* c_buf[2] = {base + 2 * a_slot, base + 2 * a_slot + c_slot};
+  if ((size_t)(c_buf[1] + c_slot - (uint8_t*)ring) > ring_bytes)
+    return uk::fail(UK_EINVAL, "gemm_streamed: ring too small after alignment");
+
+  if (cudaEventRecord(p->start, st) != cudaSuccess || cudaStreamWaitEvent(p->in, p->start, 0) != cudaSuccess ||
+      cudaStreamWaitEvent(p->out, p->start, 0) != cudaSuccess)
+    return uk::check_launch("gemm_streamed: ordering");
+  if (cudaMemcpyAsync(dB, hB, (size_t)K * N * es, cudaMemcpyHostToDevice, p->in) != cudaSuccess ||
+      cudaEventRecord(p->b_ready, p->in) != cudaSuccess || cudaStreamWaitEvent(st, p->b_ready, 0) != cudaSuccess)
+    return uk::check_launch("gemm_streamed: upload B");
+  for (int i = 0; i < nblk; ++i) {
+    const int slot = i & 1;
+    const int64_t r0 = (int64_t)i * rows, r1 = r0 + rows < M ? r0 + rows : M, nr = r1 - r0;
+    // upload: after block i-2's GEMM released the slot's A rows
+    if ((i >= 2 && cudaStreamWaitEvent(p->in, q->gemm_done[slot], 0) != cudaSuccess) ||
+        cudaMemcpyAsync(a_buf[slot], (const uint8_t*)hA + r0 * K * es, nr * K * es, cudaMemcpyHostToDevice, p->in) !=
+            cudaSuccess ||
+        cudaEventRecord(q->a_ready[slot], p->in) != cudaSuccess)
+      return uk::check_launch("gemm_streamed: upload A");
+    // GEMM: after its A rows landed and block i-2's C rows left the slot
+    if (cudaStreamWaitEvent(st, q->a_ready[slot], 0) != cudaSuccess ||
+        (i >= 2 && cudaStreamWaitEvent(st, q->c_home[slot], 0) != cudaSuccess))
+      return uk::check_launch("gemm_streamed: wait");
+    const int rc = f16 ? uk_cuda_gemm_f16_ld((const uint16_t*)a_buf[slot], K, (const uint16_t*)dB, N,
+                                             (uint16_t*)c_buf[slot], N, (int)nr, N, K, stream)
+                       : uk_cuda_gemm_f32((const float*)a_buf[slot], (const float*)dB, (float*)c_buf[slot], (int)nr,
+                                          N, K, stream);
+    if (rc != UK_OK) return rc;
+    if (cudaEventRecord(q->gemm_done[slot], st) != cudaSuccess ||
+        cudaStreamWaitEvent(p->out, q->gemm_done[slot], 0) != cudaSuccess ||
+        cudaMemcpyAsync((uint8_t*)hC + r0 * N * es, c_buf[slot], nr * N * es, cudaMemcpyDeviceToHost, p->out) !=
+            cudaSuccess ||
+        cudaEventRecord(q->c_home[slot], p->out) != cudaSuccess)
+      return uk::check_launch("gemm_streamed: download C");
+  }
+  if (cudaEventRecord(p->done, p->out) != cudaSuccess || cudaStreamWaitEvent(st, p->done, 0) != cudaSuccess)
+    return uk::check_launch("gemm_streamed: join");
   return UK_OK;
 }

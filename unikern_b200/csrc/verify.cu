@@ -31,14 +31,15 @@ __device__ __forceinline__ float saw_value(int64_t i, int kind) {
   }
 }
 
-__global__ void k_saw_f32(float* p, int64_t n, int kind) {
+// element i of the buffer holds the initialiser's value at index offset + i
+__global__ void k_saw_f32(float* p, int64_t n, int64_t offset, int kind) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    p[i] = saw_value(i, kind);
+    p[i] = saw_value(offset + i, kind);
 }
 
-__global__ void k_saw_f16(__half* p, int64_t n, int kind) {
+__global__ void k_saw_f16(__half* p, int64_t n, int64_t offset, int kind) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    p[i] = __float2half_rn(saw_value(i, kind));
+    p[i] = __float2half_rn(saw_value(offset + i, kind));
 }
 
 __device__ __forceinline__ double rel_of(double got, double ref) {
@@ -144,12 +145,16 @@ int grid_for(int64_t n, int threads) {
 
 extern "C" {
 
-int ukr_saw_fill(void* p, int64_t n, int kind, int f16, void* stream) {
+int ukr_saw_fill_at(void* p, int64_t n, int64_t offset, int kind, int f16, void* stream) {
   if (n <= 0) return UK_OK;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (f16) k_saw_f16<<<grid_for(n, 256), 256, 0, s>>>(static_cast<__half*>(p), n, kind);
-  else k_saw_f32<<<grid_for(n, 256), 256, 0, s>>>(static_cast<float*>(p), n, kind);
+  if (f16) k_saw_f16<<<grid_for(n, 256), 256, 0, s>>>(static_cast<__half*>(p), n, offset, kind);
+  else k_saw_f32<<<grid_for(n, 256), 256, 0, s>>>(static_cast<float*>(p), n, offset, kind);
   return uk::check_launch("saw fill");
+}
+
+int ukr_saw_fill(void* p, int64_t n, int kind, int f16, void* stream) {
+  return ukr_saw_fill_at(p, n, 0, kind, f16, stream);
 }
 
 int ukr_check_gemm(const void* A, const void* B, const void* C, int M, int N, int K, int f16, double* worst,
