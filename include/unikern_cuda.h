@@ -293,6 +293,19 @@ int uk_kml_describe(const char* kml_json, const char* hcs_json, int sms, char* o
 int uk_run_kml(const char* hcs_json, const char* kml_json, const char* ledger_path, int write_ledger, char* out,
                size_t out_cap);
 
+/* `unikern calibrate` (src/main.cpp:573-652, src/solver.cpp:188-245): read the
+ * rows the ledger at ledger_path measured under the HCS's fingerprint, take
+ * per usable row (measured_ms > kernel_ms > 0) the compulsory bytes of its
+ * signature's tree over measured_ms - kernel_ms, and write the HCS with
+ * link_bw_gbps = the median and constants_version + 1 (flat JSON that
+ * round-trips through the importer) to hcs_out; the report ("CALIBRATED
+ * link_bw_gbps a -> b constants_version ...", the per-row detail, "PREDICTED
+ * demo c_ms ...") or the skip reason goes to out.  Returns 0 calibrated, 2 bad
+ * input, 3 skipped: a unified-memory HCS without allow_unified (checked before
+ * the ledger is read), no measured rows, or none usable.  No GPU needed. */
+int uk_calibrate(const char* hcs_json, const char* ledger_path, int allow_unified, char* hcs_out, size_t hcs_cap,
+                 char* out, size_t out_cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -128,3 +128,21 @@ def test_streamed_refused_for_non_gemm(tmp_path):
     rc, out = abi.run_kml(small_vram_hcs(16), '{"op":"softmax","dtype":"fp32","dims":[8192,1024]}',
                           str(tmp_path / "l"))
     assert rc == 1 and "UNIKERN_ERROR what=stream_refused" in out
+
+
+def test_calibrate_from_measured_runs(tmp_path):
+    # resident runs record measured (upload + kernel + download) and kernel
+    # time; calibration turns their difference into the host link bandwidth
+    import json
+    ledger = tmp_path / "ledger.jsonl"
+    for kml in ('{"op":"gemm","dtype":"fp32","dims":[2048,2048,2048]}',
+                '{"op":"gemm","dtype":"fp16","dims":[4096,4096,4096]}',
+                '{"op":"gemm","dtype":"fp16","dims":[8192,4096,2048]}'):
+        rc, out = abi.run_kml(HCS, kml, str(ledger))
+        assert rc == 0, out
+    rc, cal, out = abi.calibrate(HCS, str(ledger))
+    assert rc == 0, out
+    assert "usable_rows=3" in out
+    bw = json.loads(cal)["link_bw_gbps"]
+    assert 2.0 < bw < 1000.0, out   # a page-locked host link, PCIe or C2C
+    assert json.loads(cal)["constants_version"] == 2

@@ -54,6 +54,7 @@ PROTOTYPES = {
     "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
+    "uk_calibrate": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz, C.c_char_p, sz]),
 }
 
 UK_CONV_KML, UK_CONV_NCHW = 0, 1
@@ -255,6 +256,14 @@ def run_kml(hcs_json: str, kml_json: str, ledger: str | None = None, write_ledge
     rc = lib().uk_run_kml(hcs_json.encode(), kml_json.encode(), ledger.encode() if ledger else None,
                           int(write_ledger), buf, len(buf))
     return rc, buf.value.decode()
+
+
+def calibrate(hcs_json: str, ledger: str, allow_unified: bool = False):
+    """`unikern calibrate`: returns (exit code, calibrated HCS JSON or "",
+    report)."""
+    hbuf, buf = C.create_string_buffer(1 << 14), C.create_string_buffer(1 << 16)
+    rc = lib().uk_calibrate(hcs_json.encode(), ledger.encode(), int(allow_unified), hbuf, len(hbuf), buf, len(buf))
+    return rc, hbuf.value.decode() if rc == 0 else "", buf.value.decode()
 
 
 def result_tokens(transcript: str):

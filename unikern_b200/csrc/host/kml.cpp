@@ -8,6 +8,7 @@
 #include <climits>
 #include <cstdio>
 #include <cstdlib>
+#include <limits>
 #include <sstream>
 
 namespace ukb {
@@ -451,6 +452,7 @@ std::optional<Hcs> hcs_import(const std::string& json, std::string* err) {
       if (t.name.empty()) continue;
       t.bytes = std::stoll(field(body, "bytes").value_or("0"));
       t.bw_gbps = std::stod(field(body, "bw_gbps").value_or("0"));
+      t.confidence = field(body, "confidence").value_or("official");
       h.tiers.push_back(t);
     }
     if (h.tiers.empty()) {  // legacy flat form
@@ -460,6 +462,15 @@ std::optional<Hcs> hcs_import(const std::string& json, std::string* err) {
     }
     h.constants_version = std::stoi(num("constants_version", "1"));
     if (h.constants_version < 1) h.constants_version = 1;
+    // the top-level confidence: looked up outside the tiers array, whose
+    // entries carry their own
+    std::string top = json;
+    const size_t tk = top.find("\"tiers\"");
+    if (tk != std::string::npos) {
+      const size_t close = top.find(']', tk);
+      top.erase(tk, close == std::string::npos ? std::string::npos : close - tk + 1);
+    }
+    h.confidence = field(top, "confidence").value_or("official");
   } catch (const std::exception&) {
     if (err) *err = "malformed numeric field";
     return std::nullopt;
@@ -492,6 +503,23 @@ std::string hcs_fingerprint(const Hcs& h) {
   for (const auto& t : h.tiers) os << ";tier=" << t.name << ":" << t.bytes << ":" << t.bw_gbps;
   os << ";schema=2";
   return fnv1a_hex(os.str());
+}
+
+std::string hcs_export(const Hcs& h) {
+  std::ostringstream os;
+  os.precision(std::numeric_limits<double>::max_digits10);
+  os << "{\n  \"vendor\": \"" << h.vendor << "\",\n  \"device\": \"" << h.device << "\",\n  \"unified_memory\": "
+     << (h.unified_memory ? "true" : "false") << ",\n  \"link_bw_gbps\": " << h.link_bw_gbps
+     << ",\n  \"flops_gflops\": " << h.flops_gflops << ",\n  \"compute_units\": " << h.compute_units
+     << ",\n  \"toolchain\": \"" << h.toolchain << "\",\n  \"constants_version\": " << h.constants_version
+     << ",\n  \"confidence\": \"" << h.confidence << "\",\n  \"tiers\": [\n";
+  for (size_t i = 0; i < h.tiers.size(); ++i) {
+    const Tier& t = h.tiers[i];
+    os << "    { \"name\": \"" << t.name << "\", \"bytes\": " << t.bytes << ", \"bw_gbps\": " << t.bw_gbps
+       << ", \"confidence\": \"" << t.confidence << "\" }" << (i + 1 < h.tiers.size() ? "," : "") << "\n";
+  }
+  os << "  ]\n}\n";
+  return os.str();
 }
 
 std::string ledger_key(const Hcs& h, const KmlTree& t) {

@@ -62,6 +62,7 @@ struct Tier {
   std::string name;
   int64_t bytes = 0;
   double bw_gbps = 0;
+  std::string confidence = "official";  // provenance: official | measured | predicted
 };
 
 struct Hcs {
@@ -70,6 +71,7 @@ struct Hcs {
   double link_bw_gbps = 0, flops_gflops = 0;
   int compute_units = 0;
   int constants_version = 1;
+  std::string confidence = "official";  // provenance, outside the fingerprint
   std::vector<Tier> tiers;
   int64_t tier_bytes(const std::string& name) const;
   double tier_bw(const std::string& name) const;
@@ -78,6 +80,9 @@ struct Hcs {
 
 std::optional<Hcs> hcs_import(const std::string& json, std::string* err);
 std::string hcs_fingerprint(const Hcs& h);
+// flat JSON that round-trips through hcs_import, doubles to max_digits10
+// (src/hcs.cpp:117-148 of UNIKERN); calibration writes its HCS with it
+std::string hcs_export(const Hcs& h);
 
 // "op_sig|hcs_fp|tree_hash"
 std::string ledger_key(const Hcs& h, const KmlTree& t);

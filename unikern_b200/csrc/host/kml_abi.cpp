@@ -78,4 +78,17 @@ int uk_run_kml(const char* hcs_json, const char* kml_json, const char* ledger_pa
   return rc;
 }
 
+int uk_calibrate(const char* hcs_json, const char* ledger_path, int allow_unified, char* hcs_out, size_t hcs_cap,
+                 char* out, size_t out_cap) {
+  if (hcs_json == nullptr || ledger_path == nullptr) {
+    put("hcs_json and ledger_path are required", out, out_cap);
+    return 2;
+  }
+  std::string cal, transcript;
+  const int rc = ukb::calibrate(hcs_json, ledger_path, allow_unified != 0, &cal, &transcript);
+  if (out != nullptr && out_cap > 0) put(transcript, out, out_cap);
+  if (rc == 0 && hcs_out != nullptr && hcs_cap > 0 && put(cal, hcs_out, hcs_cap) != UK_OK) return 2;
+  return rc;
+}
+
 }  // extern "C"

@@ -17,6 +17,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <fstream>
@@ -360,6 +361,30 @@ std::optional<Solution> FileLedger::lookup(const std::string& key) const {
   return std::nullopt;
 }
 
+std::vector<MeasuredRow> FileLedger::measured_rows(const std::string& hcs_fp) const {
+  std::vector<MeasuredRow> out;
+  std::ifstream in(path_);
+  std::string line;
+  while (std::getline(in, line)) {
+    const std::vector<std::string> f = split_tabs(line);
+    if (f.size() < 4) continue;
+    // key = op_sig|hcs_fp|tree_hash (violation rows start with their marker)
+    const size_t b1 = f[0].find('|'), b2 = b1 == std::string::npos ? b1 : f[0].find('|', b1 + 1);
+    if (b2 == std::string::npos || f[0].compare(b1 + 1, b2 - b1 - 1, hcs_fp) != 0) continue;
+    MeasuredRow r;
+    r.op_sig = f[0].substr(0, b1);
+    try {
+      r.c_ms = std::stod(f[1]);
+      r.measured_ms = std::stod(f[2]);
+      if (f.size() >= 7) r.kernel_ms = std::stod(f[3]);  // only the 7-field row carries it
+    } catch (...) {
+      continue;  // a corrupt row is no calibration material
+    }
+    if (r.measured_ms > 0) out.push_back(r);
+  }
+  return out;
+}
+
 void FileLedger::commit(const std::string& key, const Solution& s, double measured_ms, double kernel_ms) const {
   std::ofstream out(path_, std::ios::app);
   out.precision(std::numeric_limits<double>::max_digits10);
@@ -698,6 +723,102 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
   r.result_line = res.str();
   log << r.result_line << "\n";
   return finish();
+}
+
+// ---- calibration -----------------------------------------------------------------
+
+double calibrated_link_bw(const std::vector<MeasuredRow>& rows, std::string* detail) {
+  std::vector<double> bws;
+  std::ostringstream log;
+  for (const MeasuredRow& r : rows) {
+    if (r.measured_ms <= 0 || r.kernel_ms <= 0 || r.measured_ms <= r.kernel_ms) continue;  // no copy time known
+    // rebuild the tree from "op:dtype:d0xd1x..." (the signature keeps the
+    // leading dims only; a gemm row is exact)
+    const size_t c1 = r.op_sig.find(':'), c2 = c1 == std::string::npos ? c1 : r.op_sig.find(':', c1 + 1);
+    if (c2 == std::string::npos) continue;
+    const auto op = op_from_name(r.op_sig.substr(0, c1));
+    const auto dt = dtype_from_name(r.op_sig.substr(c1 + 1, c2 - c1 - 1));
+    if (!op || !dt) continue;
+    KmlTree t;
+    t.op = *op;
+    t.dtype = *dt;
+    bool bad = false;
+    std::stringstream ds(r.op_sig.substr(c2 + 1));
+    std::string tok;
+    for (int i = 0; i < 6 && std::getline(ds, tok, 'x'); ++i) {
+      try {
+        t.dims[i] = std::stoi(tok);
+      } catch (...) {
+        bad = true;
+        break;
+      }
+    }
+    if (bad) continue;
+    if (t.op == OpKind::Reduction)
+      for (int i = 1; i < 6; ++i) t.dims[i] = 0;
+    const Workload w = workload_of(t);
+    if (w.bytes <= 0) continue;
+    const double copy_ms = r.measured_ms - r.kernel_ms;
+    const double bw = double(w.bytes) / (copy_ms * 1e6);
+    bws.push_back(bw);
+    log << r.op_sig << " bytes=" << w.bytes << " copy_ms=" << copy_ms << " eff_bw=" << bw << "GB/s; ";
+  }
+  if (bws.empty()) {
+    if (detail) *detail = "no usable rows (need measured_ms > kernel_ms > 0)";
+    return 0;
+  }
+  std::sort(bws.begin(), bws.end());
+  const size_t n = bws.size();
+  const double med = n % 2 ? bws[n / 2] : 0.5 * (bws[n / 2 - 1] + bws[n / 2]);
+  if (detail)
+    *detail = "usable_rows=" + std::to_string(n) + " median_link_bw=" + std::to_string(med) + "GB/s [" + log.str() + "]";
+  return med;
+}
+
+int calibrate(const std::string& hcs_json, const std::string& ledger_path, bool allow_unified, std::string* hcs_out,
+              std::string* transcript) {
+  std::ostringstream out;
+  auto done = [&](int rc) {
+    if (transcript) *transcript = out.str();
+    return rc;
+  };
+  std::string err;
+  const std::optional<Hcs> hcs = hcs_import(hcs_json, &err);
+  if (!hcs) {
+    out << "HCS rejected: " << err << "\n";
+    return done(2);
+  }
+  // on a unified-memory device measured - kernel is dispatch overhead, not a
+  // copy: refused before the ledger is read unless explicitly allowed
+  if (hcs->unified_memory && !allow_unified) {
+    out << "CALIBRATE SKIP: scenario A (unified memory, zero-copy) -- measured_ms-kernel_ms is host dispatch "
+           "overhead, not link copy time; link_bw_gbps is a scenario-B constant. Pass allow_unified to force it.\n";
+    return done(3);
+  }
+  const std::string fp = hcs_fingerprint(*hcs);
+  const std::vector<MeasuredRow> rows = FileLedger(ledger_path).measured_rows(fp);
+  if (rows.empty()) {
+    out << "CALIBRATE SKIP: no measured rows for hcs_fp=" << fp.substr(0, 8) << " (run first, then calibrate)\n";
+    return done(3);
+  }
+  std::string detail;
+  const double bw = calibrated_link_bw(rows, &detail);
+  if (bw <= 0) {
+    out << "CALIBRATE SKIP: " << detail << "\n";
+    return done(3);
+  }
+  Hcs cal = *hcs;
+  cal.link_bw_gbps = bw;
+  cal.constants_version = hcs->constants_version + 1;
+  if (hcs_out) *hcs_out = hcs_export(cal);
+  const KmlTree demo;  // the default 4096^3 fp32 gemm
+  const int sms = hcs->compute_units > 0 ? hcs->compute_units : 148;
+  out << "CALIBRATED link_bw_gbps " << hcs->link_bw_gbps << " -> " << bw << " constants_version "
+      << hcs->constants_version << " -> " << cal.constants_version << "\n"
+      << detail << "\n"
+      << "PREDICTED demo c_ms " << solve_b200(*hcs, demo, sms).c_ms << " -> " << solve_b200(cal, demo, sms).c_ms
+      << "\n";
+  return done(0);
 }
 
 // ---- cmd_run's nvidia branch -------------------------------------------------

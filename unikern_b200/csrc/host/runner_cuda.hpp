@@ -14,6 +14,7 @@
 
 #include <optional>
 #include <string>
+#include <vector>
 
 #include "kml.hpp"
 
@@ -55,14 +56,24 @@ class BackendNvidia {
   bool available() const;  // a CUDA device of compute capability 10.0
   // provenance text: no source is generated, the kernels are precompiled
   std::string generate(const Solution& s, const Hcs& h, const KmlTree& t) const;
-  bool supports_streaming() const { return false; }
+  bool supports_streaming() const { return true; }  // gemm operands, with B resident
   std::string capability_gap(const KmlTree& t) const;  // "" = supported
+};
+
+// one measured ledger row under an HCS fingerprint (calibration input)
+struct MeasuredRow {
+  std::string op_sig;      // carries the dims, e.g. "gemm:fp32:1024x1024x1024"
+  double c_ms = 0;         // predicted at record time
+  double measured_ms = 0;  // end to end per pass
+  double kernel_ms = 0;    // kernel only; 0 in rows that predate it
 };
 
 class FileLedger {
  public:
   explicit FileLedger(std::string path) : path_(std::move(path)) {}
   std::optional<Solution> lookup(const std::string& key) const;
+  // rows with a measurement (> 0) recorded under hcs_fp, in file order
+  std::vector<MeasuredRow> measured_rows(const std::string& hcs_fp) const;
   void commit(const std::string& key, const Solution& s, double measured_ms, double kernel_ms) const;
   void record_violation(const std::string& key, double rate, double threshold, int migrations, int checks,
                         unsigned long long vram_free) const;
@@ -71,6 +82,20 @@ class FileLedger {
  private:
   std::string path_;
 };
+
+// The effective host link bandwidth (GB/s) from measured rows: per row the
+// compulsory bytes of its signature's tree over measured_ms - kernel_ms, and
+// the median over usable rows (the mean of the middle two for an even
+// count); 0 when no row is usable (src/solver.cpp:188-245 of UNIKERN).
+double calibrated_link_bw(const std::vector<MeasuredRow>& rows, std::string* detail);
+
+// cmd_calibrate (src/main.cpp:573-652 of UNIKERN): reads the rows measured
+// under the HCS's fingerprint, writes the HCS with the calibrated
+// link_bw_gbps and constants_version + 1 to *hcs_out, and the report to
+// *transcript.  Returns 0 calibrated, 2 bad HCS, 3 skipped (a unified-memory
+// HCS without allow_unified, no measured rows, or no usable row).
+int calibrate(const std::string& hcs_json, const std::string& ledger_path, bool allow_unified,
+              std::string* hcs_out, std::string* transcript);
 
 // cmd_run's nvidia branch (run: write_ledger = true; verify: false).  Returns
 // cmd_run's exit code: 0 committed / verified, 1 run failed, 2 bad input or
