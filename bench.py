@@ -505,6 +505,19 @@ def bench_gemm_f32(ctx, steps, warmup, M=512, N=512, K=512):
     return {"ms": ms, "value": 2.0 * M * N * K / ms / 1e9, "graph": True}
 
 
+def bench_gemm_f32_tc(ctx, steps, warmup, M=8192, N=8192, K=8192):
+    """fp32 GEMM on the tensor cores (split-tf32 through the convolution's
+    pair kernel); the step includes both tf32 pre-passes."""
+    import unikern_b200.abi as abi
+    torch = ctx.torch
+    A = gen(torch, (M, K), "uniform", 11, lo=-1, hi=1)
+    B = gen(torch, (K, N), "uniform", 12, lo=-1, hi=1)
+    Cm = torch.empty((M, N), device="cuda")
+    ws = abi.gemm_f32_workspace(M, N, K)
+    ms = ctx.time_steps(lambda: abi.gemm_f32_tc(A, B, Cm, ws, ctx.stream), steps, warmup)
+    return {"ms": ms, "value": 2.0 * M * N * K / ms / 1e9}
+
+
 def bench_decode(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
     """Decode-layer chain: RMSNorm [B x 4096] fused into
     the f16 skinny GEMM [B x 4096] x [4096 x 14336] (one kernel), then softmax
@@ -772,11 +785,16 @@ def run_single(args, ctx, pk):
     elif op == "gemm_f32":
         r = bench_gemm_f32(ctx, args.steps, args.warmup)
         val, unit, bound = r["value"], "TFLOP/s", "fp32"
+    elif op == "gemm_f32_tc":
+        M, N, K = (int(v) for v in args.gemm_shape.split(","))
+        r = bench_gemm_f32_tc(ctx, args.steps, args.warmup, M, N, K)
+        val, unit, bound = r["value"], "TFLOP/s", "tensor_3xtf32"
+        extra = {"config": {"workload": "fp32 GEMM %dx%dx%d, split-tf32 tensor cores, pre-passes included" % (M, N, K)}}
     elif op in ("gemm_streamed", "gemm_streamed_f16"):
         M, N, K = (int(v) for v in args.gemm_shape.split(",")) if args.gemm_shape != "8192,8192,8192" else \
             (32768, 32768, 32768)
         r = bench_gemm_streamed(ctx, args.steps, args.warmup, M, N, K, f16=op.endswith("f16"))
-        val, unit, bound = r["value"], "TFLOP/s", "tensor" if op.endswith("f16") else "fp32"
+        val, unit, bound = r["value"], "TFLOP/s", "tensor" if op.endswith("f16") else "tensor_3xtf32"
         es = 2 if op.endswith("f16") else 4
         extra = {"e2e": {"value": round(val, 3), "unit": unit, "h2d_bytes_per_step": (M * K + K * N) * es,
                          "d2h_bytes_per_step": M * N * es},
@@ -805,7 +823,7 @@ def main():
     ap.add_argument("--op", default="all",
                     choices=["all", "gemm_f16", "reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar",
                              "conv", "gemm_f32", "decode", "softmax_f16", "rmsnorm_f16", "channelscale_f16",
-                             "conv_f16", "gemm_streamed", "gemm_streamed_f16"],
+                             "conv_f16", "gemm_streamed", "gemm_streamed_f16", "gemm_f32_tc"],
                     help="all = headline f16 GEMM + every other op; otherwise one op alone (profiling)")
     ap.add_argument("--gemm-shape", default="8192,8192,8192", help="M,N,K of the f16 GEMM")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")

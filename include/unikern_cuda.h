@@ -129,6 +129,23 @@ int uk_cuda_channelscale_f16(const uint16_t* X, const uint16_t* S, uint16_t* Y, 
 int uk_cuda_gemm_f32(const float* A, const float* B, float* C, int M, int N, int K,
                      void* stream);
 
+/* The same GEMM on the tcgen05 tensor cores at fp32 accuracy: every operand
+ * is carried as a tf32 (hi, lo) pair and each product as lo*hi + hi*lo +
+ * hi*hi in the fp32 accumulator ("3xTF32"), so results agree with the FFMA
+ * kernel to a few ulps of the output scale (exactly, where every partial sum
+ * is representable).  C = A * B runs as the 1 x 1 convolution of B^T's pixels
+ * with A's rows as filters, on the convolution's kernels.
+ * uk_cuda_gemm_f32_workspace_size returns the workspace (2 (N + M) K fp32 plus
+ * alignment) when the shape can take the tensor cores (K % 32 == 0 and
+ * N % 64 == 0), else 0; uk_cuda_gemm_f32_prefers_tc says whether it gains
+ * from them (M N K >= 2^30: below, the FFMA kernel is as fast).
+ * uk_cuda_gemm_f32_ws with a workspace of at least that size runs the
+ * tensor-core path; with workspace NULL or 0 bytes it is uk_cuda_gemm_f32. */
+size_t uk_cuda_gemm_f32_workspace_size(int M, int N, int K);
+int uk_cuda_gemm_f32_prefers_tc(int M, int N, int K);
+int uk_cuda_gemm_f32_ws(const float* A, const float* B, float* C, int M, int N, int K, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 /* ---- gemm f16 --------------------------------------------------------------
  * C(f16) = A(f16) * B(f16) with fp32 accumulation on the tcgen05 tensor
  * cores; A, B, C are IEEE binary16 bit patterns (uint16_t).  Row-major A[M][K],
@@ -160,14 +177,18 @@ int uk_cuda_gemm_f16_host(const uint16_t* hA, const uint16_t* hB, uint16_t* hC, 
  * src/codegen_hip.cpp:1143-1238): C = A * B from and to page-locked host
  * memory with only B resident (dB, K*N elements) and A, C passing through a
  * two-slot ring of block_rows-row blocks in `ring` (at least
- * uk_cuda_gemm_streamed_ring_size(M, N, K, f16, block_rows) bytes of device
+ * uk_cuda_gemm_streamed_ring_size(M, N, K, kind, block_rows) bytes of device
  * memory).  Block i's upload, GEMM and download overlap blocks i+-1; a slot is
- * reused only after its previous block's GEMM and download finished.  f16 != 0:
- * binary16 data on the tensor cores; 0: fp32 on the FFMA kernel.  Asynchronous
- * on `stream`; shares the copy streams of uk_cuda_gemm_f16_host. */
-size_t uk_cuda_gemm_streamed_ring_size(int M, int N, int K, int f16, int block_rows);
+ * reused only after its previous block's GEMM and download finished.  kind:
+ *   1  binary16 data on the tensor cores;
+ *   0  fp32, on the tensor cores (split-tf32, uk_cuda_gemm_f32_ws) when a
+ *      block gains from them, the ring then also holding the tf32 pairs of
+ *      B^T (made once per call) and of one block of A; else FFMA;
+ *   2  fp32 on the FFMA kernel (the smallest ring).
+ * Asynchronous on `stream`; shares the copy streams of uk_cuda_gemm_f16_host. */
+size_t uk_cuda_gemm_streamed_ring_size(int M, int N, int K, int kind, int block_rows);
 int uk_cuda_gemm_streamed(const void* hA, const void* hB, void* hC, void* dB, void* ring, size_t ring_bytes,
-                          int M, int N, int K, int f16, int block_rows, void* stream);
+                          int M, int N, int K, int kind, int block_rows, void* stream);
 
 /* ---- multi-GPU f16 GEMM (one process per GPU, NVLink peers) ----------------
  * N-sharded GEMM with the all-gather fused into the store: computes columns

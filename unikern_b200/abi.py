@@ -29,6 +29,9 @@ PROTOTYPES = {
     "uk_cuda_rmsnorm_f32": (i32, [vp, vp, vp, i64, i64, f32, vp]),
     "uk_cuda_softmax_f32": (i32, [vp, vp, i64, i64, vp]),
     "uk_cuda_gemm_f32": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+    "uk_cuda_gemm_f32_workspace_size": (sz, [i32, i32, i32]),
+    "uk_cuda_gemm_f32_prefers_tc": (i32, [i32, i32, i32]),
+    "uk_cuda_gemm_f32_ws": (i32, [vp, vp, vp, i32, i32, i32, vp, sz, vp]),
     "uk_cuda_gemm_f16": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "uk_cuda_gemm_f16_ld": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, i32, vp]),
     "uk_cuda_conv2d_f32": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp]),
@@ -146,6 +149,24 @@ def gemm_f32(A, B, Cm, stream=None):
     check(lib().uk_cuda_gemm_f32(_p(A), _p(B), _p(Cm), M, N, K, _stream(stream)))
 
 
+def gemm_f32_workspace(M, N, K):
+    """The tensor-core f32 GEMM's workspace (a torch uint8 tensor), or None
+    when the shape cannot take the tensor cores (K % 32 or N % 64 nonzero)."""
+    import torch
+    n = lib().uk_cuda_gemm_f32_workspace_size(M, N, K)
+    return torch.empty(n, dtype=torch.uint8, device="cuda") if n else None
+
+
+def gemm_f32_tc(A, B, Cm, workspace=None, stream=None):
+    """C = A * B in fp32 on the tensor cores (split-tf32); allocates the
+    workspace through torch when none is passed (FFMA when the shape has none)."""
+    M, K = A.shape
+    N = B.shape[1]
+    ws = workspace if workspace is not None else gemm_f32_workspace(M, N, K)
+    check(lib().uk_cuda_gemm_f32_ws(_p(A), _p(B), _p(Cm), M, N, K, _p(ws),
+                                    0 if ws is None else ws.numel(), _stream(stream)))
+
+
 def gemm_f16(A, B, Cm, stream=None):
     """A, B, C: torch.float16 (or int16/uint16 bit patterns) row-major, any strides
     with unit inner stride."""
@@ -185,15 +206,22 @@ def gemm_f16_host(Ah, Bh, Ch, Ad, Bd, Cd, chunks=0, stream=None):
                                       _stream(stream)))
 
 
-def gemm_streamed(Ah, Bh, Ch, Bd, ring, block_rows, stream=None):
+def gemm_streamed(Ah, Bh, Ch, Bd, ring, block_rows, stream=None, ffma=False):
     """C = A * B (host tensors, f16 or fp32) with only B resident and A / C
-    streamed through a two-slot device ring of block_rows-row blocks."""
+    streamed through a two-slot device ring of block_rows-row blocks (fp32:
+    the tensor cores where a block gains, unless ffma)."""
     import torch
     M, K = Ah.shape
     N = Bh.shape[1]
-    f16 = int(Ah.dtype == torch.float16)
+    kind = 1 if Ah.dtype == torch.float16 else (2 if ffma else 0)
     check(lib().uk_cuda_gemm_streamed(_p(Ah), _p(Bh), _p(Ch), _p(Bd), _p(ring), ring.numel() * ring.element_size(),
-                                      M, N, K, f16, block_rows, _stream(stream)))
+                                      M, N, K, kind, block_rows, _stream(stream)))
+
+
+def gemm_streamed_ring(M, N, K, kind, block_rows):
+    import torch
+    n = lib().uk_cuda_gemm_streamed_ring_size(M, N, K, kind, block_rows)
+    return torch.empty(n, dtype=torch.uint8, device="cuda")
 
 
 def conv2d_workspace(N, H, W, Cc, Kh, Kw, Oc, pad=0, layout=UK_CONV_NCHW):

@@ -290,12 +290,25 @@ struct PairF16 {
   static constexpr uint32_t IDESC = uk_idesc_f16_ab(2 * BM, BN, 0, 0);
 };
 
+// fp32 accuracy over long K: the tensor cores' fp32 accumulator does not round
+// to nearest, and its error grows with the number of MMAs summed into it.  The
+// fp32 kernel therefore accumulates at most P_KC k-steps (1024 channels) in
+// TMEM: the first chunk of a tile goes to the tile's accumulator, each later
+// chunk to the other TMEM buffer, and the epilogue warps add it into the
+// tile's accumulator with CUDA-core fp32 adds ("promotion") before the MMAs
+// reuse that buffer.  A K of at most P_KC k-steps (1024 fp32 channels x
+// taps) is one chunk and needs no promotion; the 3 x 3 x 256 convolution
+// (72 k-steps) promotes twice per tile.
+constexpr int P_KC = 32;
+
 template <class Tr>
 struct PairCtl {
   uint64_t full[Tr::STAGES];
   uint64_t empty[Tr::STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
+  uint64_t pfull;   // a later chunk's partial sum is in the other buffer (MMA -> epilogue)
+  uint64_t pempty;  // it was added into the tile's accumulator (epilogue -> MMA)
   uint64_t teardown;
   uint32_t tmem_base;
   int abort;
@@ -349,6 +362,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int csteps = p.C / Tr::BKE;
   const int ksteps = p.Kh * p.Kw * csteps;
+  const int kc = Tr::TILES == 2 ? P_KC : ksteps;  // k-steps per TMEM chunk
+  const int nchunks = (ksteps + kc - 1) / kc;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -359,6 +374,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uk_mbar_init(&ctl->tfull[b], 1);
       uk_mbar_init(&ctl->tempty[b], 2 * EPI_WARPS);
     }
+    uk_mbar_init(&ctl->pfull, 1);
+    uk_mbar_init(&ctl->pempty, 2 * EPI_WARPS);
     uk_mbar_init(&ctl->teardown, 1);
     ctl->abort = 0;
     uk_fence_mbar_init();
@@ -414,18 +431,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (crank == 0 && lane == 0) {
-      uint32_t it = 0, tl = 0;
+      uint32_t it = 0, tl = 0, np = 0;  // np: chunks handed to the epilogue for promotion
       for (int t = pair; t < p.num_tiles && !*abort; t += npairs, ++tl) {
         const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
-        if (!uk_mbar_wait_cluster(&ctl->tempty[buf], tph ^ 1u, abort, WAIT_NS)) {
+        // the tile's accumulator: drained two tiles ago, and no longer read
+        // by the previous tile's last promotion
+        if (!uk_mbar_wait_cluster(&ctl->tempty[buf], tph ^ 1u, abort, WAIT_NS) ||
+            (np > 0 && !uk_mbar_wait_cluster(&ctl->pempty, (np - 1) & 1u, abort, WAIT_NS))) {
           atomicOr(&uk::g_conv_fault, UK_FAULT_MMA);
           ctl->abort = 1;
           break;
         }
         uk_tc_fence_after();
-        const uint32_t d = tmem + buf * BN;
         bool ok = true;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          const int c = ks / kc, kin = ks - c * kc;
+          if (c >= 1 && kin == 0) {
+            // a later chunk goes to the other buffer: the previous tile's
+            // accumulator until drained (chunk 1), then the previous chunk's
+            // partial until promoted
+            const bool w = c == 1 ? uk_mbar_wait_cluster(&ctl->tempty[buf ^ 1u], ((tl - 1u) >> 1) & 1u, abort, WAIT_NS)
+                                  : uk_mbar_wait_cluster(&ctl->pempty, (np - 1) & 1u, abort, WAIT_NS);
+            if (!w) {
+              atomicOr(&uk::g_conv_fault, UK_FAULT_MMA);
+              ctl->abort = 1;
+              ok = false;
+              break;
+            }
+            uk_tc_fence_after();
+          }
+          const uint32_t d = tmem + (c == 0 ? buf : (buf ^ 1u)) * BN;
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!uk_mbar_wait_cluster(&ctl->full[s], ph, abort, WAIT_NS)) {
@@ -443,7 +478,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // 16 f16) inside the atom, 8-row groups 1 KiB apart
             const uint64_t da = uk_desc_sw128(a0 + kk * 32, 16, 1024);
             const uint64_t db = uk_desc_sw128(b0 + kk * 32, 16, 1024);
-            const uint32_t acc = (ks > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t acc = (kin > 0 || kk > 0) ? 1u : 0u;
             if constexpr (Tr::TILES == 2) {
               const uint64_t dal = uk_desc_sw128(a0 + P_TILE_BYTES + kk * 32, 16, 1024);
               const uint64_t dbl = uk_desc_sw128(b0 + P_TILE_BYTES + kk * 32, 16, 1024);
@@ -455,6 +490,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
           }
           uk_umma_commit_cg2(&ctl->empty[s], P_PAIR);
+          if (c >= 1 && (kin == kc - 1 || ks == ksteps - 1)) {
+            uk_umma_commit_cg2(&ctl->pfull, P_PAIR);
+            ++np;
+          }
         }
         if (!ok) break;
         uk_umma_commit_cg2(&ctl->tfull[buf], P_PAIR);
@@ -467,11 +506,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int m = q * 32 + lane;
     const uint32_t tempty_leader[2] = {uk_mapa(uk_smem_u32(&ctl->tempty[0]), 0),
                                        uk_mapa(uk_smem_u32(&ctl->tempty[1]), 0)};
-    uint32_t tl = 0;
+    const uint32_t pempty_leader = uk_mapa(uk_smem_u32(&ctl->pempty), 0);
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t tl = 0, pi = 0;  // pi: promotions done
     for (int t = pair; t < p.num_tiles && !*abort; t += npairs, ++tl) {
       int n, ho0, wo0, oc0;
       pair_tile_coords(p, t, n, ho0, wo0, oc0);
       const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
+      // promotions: each later chunk's partial sum, added in fp32 (round to
+      // nearest) into the tile's accumulator
+      bool ok = true;
+      for (int c = 1; c < nchunks; ++c, ++pi) {
+        if (!uk_mbar_wait_cluster(&ctl->pfull, pi & 1u, abort, WAIT_NS)) {
+          atomicOr(&uk::g_conv_fault, UK_FAULT_EPILOGUE);
+          ctl->abort = 1;
+          ok = false;
+          break;
+        }
+        uk_tc_fence_after();
+#pragma unroll 1
+        for (int j = 0; j < BN / 32; ++j) {
+          uint32_t x[32], a[32];
+          uk_tmem_ld32(trow + (buf ^ 1u) * BN + j * 32, x);
+          uk_tmem_ld32(trow + buf * BN + j * 32, a);
+          uk_tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) a[i] = __float_as_uint(__uint_as_float(a[i]) + __uint_as_float(x[i]));
+          uk_tmem_st32(trow + buf * BN + j * 32, a);
+        }
+        uk_tmem_st_wait();
+        uk_tc_fence_before();
+        __syncwarp();
+        if (lane == 0) uk_mbar_arrive_cluster(pempty_leader);
+      }
+      if (!ok) break;
       if (!uk_mbar_wait_cluster(&ctl->tfull[buf], tph, abort, WAIT_NS)) {
         atomicOr(&uk::g_conv_fault, UK_FAULT_EPILOGUE);
         ctl->abort = 1;
@@ -637,6 +705,25 @@ __global__ void k_split_weights(const float* __restrict__ Wt, float* __restrict_
   }
 }
 
+// B[K][N] -> Bt[N][K] as (hi, lo) pairs, 32 x 32 tiles through shared memory
+// (K % 32 == 0 and N % 32 == 0: every tile is whole)
+__global__ void __launch_bounds__(256) k_split_transpose(const float* __restrict__ B, float* __restrict__ Th,
+                                                         float* __restrict__ Tl, int K, int N) {
+  __shared__ float t[32][33];
+  const int64_t n0 = (int64_t)blockIdx.x * 32, k0 = (int64_t)blockIdx.y * 32;
+#pragma unroll
+  for (int i = threadIdx.y; i < 32; i += 8) t[i][threadIdx.x] = __ldcs(B + (k0 + i) * N + n0 + threadIdx.x);
+  __syncthreads();
+#pragma unroll
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    float hi, lo;
+    split(t[threadIdx.x][i], hi, lo);
+    const int64_t o = (n0 + i) * K + k0 + threadIdx.x;
+    Th[o] = hi;
+    Tl[o] = lo;
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -683,91 +770,11 @@ bool tc_applies(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad, int
   return true;
 }
 
-}  // namespace
-
-namespace uk {
-
-unsigned conv_fault_take() {
-  unsigned v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_conv_fault, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
-  const unsigned zero = 0;
-  cudaMemcpyToSymbol(g_conv_fault, &zero, sizeof(zero));
-  return v;
-}
-
-}  // namespace uk
-
-extern "C" size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad,
-                                                int layout) {
-  if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout)) return 0;
-  const size_t xs = align256((size_t)N * H * W * C * 4), ws = align256((size_t)Oc * Kh * Kw * C * 4);
-  return 2 * xs + 2 * ws;
-}
-
-extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh,
-                                     int Kw, int Oc, int pad, const float* scale, int layout, void* workspace,
-                                     size_t workspace_bytes, void* stream) {
-  const cudaStream_t st = (cudaStream_t)stream;
-  if (layout != UK_CONV_KML && layout != UK_CONV_NCHW)
-    return uk::fail(UK_EINVAL, "conv2d: unknown layout %d", layout);
-  if (N < 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0 || pad < 0)
-    return uk::fail(UK_EINVAL, "conv2d: invalid dims N=%d H=%d W=%d C=%d Kh=%d Kw=%d Oc=%d pad=%d", N, H, W, C, Kh,
-                    Kw, Oc, pad);
-  if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout))
-    return uk::conv2d_ffma(X, Wt, Y, N, H, W, C, Kh, Kw, Oc, pad, scale, layout, st);
-  const size_t need = uk_cuda_conv2d_workspace_size(N, H, W, C, Kh, Kw, Oc, pad, layout);
-  if (workspace == nullptr || workspace_bytes < need)
-    return uk::fail(UK_EINVAL, "conv2d: needs a %zu-byte workspace (uk_cuda_conv2d_workspace_size), got %zu", need,
-                    workspace ? workspace_bytes : (size_t)0);
-  if ((int64_t)N * H * W * C > ((int64_t)1 << 40)) return uk::fail(UK_EINVAL, "conv2d: input too large");
-  if (int rc = uk::check_device_ptr(X, "X")) return rc;
-  if (int rc = uk::check_device_ptr(Wt, "Wt")) return rc;
-  if (int rc = uk::check_device_ptr(Y, "Y")) return rc;
-  if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
-  if (scale)
-    if (int rc = uk::check_device_ptr(scale, "scale")) return rc;
-  if (!uk::aligned16(workspace)) return uk::fail(UK_EINVAL, "conv2d: the workspace must be 16-byte aligned");
-
+// the split-tf32 kernel over prepared operands: Xh/Xl the input as NHWC
+// (hi, lo) pairs, Wh/Wl the weights as [Oc][kh][kw][c] pairs
+int run_tc(const float* Xh, const float* Xl, const float* Wh, const float* Wl, float* Y, const float* scale, int N,
+           int H, int W, int C, int Kh, int Kw, int Oc, int pad, cudaStream_t st) {
   const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
-  const size_t xs = align256((size_t)N * H * W * C * 4), wsz = align256((size_t)Oc * Kh * Kw * C * 4);
-  float* Xh = (float*)workspace;
-  float* Xl = (float*)((uint8_t*)workspace + xs);
-  float* Wh = (float*)((uint8_t*)workspace + 2 * xs);
-  float* Wl = (float*)((uint8_t*)workspace + 2 * xs + wsz);
-
-  // pre-pass: operands as tf32 (hi, lo) pairs, input as NHWC
-  if (N == 0) return UK_OK;
-  const size_t plane_bytes = (size_t)W * (C + 1) * 4;
-  // the row-staged pre-pass needs 16-byte aligned rows of X for its vector loads
-  if (layout == UK_CONV_NCHW && plane_bytes <= 100 * 1024 && (W % 4 != 0 || uk::aligned16(X))) {
-    static bool plane_attr[64] = {false};
-    int d = 0;
-    cudaGetDevice(&d);
-    if (d >= 0 && d < 64 && !plane_attr[d]) {
-      if (cudaFuncSetAttribute(k_split_row_nhwc, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) !=
-          cudaSuccess)
-        return uk::check_launch("conv2d: pre-pass attribute");
-      plane_attr[d] = true;
-    }
-    if ((int64_t)N * H > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d: N*H too large");
-    k_split_row_nhwc<<<(unsigned)((int64_t)N * H), ROW_THREADS, plane_bytes, st>>>(X, Xh, Xl, C, H, W);
-  } else if (layout == UK_CONV_NCHW) {
-    const int64_t gx = (int64_t)((W + 31) / 32) * N * H;
-    if (gx > 2147483647LL || C / 32 > 65535) return uk::fail(UK_EINVAL, "conv2d: input too large for the pre-pass");
-    const dim3 g((unsigned)gx, (unsigned)(C / 32), 1);
-    k_split_nchw_nhwc<<<g, dim3(32, 8), 0, st>>>(X, Xh, Xl, C, H, W);
-  } else {
-    const int64_t n = (int64_t)H * W * C;
-    k_split_flat<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 16), 256, 0, st>>>(X, Xh,
-                                                                                                            Xl, n);
-  }
-  {
-    const int64_t n = (int64_t)Oc * Kh * Kw * C;
-    k_split_weights<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 8), 256, 0, st>>>(
-        Wt, Wh, Wl, Oc, C, Kh, Kw, layout == UK_CONV_NCHW ? 1 : 0);
-  }
-  if (int rc = uk::check_launch("conv2d(split)")) return rc;
-
   // tensor maps: input [N][H][W][C] as 4-D (C innermost), weights [Oc][K]
   CUtensorMap txh, txl, twh, twl;
   const cuuint64_t xdims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
@@ -832,6 +839,163 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   const cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_pair<PairF32>, txh, txl, twh, twl, p);
   if (e != cudaSuccess) return uk::fail(UK_ECUDA, "conv2d(pair): launch: %s", cudaGetErrorString(e));
   return uk::check_launch("conv2d(tcgen05 pair)");
+}
+}  // namespace
+
+namespace uk {
+
+unsigned conv_fault_take() {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_conv_fault, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  const unsigned zero = 0;
+  cudaMemcpyToSymbol(g_conv_fault, &zero, sizeof(zero));
+  return v;
+}
+
+}  // namespace uk
+
+extern "C" size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad,
+                                                int layout) {
+  if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout)) return 0;
+  const size_t xs = align256((size_t)N * H * W * C * 4), ws = align256((size_t)Oc * Kh * Kw * C * 4);
+  return 2 * xs + 2 * ws;
+}
+
+extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh,
+                                     int Kw, int Oc, int pad, const float* scale, int layout, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (layout != UK_CONV_KML && layout != UK_CONV_NCHW)
+    return uk::fail(UK_EINVAL, "conv2d: unknown layout %d", layout);
+  if (N < 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0 || pad < 0)
+    return uk::fail(UK_EINVAL, "conv2d: invalid dims N=%d H=%d W=%d C=%d Kh=%d Kw=%d Oc=%d pad=%d", N, H, W, C, Kh,
+                    Kw, Oc, pad);
+  if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout))
+    return uk::conv2d_ffma(X, Wt, Y, N, H, W, C, Kh, Kw, Oc, pad, scale, layout, st);
+  const size_t need = uk_cuda_conv2d_workspace_size(N, H, W, C, Kh, Kw, Oc, pad, layout);
+  if (workspace == nullptr || workspace_bytes < need)
+    return uk::fail(UK_EINVAL, "conv2d: needs a %zu-byte workspace (uk_cuda_conv2d_workspace_size), got %zu", need,
+                    workspace ? workspace_bytes : (size_t)0);
+  if ((int64_t)N * H * W * C > ((int64_t)1 << 40)) return uk::fail(UK_EINVAL, "conv2d: input too large");
+  if (int rc = uk::check_device_ptr(X, "X")) return rc;
+  if (int rc = uk::check_device_ptr(Wt, "Wt")) return rc;
+  if (int rc = uk::check_device_ptr(Y, "Y")) return rc;
+  if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
+  if (scale)
+    if (int rc = uk::check_device_ptr(scale, "scale")) return rc;
+  if (!uk::aligned16(workspace)) return uk::fail(UK_EINVAL, "conv2d: the workspace must be 16-byte aligned");
+
+  const size_t xs = align256((size_t)N * H * W * C * 4), wsz = align256((size_t)Oc * Kh * Kw * C * 4);
+  float* Xh = (float*)workspace;
+  float* Xl = (float*)((uint8_t*)workspace + xs);
+  float* Wh = (float*)((uint8_t*)workspace + 2 * xs);
+  float* Wl = (float*)((uint8_t*)workspace + 2 * xs + wsz);
+
+  // pre-pass: operands as tf32 (hi, lo) pairs, input as NHWC
+  if (N == 0) return UK_OK;
+  const size_t plane_bytes = (size_t)W * (C + 1) * 4;
+  // the row-staged pre-pass needs 16-byte aligned rows of X for its vector loads
+  if (layout == UK_CONV_NCHW && plane_bytes <= 100 * 1024 && (W % 4 != 0 || uk::aligned16(X))) {
+    static bool plane_attr[64] = {false};
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d >= 0 && d < 64 && !plane_attr[d]) {
+      if (cudaFuncSetAttribute(k_split_row_nhwc, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) !=
+          cudaSuccess)
+        return uk::check_launch("conv2d: pre-pass attribute");
+      plane_attr[d] = true;
+    }
+    if ((int64_t)N * H > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d: N*H too large");
+    k_split_row_nhwc<<<(unsigned)((int64_t)N * H), ROW_THREADS, plane_bytes, st>>>(X, Xh, Xl, C, H, W);
+  } else if (layout == UK_CONV_NCHW) {
+    const int64_t gx = (int64_t)((W + 31) / 32) * N * H;
+    if (gx > 2147483647LL || C / 32 > 65535) return uk::fail(UK_EINVAL, "conv2d: input too large for the pre-pass");
+    const dim3 g((unsigned)gx, (unsigned)(C / 32), 1);
+    k_split_nchw_nhwc<<<g, dim3(32, 8), 0, st>>>(X, Xh, Xl, C, H, W);
+  } else {
+    const int64_t n = (int64_t)H * W * C;
+    k_split_flat<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 16), 256, 0, st>>>(X, Xh,
+                                                                                                            Xl, n);
+  }
+  {
+    const int64_t n = (int64_t)Oc * Kh * Kw * C;
+    k_split_weights<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 8), 256, 0, st>>>(
+        Wt, Wh, Wl, Oc, C, Kh, Kw, layout == UK_CONV_NCHW ? 1 : 0);
+  }
+  if (int rc = uk::check_launch("conv2d(split)")) return rc;
+
+  return run_tc(Xh, Xl, Wh, Wl, Y, scale, N, H, W, C, Kh, Kw, Oc, pad, st);
+}
+
+// ---- the fp32 GEMM as a 1 x 1 convolution -------------------------------------------
+// C[M][N] = A[M][K] * B[K][N] is the 1 x 1 convolution of one (N/64) x 64
+// image of K channels, X[h][w][c] = B[c][64h + w] (B transposed), with M
+// filters Wt[m][c] = A[m][c]: output channel m at pixel n = 64h + w is
+// C[m][n], and the output planes Y[m][h][w] are C row-major.  So the
+// split-tf32 convolution kernels above run it unchanged, at fp32 accuracy on
+// the tensor cores; the pre-passes write B^T and A as tf32 (hi, lo) pairs.
+namespace uk {
+
+bool gemm_f32_tc_shape(int M, int N, int K) { return M > 0 && N >= 64 && N % 64 == 0 && K >= BK && K % BK == 0; }
+
+size_t gemm_f32_tc_b_bytes(int N, int K) { return 2 * align256((size_t)N * K * 4); }
+size_t gemm_f32_tc_a_bytes(int M, int K) { return 2 * align256((size_t)M * K * 4); }
+
+// B (device, K x N) -> the (hi, lo) pairs of B^T in bws (gemm_f32_tc_b_bytes)
+int gemm_f32_tc_prep_b(const float* B, void* bws, int N, int K, cudaStream_t st) {
+  if ((int64_t)K / 32 > 65535) return uk::fail(UK_EINVAL, "gemm_f32: K=%d too large for the transpose pre-pass", K);
+  float* Th = (float*)bws;
+  float* Tl = (float*)((uint8_t*)bws + align256((size_t)N * K * 4));
+  k_split_transpose<<<dim3((unsigned)(N / 32), (unsigned)(K / 32)), dim3(32, 8), 0, st>>>(B, Th, Tl, K, N);
+  return uk::check_launch("gemm_f32(transpose split)");
+}
+
+// C = A * B over a prepared B: splits A into aws (gemm_f32_tc_a_bytes), then
+// runs the convolution kernel
+int gemm_f32_tc_run(const float* A, const void* bws, void* aws, float* C, int M, int N, int K, cudaStream_t st) {
+  float* Ah = (float*)aws;
+  float* Al = (float*)((uint8_t*)aws + align256((size_t)M * K * 4));
+  const int64_t n = (int64_t)M * K;
+  k_split_flat<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 16), 256, 0, st>>>(A, Ah, Al,
+                                                                                                          n);
+  if (int rc = uk::check_launch("gemm_f32(split)")) return rc;
+  const float* Th = (const float*)bws;
+  const float* Tl = (const float*)((const uint8_t*)bws + align256((size_t)N * K * 4));
+  return run_tc(Th, Tl, Ah, Al, C, nullptr, 1, N / 64, 64, K, 1, 1, M, 0, st);
+}
+
+}  // namespace uk
+
+extern "C" size_t uk_cuda_gemm_f32_workspace_size(int M, int N, int K) {
+  if (!uk::gemm_f32_tc_shape(M, N, K)) return 0;
+  return uk::gemm_f32_tc_b_bytes(N, K) + uk::gemm_f32_tc_a_bytes(M, K);
+}
+
+extern "C" int uk_cuda_gemm_f32_prefers_tc(int M, int N, int K) {
+  // from about 2^30 multiply-adds the tensor cores win; below, the FFMA
+  // kernel is as fast and needs no workspace
+  return uk::gemm_f32_tc_shape(M, N, K) && (int64_t)M * N * K >= ((int64_t)1 << 30);
+}
+
+extern "C" int uk_cuda_gemm_f32_ws(const float* A, const float* B, float* C, int M, int N, int K, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (M < 0 || N < 0 || K < 0) return uk::fail(UK_EINVAL, "gemm_f32: negative dims %d %d %d", M, N, K);
+  if (workspace == nullptr || workspace_bytes == 0) return uk_cuda_gemm_f32(A, B, C, M, N, K, stream);
+  if (!uk::gemm_f32_tc_shape(M, N, K))
+    return uk::fail(UK_EINVAL, "gemm_f32: the tensor-core path needs K %% 32 == 0 and N %% 64 == 0 (M=%d N=%d K=%d); "
+                    "call without a workspace", M, N, K);
+  const size_t bb = uk::gemm_f32_tc_b_bytes(N, K), need = bb + uk::gemm_f32_tc_a_bytes(M, K);
+  if (workspace_bytes < need)
+    return uk::fail(UK_EINVAL, "gemm_f32: the tensor-core path needs a %zu-byte workspace, got %zu", need,
+                    workspace_bytes);
+  if (int rc = uk::check_device_ptr(A, "A")) return rc;
+  if (int rc = uk::check_device_ptr(B, "B")) return rc;
+  if (int rc = uk::check_device_ptr(C, "C")) return rc;
+  if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
+  if (!uk::aligned16(workspace)) return uk::fail(UK_EINVAL, "gemm_f32: the workspace must be 16-byte aligned");
+  if (int rc = uk::gemm_f32_tc_prep_b(B, workspace, N, K, st)) return rc;
+  return uk::gemm_f32_tc_run(A, workspace, (uint8_t*)workspace + bb, C, M, N, K, st);
 }
 
 // ---- fp16 convolution -------------------------------------------------------------

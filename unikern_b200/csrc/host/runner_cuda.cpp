@@ -118,15 +118,17 @@ struct OpCall {
   void* in0 = nullptr;   // A / X
   void* in1 = nullptr;   // B / Wt / W / S (null for softmax, reduce)
   void* out = nullptr;   // C / Y
-  void* ws = nullptr;    // reduce / conv workspace
+  void* ws = nullptr;    // reduce / conv / tensor-core fp32 gemm workspace
   size_t ws_bytes = 0;
+  bool tc32 = false;     // fp32 gemm on the tensor cores (split-tf32)
   int launch(cudaStream_t st) const {
     switch (op) {
       case OpKind::Gemm:
-        return f16 ? uk_cuda_gemm_f16((const uint16_t*)in0, (const uint16_t*)in1, (uint16_t*)out, (int)d[0],
-                                      (int)d[1], (int)d[2], st)
-                   : uk_cuda_gemm_f32((const float*)in0, (const float*)in1, (float*)out, (int)d[0], (int)d[1],
-                                      (int)d[2], st);
+        if (f16)
+          return uk_cuda_gemm_f16((const uint16_t*)in0, (const uint16_t*)in1, (uint16_t*)out, (int)d[0], (int)d[1],
+                                  (int)d[2], st);
+        return uk_cuda_gemm_f32_ws((const float*)in0, (const float*)in1, (float*)out, (int)d[0], (int)d[1], (int)d[2],
+                                   tc32 ? ws : nullptr, tc32 ? ws_bytes : 0, st);
       case OpKind::Conv:
         if (f16)  // fp16: kind::f16 tensor cores, the KML input read in place
           return uk_cuda_conv2d_f16((const uint16_t*)in0, (const uint16_t*)in1, (uint16_t*)out, 1, (int)d[0],
@@ -188,6 +190,8 @@ bool stage_operands(OpCall* c, DevArena* ar, cudaStream_t st, std::string* err) 
   if (c->n_in1() > 0) c->in1 = ar->alloc(c->n_in1() * c->es(), "in1");
   c->out = ar->alloc(c->n_out() * c->es(), "out");
   if (c->op == OpKind::Reduction) c->ws_bytes = uk_cuda_reduce_workspace_size(1, c->d[0]);
+  if (c->op == OpKind::Gemm && c->tc32)
+    c->ws_bytes = uk_cuda_gemm_f32_workspace_size((int)c->d[0], (int)c->d[1], (int)c->d[2]);
   if (c->op == OpKind::Conv && !c->f16)
     c->ws_bytes = uk_cuda_conv2d_workspace_size(1, (int)c->d[0], (int)c->d[1], (int)c->d[2], (int)c->d[3],
                                                 (int)c->d[4], (int)c->d[5], 0, UK_CONV_KML);
@@ -254,13 +258,50 @@ std::string BackendNvidia::generate(const Solution& s, const Hcs& h, const KmlTr
 // rows (a multiple of 256 where the budget allows, else of 32), or 0 when
 // the payload fits (resident), the op is not a GEMM, or B plus the smallest
 // ring does not fit the budget.
-int64_t stream_block_rows(const KmlTree& t, int64_t payload, double budget_bytes) {
+int64_t stream_block_rows(const KmlTree& t, int64_t payload, double budget_bytes, int* kind_out) {
   if (double(payload) <= 0.85 * budget_bytes || t.op != OpKind::Gemm) return 0;
-  const int64_t M = t.dims[0], N = t.dims[1], K = t.dims[2], es = dtype_bytes(t.dtype);
-  const double left = 0.85 * budget_bytes - double(K) * double(N) * double(es) - 1024.0;
-  int64_t rows = left > 0 ? (int64_t)(left / (2.0 * double(K + N) * double(es))) : 0;
-  rows = rows >= 256 ? rows / 256 * 256 : rows / 32 * 32;
-  if (rows < 32) return 0;
+  const int M = t.dims[0], N = t.dims[1], K = t.dims[2];
+  const double room = 0.85 * budget_bytes - double(K) * double(N) * double(dtype_bytes(t.dtype));
+  // the largest multiple of 32 rows in [32 * lo, M] whose ring fits, 0 if
+  // none (in that range the ring of this kind takes one kernel and grows with
+  // the rows)
+  auto largest = [&](int kind, int64_t lo) -> int64_t {
+    auto fits = [&](int64_t rows) {
+      return double(uk_cuda_gemm_streamed_ring_size(M, N, K, kind, (int)rows)) <= room;
+    };
+    int64_t hi = ((int64_t)M + 31) / 32;
+    if (room <= 0 || lo > hi || !fits(lo * 32)) return 0;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) / 2;
+      if (fits(mid * 32)) lo = mid;
+      else hi = mid - 1;
+    }
+    return lo * 32;
+  };
+  auto round256 = [](int64_t r) { return r >= 256 ? r / 256 * 256 : r; };
+  if (t.dtype == DType::F16) {
+    const int64_t rows = round256(largest(1, 1));
+    if (rows == 0) return 0;
+    if (kind_out) *kind_out = 1;
+    return rows < M ? rows : M;
+  }
+  // fp32: blocks from the first 256-multiple of rows that gains from the
+  // tensor cores (their ring also holds the tf32 pairs of B^T) when such a
+  // ring fits, else the FFMA ring
+  int64_t rows = 0;
+  int kind = 2;
+  if (uk_cuda_gemm_f32_prefers_tc(M, N, K)) {
+    int64_t r_tc = 256;
+    while (r_tc < M && !uk_cuda_gemm_f32_prefers_tc((int)r_tc, N, K)) r_tc += 256;
+    const int64_t r = round256(largest(0, std::min<int64_t>(r_tc, M) / 32));
+    if (r > 0 && uk_cuda_gemm_f32_prefers_tc((int)std::min<int64_t>(r, M), N, K)) {
+      rows = r;
+      kind = 0;
+    }
+  }
+  if (rows == 0) rows = round256(largest(2, 1));
+  if (rows == 0) return 0;
+  if (kind_out) *kind_out = kind;
   return rows < M ? rows : M;
 }
 
@@ -291,7 +332,8 @@ Solution solve_b200(const Hcs& h, const KmlTree& t, int sms) {
   }
   const double copy = h.unified_memory || h.link_bw_gbps <= 0 ? 0.0 : double(w.bytes) / (h.link_bw_gbps * 1e9) * 1e3;
   const int64_t payload = payload_bytes(t, 0);
-  const int64_t rows = stream_block_rows(t, payload, double(h.device_capacity()));
+  int kind = 0;
+  const int64_t rows = stream_block_rows(t, payload, double(h.device_capacity()), &kind);
   std::ostringstream pr;
   if (rows == 0 && h.device_capacity() > 0 && double(payload) > 0.85 * double(h.device_capacity())) {
     s.c_ms = std::max(comp, mem) + copy;
@@ -301,7 +343,7 @@ Solution solve_b200(const Hcs& h, const KmlTree& t, int sms) {
     // streamed: the ring overlaps the copies with the block GEMMs
     s.c_ms = std::max(std::max(comp, mem), copy);
     pr << "placement: streamed on " << h.device << " (sm_100a; B resident, A/C in a two-slot ring of " << rows
-       << "-row blocks) tile=" << tile[0] << "x" << tile[1] << " k_block=" << tile[2] << " stages=" << tile[3]
+       << "-row blocks" << (kind == 0 ? ", split-tf32 tensor cores" : kind == 2 ? ", FFMA" : "") << ") tile=" << tile[0] << "x" << tile[1] << " k_block=" << tile[2] << " stages=" << tile[3]
        << " path=pinned-copy";
   } else {
     s.c_ms = std::max(comp, mem) + copy;
@@ -443,18 +485,26 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
   timed.op = tree.op;
   timed.f16 = tree.dtype == DType::F16;
   for (int i = 0; i < 6; ++i) timed.d[i] = tree.dims[i];
+  // an fp32 gemm large enough to gain from the tensor cores runs split-tf32
+  timed.tc32 = tree.op == OpKind::Gemm && !timed.f16 &&
+               uk_cuda_gemm_f32_prefers_tc(tree.dims[0], tree.dims[1], tree.dims[2]);
   const size_t ws = tree.op == OpKind::Reduction ? uk_cuda_reduce_workspace_size(1, tree.dims[0])
                     : tree.op == OpKind::Conv && tree.dtype == DType::F32
                         ? uk_cuda_conv2d_workspace_size(1, tree.dims[0], tree.dims[1], tree.dims[2], tree.dims[3],
                                                         tree.dims[4], tree.dims[5], 0, UK_CONV_KML)
-                        : 0;
+                    : timed.tc32 ? uk_cuda_gemm_f32_workspace_size(tree.dims[0], tree.dims[1], tree.dims[2])
+                                 : 0;
   const int64_t payload = payload_bytes(tree, ws);
   const double payload_mb = double(payload) / (1024.0 * 1024.0);
   // the device budget: the HCS's declared device tier, never more than the
   // device reports (a smaller HCS tier models a smaller device)
   const int64_t declared = hcs.device_capacity();
   const double budget = double(declared > 0 && (uint64_t)declared < tot ? (uint64_t)declared : tot);
-  const int64_t stream_rows = stream_block_rows(tree, payload, budget);  // > 0: scenario B
+  int stream_kind = 0;  // uk_cuda_gemm_streamed's kind
+  const int64_t stream_rows = stream_block_rows(tree, payload, budget, &stream_kind);  // > 0: scenario B
+  // the streamed fp32 blocks take the tensor cores when the block shape gains
+  const bool stream_tc = stream_rows > 0 && stream_kind == 0 &&
+                         uk_cuda_gemm_f32_prefers_tc((int)stream_rows, tree.dims[1], tree.dims[2]);
   if (double(payload) > 0.85 * budget) {
     // the streamed operands live in page-locked host memory: at most half of
     // the host's RAM (and of the HCS's host tier where it declares one)
@@ -496,8 +546,14 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
   // ---- 1. verify instance ----
   {
     OpCall v = timed;
+    v.tc32 = timed.tc32 && stream_rows == 0;  // a streamed run verifies through the ring
     if (tree.op == OpKind::Gemm) {
+      // the reference's 256^3; a streamed fp32 gemm on the tensor cores
+      // verifies 2048 x 1024 x 1024 in two 1024-row blocks, the smallest
+      // streamed instance whose blocks take them (still exact: every partial
+      // sum of the sawtooth operands is representable)
       v.d[0] = v.d[1] = v.d[2] = 256;
+      if (stream_tc) v.d[0] = 2048, v.d[1] = v.d[2] = 1024;
     } else if (tree.op == OpKind::Conv) {
       // the reference's instance (32 x 32 x 8 -> 16, 3 x 3); the fp16 conv
       // takes 64-channel steps, so its instance has 64 input channels
@@ -510,21 +566,26 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
     ok = worst && stage_operands(&v, &ar, st, &err) &&
          cuda_ok(cudaMemsetAsync(worst, 0, sizeof(double), st), "memset max_rel", &err);
     if (ok && stream_rows > 0) {
-      // scenario B verifies the streamed path itself: the 256^3 instance
-      // through the ring in four 64-row blocks, from and to pinned memory
-      const size_t es = v.es(), nb = 256 * 256 * es;
-      const size_t rb = uk_cuda_gemm_streamed_ring_size(256, 256, 256, v.f16, 64);
-      void *hA = ar.pinned(nb, "A"), *hB = ar.pinned(nb, "B"), *hC = ar.pinned(nb, "C");
+      // scenario B verifies the streamed path itself: the instance through
+      // the ring (256^3 in four 64-row blocks, or the tensor-core instance
+      // above in two), from and to pinned memory
+      const int vm = (int)v.d[0], vn = (int)v.d[1], vk = (int)v.d[2], vr = stream_tc ? 1024 : 64;
+      const size_t es = v.es();
+      const size_t rb = uk_cuda_gemm_streamed_ring_size(vm, vn, vk, stream_kind, vr);
+      void* hA = ar.pinned((size_t)vm * vk * es, "A");
+      void* hB = ar.pinned((size_t)vk * vn * es, "B");
+      void* hC = ar.pinned((size_t)vm * vn * es, "C");
       void* ring = ar.alloc(rb, "ring");
       ok = ar.err.empty();
       if (!ok) err = ar.err;
-      ok = ok && cuda_ok(cudaMemcpyAsync(hA, v.in0, nb, cudaMemcpyDeviceToHost, st), "stage A", &err) &&
-           cuda_ok(cudaMemcpyAsync(hB, v.in1, nb, cudaMemcpyDeviceToHost, st), "stage B", &err);
-      if (ok && uk_cuda_gemm_streamed(hA, hB, hC, v.in1, ring, rb, 256, 256, 256, v.f16, 64, st) != UK_OK) {
+      ok = ok && cuda_ok(cudaMemcpyAsync(hA, v.in0, (size_t)vm * vk * es, cudaMemcpyDeviceToHost, st), "stage A", &err) &&
+           cuda_ok(cudaMemcpyAsync(hB, v.in1, (size_t)vk * vn * es, cudaMemcpyDeviceToHost, st), "stage B", &err);
+      if (ok && uk_cuda_gemm_streamed(hA, hB, hC, v.in1, ring, rb, vm, vn, vk, stream_kind, vr, st) != UK_OK) {
         err = uk_cuda_last_error();
         ok = false;
       }
-      ok = ok && cuda_ok(cudaMemcpyAsync(v.out, hC, nb, cudaMemcpyHostToDevice, st), "return C", &err);
+      ok = ok && cuda_ok(cudaMemcpyAsync(v.out, hC, (size_t)vm * vn * es, cudaMemcpyHostToDevice, st), "return C",
+                         &err);
     } else if (ok && (rc = v.launch(st)) != UK_OK) {
       err = uk_cuda_last_error();
       ok = false;
@@ -573,7 +634,7 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
   if (ok && stream_rows > 0) {
     const int64_t M = tree.dims[0], N = tree.dims[1], K = tree.dims[2];
     const size_t es = timed.es();
-    const size_t ring_bytes = uk_cuda_gemm_streamed_ring_size((int)M, (int)N, (int)K, timed.f16, (int)stream_rows);
+    const size_t ring_bytes = uk_cuda_gemm_streamed_ring_size((int)M, (int)N, (int)K, stream_kind, (int)stream_rows);
     void* dB = ar.alloc((size_t)K * N * es, "B");
     void* ring = ar.alloc(ring_bytes, "ring");
     void* hA = ar.pinned((size_t)M * K * es, "A");
@@ -594,7 +655,7 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
            cuda_ok(cudaStreamSynchronize(st), "stage", &err);
     }
     auto pass = [&]() -> bool {
-      if (uk_cuda_gemm_streamed(hA, hB, hC, dB, ring, ring_bytes, (int)M, (int)N, (int)K, timed.f16,
+      if (uk_cuda_gemm_streamed(hA, hB, hC, dB, ring, ring_bytes, (int)M, (int)N, (int)K, stream_kind,
                                 (int)stream_rows, st) != UK_OK) {
         err = uk_cuda_last_error();
         return false;
@@ -613,25 +674,17 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
       total += ms;
     }
     if (ok) {
-      // kernel-only: the block GEMMs of one pass, run on the ring's first slot
+      // kernel-only: the device work of one pass (B's pre-pass on the tensor
+      // cores, every block's GEMM) without the copies, on the ring's first slot
       r.measured_ms = total / iters;
-      const int64_t nblk = (M + stream_rows - 1) / stream_rows;
-      uint8_t* a0 = (uint8_t*)(((uintptr_t)ring + 255) & ~(uintptr_t)255);
-      const size_t a_slot = ((size_t)stream_rows * K * es + 255) / 256 * 256;
-      uint8_t* c0 = a0 + 2 * a_slot;
       float ms = 0;
       ok = cuda_ok(cudaEventRecord(e0, st), "record", &err);
-      for (int64_t b = 0; ok && b < nblk * iters; ++b) {
-        const int nr = (int)((b % nblk) == nblk - 1 ? M - (nblk - 1) * stream_rows : stream_rows);
-        const int rc = timed.f16 ? uk_cuda_gemm_f16((const uint16_t*)a0, (const uint16_t*)dB, (uint16_t*)c0, nr,
-                                                    (int)N, (int)K, st)
-                                 : uk_cuda_gemm_f32((const float*)a0, (const float*)dB, (float*)c0, nr, (int)N,
-                                                    (int)K, st);
-        if (rc != UK_OK) {
+      for (int i = 0; ok && i < iters; ++i)
+        if (ukr_gemm_streamed_kernels(dB, ring, ring_bytes, (int)M, (int)N, (int)K, stream_kind, (int)stream_rows,
+                                      st) != UK_OK) {
           err = uk_cuda_last_error();
           ok = false;
         }
-      }
       ok = ok && cuda_ok(cudaEventRecord(e1, st), "record", &err) &&
            cuda_ok(cudaEventSynchronize(e1), "sync", &err) && cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "elapsed", &err);
       r.kernel_ms = double(ms) / iters;

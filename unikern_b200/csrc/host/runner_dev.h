@@ -3,6 +3,7 @@
 // that accumulate the worst per-element relative error into one device double.
 #pragma once
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -23,6 +24,10 @@ extern "C" {
 int ukr_saw_fill(void* p, int64_t n, int kind, int f16, void* stream);
 // the initialiser's values for indices [offset, offset + n)
 int ukr_saw_fill_at(void* p, int64_t n, int64_t offset, int kind, int f16, void* stream);
+// the device work of uk_cuda_gemm_streamed without its copies (B's pre-pass
+// and every block's GEMM, on the ring's first slot): kernel-only timing
+int ukr_gemm_streamed_kernels(void* dB, void* ring, size_t ring_bytes, int M, int N, int K, int kind,
+                              int block_rows, void* stream);
 int ukr_check_gemm(const void* A, const void* B, const void* C, int M, int N, int K, int f16, double* worst,
                    void* stream);
 // f16 != 0: the operands and the result are IEEE binary16, else fp32

@@ -21,6 +21,14 @@
 #include "uk_common.cuh"
 
 extern "C" int uk_cuda_gemm_f32(const float* A, const float* B, float* C, int M, int N, int K, void* stream);
+extern "C" int uk_cuda_gemm_f32_prefers_tc(int M, int N, int K);
+
+namespace uk {  // the tensor-core fp32 GEMM's stages (conv_tc.cu)
+size_t gemm_f32_tc_b_bytes(int N, int K);
+size_t gemm_f32_tc_a_bytes(int M, int K);
+int gemm_f32_tc_prep_b(const float* B, void* bws, int N, int K, cudaStream_t st);
+int gemm_f32_tc_run(const float* A, const void* bws, void* aws, float* C, int M, int N, int K, cudaStream_t st);
+}  // namespace uk
 
 namespace {
 
@@ -130,7 +138,9 @@ extern "C" int uk_cuda_gemm_f16_host(const uint16_t* hA, const uint16_t* hB, uin
 // the caller's device buffer.  Block i uses slot i % 2: its upload waits until
 // block i-2's GEMM has finished reading the slot's A rows, its GEMM waits
 // until block i-2's C rows have left the slot.  Device memory: K*N elements
-// for B plus 2 * block_rows * (K + N) for the ring.
+// for B plus 2 * block_rows * (K + N) for the ring, and for an fp32 GEMM on
+// the tensor cores (split-tf32) 2 * (K*N + block_rows*K) more for the tf32
+// pairs of B^T and of one block of A.
 namespace {
 
 struct StreamPipe {
@@ -158,17 +168,82 @@ int get_stream_pipe(StreamPipe** out) {
   return UK_OK;
 }
 
+// ring layout (each part 256-byte aligned from the first aligned address):
+// A slot 0, A slot 1, C slot 0, C slot 1, and for an fp32 GEMM on the tensor
+// cores the tf32 pairs of B^T (made once per call) and of one A block
+struct RingLayout {
+  int64_t rows = 0;
+  size_t a_slot = 0, c_slot = 0, b_split = 0, a_split = 0, total = 0;
+  bool tc = false;
+};
+
+// kind: 1 binary16; 0 fp32, on the tensor cores where a block gains; 2 fp32
+// on the FFMA kernel (no tf32 pairs, the smallest ring)
+RingLayout ring_layout(int M, int N, int K, int kind, int block_rows) {
+  RingLayout r;
+  if (M <= 0 || N <= 0 || K <= 0 || block_rows <= 0 || kind < 0 || kind > 2) return r;
+  const int f16 = kind == 1;
+  auto align = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t es = f16 ? 2 : 4;
+  r.rows = block_rows < M ? block_rows : M;
+  r.a_slot = align((size_t)r.rows * K * es);
+  r.c_slot = align((size_t)r.rows * N * es);
+  r.tc = kind == 0 && uk_cuda_gemm_f32_prefers_tc((int)r.rows, N, K);
+  if (r.tc) {
+    r.b_split = uk::gemm_f32_tc_b_bytes(N, K);
+    r.a_split = uk::gemm_f32_tc_a_bytes((int)r.rows, K);
+  }
+  r.total = 255 + 2 * r.a_slot + 2 * r.c_slot + r.b_split + r.a_split;
+  return r;
+}
+
 }  // namespace
 
-extern "C" size_t uk_cuda_gemm_streamed_ring_size(int M, int N, int K, int f16, int block_rows) {
-  if (M <= 0 || N <= 0 || K <= 0 || block_rows <= 0) return 0;
-  const int64_t rows = block_rows < M ? block_rows : M;
-  return (size_t)(2 * rows * ((int64_t)K + N) * (f16 ? 2 : 4) + 512);
+extern "C" size_t uk_cuda_gemm_streamed_ring_size(int M, int N, int K, int kind, int block_rows) {
+  return ring_layout(M, N, K, kind, block_rows).total;
+}
+
+namespace {
+
+// the device work of one streamed call over data already in the ring: B's
+// pre-pass (tensor-core fp32) and one GEMM per block, all on slot 0
+int streamed_block_gemms(const RingLayout& L, void* dB, uint8_t* base, int M, int N, int K, int f16,
+                         cudaStream_t st, bool prep_b) {
+  // f16: the data type (kind 1); the fp32 kernel choice is L.tc
+  uint8_t* b_split = base + 2 * L.a_slot + 2 * L.c_slot;
+  if (L.tc && prep_b)
+    if (int rc = uk::gemm_f32_tc_prep_b((const float*)dB, b_split, N, K, st)) return rc;
+  const int nblk = (int)((M + L.rows - 1) / L.rows);
+  for (int i = 0; i < nblk; ++i) {
+    const int nr = (int)(i == nblk - 1 ? M - (int64_t)(nblk - 1) * L.rows : L.rows);
+    uint8_t* a = base;
+    uint8_t* c = base + 2 * L.a_slot;
+    const int rc = f16 ? uk_cuda_gemm_f16_ld((const uint16_t*)a, K, (const uint16_t*)dB, N, (uint16_t*)c, N, nr, N,
+                                             K, st)
+                   : L.tc ? uk::gemm_f32_tc_run((const float*)a, b_split, b_split + L.b_split, (float*)c, nr, N, K,
+                                                st)
+                          : uk_cuda_gemm_f32((const float*)a, (const float*)dB, (float*)c, nr, N, K, st);
+    if (rc != UK_OK) return rc;
+  }
+  return UK_OK;
+}
+
+}  // namespace
+
+// kernel-only timing aid of the runner (declared in host/runner_dev.h)
+extern "C" int ukr_gemm_streamed_kernels(void* dB, void* ring, size_t ring_bytes, int M, int N, int K, int kind,
+                                         int block_rows, void* stream) {
+  const RingLayout L = ring_layout(M, N, K, kind, block_rows);
+  if (L.total == 0 || ring_bytes < L.total) return uk::fail(UK_EINVAL, "gemm_streamed: ring too small");
+  uint8_t* base = (uint8_t*)(((uintptr_t)ring + 255) & ~(uintptr_t)255);
+  return streamed_block_gemms(L, dB, base, M, N, K, kind == 1, (cudaStream_t)stream, true);
 }
 
 extern "C" int uk_cuda_gemm_streamed(const void* hA, const void* hB, void* hC, void* dB, void* ring,
-                                     size_t ring_bytes, int M, int N, int K, int f16, int block_rows, void* stream) {
+                                     size_t ring_bytes, int M, int N, int K, int kind, int block_rows, void* stream) {
   if (M < 0 || N < 0 || K < 0) return uk::fail(UK_EINVAL, "gemm_streamed: negative dims %d %d %d", M, N, K);
+  if (kind < 0 || kind > 2) return uk::fail(UK_EINVAL, "gemm_streamed: kind must be 0, 1 or 2 (got %d)", kind);
+  const int f16 = kind == 1;
   if (block_rows <= 0) return uk::fail(UK_EINVAL, "gemm_streamed: block_rows must be positive");
   if (M == 0 || N == 0) return UK_OK;
   if (int rc = check_host(hA, "hA")) return rc;
@@ -176,26 +251,23 @@ extern "C" int uk_cuda_gemm_streamed(const void* hA, const void* hB, void* hC, v
   if (int rc = check_host(hC, "hC")) return rc;
   if (int rc = uk::check_device_ptr(dB, "dB")) return rc;
   if (int rc = uk::check_device_ptr(ring, "ring")) return rc;
-  const size_t need = uk_cuda_gemm_streamed_ring_size(M, N, K, f16, block_rows);
-  if (ring_bytes < need)
+  const RingLayout L = ring_layout(M, N, K, kind, block_rows);
+  if (ring_bytes < L.total)
     return uk::fail(UK_EINVAL, "gemm_streamed: the ring needs %zu bytes (uk_cuda_gemm_streamed_ring_size), got %zu",
-                    need, ring_bytes);
+                    L.total, ring_bytes);
   DevPipe* p = nullptr;
   StreamPipe* q = nullptr;
   if (int rc = get_pipe(&p)) return rc;
   if (int rc = get_stream_pipe(&q)) return rc;
   const cudaStream_t st = (cudaStream_t)stream;
   const size_t es = f16 ? 2 : 4;
-  const int64_t rows = block_rows < M ? block_rows : M;
+  const int64_t rows = L.rows;
   const int nblk = (int)((M + rows - 1) / rows);
-  // ring layout: A slot 0, A slot 1, C slot 0, C slot 1 (each 256-byte aligned)
-  auto align = [](size_t b) { return (b + 255) / 256 * 256; };
   uint8_t* base = (uint8_t*)(((uintptr_t)ring + 255) & ~(uintptr_t)255);
-  const size_t a_slot = align(rows * (size_t)K * es), c_slot = align(rows * (size_t)N * es);
-  uint8_t* a_buf[2] = {base, base + a_slot};
-  uint8_t* c_buf[2] = {base + 2 * a_slot, base + 2 * a_slot + c_slot};
-  if ((size_t)(c_buf[1] + c_slot - (uint8_t*)ring) > ring_bytes)
-    return uk::fail(UK_EINVAL, "gemm_streamed: ring too small after alignment");
+  uint8_t* a_buf[2] = {base, base + L.a_slot};
+  uint8_t* c_buf[2] = {base + 2 * L.a_slot, base + 2 * L.a_slot + L.c_slot};
+  uint8_t* b_split = base + 2 * L.a_slot + 2 * L.c_slot;
+  uint8_t* a_split = b_split + L.b_split;
 
   if (cudaEventRecord(p->start, st) != cudaSuccess || cudaStreamWaitEvent(p->in, p->start, 0) != cudaSuccess ||
       cudaStreamWaitEvent(p->out, p->start, 0) != cudaSuccess)
@@ -203,6 +275,8 @@ extern "C" int uk_cuda_gemm_streamed(const void* hA, const void* hB, void* hC, v
   if (cudaMemcpyAsync(dB, hB, (size_t)K * N * es, cudaMemcpyHostToDevice, p->in) != cudaSuccess ||
       cudaEventRecord(p->b_ready, p->in) != cudaSuccess || cudaStreamWaitEvent(st, p->b_ready, 0) != cudaSuccess)
     return uk::check_launch("gemm_streamed: upload B");
+  if (L.tc)  // B^T as tf32 pairs, once for every block
+    if (int rc = uk::gemm_f32_tc_prep_b((const float*)dB, b_split, N, K, st)) return rc;
   for (int i = 0; i < nblk; ++i) {
     const int slot = i & 1;
     const int64_t r0 = (int64_t)i * rows, r1 = r0 + rows < M ? r0 + rows : M, nr = r1 - r0;
@@ -218,8 +292,10 @@ extern "C" int uk_cuda_gemm_streamed(const void* hA, const void* hB, void* hC, v
       return uk::check_launch("gemm_streamed: wait");
     const int rc = f16 ? uk_cuda_gemm_f16_ld((const uint16_t*)a_buf[slot], K, (const uint16_t*)dB, N,
                                              (uint16_t*)c_buf[slot], N, (int)nr, N, K, stream)
-                       : uk_cuda_gemm_f32((const float*)a_buf[slot], (const float*)dB, (float*)c_buf[slot], (int)nr,
-                                          N, K, stream);
+                   : L.tc ? uk::gemm_f32_tc_run((const float*)a_buf[slot], b_split, a_split, (float*)c_buf[slot],
+                                                (int)nr, N, K, st)
+                          : uk_cuda_gemm_f32((const float*)a_buf[slot], (const float*)dB, (float*)c_buf[slot],
+                                             (int)nr, N, K, stream);
     if (rc != UK_OK) return rc;
     if (cudaEventRecord(q->gemm_done[slot], st) != cudaSuccess ||
         cudaStreamWaitEvent(p->out, q->gemm_done[slot], 0) != cudaSuccess ||

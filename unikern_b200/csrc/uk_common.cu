@@ -84,11 +84,15 @@ int uk_cuda_tile_plan(int op, int f16, const int64_t* dims, int sms, int* out4) 
   switch (op) {
     case UK_OP_GEMM:  // dims M, N, K
       if (f16 && dims[2] % 8 == 0 && dims[1] % 8 == 0) t = dims[0] > 128 ? uk::kGemmF16PairTile : uk::kGemmF16Tile;
+      else if (!f16 && uk_cuda_gemm_f32_prefers_tc((int)dims[0], (int)dims[1], (int)dims[2]))
+        t = uk::kConvPairF32Tile;  // split-tf32 on the convolution's pair kernel
       else t = uk::sgemm_tile(dims[0], dims[1], n_sm);
       break;
     case UK_OP_CONV: {  // KML dims H, W, C, Kh, Kw, Oc (one image, valid)
       const int64_t npix = (dims[0] - dims[3] + 1) * (dims[1] - dims[4] + 1);
-      t = uk::conv_tile(npix, dims[5], n_sm);
+      if (f16) t = uk::kConvPairF16Tile;
+      else if (dims[2] >= 32 && dims[2] % 32 == 0) t = uk::kConvPairF32Tile;
+      else t = uk::conv_tile(npix, dims[5], n_sm);
       break;
     }
     case UK_OP_REDUCE: {  // dims L: one row of L columns
