@@ -22,6 +22,7 @@ def half(a):
     (3, 128, 13, 70, 300, 3, 1, True),
     (1, 256, 14, 14, 256, 3, 1, False),
     (2, 64, 7, 5, 40, 1, 0, True),
+    (2, 192, 12, 12, 72, 3, 1, True),      # tiled pre-pass, three channel tiles, a partial hw tile
     (32, 256, 56, 56, 256, 3, 1, True),   # the BASELINE conv shape in fp16 (two images checked)
 ])
 def test_conv_f16_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):

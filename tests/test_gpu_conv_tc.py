@@ -33,6 +33,7 @@ def run_nchw(x, w, s, pad, tc=True):
     (3, 64, 13, 70, 300, 3, 1, True),     # two w tiles, two channel tiles
     (1, 256, 14, 14, 256, 3, 1, True),
     (2, 96, 7, 5, 40, 1, 0, False),        # 1x1
+    (2, 96, 8, 10, 40, 3, 1, True),        # tiled pre-pass with a partial channel tile (H*W % 4 == 0)
     (1, 32, 6, 66, 8, 3, 0, True),         # valid padding, ragged tiles
     (1, 64, 20, 20, 64, 5, 2, False),      # 5x5, pad 2
 ])

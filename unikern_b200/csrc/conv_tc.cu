@@ -676,6 +676,65 @@ __global__ void __launch_bounds__(ROW_THREADS) k_split_row_nhwc(const float* __r
   }
 }
 
+// X[n][c][hw] -> [n][hw][c] through a 64 (c) x 64 (hw) shared-memory tile held
+// as fp32 (exact for halves): 16- (fp32) or 8-byte (f16) loads along hw by 16
+// threads per row, stores of 4 consecutive channels along c.  F16: binary16
+// in and out (O0); else fp32 in and tf32 (hi, lo) pairs out (O0, O1).  Needs
+// HW % 4 == 0, C % 4 == 0, X aligned to its vector size.
+template <bool F16>
+__global__ void __launch_bounds__(256) k_tile_nhwc(const void* __restrict__ Xv, void* __restrict__ O0,
+                                                   void* __restrict__ O1, int C, int64_t HW) {
+  __shared__ float t[64][65];
+  const int64_t hw0 = (int64_t)blockIdx.x * 64;
+  const int c0 = blockIdx.y * 64;
+  const int64_t n = blockIdx.z;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int c = ty + 16 * r;
+    const int64_t hw = hw0 + 4 * tx;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (c0 + c < C && hw < HW) {
+      const int64_t off = (n * C + c0 + c) * HW + hw;
+      if constexpr (F16) {
+        const uint2 u = __ldcs(reinterpret_cast<const uint2*>((const __half*)Xv + off));
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+      } else {
+        const float4 f = __ldcs(reinterpret_cast<const float4*>((const float*)Xv + off));
+        v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[c][4 * tx + j] = v[j];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int hl = ty + 16 * r, c = 4 * tx;
+    const int64_t hw = hw0 + hl;
+    if (hw >= HW || c0 + c >= C) continue;
+    const int64_t off = (n * HW + hw) * C + c0 + c;
+    if constexpr (F16) {
+      const __half2 a = __floats2half2_rn(t[c][hl], t[c + 1][hl]);
+      const __half2 b = __floats2half2_rn(t[c + 2][hl], t[c + 3][hl]);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t*>(&a);
+      u.y = *reinterpret_cast<const uint32_t*>(&b);
+      *reinterpret_cast<uint2*>((__half*)O0 + off) = u;
+    } else {
+      float4 h, l;
+      split(t[c][hl], h.x, l.x);
+      split(t[c + 1][hl], h.y, l.y);
+      split(t[c + 2][hl], h.z, l.z);
+      split(t[c + 3][hl], h.w, l.w);
+      *reinterpret_cast<float4*>((float*)O0 + off) = h;
+      *reinterpret_cast<float4*>((float*)O1 + off) = l;
+    }
+  }
+}
+
 // elementwise split (the KML input is already HWC)
 __global__ void k_split_flat(const float* __restrict__ X, float* __restrict__ Xh, float* __restrict__ Xl, int64_t n) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -894,8 +953,12 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   // pre-pass: operands as tf32 (hi, lo) pairs, input as NHWC
   if (N == 0) return UK_OK;
   const size_t plane_bytes = (size_t)W * (C + 1) * 4;
-  // the row-staged pre-pass needs 16-byte aligned rows of X for its vector loads
-  if (layout == UK_CONV_NCHW && plane_bytes <= 100 * 1024 && (W % 4 != 0 || uk::aligned16(X))) {
+  const int64_t HW = (int64_t)H * W;
+  if (layout == UK_CONV_NCHW && HW % 4 == 0 && uk::aligned16(X) && (HW + 63) / 64 <= 2147483647LL && N <= 65535) {
+    // the tiled transpose: vector loads along hw, vector stores along c
+    const dim3 g((unsigned)((HW + 63) / 64), (unsigned)((C + 63) / 64), (unsigned)N);
+    k_tile_nhwc<false><<<g, 256, 0, st>>>(X, Xh, Xl, C, HW);
+  } else if (layout == UK_CONV_NCHW && plane_bytes <= 100 * 1024 && (W % 4 != 0 || uk::aligned16(X))) {
     static bool plane_attr[64] = {false};
     int d = 0;
     cudaGetDevice(&d);
@@ -1011,9 +1074,41 @@ __global__ void __launch_bounds__(ROW_THREADS) k_row_nhwc_h(const __half* __rest
   const int cp = C + 1;
   const __half* src = X + ((int64_t)n * C * H + h) * W;
   const int64_t cw = (int64_t)C * W;
-  for (int64_t i = threadIdx.x; i < cw; i += ROW_THREADS) {
-    const int c = (int)(i / W), w = (int)(i - (int64_t)c * W);
-    plane_h[w * cp + c] = __half2float(__ldcs(src + (int64_t)c * H * W + w));
+  if (W % 8 == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0) {
+    // 16-byte loads of 8 w, eight per thread issued before any is consumed
+    constexpr int UNR = 8;
+    const int w8n = W / 8;
+    const int64_t n8 = cw / 8;
+    for (int64_t base = threadIdx.x; base < n8; base += (int64_t)ROW_THREADS * UNR) {
+      uint4 v[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int64_t i = base + (int64_t)u * ROW_THREADS;
+        if (i < n8) {
+          const int c = (int)(i / w8n), w8 = (int)(i - (int64_t)c * w8n);
+          v[u] = __ldcs(reinterpret_cast<const uint4*>(src + (int64_t)c * H * W) + w8);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int64_t i = base + (int64_t)u * ROW_THREADS;
+        if (i < n8) {
+          const int c = (int)(i / w8n), w = 8 * (int)(i - (int64_t)c * w8n);
+          const uint32_t q[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[j]));
+            plane_h[(w + 2 * j) * cp + c] = f.x;
+            plane_h[(w + 2 * j + 1) * cp + c] = f.y;
+          }
+        }
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < cw; i += ROW_THREADS) {
+      const int c = (int)(i / W), w = (int)(i - (int64_t)c * W);
+      plane_h[w * cp + c] = __half2float(__ldcs(src + (int64_t)c * H * W + w));
+    }
   }
   __syncthreads();
   uint4* dst = reinterpret_cast<uint4*>(Xt + nh * cw);
@@ -1107,7 +1202,13 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
       attr[d] = true;
     }
     if ((int64_t)N * H > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d_f16: N*H too large");
-    k_row_nhwc_h<<<(unsigned)((int64_t)N * H), ROW_THREADS, plane, st>>>((const __half*)X, (__half*)Xt, C, H, W);
+    const int64_t HW = (int64_t)H * W;
+    if (HW % 4 == 0 && ((uintptr_t)X & 7) == 0 && N <= 65535) {
+      const dim3 g((unsigned)((HW + 63) / 64), (unsigned)(C / 64), (unsigned)N);
+      k_tile_nhwc<true><<<g, 256, 0, st>>>(X, Xt, nullptr, C, HW);
+    } else {
+      k_row_nhwc_h<<<(unsigned)((int64_t)N * H), ROW_THREADS, plane, st>>>((const __half*)X, (__half*)Xt, C, H, W);
+    }
     const int64_t nw = (int64_t)Oc * Kh * Kw * C;
     k_permute_weights_h<<<(unsigned)std::min<int64_t>((nw + 255) / 256, (int64_t)uk::sm_count() * 8), 256, 0, st>>>(
         (const __half*)Wt, (__half*)Wp, Oc, C, Kh, Kw);

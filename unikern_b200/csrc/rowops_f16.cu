@@ -200,7 +200,9 @@ void dispatch(const __half* X, const __half* G, __half* Y, int64_t L, int64_t C,
     return;                                                                            \
   }
   if constexpr (W == 8) {
-    UK_TRY(32, 1) UK_TRY(32, 2) UK_TRY(64, 2) UK_TRY(128, 2) UK_TRY(128, 4) UK_TRY(256, 4) UK_TRY(256, 8)
+    // the most threads for a row, at most 4 vectors (32 halves) each: more
+    // loads in flight and shorter per-thread chains
+    UK_TRY(32, 1) UK_TRY(32, 2) UK_TRY(64, 2) UK_TRY(128, 2) UK_TRY(128, 4) UK_TRY(256, 4) UK_TRY(512, 4)
     UK_TRY(512, 8)
   } else {
     UK_TRY(32, 1) UK_TRY(64, 2) UK_TRY(128, 4) UK_TRY(256, 4) UK_TRY(256, 8)
