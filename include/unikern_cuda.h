@@ -79,6 +79,17 @@ size_t uk_cuda_reduce_workspace_size(int64_t rows, int64_t cols);
 int uk_cuda_reduce_f32(const float* X, float* Y, int64_t rows, int64_t cols,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same reduce with the pass-1 width pinned: each row is cut into chunks of
+ * ceil(cols / width) elements, one partial sum per chunk, folded in a fixed
+ * order (the reference's UK_REDUCE_WIDTH knob, src/codegen_hip.cpp:874-908;
+ * the runner validates a pin against the reference's range [256, cols]).
+ * width >= 1; the partial count is ceil(cols / ceil(cols / width)), which is
+ * width whenever width divides the chunking exactly.  Workspace:
+ * uk_cuda_reduce_workspace_size_width(rows, cols, width) bytes. */
+size_t uk_cuda_reduce_workspace_size_width(int64_t rows, int64_t cols, int64_t width);
+int uk_cuda_reduce_f32_width(const float* X, float* Y, int64_t rows, int64_t cols, int64_t width,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* Reduce without a workspace: the same result as uk_cuda_reduce_f32 (same
  * kernels, same plan), for callers that cannot allocate device memory -- a
  * plugin inside a host application that owns every device allocation through

@@ -89,6 +89,21 @@ def test_reduce_deterministic_and_matches_blocked_basis():
     assert abs(a[0] - basis) / max(abs(basis), 1e-6) <= 0.03125
 
 
+@pytest.mark.parametrize("width", [256, 1000, 4096, 1 << 20, (1 << 20) + 7])
+def test_reduce_pinned_width(width):
+    # the UK_REDUCE_WIDTH knob: any pass-1 width gives the exact verify sum,
+    # and the f64 gate on random rows
+    X = np.full((1, 1 << 20), 0.015625, np.float32)
+    Y = empty((1,))
+    abi.reduce_width(dev(X), Y, width)
+    assert host(Y)[0] == 16384.0
+    R = np.random.default_rng(width).normal(0, 1, (3, 1000003)).astype(np.float32)
+    Y = empty((3,))
+    abi.reduce_width(dev(R), Y, width)
+    ref = O.row_reduce_f64(R)
+    assert O.rel_err(host(Y), ref, SUM_TAU * max(O.rms(ref), 1000.0)) <= F32_TOL
+
+
 def test_reduce_alternating_wide_range():
     # tests/acceptance.cpp:1555-1608: the parallel sum must be at least as close
     # to the exact f64 sum as the reference's blocked basis

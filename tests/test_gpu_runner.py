@@ -146,3 +146,33 @@ def test_calibrate_from_measured_runs(tmp_path):
     bw = json.loads(cal)["link_bw_gbps"]
     assert 2.0 < bw < 1000.0, out   # a page-locked host link, PCIe or C2C
     assert json.loads(cal)["constants_version"] == 2
+
+
+def test_reduce_width_knob(tmp_path, monkeypatch):
+    # UK_REDUCE_WIDTH pins the pass-1 width and is reported; a value outside
+    # [256, n] is refused, never silently dropped (src/codegen_hip.cpp:874-908)
+    kml = '{"op":"reduce","dtype":"fp32","dims":[1048576]}'
+    rc, out = abi.run_kml(HCS, kml, None, write_ledger=False)
+    assert rc == 0 and "UNIKERN_INFO reduce_width source=plan" in out, out
+    monkeypatch.setenv("UK_REDUCE_WIDTH", "4096")
+    rc, out = abi.run_kml(HCS, kml, None, write_ledger=False)
+    assert rc == 0 and "UNIKERN_INFO reduce_width source=env width=4096 cap=0 n=1048576" in out, out
+    assert abi.result_tokens(out)["max_rel"] == "0.000000e+00"
+    for bad in ("100", "2000000", "abc"):
+        monkeypatch.setenv("UK_REDUCE_WIDTH", bad)
+        rc, out = abi.run_kml(HCS, kml, str(tmp_path / "l"), write_ledger=True)
+        assert rc == 1 and "UNIKERN_ERROR what=reduce_width_pin_unfit value=" + bad in out, out
+        assert not (tmp_path / "l").exists()
+
+
+def test_stream_path_knob(tmp_path, monkeypatch):
+    # UK_GEMM_STREAM_PATH: pinned (the only arm here) is accepted and reported;
+    # mmap and unknown values are refused (src/codegen_hip.cpp:1338-1355)
+    kml = '{"op":"gemm","dtype":"fp16","dims":[4096,1024,1024]}'
+    monkeypatch.setenv("UK_GEMM_STREAM_PATH", "pinned")
+    rc, out = abi.run_kml(small_vram_hcs(16), kml, None, write_ledger=False)
+    assert rc == 0 and "UNIKERN_INFO mode=streamed shards=4 shard_rows=1280" in out and "source=env" in out, out
+    for bad in ("mmap", "zerocopy"):
+        monkeypatch.setenv("UK_GEMM_STREAM_PATH", bad)
+        rc, out = abi.run_kml(small_vram_hcs(16), kml, None, write_ledger=False)
+        assert rc == 1 and "UNIKERN_ERROR what=stream_path_pin_unfit val=" + bad in out, out

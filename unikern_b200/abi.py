@@ -25,6 +25,8 @@ PROTOTYPES = {
     "uk_cuda_channelscale_f32": (i32, [vp, vp, vp, i64, i64, vp]),
     "uk_cuda_reduce_workspace_size": (sz, [i64, i64]),
     "uk_cuda_reduce_f32": (i32, [vp, vp, i64, i64, vp, sz, vp]),
+    "uk_cuda_reduce_workspace_size_width": (sz, [i64, i64, i64]),
+    "uk_cuda_reduce_f32_width": (i32, [vp, vp, i64, i64, i64, vp, sz, vp]),
     "uk_cuda_reduce_f32_noalloc": (i32, [vp, vp, i64, i64, vp]),
     "uk_cuda_rmsnorm_f32": (i32, [vp, vp, vp, i64, i64, f32, vp]),
     "uk_cuda_softmax_f32": (i32, [vp, vp, i64, i64, vp]),
@@ -116,6 +118,16 @@ def reduce(X, Y, workspace=None, stream=None):
     rows, cols = X.shape
     ws = workspace.numel() * workspace.element_size() if workspace is not None else 0
     check(lib().uk_cuda_reduce_f32(_p(X), _p(Y), rows, cols, _p(workspace), ws, _stream(stream)))
+
+
+def reduce_width(X, Y, width, stream=None):
+    """Row sums with the pass-1 width pinned (the UK_REDUCE_WIDTH knob);
+    allocates its workspace through torch."""
+    import torch
+    rows, cols = X.shape
+    n = lib().uk_cuda_reduce_workspace_size_width(rows, cols, width)
+    ws = torch.empty(max(1, n), dtype=torch.uint8, device="cuda") if n else None
+    check(lib().uk_cuda_reduce_f32_width(_p(X), _p(Y), rows, cols, width, _p(ws), n, _stream(stream)))
 
 
 def rmsnorm(X, W, Y, eps=1e-6, stream=None):

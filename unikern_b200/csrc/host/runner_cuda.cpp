@@ -20,6 +20,8 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <fstream>
 #include <iomanip>
 #include <limits>
@@ -121,6 +123,7 @@ struct OpCall {
   void* ws = nullptr;    // reduce / conv / tensor-core fp32 gemm workspace
   size_t ws_bytes = 0;
   bool tc32 = false;     // fp32 gemm on the tensor cores (split-tf32)
+  int64_t width = 0;     // reduce: pinned pass-1 width (UK_REDUCE_WIDTH), 0 = the plan
   int launch(cudaStream_t st) const {
     switch (op) {
       case OpKind::Gemm:
@@ -139,7 +142,8 @@ struct OpCall {
                                      (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML, ws,
                                      ws_bytes, st);
       case OpKind::Reduction:
-        return uk_cuda_reduce_f32((const float*)in0, (float*)out, 1, d[0], ws, ws_bytes, st);
+        return width > 0 ? uk_cuda_reduce_f32_width((const float*)in0, (float*)out, 1, d[0], width, ws, ws_bytes, st)
+                         : uk_cuda_reduce_f32((const float*)in0, (float*)out, 1, d[0], ws, ws_bytes, st);
       case OpKind::Softmax:
         return f16 ? uk_cuda_softmax_f16((const uint16_t*)in0, (uint16_t*)out, d[0], d[1], st)
                    : uk_cuda_softmax_f32((const float*)in0, (float*)out, d[0], d[1], st);
@@ -189,7 +193,9 @@ bool stage_operands(OpCall* c, DevArena* ar, cudaStream_t st, std::string* err) 
   c->in0 = ar->alloc(c->n_in0() * c->es(), "in0");
   if (c->n_in1() > 0) c->in1 = ar->alloc(c->n_in1() * c->es(), "in1");
   c->out = ar->alloc(c->n_out() * c->es(), "out");
-  if (c->op == OpKind::Reduction) c->ws_bytes = uk_cuda_reduce_workspace_size(1, c->d[0]);
+  if (c->op == OpKind::Reduction)
+    c->ws_bytes = c->width > 0 ? uk_cuda_reduce_workspace_size_width(1, c->d[0], c->width)
+                               : uk_cuda_reduce_workspace_size(1, c->d[0]);
   if (c->op == OpKind::Gemm && c->tc32)
     c->ws_bytes = uk_cuda_gemm_f32_workspace_size((int)c->d[0], (int)c->d[1], (int)c->d[2]);
   if (c->op == OpKind::Conv && !c->f16)
@@ -488,7 +494,50 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
   // an fp32 gemm large enough to gain from the tensor cores runs split-tf32
   timed.tc32 = tree.op == OpKind::Gemm && !timed.f16 &&
                uk_cuda_gemm_f32_prefers_tc(tree.dims[0], tree.dims[1], tree.dims[2]);
-  const size_t ws = tree.op == OpKind::Reduction ? uk_cuda_reduce_workspace_size(1, tree.dims[0])
+  // measurement knobs, requested through the environment and reported, never
+  // silently dropped (src/codegen_hip.cpp:874-908, :1338-1355)
+  if (tree.op == OpKind::Reduction) {
+    const int64_t n = tree.dims[0];
+    const char* pin = std::getenv("UK_REDUCE_WIDTH");
+    if (pin != nullptr && *pin != 0) {
+      char* end = nullptr;
+      const long long pw = std::strtoll(pin, &end, 10);
+      if (end == pin || *end != 0 || pw < 256 || pw > n) {
+        r.result_line = std::string("UNIKERN_ERROR what=reduce_width_pin_unfit value=") + pin +
+                        " needs an integer in [256, n=" + std::to_string(n) + "]; the plan is NOT silently fallen back";
+        log << r.result_line << "\n";
+        r.exit_code = 2;
+        return finish();
+      }
+      timed.width = pw;
+      log << "UNIKERN_INFO reduce_width source=env width=" << pw << " cap=0 n=" << n << "\n";
+    } else {
+      int out4[4] = {0, 0, 0, 0};
+      const int64_t dims[6] = {n, 0, 0, 0, 0, 0};
+      const int sms = hcs.compute_units > 0 ? hcs.compute_units : 148;
+      uk_cuda_tile_plan(UK_OP_REDUCE, 0, dims, 0, out4);
+      log << "UNIKERN_INFO reduce_width source=plan width=" << out4[3] << " cap=" << 8 * sms << " n=" << n << "\n";
+    }
+  }
+  std::string stream_path_src = "plan";
+  if (tree.op == OpKind::Gemm) {
+    const char* pin = std::getenv("UK_GEMM_STREAM_PATH");
+    if (pin != nullptr && *pin != 0 && std::strcmp(pin, "auto") != 0) {
+      if (std::strcmp(pin, "pinned") != 0) {
+        r.result_line = std::string("UNIKERN_ERROR what=stream_path_pin_unfit val=") + pin +
+                        (std::strcmp(pin, "mmap") == 0
+                             ? " (nvidia:cuda streams through page-locked copies only; the emulated mmap arm is not built)"
+                             : "");
+        log << r.result_line << "\n";
+        r.exit_code = 2;
+        return finish();
+      }
+      stream_path_src = "env";
+    }
+  }
+  const size_t ws = tree.op == OpKind::Reduction
+                        ? (timed.width > 0 ? uk_cuda_reduce_workspace_size_width(1, tree.dims[0], timed.width)
+                                           : uk_cuda_reduce_workspace_size(1, tree.dims[0]))
                     : tree.op == OpKind::Conv && tree.dtype == DType::F32
                         ? uk_cuda_conv2d_workspace_size(1, tree.dims[0], tree.dims[1], tree.dims[2], tree.dims[3],
                                                         tree.dims[4], tree.dims[5], 0, UK_CONV_KML)
@@ -632,6 +681,9 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
 
   // ---- 2a. scenario B: the GEMM streamed through a ring (B resident) ----
   if (ok && stream_rows > 0) {
+    log << "UNIKERN_INFO mode=streamed shards=" << (tree.dims[0] + stream_rows - 1) / stream_rows
+        << " shard_rows=" << stream_rows << " prefetch_d=2 stream_path=pinned source=" << stream_path_src
+        << " plan=pinned kernel=" << (stream_kind == 1 ? "f16" : stream_tc ? "split-tf32" : "ffma") << "\n";
     const int64_t M = tree.dims[0], N = tree.dims[1], K = tree.dims[2];
     const size_t es = timed.es();
     const size_t ring_bytes = uk_cuda_gemm_streamed_ring_size((int)M, (int)N, (int)K, stream_kind, (int)stream_rows);
@@ -933,13 +985,14 @@ int run_kml(const std::string& hcs_json, const std::string& kml_json, const std:
         << " vram_total=" << r.vram_total << " committed=no\n";
     if (write_ledger && !ledger_path.empty())
       ledger.record_violation(key, rate, 0.0, r.migrations, r.checks, r.vram_free);
-    // a re-solve would need a streamed plan, which this backend refuses
-    out << "RESOLVE STOP: nvidia:cuda is resident-only; violation recorded, nothing committed.\n";
+    // cudaMalloc memory does not migrate on this device, so a violation means
+    // something outside the plan's control: record it and stop
+    out << "RESOLVE STOP: nvidia:cuda allocates device memory only; violation recorded, nothing committed.\n";
     return done(5);
   }
   if (!r.built || !r.ran || !r.verified) {
     out << "RUN FAILED; solution NOT committed to ledger\n";
-    return done(r.exit_code == 2 ? 2 : 1);
+    return done(1);
   }
   if (!write_ledger || ledger_path.empty()) {
     out << "VERIFY PASS (no ledger write)\n";

@@ -457,6 +457,42 @@ int uk_cuda_reduce_f32(const float* X, float* Y, int64_t rows, int64_t cols, voi
   return uk::check_launch("reduce");
 }
 
+size_t uk_cuda_reduce_workspace_size_width(int64_t rows, int64_t cols, int64_t width) {
+  if (rows <= 0 || cols <= 0 || width <= 0) return 0;
+  const int64_t chunk = (cols + width - 1) / width, parts = (cols + chunk - 1) / chunk;
+  return (size_t)(rows * parts) * sizeof(float);
+}
+
+int uk_cuda_reduce_f32_width(const float* X, float* Y, int64_t rows, int64_t cols, int64_t width, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (int rc = check_rows(rows, cols, "reduce")) return rc;
+  if (width < 1) return uk::fail(UK_EINVAL, "reduce: width must be >= 1 (got %lld)", (long long)width);
+  if (rows == 0) return UK_OK;
+  if (int rc = uk::check_device_ptr(Y, "Y")) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cols == 0) {
+    k_fill_zero<<<(unsigned)((rows + 255) / 256 < 4096 ? (rows + 255) / 256 : 4096), 256, 0, st>>>(Y, rows);
+    return uk::check_launch("reduce(zero)");
+  }
+  if (int rc = uk::check_device_ptr(X, "X")) return rc;
+  if (rows > 65535) return uk::fail(UK_EINVAL, "reduce: a pinned width takes at most 65535 rows");
+  const int64_t chunk = (cols + width - 1) / width, parts = (cols + chunk - 1) / chunk;
+  if (parts > 2147483647LL) return uk::fail(UK_EINVAL, "reduce: width too large");
+  const size_t need = (size_t)(rows * parts) * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need)
+    return uk::fail(UK_EINVAL, "reduce: needs a %zu-byte workspace (uk_cuda_reduce_workspace_size_width), got %zu",
+                    need, workspace ? workspace_bytes : (size_t)0);
+  if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
+  float* P = (float*)workspace;
+  // 16-byte loads when every chunk starts on a 16-byte boundary
+  const bool vec = cols % 4 == 0 && chunk % 4 == 0 && uk::aligned16(X);
+  dim3 g1((unsigned)parts, (unsigned)rows);
+  if (vec) k_rowsum_split<4><<<g1, 256, 0, st>>>(X, P, cols, parts, chunk);
+  else k_rowsum_split<1><<<g1, 256, 0, st>>>(X, P, cols, parts, chunk);
+  k_rowsum_fold<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, parts);
+  return uk::check_launch("reduce(width)");
+}
+
 int uk_cuda_rmsnorm_f32(const float* X, const float* W, float* Y, int64_t L, int64_t C, float eps, void* stream) {
   if (int rc = check_rows(L, C, "rmsnorm")) return rc;
   if (L == 0 || C == 0) return UK_OK;
