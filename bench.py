@@ -606,6 +606,10 @@ def bench_rowop_f16(ctx, op, steps, warmup, L=8192, C=16384):
     elif op == "rmsnorm":
         step = lambda: abi.rmsnorm_f16(X, W, Y, 1e-5)  # noqa: E731
         nbytes = 2 * L * C * 2 + C * 2
+    elif op == "reduce":
+        Yr = torch.empty((L,), dtype=torch.float16, device="cuda")
+        step = lambda: abi.reduce_f16(X, Yr)  # noqa: E731
+        nbytes = L * C * 2 + L * 2
     else:
         step = lambda: abi.channelscale_f16(X, W, Y)  # noqa: E731
         nbytes = 2 * L * C * 2 + C * 2
@@ -776,7 +780,7 @@ def run_single(args, ctx, pk):
     elif op == "conv":
         r = bench_conv(ctx, args.steps, args.warmup)
         val, unit, bound = r["value"], "TFLOP/s", "tensor_3xtf32"
-    elif op in ("softmax_f16", "rmsnorm_f16", "channelscale_f16"):
+    elif op in ("softmax_f16", "rmsnorm_f16", "channelscale_f16", "reduce_f16"):
         r = bench_rowop_f16(ctx, op[:-4], args.steps, args.warmup)
         val, unit, bound = r["value"], "GB/s", "hbm"
     elif op == "conv_f16":
@@ -823,7 +827,7 @@ def main():
     ap.add_argument("--op", default="all",
                     choices=["all", "gemm_f16", "reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar",
                              "conv", "gemm_f32", "decode", "softmax_f16", "rmsnorm_f16", "channelscale_f16",
-                             "conv_f16", "gemm_streamed", "gemm_streamed_f16", "gemm_f32_tc"],
+                             "conv_f16", "gemm_streamed", "gemm_streamed_f16", "gemm_f32_tc", "reduce_f16"],
                     help="all = headline f16 GEMM + every other op; otherwise one op alone (profiling)")
     ap.add_argument("--gemm-shape", default="8192,8192,8192", help="M,N,K of the f16 GEMM")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
@@ -875,7 +879,7 @@ def main():
         ops["decode_chain_b32"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
                                    "roofline": roofline("hbm", r["value"], pk)}
         # fp16 variants (beyond the reference's dtype interval)
-        for op in ("softmax", "rmsnorm", "channelscale"):
+        for op in ("softmax", "rmsnorm", "channelscale", "reduce"):
             r = bench_rowop_f16(Ctx(1, 0, local_rank), op, s, 3)
             ops[op + "_f16"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
                                 "roofline": roofline("hbm", r["value"], pk)}

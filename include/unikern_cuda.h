@@ -90,6 +90,15 @@ size_t uk_cuda_reduce_workspace_size_width(int64_t rows, int64_t cols, int64_t w
 int uk_cuda_reduce_f32_width(const float* X, float* Y, int64_t rows, int64_t cols, int64_t width,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/* Row sums of binary16 rows (fp32 accumulation, one rounding into the
+ * binary16 result Y[rows]); the same plans, workspace sizes and determinism
+ * as the fp32 reduce.  The reference refuses fp16 for reduce
+ * (src/codegen_hip.cpp:81-89); this widens the dtype interval. */
+int uk_cuda_reduce_f16(const uint16_t* X, uint16_t* Y, int64_t rows, int64_t cols, void* workspace,
+                       size_t workspace_bytes, void* stream);
+int uk_cuda_reduce_f16_width(const uint16_t* X, uint16_t* Y, int64_t rows, int64_t cols, int64_t width,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* Reduce without a workspace: the same result as uk_cuda_reduce_f32 (same
  * kernels, same plan), for callers that cannot allocate device memory -- a
  * plugin inside a host application that owns every device allocation through

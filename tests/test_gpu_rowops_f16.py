@@ -1,4 +1,4 @@
-"""fp16 softmax / RMSNorm / channelscale (f16 rows, fp32 arithmetic) against
+"""fp16 softmax / RMSNorm / channelscale / reduce (f16 rows, fp32 arithmetic) against
 the fp64 oracle on the same half inputs (oracle/uk_oracle.c restates the
 reference's cpu_softmax / cpu_rmsnorm / cpu_channelscale,
 src/codegen_hip.cpp:1999-2009, :2168-2178, :2339-2344).
@@ -65,3 +65,26 @@ def test_f16_row_ops_deterministic():
     abi.softmax_f16(Xh, Y1)
     abi.softmax_f16(Xh, Y2)
     assert np.array_equal(host(Y1), host(Y2))
+
+
+@pytest.mark.parametrize("rows,cols,width", [(8192, 16384, 0), (1, 1 << 24, 0), (3, 1000003, 0), (17, 7, 0),
+                                             (4096, 300, 0), (2, 1 << 20, 4096), (1, 999999, 1000)])
+def test_reduce_f16(rows, cols, width):
+    # the widening of reduce: fp32 sums of the half inputs, one rounding
+    rng = np.random.default_rng(rows + cols + width)
+    Xh = half(rng.normal(0, 1, (rows, cols)))
+    Y = empty((rows,), "f16")
+    abi.reduce_f16(dev(Xh), Y, width)
+    ref = O.f16_to_f32(Xh).astype(np.float64).sum(axis=1)
+    got = O.f16_to_f32(host(Y)).astype(np.float64)
+    # one binary16 rounding of a sum accurate to fp32 (floor: the sum's scale)
+    tau = max(np.sqrt(cols), 1.0)
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), tau)) <= F16_OUT_TOL
+
+
+def test_reduce_f16_exact_instance():
+    # the KML verify instance: 2^20 x 2^-6 = 16384, exact in binary16
+    Xh = half(np.full((1, 1 << 20), 0.015625))
+    Y = empty((1,), "f16")
+    abi.reduce_f16(dev(Xh), Y)
+    assert O.f16_to_f32(host(Y))[0] == 16384.0

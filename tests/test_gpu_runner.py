@@ -37,6 +37,7 @@ CASES = [
     ('{"op":"rmsnorm","dtype":"fp16","dims":[4096,1000]}', 2 ** -10),
     ('{"op":"channelscale","dtype":"fp16","dims":[65536,256]}', 0.0),
     ('{"op":"conv","dtype":"fp16","dims":[58,58,256,3,3,256]}', 2 ** -10),
+    ('{"op":"reduce","dtype":"fp16","dims":[1048576]}', 0.0),          # 16384 is exact in binary16
 ]
 
 

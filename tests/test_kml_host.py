@@ -93,7 +93,7 @@ def test_placement_resident_streamed_or_refused(kml, mib, want):
 
 
 @pytest.mark.parametrize("kml,gap", [
-    ('{"op":"reduce","dtype":"fp16","dims":[4]}', "dtype=fp16 for op=reduce"),
+    ('{"op":"reduce","dtype":"int8","dims":[4]}', "dtype=int8 for op=reduce"),
     ('{"op":"conv","dtype":"fp16","dims":[32,32,8,3,3,16]}', "needs C a multiple of 64"),
     ('{"op":"gemm","dtype":"int8","dims":[4,4,4]}', "dtype=int8"),
     ('{"op":"gemm","dtype":"fp32","dims":[4,4,4],"children":[{"op":"reduce","dtype":"fp32","dims":[8]}]}',
@@ -164,8 +164,8 @@ def test_bad_inputs_return_2():
     assert rc == 2 and out.startswith("HCS missing required fields:")
     rc, out = abi.run_kml(B200_HCS, '{"op":"gemm","dtype":"fp32","dims":[4,4]}')
     assert rc == 2 and "rejected (1 violations)" in out
-    rc, out = abi.run_kml(B200_HCS, '{"op":"reduce","dtype":"fp16","dims":[4]}')
-    assert rc == 2 and out.startswith("UNSUPPORTED: dtype=fp16")
+    rc, out = abi.run_kml(B200_HCS, '{"op":"conv","dtype":"fp16","dims":[32,32,8,3,3,16]}')
+    assert rc == 2 and out.startswith("UNSUPPORTED: dtype=fp16 conv")
 
 
 @pytest.mark.parametrize("kml", ['{"op":"softmax","dtype":"fp16","dims":[4,4]}',

@@ -27,6 +27,8 @@ PROTOTYPES = {
     "uk_cuda_reduce_f32": (i32, [vp, vp, i64, i64, vp, sz, vp]),
     "uk_cuda_reduce_workspace_size_width": (sz, [i64, i64, i64]),
     "uk_cuda_reduce_f32_width": (i32, [vp, vp, i64, i64, i64, vp, sz, vp]),
+    "uk_cuda_reduce_f16": (i32, [vp, vp, i64, i64, vp, sz, vp]),
+    "uk_cuda_reduce_f16_width": (i32, [vp, vp, i64, i64, i64, vp, sz, vp]),
     "uk_cuda_reduce_f32_noalloc": (i32, [vp, vp, i64, i64, vp]),
     "uk_cuda_rmsnorm_f32": (i32, [vp, vp, vp, i64, i64, f32, vp]),
     "uk_cuda_softmax_f32": (i32, [vp, vp, i64, i64, vp]),
@@ -128,6 +130,20 @@ def reduce_width(X, Y, width, stream=None):
     n = lib().uk_cuda_reduce_workspace_size_width(rows, cols, width)
     ws = torch.empty(max(1, n), dtype=torch.uint8, device="cuda") if n else None
     check(lib().uk_cuda_reduce_f32_width(_p(X), _p(Y), rows, cols, width, _p(ws), n, _stream(stream)))
+
+
+def reduce_f16(X, Y, width=0, stream=None):
+    """Row sums of binary16 rows into binary16 Y (fp32 accumulation);
+    width > 0 pins the pass-1 width.  Allocates its workspace through torch."""
+    import torch
+    rows, cols = X.shape
+    n = (lib().uk_cuda_reduce_workspace_size_width(rows, cols, width) if width
+         else lib().uk_cuda_reduce_workspace_size(rows, cols))
+    ws = torch.empty(max(1, n), dtype=torch.uint8, device="cuda") if n else None
+    if width:
+        check(lib().uk_cuda_reduce_f16_width(_p(X), _p(Y), rows, cols, width, _p(ws), n, _stream(stream)))
+    else:
+        check(lib().uk_cuda_reduce_f16(_p(X), _p(Y), rows, cols, _p(ws), n, _stream(stream)))
 
 
 def rmsnorm(X, W, Y, eps=1e-6, stream=None):

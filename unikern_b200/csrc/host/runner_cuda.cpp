@@ -66,7 +66,7 @@ int64_t payload_bytes(const KmlTree& t, size_t op_ws) {  // op_ws: the reduce / 
     case OpKind::Conv:
       return (d[0] * d[1] * d[2] + d[5] * d[3] * d[4] * d[2] + d[5] * (d[0] - d[3] + 1) * (d[1] - d[4] + 1)) * es +
              (int64_t)op_ws;
-    case OpKind::Reduction: return d[0] * 4 + (int64_t)op_ws + 4;
+    case OpKind::Reduction: return d[0] * es + (int64_t)op_ws + es;
     case OpKind::Softmax: return 2 * d[0] * d[1] * es;
     case OpKind::RmsNorm:
     case OpKind::ChannelScale: return (2 * d[0] * d[1] + d[1]) * es;
@@ -142,6 +142,10 @@ struct OpCall {
                                      (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML, ws,
                                      ws_bytes, st);
       case OpKind::Reduction:
+        if (f16)  // widening: binary16 in and out, fp32 sums
+          return width > 0 ? uk_cuda_reduce_f16_width((const uint16_t*)in0, (uint16_t*)out, 1, d[0], width, ws,
+                                                      ws_bytes, st)
+                           : uk_cuda_reduce_f16((const uint16_t*)in0, (uint16_t*)out, 1, d[0], ws, ws_bytes, st);
         return width > 0 ? uk_cuda_reduce_f32_width((const float*)in0, (float*)out, 1, d[0], width, ws, ws_bytes, st)
                          : uk_cuda_reduce_f32((const float*)in0, (float*)out, 1, d[0], ws, ws_bytes, st);
       case OpKind::Softmax:
@@ -238,8 +242,6 @@ bool BackendNvidia::available() const {
 std::string BackendNvidia::capability_gap(const KmlTree& t) const {
   if (t.layout != "NT") return "layout=" + t.layout + " (only NT is implemented)";
   if (t.dtype == DType::I8) return std::string("dtype=int8 for op=") + op_name(t.op) + " (nvidia:cuda runs fp32 ops and the fp16 gemm)";
-  if (t.dtype == DType::F16 && t.op == OpKind::Reduction)
-    return "dtype=fp16 for op=reduce (nvidia:cuda runs fp16 gemm, conv, softmax, rmsnorm and channelscale)";
   if (t.dtype == DType::F16 && t.op == OpKind::Conv && t.dims[2] % 64 != 0)
     return "dtype=fp16 conv with C=" + std::to_string(t.dims[2]) + " (the fp16 conv needs C a multiple of 64)";
   if (!t.children.empty()) return "children (a composite tree executes per op; declare each op on its own)";
@@ -649,7 +651,7 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
                               (int)v.d[4], (int)v.d[5], v.f16, worst, st);
           break;
         case OpKind::Reduction:
-          rc = ukr_check_rows(UKR_OP_REDUCE, v.in0, nullptr, v.out, 1, v.d[0], 0.0, 0, worst, st);
+          rc = ukr_check_rows(UKR_OP_REDUCE, v.in0, nullptr, v.out, 1, v.d[0], 0.0, v.f16, worst, st);
           break;
         case OpKind::Softmax:
           rc = ukr_check_rows(UKR_OP_SOFTMAX, v.in0, nullptr, v.out, v.d[0], v.d[1], 0.0, v.f16, worst, st);

@@ -10,6 +10,8 @@
 //   * reductions are warp shuffles + a fixed-order cross-warp step, so the
 //     result bits are the same on every call (deterministic);
 //   * grids are sized from the SM count (148 on B200), not from a label.
+#include <cuda_fp16.h>
+
 #include <cmath>
 #include <mutex>
 
@@ -60,10 +62,35 @@ __global__ void __launch_bounds__(256) k_channelscale(const float* __restrict__ 
 // ---------------------------------------------------------------------------
 // reduce
 // ---------------------------------------------------------------------------
-// U loads of W floats in flight per thread; U partial sums combined in a
-// fixed order, so the result does not depend on timing
-template <int W, int U = 4>
-__device__ __forceinline__ float sum_span(const float* __restrict__ x, int64_t nv, int tid, int nthr) {
+// W consecutive elements as fp32: floats (W = 1 or 4) or binary16 (W = 1 or
+// 8, one 16-byte load), streaming cache hint
+template <int W>
+__device__ __forceinline__ void ld_span(float (&d)[W], const float* p) {
+  uk_ld_cs<W>(d, p);
+}
+template <int W>
+__device__ __forceinline__ void ld_span(float (&d)[W], const __half* p) {
+  if constexpr (W == 8) {
+    const uint4 t = __ldcs(reinterpret_cast<const uint4*>(p));
+    const uint32_t q[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[i]));
+      d[2 * i] = f.x;
+      d[2 * i + 1] = f.y;
+    }
+  } else {
+    static_assert(W == 1, "binary16 spans are 1 or 8 wide");
+    d[0] = __half2float(__ldcs(p));
+  }
+}
+__device__ __forceinline__ void st_sum(float* y, float v) { *y = v; }
+__device__ __forceinline__ void st_sum(__half* y, float v) { *y = __float2half_rn(v); }
+
+// U loads of W elements in flight per thread, summed in fp32; U partial sums
+// combined in a fixed order, so the result does not depend on timing
+template <int W, int U = 4, class T = float>
+__device__ __forceinline__ float sum_span(const T* __restrict__ x, int64_t nv, int tid, int nthr) {
   float acc[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) acc[u] = 0.f;
@@ -71,7 +98,7 @@ __device__ __forceinline__ float sum_span(const float* __restrict__ x, int64_t n
   for (; v + (U - 1) * (int64_t)nthr < nv; v += U * (int64_t)nthr) {
     float d[U][W];
 #pragma unroll
-    for (int u = 0; u < U; ++u) uk_ld_cs<W>(d[u], x + (v + u * (int64_t)nthr) * W);
+    for (int u = 0; u < U; ++u) ld_span<W>(d[u], x + (v + u * (int64_t)nthr) * W);
 #pragma unroll
     for (int u = 0; u < U; ++u)
 #pragma unroll
@@ -79,7 +106,7 @@ __device__ __forceinline__ float sum_span(const float* __restrict__ x, int64_t n
   }
   for (; v < nv; v += nthr) {
     float d[W];
-    uk_ld_cs<W>(d, x + v * W);
+    ld_span<W>(d, x + v * W);
 #pragma unroll
     for (int w = 0; w < W; ++w) acc[0] += d[w];
   }
@@ -91,56 +118,61 @@ __device__ __forceinline__ float sum_span(const float* __restrict__ x, int64_t n
 }
 
 // one 256-thread CTA per row
-template <int W>
-__global__ void __launch_bounds__(256) k_rowsum_cta(const float* __restrict__ X, float* __restrict__ Y,
-                                                    int64_t cols) {
+template <int W, class T = float, class O = float>
+__global__ void __launch_bounds__(256) k_rowsum_cta(const T* __restrict__ X, O* __restrict__ Y, int64_t cols) {
   __shared__ float red[33];
-  const float* x = X + (int64_t)blockIdx.x * cols;
-  float t = sum_span<W>(x, cols / W, threadIdx.x, 256);
+  const T* x = X + (int64_t)blockIdx.x * cols;
+  float t = sum_span<W, 4, T>(x, cols / W, threadIdx.x, 256);
   t = uk_block_sum<256>(t, red);
-  if (threadIdx.x == 0) Y[blockIdx.x] = t;
+  if (threadIdx.x == 0) st_sum(Y + blockIdx.x, t);
 }
 
 // one warp per row (short rows), 8 rows per CTA
-template <int W>
-__global__ void __launch_bounds__(256) k_rowsum_warp(const float* __restrict__ X, float* __restrict__ Y,
-                                                     int64_t rows, int64_t cols) {
+template <int W, class T = float, class O = float>
+__global__ void __launch_bounds__(256) k_rowsum_warp(const T* __restrict__ X, O* __restrict__ Y, int64_t rows,
+                                                     int64_t cols) {
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
-  float t = sum_span<W>(X + row * cols, cols / W, threadIdx.x & 31, 32);
+  float t = sum_span<W, 4, T>(X + row * cols, cols / W, threadIdx.x & 31, 32);
   t = uk_warp_sum(t);
-  if ((threadIdx.x & 31) == 0) Y[row] = t;
+  if ((threadIdx.x & 31) == 0) st_sum(Y + row, t);
 }
 
 // split rows: CTA (s, r) sums chunk s of row r into P[r * splits + s]
-template <int W>
-__global__ void __launch_bounds__(256) k_rowsum_split(const float* __restrict__ X, float* __restrict__ P,
-                                                      int64_t cols, int64_t splits, int64_t chunk) {
+template <int W, class T = float>
+__global__ void __launch_bounds__(256) k_rowsum_split(const T* __restrict__ X, float* __restrict__ P, int64_t cols,
+                                                      int64_t splits, int64_t chunk) {
   __shared__ float red[33];
   const int64_t r = blockIdx.y, s = blockIdx.x;
   const int64_t c0 = s * chunk;
   const int64_t c1 = c0 + chunk < cols ? c0 + chunk : cols;
   float t = 0.f;
-  if (c0 < c1) t = sum_span<W>(X + r * cols + c0, (c1 - c0) / W, threadIdx.x, 256);
+  if (c0 < c1) t = sum_span<W, 4, T>(X + r * cols + c0, (c1 - c0) / W, threadIdx.x, 256);
   t = uk_block_sum<256>(t, red);
   if (threadIdx.x == 0) P[r * splits + s] = t;
 }
 
 // fold the partials of each row in a fixed order (one warp per row)
-__global__ void __launch_bounds__(256) k_rowsum_fold(const float* __restrict__ P, float* __restrict__ Y,
-                                                     int64_t rows, int64_t splits) {
+template <class O = float>
+__global__ void __launch_bounds__(256) k_rowsum_fold(const float* __restrict__ P, O* __restrict__ Y, int64_t rows,
+                                                     int64_t splits) {
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;
   float t = 0.f;
   for (int64_t i = lane; i < splits; i += 32) t += P[row * splits + i];
   t = uk_warp_sum(t);
-  if (lane == 0) Y[row] = t;
+  if (lane == 0) st_sum(Y + row, t);
 }
 
 __global__ void k_fill_zero(float* __restrict__ Y, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     Y[i] = 0.f;
+}
+
+__global__ void k_fill_zero_h(__half* __restrict__ Y, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    Y[i] = __float2half_rn(0.f);
 }
 
 // ---------------------------------------------------------------------------
@@ -377,6 +409,50 @@ int check_rows(int64_t L, int64_t C, const char* op) {
   return UK_OK;
 }
 
+// binary16 rows summed in fp32, one rounding into the binary16 result; the
+// f32 reduce's plan (width 0) or a pinned pass-1 width
+int reduce_h(const uint16_t* Xv, uint16_t* Yv, int64_t rows, int64_t cols, int64_t width, void* workspace,
+             size_t workspace_bytes, cudaStream_t st) {
+  if (int rc = check_rows(rows, cols, "reduce_f16")) return rc;
+  if (rows == 0) return UK_OK;
+  if (int rc = uk::check_device_ptr(Yv, "Y")) return rc;
+  const __half* X = (const __half*)Xv;
+  __half* Y = (__half*)Yv;
+  if (cols == 0) {
+    k_fill_zero_h<<<(unsigned)((rows + 255) / 256 < 4096 ? (rows + 255) / 256 : 4096), 256, 0, st>>>(Y, rows);
+    return uk::check_launch("reduce_f16(zero)");
+  }
+  if (int rc = uk::check_device_ptr(X, "X")) return rc;
+  ReducePlan p = plan_reduce(rows, cols);
+  if (width > 0) {
+    const int64_t chunk = (cols + width - 1) / width;
+    p = {3, (cols + chunk - 1) / chunk, chunk};
+  }
+  const bool vec = cols % 8 == 0 && uk::aligned16(X) && (p.mode != 3 || p.chunk % 8 == 0);
+  if (p.mode == 1) {
+    if (vec) k_rowsum_cta<8, __half, __half><<<(unsigned)rows, 256, 0, st>>>(X, Y, cols);
+    else k_rowsum_cta<1, __half, __half><<<(unsigned)rows, 256, 0, st>>>(X, Y, cols);
+  } else if (p.mode == 2) {
+    const unsigned g = (unsigned)((rows + 7) / 8);
+    if (vec) k_rowsum_warp<8, __half, __half><<<g, 256, 0, st>>>(X, Y, rows, cols);
+    else k_rowsum_warp<1, __half, __half><<<g, 256, 0, st>>>(X, Y, rows, cols);
+  } else {
+    if (rows > 65535) return uk::fail(UK_EINVAL, "reduce_f16: a split plan takes at most 65535 rows");
+    if (p.splits > 2147483647LL) return uk::fail(UK_EINVAL, "reduce_f16: width too large");
+    const size_t need = (size_t)(rows * p.splits) * sizeof(float);
+    if (workspace == nullptr || workspace_bytes < need)
+      return uk::fail(UK_EINVAL, "reduce_f16: needs a %zu-byte workspace (uk_cuda_reduce_workspace_size%s), got %zu",
+                      need, width > 0 ? "_width" : "", workspace ? workspace_bytes : (size_t)0);
+    if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
+    float* P = (float*)workspace;
+    const dim3 g1((unsigned)p.splits, (unsigned)rows);
+    if (vec) k_rowsum_split<8, __half><<<g1, 256, 0, st>>>(X, P, cols, p.splits, p.chunk);
+    else k_rowsum_split<1, __half><<<g1, 256, 0, st>>>(X, P, cols, p.splits, p.chunk);
+    k_rowsum_fold<__half><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, p.splits);
+  }
+  return uk::check_launch("reduce_f16");
+}
+
 }  // namespace
 
 extern "C" {
@@ -452,7 +528,7 @@ int uk_cuda_reduce_f32(const float* X, float* Y, int64_t rows, int64_t cols, voi
     if (rows > 65535) return uk::fail(UK_EINVAL, "reduce: internal split plan with rows > 65535");
     if (vec) k_rowsum_split<4><<<g1, 256, 0, st>>>(X, P, cols, p.splits, p.chunk);
     else k_rowsum_split<1><<<g1, 256, 0, st>>>(X, P, cols, p.splits, p.chunk);
-    k_rowsum_fold<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, p.splits);
+    k_rowsum_fold<float><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, p.splits);
   }
   return uk::check_launch("reduce");
 }
@@ -489,8 +565,19 @@ int uk_cuda_reduce_f32_width(const float* X, float* Y, int64_t rows, int64_t col
   dim3 g1((unsigned)parts, (unsigned)rows);
   if (vec) k_rowsum_split<4><<<g1, 256, 0, st>>>(X, P, cols, parts, chunk);
   else k_rowsum_split<1><<<g1, 256, 0, st>>>(X, P, cols, parts, chunk);
-  k_rowsum_fold<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, parts);
+  k_rowsum_fold<float><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, parts);
   return uk::check_launch("reduce(width)");
+}
+
+int uk_cuda_reduce_f16(const uint16_t* X, uint16_t* Y, int64_t rows, int64_t cols, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return reduce_h(X, Y, rows, cols, 0, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int uk_cuda_reduce_f16_width(const uint16_t* X, uint16_t* Y, int64_t rows, int64_t cols, int64_t width,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (width < 1) return uk::fail(UK_EINVAL, "reduce_f16: width must be >= 1 (got %lld)", (long long)width);
+  return reduce_h(X, Y, rows, cols, width, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 int uk_cuda_rmsnorm_f32(const float* X, const float* W, float* Y, int64_t L, int64_t C, float eps, void* stream) {
@@ -555,7 +642,7 @@ int uk_cuda_reduce_f32_noalloc(const float* X, float* Y, int64_t rows, int64_t c
     dim3 g1((unsigned)p.splits, (unsigned)rows);
     if (vec) k_rowsum_split<4><<<g1, 256, 0, st>>>(X, P, cols, p.splits, p.chunk);
     else k_rowsum_split<1><<<g1, 256, 0, st>>>(X, P, cols, p.splits, p.chunk);
-    k_rowsum_fold<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, p.splits);
+    k_rowsum_fold<float><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(P, Y, rows, p.splits);
   }
   return uk::check_launch("reduce_noalloc");
 }
