@@ -53,67 +53,154 @@ __device__ __forceinline__ void st_h(__half* p, const float (&d)[W]) {
   }
 }
 
+// 8 halves of a 16-byte vector as fp32
+__device__ __forceinline__ void unpack8(float (&d)[8], const uint4& t) {
+  const uint32_t q[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[i]));
+    d[2 * i] = f.x;
+    d[2 * i + 1] = f.y;
+  }
+}
+
+// The row stays in registers as packed halves (one uint4 per 8 columns, half
+// the registers of fp32 copies), so four 512-thread CTAs fit on an SM and
+// twice the bytes are in flight; values are unpacked to fp32 where used.
+// Softmax takes exp(x - max) twice (for the sum, then for the output) rather
+// than keep fp32 copies.
+// CTAs per SM asked of the register allocator: a full SM (2048 threads) for
+// short rows, three quarters for four vectors per thread
+template <int THREADS, int VPT, int W>
+constexpr int rowop_h_min_blocks() {
+  return W != 8 ? 1 : VPT <= 2 ? 2048 / THREADS : VPT <= 4 ? (1536 / THREADS > 0 ? 1536 / THREADS : 1) : 1;
+}
+
 template <int OP, int THREADS, int VPT, int W>
-__global__ void __launch_bounds__(THREADS) k_rowop_h(const __half* __restrict__ X, const __half* __restrict__ G,
-                                                     __half* __restrict__ Y, int64_t C, float eps) {
+__global__ void __launch_bounds__(THREADS, (rowop_h_min_blocks<THREADS, VPT, W>()))
+    k_rowop_h(const __half* __restrict__ X, const __half* __restrict__ G, __half* __restrict__ Y, int64_t C,
+              float eps) {
   __shared__ float red[33];
   const int64_t row = blockIdx.x;
   const __half* x = X + row * C;
   __half* y = Y + row * C;
   const int64_t nv = C / W;
-  float v[VPT][W];
+  if constexpr (W == 8) {
+    uint4 raw[VPT];
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int64_t j = threadIdx.x + (int64_t)k * THREADS;
-    if (j < nv) {
-      ld_h<W>(v[k], x + j * W, true);
-    } else {
-#pragma unroll
-      for (int w = 0; w < W; ++w) v[k][w] = OP == kOpSoftmax ? -INFINITY : 0.f;
+    for (int k = 0; k < VPT; ++k) {
+      const int64_t j = threadIdx.x + (int64_t)k * THREADS;
+      // -inf halves (0xFC00) pad softmax rows; zeros pad the others
+      raw[k] = j < nv ? __ldcs(reinterpret_cast<const uint4*>(x + j * 8))
+                      : (OP == kOpSoftmax ? make_uint4(0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u, 0xFC00FC00u)
+                                          : make_uint4(0u, 0u, 0u, 0u));
     }
-  }
-  float scale = 1.f;
-  if constexpr (OP == kOpRms) {
-    float ss = 0.f;
+    float scale = 1.f, m = 0.f;
+    if constexpr (OP == kOpRms) {
+      float ss = 0.f;
 #pragma unroll
-    for (int k = 0; k < VPT; ++k)
+      for (int k = 0; k < VPT; ++k) {
+        float d[8];
+        unpack8(d, raw[k]);
 #pragma unroll
-      for (int w = 0; w < W; ++w) ss += v[k][w] * v[k][w];
-    ss = uk_block_sum<THREADS>(ss, red);
-    scale = 1.0f / sqrtf(ss / (float)C + eps);
-  } else if constexpr (OP == kOpSoftmax) {
-    float m = -INFINITY;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k)
-#pragma unroll
-      for (int w = 0; w < W; ++w) m = fmaxf(m, v[k][w]);
-    m = uk_block_max<THREADS>(m, red);
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k)
-#pragma unroll
-      for (int w = 0; w < W; ++w) {
-        const float e = __expf(v[k][w] - m);
-        v[k][w] = e;
-        s += e;
+        for (int w = 0; w < 8; ++w) ss += d[w] * d[w];
       }
-    s = uk_block_sum<THREADS>(s, red);
-    scale = 1.0f / s;
-  }
+      ss = uk_block_sum<THREADS>(ss, red);
+      scale = 1.0f / sqrtf(ss / (float)C + eps);
+    } else if constexpr (OP == kOpSoftmax) {
+      m = -INFINITY;
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int64_t j = threadIdx.x + (int64_t)k * THREADS;
-    if (j < nv) {
-      if constexpr (OP == kOpSoftmax) {
+      for (int k = 0; k < VPT; ++k) {
+        float d[8];
+        unpack8(d, raw[k]);
 #pragma unroll
-        for (int w = 0; w < W; ++w) v[k][w] = v[k][w] * scale;
+        for (int w = 0; w < 8; ++w) m = fmaxf(m, d[w]);
+      }
+      m = uk_block_max<THREADS>(m, red);
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        float d[8];
+        unpack8(d, raw[k]);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sum += __expf(d[w] - m);
+      }
+      sum = uk_block_sum<THREADS>(sum, red);
+      scale = 1.0f / sum;
+    }
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int64_t j = threadIdx.x + (int64_t)k * THREADS;
+      if (j < nv) {
+        float d[8];
+        unpack8(d, raw[k]);
+        if constexpr (OP == kOpSoftmax) {
+#pragma unroll
+          for (int w = 0; w < 8; ++w) d[w] = __expf(d[w] - m) * scale;
+        } else {
+          float g[8];
+          ld_h<8>(g, G + j * 8, false);
+#pragma unroll
+          for (int w = 0; w < 8; ++w) d[w] = OP == kOpRms ? (d[w] * scale) * g[w] : d[w] * g[w];
+        }
+        st_h<8>(y + j * 8, d);
+      }
+    }
+  } else {
+    float v[VPT][W];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int64_t j = threadIdx.x + (int64_t)k * THREADS;
+      if (j < nv) {
+        ld_h<W>(v[k], x + j * W, true);
       } else {
-        float g[W];
-        ld_h<W>(g, G + j * W, false);
 #pragma unroll
-        for (int w = 0; w < W; ++w) v[k][w] = OP == kOpRms ? (v[k][w] * scale) * g[w] : v[k][w] * g[w];
+        for (int w = 0; w < W; ++w) v[k][w] = OP == kOpSoftmax ? -INFINITY : 0.f;
       }
-      st_h<W>(y + j * W, v[k]);
+    }
+    float scale = 1.f;
+    if constexpr (OP == kOpRms) {
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k)
+#pragma unroll
+        for (int w = 0; w < W; ++w) ss += v[k][w] * v[k][w];
+      ss = uk_block_sum<THREADS>(ss, red);
+      scale = 1.0f / sqrtf(ss / (float)C + eps);
+    } else if constexpr (OP == kOpSoftmax) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k)
+#pragma unroll
+        for (int w = 0; w < W; ++w) m = fmaxf(m, v[k][w]);
+      m = uk_block_max<THREADS>(m, red);
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k)
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          const float e = __expf(v[k][w] - m);
+          v[k][w] = e;
+          sum += e;
+        }
+      sum = uk_block_sum<THREADS>(sum, red);
+      scale = 1.0f / sum;
+    }
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int64_t j = threadIdx.x + (int64_t)k * THREADS;
+      if (j < nv) {
+        if constexpr (OP == kOpSoftmax) {
+#pragma unroll
+          for (int w = 0; w < W; ++w) v[k][w] = v[k][w] * scale;
+        } else {
+          float g[W];
+          ld_h<W>(g, G + j * W, false);
+#pragma unroll
+          for (int w = 0; w < W; ++w) v[k][w] = OP == kOpRms ? (v[k][w] * scale) * g[w] : v[k][w] * g[w];
+        }
+        st_h<W>(y + j * W, v[k]);
+      }
     }
   }
 }
