@@ -261,6 +261,14 @@ int uk_cuda_ipc_close(void* ptr, uint64_t offset);
  * No reference counterpart (the reference has no device-side waits). */
 unsigned uk_cuda_pipeline_fault(void);
 
+/* Failure detection check: one CTA runs the pipelines' bounded mbarrier wait
+ * (the one every producer, MMA and epilogue wait uses) on a barrier that
+ * nothing completes unless `arrive` != 0.  Without the arrival the wait gives
+ * up after timeout_ns (1 us .. 1 s), sets bit 16 of the fault word and writes
+ * *status = 0; with it *status = 1.  The context stays usable either way.
+ * status is one device int. */
+int uk_cuda_selftest_wait(int arrive, uint64_t timeout_ns, int* status, void* stream);
+
 /* ---- conv2d ----------------------------------------------------------------
  * layout UK_CONV_KML: the KML conv contract, one image, valid padding:
  *   X[H][W][C], Wt[Oc][Kh][Kw][C], Y[Oc][Ho][Wo], Ho = H-Kh+1, Wo = W-Kw+1;

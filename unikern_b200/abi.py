@@ -42,6 +42,7 @@ PROTOTYPES = {
     "uk_cuda_conv2d_workspace_size": (sz, [i32] * 9),
     "uk_cuda_conv2d_f32_ws": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp, sz, vp]),
     "uk_cuda_pipeline_fault": (C.c_uint, []),
+    "uk_cuda_selftest_wait": (i32, [i32, C.c_uint64, vp, vp]),
     "uk_cuda_gemm_f16_allgather": (i32, [vp, i64, vp, i64, C.POINTER(vp), i32, i64, i32, i32, i32, i64, vp]),
     "uk_cuda_ipc_handle_size": (sz, []),
     "uk_cuda_ipc_export": (i32, [vp, vp, C.POINTER(C.c_uint64)]),

@@ -440,6 +440,30 @@ unsigned conv_fault_take();    // conv_tc.cu
 unsigned fault_take_2sm();     // gemm_f16_2sm.cu
 }
 
+// the bounded wait of every pipeline, run alone on one mbarrier: when nothing
+// arrives it must give up after timeout_ns, record UK_FAULT_SELFTEST and
+// return, leaving the context usable
+__global__ void k_selftest_wait(int arrive, uint64_t timeout_ns, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    uk_mbar_init(&bar, 1);
+    uk_fence_mbar_init();
+    if (arrive) uk_mbar_arrive(&bar);
+    const bool ok = uk_mbar_wait(&bar, 0, nullptr, timeout_ns);
+    if (!ok) atomicOr(&uk::g_fault_word, UK_FAULT_SELFTEST);
+    *status = ok ? 1 : 0;
+  }
+}
+
+extern "C" int uk_cuda_selftest_wait(int arrive, uint64_t timeout_ns, int* status, void* stream) {
+  if (timeout_ns < 1000 || timeout_ns > 1000000000ull)
+    return uk::fail(UK_EINVAL, "selftest_wait: timeout_ns must be in [1e3, 1e9] (got %llu)",
+                    (unsigned long long)timeout_ns);
+  if (int rc = uk::check_device_ptr(status, "status")) return rc;
+  k_selftest_wait<<<1, 32, 0, (cudaStream_t)stream>>>(arrive, timeout_ns, status);
+  return uk::check_launch("selftest_wait");
+}
+
 extern "C" unsigned uk_cuda_pipeline_fault(void) {
   unsigned v = 0;
   if (cudaMemcpyFromSymbol(&v, uk::g_fault_word, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
