@@ -23,6 +23,7 @@ def half(a):
     (1, 256, 14, 14, 256, 3, 1, False),
     (2, 64, 7, 5, 40, 1, 0, True),
     (2, 192, 12, 12, 72, 3, 1, True),      # tiled pre-pass, three channel tiles, a partial hw tile
+    (1, 1024, 8, 64, 64, 1, 0, False),     # a C x W plane beyond the row-staged pre-pass (tiled path only)
     (32, 256, 56, 56, 256, 3, 1, True),   # the BASELINE conv shape in fp16 (two images checked)
 ])
 def test_conv_f16_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):

@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //            kind::tf32 MMAs (lo*hi, hi*lo, hi*hi) per 8-deep slice; 64 KiB
 //            per stage per SM, 3 stages; fp32 output
 //   PairF16  fp16 data, 64 channels per k-step, one kind::f16 MMA per 16-deep
-//            slice; 32 KiB per stage per SM, 6 stages; fp16 output (fp32
+//            slice; 32 KiB per stage per SM, 7 stages; fp16 output (fp32
 //            accumulation and scale, one rounding)
 constexpr int P_BH = 4;                       // output rows per pair tile
 constexpr int P_BNC = BN / 2;                 // channels of B per CTA
@@ -286,7 +286,7 @@ struct PairF32 {
 };
 struct PairF16 {
   using Out = __half;
-  static constexpr int BKE = 64, TILES = 1, STAGES = 6;
+  static constexpr int BKE = 64, TILES = 1, STAGES = 7;
   static constexpr uint32_t IDESC = uk_idesc_f16_ab(2 * BM, BN, 0, 0);
 };
 
@@ -1190,7 +1190,6 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
     if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
     if (!uk::aligned16(workspace)) return uk::fail(UK_EINVAL, "conv2d_f16: the workspace must be 16-byte aligned");
     const size_t plane = (size_t)W * (C + 1) * 4;
-    if (plane > 200 * 1024) return uk::fail(UK_EINVAL, "conv2d_f16: W*C too large for the layout pre-pass");
     uint16_t* Xt = (uint16_t*)workspace;
     uint16_t* Wp = (uint16_t*)((uint8_t*)workspace + align256((size_t)N * H * W * C * 2));
     static bool attr[64] = {false};
@@ -1207,6 +1206,8 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
       const dim3 g((unsigned)((HW + 63) / 64), (unsigned)(C / 64), (unsigned)N);
       k_tile_nhwc<true><<<g, 256, 0, st>>>(X, Xt, nullptr, C, HW);
     } else {
+      // the row-staged fallback holds one C x W plane in shared memory
+      if (plane > 200 * 1024) return uk::fail(UK_EINVAL, "conv2d_f16: W*C too large for the layout pre-pass");
       k_row_nhwc_h<<<(unsigned)((int64_t)N * H), ROW_THREADS, plane, st>>>((const __half*)X, (__half*)Xt, C, H, W);
     }
     const int64_t nw = (int64_t)Oc * Kh * Kw * C;
