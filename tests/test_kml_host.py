@@ -113,7 +113,7 @@ def test_capability_gaps(kml, gap):
     ("gemm", (4096, 4096, 4096), False, (256, 256, 32, 3)),    # split-tf32 on the conv pair kernel
     ("gemm", (4096, 4096, 4090), False, (128, 128, 8, 2)),     # K % 32: FFMA
     ("conv", (58, 58, 256, 3, 3, 256), False, (256, 256, 32, 3)),
-    ("conv", (58, 58, 256, 3, 3, 256), True, (256, 256, 64, 7)),
+    ("conv", (58, 58, 256, 3, 3, 256), True, (256, 256, 64, 6)),
     ("conv", (32, 32, 8, 3, 3, 16), False, (64, 64, 8, 2)),     # C % 32: FFMA
     ("reduce", (134217728,), False, (1, 113360, 0, 1184)),     # 1184 splits = 8 CTAs/SM
     ("reduce", (4096,), False, (1, 4096, 0, 1)),

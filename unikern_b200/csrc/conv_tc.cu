@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //            kind::tf32 MMAs (lo*hi, hi*lo, hi*hi) per 8-deep slice; 64 KiB
 //            per stage per SM, 3 stages; fp32 output
 //   PairF16  fp16 data, 64 channels per k-step, one kind::f16 MMA per 16-deep
-//            slice; 32 KiB per stage per SM, 7 stages; fp16 output (fp32
+//            slice; 32 KiB per stage per SM, 6 stages; fp16 output (fp32
 //            accumulation and scale, one rounding)
 constexpr int P_BH = 4;                       // output rows per pair tile
 constexpr int P_BNC = BN / 2;                 // channels of B per CTA
@@ -286,7 +286,7 @@ struct PairF32 {
 };
 struct PairF16 {
   using Out = __half;
-  static constexpr int BKE = 64, TILES = 1, STAGES = 7;
+  static constexpr int BKE = 64, TILES = 1, STAGES = 6;
   static constexpr uint32_t IDESC = uk_idesc_f16_ab(2 * BM, BN, 0, 0);
 };
 
@@ -318,9 +318,15 @@ template <class Tr>
 constexpr int pair_stage_bytes() {
   return 2 * Tr::TILES * P_TILE_BYTES;  // A tiles then B tiles
 }
+// the epilogue transposes each 32-pixel x 32-channel chunk through a per-warp
+// staging tile so that it stores 16-byte vectors of consecutive pixels
+template <class Tr>
+constexpr int pair_stg_bytes() {
+  return EPI_WARPS * 32 * 32 * (int)sizeof(typename Tr::Out);
+}
 template <class Tr>
 constexpr size_t pair_smem_bytes() {
-  return 1024 + (size_t)Tr::STAGES * pair_stage_bytes<Tr>() + sizeof(PairCtl<Tr>);
+  return 1024 + (size_t)Tr::STAGES * pair_stage_bytes<Tr>() + pair_stg_bytes<Tr>() + sizeof(PairCtl<Tr>);
 }
 static_assert(pair_smem_bytes<PairF32>() <= 232448 && pair_smem_bytes<PairF16>() <= 232448,
               "shared memory per block on sm_100");
@@ -352,7 +358,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int STAGES = Tr::STAGES, STAGE_BYTES = pair_stage_bytes<Tr>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  PairCtl<Tr>* ctl = (PairCtl<Tr>*)(smem + (size_t)STAGES * STAGE_BYTES);
+  uint8_t* stg_base = smem + (size_t)STAGES * STAGE_BYTES;
+  PairCtl<Tr>* ctl = (PairCtl<Tr>*)(stg_base + pair_stg_bytes<Tr>());
   volatile int* abort = &ctl->abort;
   Out* Y = (Out*)p.y;
   const Out* scale = (const Out*)p.scale;
@@ -546,10 +553,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       uk_tc_fence_after();
-      const int ho = ho0 + (int)crank * BH + m / BW, wo = wo0 + m % BW;
-      const bool valid = ho < p.Ho && wo < p.Wo;
-      Out* ybase = Y + (((int64_t)n * p.Oc + oc0) * p.Ho + ho) * p.Wo + wo;
-      const int64_t ocs = (int64_t)p.Ho * p.Wo;
+      // the warp's 32 pixels are one run of an output row: row ho_w,
+      // columns wo_w .. wo_w + 31; lane m's accumulator row is pixel wo_w + lane
+      const int ho_w = ho0 + (int)crank * BH + (q * 32) / BW, wo_w = wo0 + (q * 32) % BW;
+      constexpr int VEC = 16 / (int)sizeof(Out);  // pixels per 16-byte store
+      constexpr int LPR = 32 / VEC;                // lanes per channel row
+      constexpr int RPR = 32 / LPR;                // channel rows per store round
+      Out* stg = (Out*)(stg_base + (size_t)(warp - 2) * 32 * 32 * sizeof(Out));  // [32 ch][32 px]
+      const bool vec_ok = p.Wo % VEC == 0 && ((uintptr_t)Y & 15) == 0;
+      const int px = (lane % LPR) * VEC, wo = wo_w + px;
 #pragma unroll 1
       for (int j = 0; j < BN / 32; ++j) {
         uint32_t v[32];
@@ -560,8 +572,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float sc = __shfl_sync(0xffffffffu, sc_lane, i);
-          if (valid && ocj + i < p.Oc) out_store(ybase + (int64_t)(j * 32 + i) * ocs, __uint_as_float(v[i]) * sc);
+          out_store(stg + i * 32 + lane, __uint_as_float(v[i]) * sc);
         }
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < 32 / RPR; ++r) {
+          const int oi = r * RPR + lane / LPR, oc = ocj + oi;
+          if (oc < p.Oc && ho_w < p.Ho && wo < p.Wo) {
+            Out* dst = Y + (((int64_t)n * p.Oc + oc) * p.Ho + ho_w) * p.Wo + wo;
+            const Out* src = stg + oi * 32 + px;
+            if (vec_ok && wo + VEC <= p.Wo) {
+              *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+            } else {
+#pragma unroll
+              for (int e = 0; e < VEC; ++e)
+                if (wo + e < p.Wo) dst[e] = src[e];
+            }
+          }
+        }
+        __syncwarp();
       }
       uk_tc_fence_before();
       __syncwarp();

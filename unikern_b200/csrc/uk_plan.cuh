@@ -47,9 +47,9 @@ inline int sgemm_ksplit(int64_t M, int64_t N, int64_t K, int64_t sms) {
 
 // the tensor-core convolutions on SM pairs (also the fp32 GEMM run as a 1 x 1
 // convolution): 256 output channels x 256 pixels per pair, 32 fp32 channels
-// (split-tf32, 3 stages) or 64 fp16 channels (7 stages) per k-step
+// (split-tf32, 3 stages) or 64 fp16 channels (6 stages) per k-step
 constexpr Tile kConvPairF32Tile{256, 256, 32, 3};
-constexpr Tile kConvPairF16Tile{256, 256, 64, 7};
+constexpr Tile kConvPairF16Tile{256, 256, 64, 6};
 
 // implicit-GEMM FFMA conv: rows = output channels, columns = output pixels
 inline Tile conv_tile(int64_t npix, int64_t Oc, int64_t sms) {
