@@ -410,6 +410,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int n, ho0, wo0, oc0;
         pair_tile_coords(p, t, n, ho0, wo0, oc0);
         const int hr = ho0 + (int)crank * BH;  // this CTA's first output row
+        // the pairs running side by side would all fetch the same weight (or,
+        // for the GEMM, the same B^T) tile at the same moment; each tile walks
+        // its k-steps from its own offset instead, a function of the tile's
+        // position in the image and channel grid only (never of the image
+        // index), so a result does not depend on which pair or which GPU of a
+        // batch shard computes it
+        const int rot = (int)(((int64_t)(ho0 / P_BH) * 7 + (int64_t)(wo0 / BW) * 3 + (int64_t)(oc0 / BN) * 5) % ksteps);
         bool ok = true;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
           const int s = it % STAGES;
@@ -420,7 +427,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          const int tap = ks / csteps, c0 = (ks - tap * csteps) * Tr::BKE;
+          const int kq = ks + rot < ksteps ? ks + rot : ks + rot - ksteps;
+          const int tap = kq / csteps, c0 = (kq - tap * csteps) * Tr::BKE;
           const int kh = tap / p.Kw, kw = tap - kh * p.Kw;
           uint8_t* st = smem + (size_t)s * STAGE_BYTES;
           const uint32_t bar = uk_mapa(uk_smem_u32(&ctl->full[s]), 0);
