@@ -875,6 +875,11 @@ def main():
         r = bench_gemm_f32(Ctx(1, 0, local_rank), s, 3)
         ops["gemm_f32_512"] = {"TFLOP/s": round(r["value"], 3), "ms": round(r["ms"], 5),
                                "roofline": roofline("fp32", r["value"], pk)}
+        r = bench_gemm_f32_tc(Ctx(1, 0, local_rank), max(3, s // 2), 3)
+        ops["gemm_f32_8192_tensor_cores"] = {
+            "TFLOP/s": round(r["value"], 2), "ms": round(r["ms"], 4),
+            "path": "split-tf32 on the convolution's SM-pair kernel, fp32 promotion every 1024 k; pre-passes included",
+            "roofline": roofline("tensor_3xtf32", r["value"], pk)}
         r = bench_decode(Ctx(1, 0, local_rank), s, 3)
         ops["decode_chain_b32"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
                                    "roofline": roofline("hbm", r["value"], pk)}
