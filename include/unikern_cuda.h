@@ -289,6 +289,10 @@ int uk_cuda_conv2d_f32(const float* X, const float* Wt, float* Y, int N, int H, 
  * an fp32 FFMA result; the fp32 gate, 1e-4 against fp64, holds).  The split
  * operands (and, for NCHW, the input transposed to NHWC) live in a caller
  * workspace of uk_cuda_conv2d_workspace_size(...) bytes (16-byte aligned).
+ * The size includes room for the fp32 partial tiles of the last round of
+ * tiles, which the kernel then splits along K over the SM pairs that round
+ * would leave idle (summed by a second, deterministic kernel); a smaller
+ * workspace that still holds the operand pairs runs without the split.
  * Takes the tensor cores when C is a multiple of 32; other shapes run the
  * FFMA kernel of uk_cuda_conv2d_f32 (the size query then returns 0 and the
  * workspace may be NULL).  Replaces uk_conv<OCB>/uk_conv_g
@@ -300,9 +304,11 @@ size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int Kh, int Kw,
  * pairs): X, Wt, scale and Y are IEEE binary16 (uint16_t bit patterns) in the
  * layouts of uk_cuda_conv2d_f32; fp32 accumulation, the scale applied in
  * fp32, one rounding to f16.  Needs C a multiple of 64.  The KML layout (HWC
- * input, [Oc][Kh][Kw][C] weights) is read in place and needs no workspace;
- * NCHW takes a workspace of uk_cuda_conv2d_f16_workspace_size(...) bytes for
- * the NHWC copy of X and the permuted weights.  The reference refuses fp16
+ * input, [Oc][Kh][Kw][C] weights) is read in place and runs without a
+ * workspace; NCHW takes a workspace of uk_cuda_conv2d_f16_workspace_size(...)
+ * bytes for the NHWC copy of X and the permuted weights.  For either layout
+ * the size also covers the last round's split partial tiles (as for fp32),
+ * used when the workspace passed has room for them.  The reference refuses fp16
  * conv (src/codegen_hip.cpp:81-89); this widens the dtype interval. */
 size_t uk_cuda_conv2d_f16_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc,
                                          int pad, int layout);

@@ -38,8 +38,11 @@ def main():
         rel = diff / ref.abs().max().item()
         print("rank %d conv N=%d C=%d %dx%d -> %d: max|Y - single GPU| = %g (rel %g)" % (rank, N, Cc, H, W, Oc, diff,
                                                                                          rel), flush=True)
-        # every image runs the same tiles in the same order on either GPU count
-        ok = ok and diff == 0.0 and not torch.isnan(Y).any().item()
+        # every image runs the same tiles with the same k-order on either GPU
+        # count, except the last round of tiles, which is split along K by the
+        # tile count: a different grouping in the tensor cores' accumulator
+        # there (~2e-5 of the output scale), so the fp32 gate, not bitwise
+        ok = ok and rel <= 1e-4 and not torch.isnan(Y).any().item()
         dist.barrier()
     dist.destroy_process_group()
     return 0 if ok else 1

@@ -44,15 +44,23 @@ def test_conv_f16_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):
 
 
 def test_conv_f16_kml_layout_in_place():
+    # the KML form reads its input in place; a workspace only adds room for
+    # the split partial tiles of the last round (here 14 tiles, all in it)
     H, W, Cc, Kh, Kw, Oc = 58, 58, 256, 3, 3, 256
-    assert abi.lib().uk_cuda_conv2d_f16_workspace_size(1, H, W, Cc, Kh, Kw, Oc, 0, abi.UK_CONV_KML) == 0
+    assert abi.lib().uk_cuda_conv2d_f16_workspace_size(1, H, W, Cc, Kh, Kw, Oc, 0, abi.UK_CONV_KML) > 0
     rng = np.random.default_rng(5)
     xh = half(rng.uniform(0, 1, H * W * Cc))
     wh = half(rng.normal(0, np.sqrt(2.0 / (9 * Cc)), Oc * Kh * Kw * Cc))
-    y = empty((Oc * (H - 2) * (W - 2),), "f16")
-    abi.conv2d_f16(dev(xh), dev(wh), y, 1, H, W, Cc, Kh, Kw, Oc, 0, None, abi.UK_CONV_KML)
     ref = O.conv_f64(O.f16_to_f32(xh), O.f16_to_f32(wh), H, W, Cc, Kh, Kw, Oc, threads=8)
+    x_d, w_d = dev(xh), dev(wh)
+    y = empty((Oc * (H - 2) * (W - 2),), "f16")
+    abi.conv2d_f16(x_d, w_d, y, 1, H, W, Cc, Kh, Kw, Oc, 0, None, abi.UK_CONV_KML)   # with the workspace
     assert O.rel_err(O.f16_to_f32(host(y)), ref, O.rms(ref)) <= F16_TOL
+    y2 = empty((Oc * (H - 2) * (W - 2),), "f16")
+    assert abi.lib().uk_cuda_conv2d_f16(x_d.data_ptr(), w_d.data_ptr(), y2.data_ptr(), 1, H, W, Cc, Kh, Kw, Oc, 0,
+                                        None, abi.UK_CONV_KML, None, 0, None) == 0      # without
+    assert O.rel_err(O.f16_to_f32(host(y2)), ref, O.rms(ref)) <= F16_TOL
+    assert abi.lib().uk_cuda_pipeline_fault() == 0
 
 
 def test_conv_f16_refuses_channel_counts_off_the_row():

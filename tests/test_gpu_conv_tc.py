@@ -52,6 +52,33 @@ def test_conv_tc_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):
     assert O.rel_err(got, ffma.astype(np.float64), SUM_TAU * O.rms(ref)) <= F32_TOL
 
 
+def test_conv_tc_last_round_split_matches_unsplit():
+    # the size query's workspace lets the last round of tiles split along K;
+    # a workspace holding only the operand pairs runs it unsplit
+    import torch
+    N, Cc, H, W, Oc, pad = 3, 128, 28, 28, 96, 1
+    rng = np.random.default_rng(77)
+    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / (9 * Cc)), (Oc, Cc, 3, 3)).astype(np.float32)
+    full = abi.lib().uk_cuda_conv2d_workspace_size(N, H, W, Cc, 3, 3, Oc, pad, abi.UK_CONV_NCHW)
+    base = 2 * (-(-N * H * W * Cc * 4 // 256) * 256) + 2 * (-(-Oc * 9 * Cc * 4 // 256) * 256)
+    assert full > base
+    out = []
+    for nbytes in (full, base):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        y = empty((N, Oc, H, W))
+        abi.check(abi.lib().uk_cuda_conv2d_f32_ws(dev(x).data_ptr(), dev(w).data_ptr(), y.data_ptr(), N, H, W, Cc, 3,
+                                                  3, Oc, pad, None, abi.UK_CONV_NCHW, ws.data_ptr(), nbytes, None))
+        out.append(host(y))
+    ref = O.conv_nchw(x, w, None, pad)
+    for got in out:
+        assert O.rel_err(got, ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+    # the two group the k-steps differently in the tensor cores' accumulator
+    # (its truncation error is ~2e-5 of the output scale): fp32-gate close
+    assert O.rel_err(out[0], out[1].astype(np.float64), SUM_TAU * O.rms(ref)) <= F32_TOL
+    assert abi.lib().uk_cuda_pipeline_fault() == 0
+
+
 def test_conv_tc_kml_layout_vs_f64():
     # the KML conv contract at its BASELINE declaration: [58, 58, 256, 3, 3, 256]
     H, W, Cc, Kh, Kw, Oc = 58, 58, 256, 3, 3, 256

@@ -45,7 +45,8 @@ def test_tc_vs_f64(M, N, K):
 
 def test_workspace_and_preference_queries():
     lib = abi.lib()
-    assert lib.uk_cuda_gemm_f32_workspace_size(256, 256, 256) == 2 * 256 * 256 * 4 * 2
+    # the tf32 pairs of B^T and A, plus room for the split partial tiles
+    assert lib.uk_cuda_gemm_f32_workspace_size(256, 256, 256) >= 2 * 256 * 256 * 4 * 2
     assert lib.uk_cuda_gemm_f32_workspace_size(256, 100, 256) == 0   # N % 64
     assert lib.uk_cuda_gemm_f32_workspace_size(256, 256, 100) == 0   # K % 32
     assert lib.uk_cuda_gemm_f32_prefers_tc(1024, 1024, 1024) == 1

@@ -76,6 +76,11 @@ struct ConvTc {
   const void* scale;  // same type as y
   int N, Ho, Wo, Oc, C, Kh, Kw, pad;
   int tiles_w, tiles_h, tiles_oc, num_tiles;
+  // SM-pair kernel work items: tiles [0, num_full) whole, then each of the
+  // remaining tiles (the last, partial round) as `splits` k-ranges whose fp32
+  // partial tiles go to `part` and are summed by k_conv_tail
+  int num_items, num_full, splits;
+  float* part;
 };
 
 __device__ __forceinline__ void tile_coords(const ConvTc& p, int t, int& n, int& ho0, int& wo0, int& oc0) {
@@ -343,6 +348,23 @@ __device__ __forceinline__ void pair_tile_coords(const ConvTc& p, int t, int& n,
   oc0 = oct * BN;
 }
 
+// work item -> tile t and k-steps [k0, k0 + kn); j = the split item's index
+// among all split items, -1 for a whole tile
+__device__ __forceinline__ void pair_item(const ConvTc& p, int item, int ksteps, int& t, int& k0, int& kn, int& j) {
+  if (item < p.num_full) {
+    t = item;
+    k0 = 0;
+    kn = ksteps;
+    j = -1;
+    return;
+  }
+  j = item - p.num_full;
+  t = p.num_full + j / p.splits;
+  const int sidx = j - (j / p.splits) * p.splits;
+  k0 = (int)((int64_t)sidx * ksteps / p.splits);
+  kn = (int)((int64_t)(sidx + 1) * ksteps / p.splits) - k0;
+}
+
 __device__ __forceinline__ float out_scale(const float* s, int i) { return __ldg(s + i); }
 __device__ __forceinline__ float out_scale(const __half* s, int i) { return __half2float(__ldg(s + i)); }
 __device__ __forceinline__ void out_store(float* y, float v) { *y = v; }
@@ -370,7 +392,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int csteps = p.C / Tr::BKE;
   const int ksteps = p.Kh * p.Kw * csteps;
   const int kc = Tr::TILES == 2 ? P_KC : ksteps;  // k-steps per TMEM chunk
-  const int nchunks = (ksteps + kc - 1) / kc;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -406,7 +427,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       uint32_t it = 0;
-      for (int t = pair; t < p.num_tiles && !*abort; t += npairs) {
+      for (int item = pair; item < p.num_items && !*abort; item += npairs) {
+        int t, k0, kn, j;
+        pair_item(p, item, ksteps, t, k0, kn, j);
         int n, ho0, wo0, oc0;
         pair_tile_coords(p, t, n, ho0, wo0, oc0);
         const int hr = ho0 + (int)crank * BH;  // this CTA's first output row
@@ -416,9 +439,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // position in the image and channel grid only (never of the image
         // index), so a result does not depend on which pair or which GPU of a
         // batch shard computes it
-        const int rot = (int)(((int64_t)(ho0 / P_BH) * 7 + (int64_t)(wo0 / BW) * 3 + (int64_t)(oc0 / BN) * 5) % ksteps);
+        const int rot =
+            j >= 0 ? 0 : (int)(((int64_t)(ho0 / P_BH) * 7 + (int64_t)(wo0 / BW) * 3 + (int64_t)(oc0 / BN) * 5) % ksteps);
         bool ok = true;
-        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+        for (int ks = 0; ks < kn; ++ks, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!uk_mbar_wait_cluster(&ctl->empty[s], ph ^ 1u, abort, WAIT_NS)) {
@@ -427,7 +451,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          const int kq = ks + rot < ksteps ? ks + rot : ks + rot - ksteps;
+          const int kq = k0 + (ks + rot < kn ? ks + rot : ks + rot - kn);
           const int tap = kq / csteps, c0 = (kq - tap * csteps) * Tr::BKE;
           const int kh = tap / p.Kw, kw = tap - kh * p.Kw;
           uint8_t* st = smem + (size_t)s * STAGE_BYTES;
@@ -447,7 +471,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     if (crank == 0 && lane == 0) {
       uint32_t it = 0, tl = 0, np = 0;  // np: chunks handed to the epilogue for promotion
-      for (int t = pair; t < p.num_tiles && !*abort; t += npairs, ++tl) {
+      for (int item = pair; item < p.num_items && !*abort; item += npairs, ++tl) {
+        int t, k0, kn, j;
+        pair_item(p, item, ksteps, t, k0, kn, j);
         const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
         // the tile's accumulator: drained two tiles ago, and no longer read
         // by the previous tile's last promotion
@@ -459,7 +485,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         uk_tc_fence_after();
         bool ok = true;
-        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+        for (int ks = 0; ks < kn; ++ks, ++it) {
           const int c = ks / kc, kin = ks - c * kc;
           if (c >= 1 && kin == 0) {
             // a later chunk goes to the other buffer: the previous tile's
@@ -505,7 +531,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
           }
           uk_umma_commit_cg2(&ctl->empty[s], P_PAIR);
-          if (c >= 1 && (kin == kc - 1 || ks == ksteps - 1)) {
+          if (c >= 1 && (kin == kc - 1 || ks == kn - 1)) {
             uk_umma_commit_cg2(&ctl->pfull, P_PAIR);
             ++np;
           }
@@ -524,14 +550,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t pempty_leader = uk_mapa(uk_smem_u32(&ctl->pempty), 0);
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t tl = 0, pi = 0;  // pi: promotions done
-    for (int t = pair; t < p.num_tiles && !*abort; t += npairs, ++tl) {
+    for (int item = pair; item < p.num_items && !*abort; item += npairs, ++tl) {
+      int t, k0, kn, j;
+      pair_item(p, item, ksteps, t, k0, kn, j);
       int n, ho0, wo0, oc0;
       pair_tile_coords(p, t, n, ho0, wo0, oc0);
       const uint32_t buf = tl & 1u, tph = (tl >> 1) & 1u;
       // promotions: each later chunk's partial sum, added in fp32 (round to
       // nearest) into the tile's accumulator
       bool ok = true;
-      for (int c = 1; c < nchunks; ++c, ++pi) {
+      const int nch = (kn + kc - 1) / kc;
+      for (int c = 1; c < nch; ++c, ++pi) {
         if (!uk_mbar_wait_cluster(&ctl->pfull, pi & 1u, abort, WAIT_NS)) {
           atomicOr(&uk::g_conv_fault, UK_FAULT_EPILOGUE);
           ctl->abort = 1;
@@ -570,35 +599,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       Out* stg = (Out*)(stg_base + (size_t)(warp - 2) * 32 * 32 * sizeof(Out));  // [32 ch][32 px]
       const bool vec_ok = p.Wo % VEC == 0 && ((uintptr_t)Y & 15) == 0;
       const int px = (lane % LPR) * VEC, wo = wo_w + px;
+      if (j >= 0) {
+        // a split item: its fp32 partial tile, [BN channels][128 pixels] per
+        // CTA, for k_conv_tail to sum (no scale yet)
+        float* pp = p.part + (size_t)(j * 2 + (int)crank) * BN * 128;
 #pragma unroll 1
-      for (int j = 0; j < BN / 32; ++j) {
-        uint32_t v[32];
-        uk_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + j * 32, v);
-        uk_tmem_ld_wait();
-        const int ocj = oc0 + j * 32;
-        const float sc_lane = (scale != nullptr && ocj + lane < p.Oc) ? out_scale(scale, ocj + lane) : 1.f;
+        for (int jc = 0; jc < BN / 32; ++jc) {
+          uint32_t v[32];
+          uk_tmem_ld32(trow + buf * BN + jc * 32, v);
+          uk_tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float sc = __shfl_sync(0xffffffffu, sc_lane, i);
-          out_store(stg + i * 32 + lane, __uint_as_float(v[i]) * sc);
+          for (int i = 0; i < 32; ++i) pp[(size_t)(jc * 32 + i) * 128 + m] = __uint_as_float(v[i]);
         }
-        __syncwarp();
+      } else {
+#pragma unroll 1
+        for (int jc = 0; jc < BN / 32; ++jc) {
+          uint32_t v[32];
+          uk_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + jc * 32, v);
+          uk_tmem_ld_wait();
+          const int ocj = oc0 + jc * 32;
+          const float sc_lane = (scale != nullptr && ocj + lane < p.Oc) ? out_scale(scale, ocj + lane) : 1.f;
 #pragma unroll
-        for (int r = 0; r < 32 / RPR; ++r) {
-          const int oi = r * RPR + lane / LPR, oc = ocj + oi;
-          if (oc < p.Oc && ho_w < p.Ho && wo < p.Wo) {
-            Out* dst = Y + (((int64_t)n * p.Oc + oc) * p.Ho + ho_w) * p.Wo + wo;
-            const Out* src = stg + oi * 32 + px;
-            if (vec_ok && wo + VEC <= p.Wo) {
-              *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-            } else {
+          for (int i = 0; i < 32; ++i) {
+            const float sc = __shfl_sync(0xffffffffu, sc_lane, i);
+            out_store(stg + i * 32 + lane, __uint_as_float(v[i]) * sc);
+          }
+          __syncwarp();
 #pragma unroll
-              for (int e = 0; e < VEC; ++e)
-                if (wo + e < p.Wo) dst[e] = src[e];
+          for (int r = 0; r < 32 / RPR; ++r) {
+            const int oi = r * RPR + lane / LPR, oc = ocj + oi;
+            if (oc < p.Oc && ho_w < p.Ho && wo < p.Wo) {
+              Out* dst = Y + (((int64_t)n * p.Oc + oc) * p.Ho + ho_w) * p.Wo + wo;
+              const Out* src = stg + oi * 32 + px;
+              if (vec_ok && wo + VEC <= p.Wo) {
+                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+              } else {
+#pragma unroll
+                for (int e = 0; e < VEC; ++e)
+                  if (wo + e < p.Wo) dst[e] = src[e];
+              }
             }
           }
+          __syncwarp();
         }
-        __syncwarp();
       }
       uk_tc_fence_before();
       __syncwarp();
@@ -615,6 +658,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     uk_tc_fence_after();
     uk_tmem_dealloc_cg2(tmem, TMEM_COLS);
+  }
+}
+
+// the split tiles of the last round: every output element of those tiles is
+// the sum of its `splits` partials in split order (deterministic), scaled
+// and stored; one thread per element, pixels fastest (coalesced reads of the
+// partials and stores along each output row)
+template <class Out>
+__global__ void __launch_bounds__(256) k_conv_tail(const ConvTc p) {
+  const int64_t total = (int64_t)(p.num_tiles - p.num_full) * 2 * BN * 128;
+  Out* Y = (Out*)p.y;
+  const Out* scale = (const Out*)p.scale;
+  for (int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * 256) {
+    const int m = (int)(idx % 128);
+    int64_t r = idx / 128;
+    const int ocl = (int)(r % BN);
+    r /= BN;
+    const int crank = (int)(r % 2), tt = (int)(r / 2);
+    int n, ho0, wo0, oc0;
+    pair_tile_coords(p, p.num_full + tt, n, ho0, wo0, oc0);
+    const int ho = ho0 + crank * BH + m / BW, wo = wo0 + m % BW, oc = oc0 + ocl;
+    if (ho >= p.Ho || wo >= p.Wo || oc >= p.Oc) continue;
+    const float* src = p.part + ((size_t)((size_t)tt * p.splits * 2 + crank) * BN + ocl) * 128 + m;
+    const size_t step = (size_t)2 * BN * 128;  // from one split's partial tile to the next
+    float v = 0.f;
+#pragma unroll 4
+    for (int sidx = 0; sidx < p.splits; ++sidx) v += src[(size_t)sidx * step];
+    out_store(Y + (((int64_t)n * p.Oc + oc) * p.Ho + ho) * p.Wo + wo, scale != nullptr ? v * out_scale(scale, oc) : v);
   }
 }
 
@@ -866,10 +937,56 @@ bool tc_applies(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad, int
   return true;
 }
 
+// Work items of the SM-pair kernels.  Tiles go round-robin over the pairs,
+// so the last round is partial (448 conv tiles on 74 pairs: 6 full rounds and
+// 4 tiles).  When there is room in the workspace, each tile of that last
+// round is cut into `splits` k-ranges (at least 4 k-steps each) so that the
+// idle pairs share it; k_conv_tail sums the fp32 partial tiles.
+struct TailPlan {
+  int pairs, num_items, num_full, splits;
+  size_t bytes;
+};
+
+TailPlan tail_plan(int64_t tiles, int ksteps, size_t room) {
+  TailPlan tp{};
+  const int sm2 = uk::sm_count() / 2;
+  const int r = (int)(tiles % sm2);  // tiles in the last round (all of them when tiles < sm2)
+  int S = r > 0 ? sm2 / r : 1;
+  if (S > ksteps / 4) S = ksteps / 4;
+  const size_t bytes = S >= 2 ? (size_t)r * S * 2 * BN * 128 * sizeof(float) : 0;
+  if (S < 2 || bytes > room) {
+    tp.num_full = (int)tiles;
+    tp.splits = 1;
+    tp.num_items = (int)tiles;
+  } else {
+    tp.num_full = (int)(tiles - r);
+    tp.splits = S;
+    tp.num_items = tp.num_full + r * S;
+    tp.bytes = bytes;
+  }
+  tp.pairs = tp.num_items < sm2 ? tp.num_items : sm2;
+  return tp;
+}
+
+size_t tail_bytes(int64_t tiles, int ksteps) { return align256(tail_plan(tiles, ksteps, (size_t)-1).bytes); }
+
+// pair tiles of a convolution (the SM-pair kernels' tiling)
+int64_t pair_tiles(int N, int Ho, int Wo, int Oc) {
+  return (int64_t)N * ((Ho + P_BH - 1) / P_BH) * ((Wo + BW - 1) / BW) * ((Oc + BN - 1) / BN);
+}
+
+// fill the work-item fields of p from the plan (launch the tail kernel after)
+void apply_tail(ConvTc& p, const TailPlan& tp, float* part) {
+  p.num_items = tp.num_items;
+  p.num_full = tp.num_full;
+  p.splits = tp.splits;
+  p.part = tp.splits >= 2 ? part : nullptr;
+}
+
 // the split-tf32 kernel over prepared operands: Xh/Xl the input as NHWC
 // (hi, lo) pairs, Wh/Wl the weights as [Oc][kh][kw][c] pairs
 int run_tc(const float* Xh, const float* Xl, const float* Wh, const float* Wl, float* Y, const float* scale, int N,
-           int H, int W, int C, int Kh, int Kw, int Oc, int pad, cudaStream_t st) {
+           int H, int W, int C, int Kh, int Kw, int Oc, int pad, float* part, size_t part_room, cudaStream_t st) {
   const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
   // tensor maps: input [N][H][W][C] as 4-D (C innermost), weights [Oc][K]
   CUtensorMap txh, txl, twh, twl;
@@ -903,6 +1020,8 @@ int run_tc(const float* Xh, const float* Xl, const float* Wh, const float* Wl, f
   const int64_t tiles = (int64_t)N * p.tiles_h * p.tiles_w * p.tiles_oc;
   if (tiles > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d: too many tiles");
   p.num_tiles = (int)tiles;
+  const TailPlan tp = tail_plan(tiles, Kh * Kw * (C / BK), pair && part != nullptr ? part_room : 0);
+  apply_tail(p, tp, part);
 
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -919,9 +1038,8 @@ int run_tc(const float* Xh, const float* Xl, const float* Wh, const float* Wl, f
     k_conv_tc<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(txh, txl, twh, twl, p);
     return uk::check_launch("conv2d(tcgen05)");
   }
-  const int pairs = p.num_tiles < uk::sm_count() / 2 ? p.num_tiles : uk::sm_count() / 2;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.gridDim = dim3((unsigned)(2 * tp.pairs), 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = pair_smem_bytes<PairF32>();
   cfg.stream = st;
@@ -934,6 +1052,11 @@ int run_tc(const float* Xh, const float* Xl, const float* Wh, const float* Wl, f
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_pair<PairF32>, txh, txl, twh, twl, p);
   if (e != cudaSuccess) return uk::fail(UK_ECUDA, "conv2d(pair): launch: %s", cudaGetErrorString(e));
+  if (tp.splits >= 2) {
+    const int64_t total = (int64_t)(p.num_tiles - p.num_full) * 2 * BN * 128;
+    const int64_t g = std::min<int64_t>((total + 255) / 256, (int64_t)uk::sm_count() * 8);
+    k_conv_tail<float><<<(unsigned)g, 256, 0, st>>>(p);
+  }
   return uk::check_launch("conv2d(tcgen05 pair)");
 }
 }  // namespace
@@ -954,7 +1077,10 @@ extern "C" size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int 
                                                 int layout) {
   if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout)) return 0;
   const size_t xs = align256((size_t)N * H * W * C * 4), ws = align256((size_t)Oc * Kh * Kw * C * 4);
-  return 2 * xs + 2 * ws;
+  const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
+  // + the last round's split partial tiles (SM-pair kernel)
+  const size_t tail = use_pair_kernel() ? tail_bytes(pair_tiles(N, Ho, Wo, Oc), Kh * Kw * (C / BK)) : 0;
+  return 2 * xs + 2 * ws + tail;
 }
 
 extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh,
@@ -968,7 +1094,9 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
                     Kw, Oc, pad);
   if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout))
     return uk::conv2d_ffma(X, Wt, Y, N, H, W, C, Kh, Kw, Oc, pad, scale, layout, st);
-  const size_t need = uk_cuda_conv2d_workspace_size(N, H, W, C, Kh, Kw, Oc, pad, layout);
+  // the operand pairs are required; the split partials of the last round
+  // are used when the workspace has room for them (the size query includes it)
+  const size_t need = 2 * align256((size_t)N * H * W * C * 4) + 2 * align256((size_t)Oc * Kh * Kw * C * 4);
   if (workspace == nullptr || workspace_bytes < need)
     return uk::fail(UK_EINVAL, "conv2d: needs a %zu-byte workspace (uk_cuda_conv2d_workspace_size), got %zu", need,
                     workspace ? workspace_bytes : (size_t)0);
@@ -1024,7 +1152,8 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   }
   if (int rc = uk::check_launch("conv2d(split)")) return rc;
 
-  return run_tc(Xh, Xl, Wh, Wl, Y, scale, N, H, W, C, Kh, Kw, Oc, pad, st);
+  return run_tc(Xh, Xl, Wh, Wl, Y, scale, N, H, W, C, Kh, Kw, Oc, pad, (float*)((uint8_t*)workspace + need),
+                workspace_bytes - need, st);
 }
 
 // ---- the fp32 GEMM as a 1 x 1 convolution -------------------------------------------
@@ -1040,6 +1169,10 @@ bool gemm_f32_tc_shape(int M, int N, int K) { return M > 0 && N >= 64 && N % 64 
 
 size_t gemm_f32_tc_b_bytes(int N, int K) { return 2 * align256((size_t)N * K * 4); }
 size_t gemm_f32_tc_a_bytes(int M, int K) { return 2 * align256((size_t)M * K * 4); }
+// the last round's split partial tiles of the GEMM's convolution
+size_t gemm_f32_tc_tail_bytes(int M, int N, int K) {
+  return use_pair_kernel() ? tail_bytes(pair_tiles(1, N / 64, 64, M), K / BK) : 0;
+}
 
 // B (device, K x N) -> the (hi, lo) pairs of B^T in bws (gemm_f32_tc_b_bytes)
 int gemm_f32_tc_prep_b(const float* B, void* bws, int N, int K, cudaStream_t st) {
@@ -1052,7 +1185,8 @@ int gemm_f32_tc_prep_b(const float* B, void* bws, int N, int K, cudaStream_t st)
 
 // C = A * B over a prepared B: splits A into aws (gemm_f32_tc_a_bytes), then
 // runs the convolution kernel
-int gemm_f32_tc_run(const float* A, const void* bws, void* aws, float* C, int M, int N, int K, cudaStream_t st) {
+int gemm_f32_tc_run(const float* A, const void* bws, void* aws, float* C, int M, int N, int K, cudaStream_t st,
+                    float* part, size_t part_room) {
   float* Ah = (float*)aws;
   float* Al = (float*)((uint8_t*)aws + align256((size_t)M * K * 4));
   const int64_t n = (int64_t)M * K;
@@ -1061,14 +1195,14 @@ int gemm_f32_tc_run(const float* A, const void* bws, void* aws, float* C, int M,
   if (int rc = uk::check_launch("gemm_f32(split)")) return rc;
   const float* Th = (const float*)bws;
   const float* Tl = (const float*)((const uint8_t*)bws + align256((size_t)N * K * 4));
-  return run_tc(Th, Tl, Ah, Al, C, nullptr, 1, N / 64, 64, K, 1, 1, M, 0, st);
+  return run_tc(Th, Tl, Ah, Al, C, nullptr, 1, N / 64, 64, K, 1, 1, M, 0, part, part_room, st);
 }
 
 }  // namespace uk
 
 extern "C" size_t uk_cuda_gemm_f32_workspace_size(int M, int N, int K) {
   if (!uk::gemm_f32_tc_shape(M, N, K)) return 0;
-  return uk::gemm_f32_tc_b_bytes(N, K) + uk::gemm_f32_tc_a_bytes(M, K);
+  return uk::gemm_f32_tc_b_bytes(N, K) + uk::gemm_f32_tc_a_bytes(M, K) + uk::gemm_f32_tc_tail_bytes(M, N, K);
 }
 
 extern "C" int uk_cuda_gemm_f32_prefers_tc(int M, int N, int K) {
@@ -1085,7 +1219,7 @@ extern "C" int uk_cuda_gemm_f32_ws(const float* A, const float* B, float* C, int
   if (!uk::gemm_f32_tc_shape(M, N, K))
     return uk::fail(UK_EINVAL, "gemm_f32: the tensor-core path needs K %% 32 == 0 and N %% 64 == 0 (M=%d N=%d K=%d); "
                     "call without a workspace", M, N, K);
-  const size_t bb = uk::gemm_f32_tc_b_bytes(N, K), need = bb + uk::gemm_f32_tc_a_bytes(M, K);
+  const size_t bb = uk::gemm_f32_tc_b_bytes(N, K), need = bb + uk::gemm_f32_tc_a_bytes(M, K);  // + optional tail
   if (workspace_bytes < need)
     return uk::fail(UK_EINVAL, "gemm_f32: the tensor-core path needs a %zu-byte workspace, got %zu", need,
                     workspace_bytes);
@@ -1095,7 +1229,8 @@ extern "C" int uk_cuda_gemm_f32_ws(const float* A, const float* B, float* C, int
   if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
   if (!uk::aligned16(workspace)) return uk::fail(UK_EINVAL, "gemm_f32: the workspace must be 16-byte aligned");
   if (int rc = uk::gemm_f32_tc_prep_b(B, workspace, N, K, st)) return rc;
-  return uk::gemm_f32_tc_run(A, workspace, (uint8_t*)workspace + bb, C, M, N, K, st);
+  return uk::gemm_f32_tc_run(A, workspace, (uint8_t*)workspace + bb, C, M, N, K, st,
+                             (float*)((uint8_t*)workspace + need), workspace_bytes - need);
 }
 
 // ---- fp16 convolution -------------------------------------------------------------
@@ -1191,9 +1326,17 @@ int encode_h(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
 
 extern "C" size_t uk_cuda_conv2d_f16_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad,
                                                     int layout) {
-  (void)pad;
-  if (layout != UK_CONV_NCHW || N <= 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0) return 0;
-  return align256((size_t)N * H * W * C * 2) + align256((size_t)Oc * Kh * Kw * C * 2);
+  if ((layout != UK_CONV_NCHW && layout != UK_CONV_KML) || N <= 0 || H <= 0 || W <= 0 || C <= 0 || C % 64 != 0 ||
+      Kh <= 0 || Kw <= 0 || Oc <= 0 || pad < 0)
+    return 0;
+  const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
+  if (Ho <= 0 || Wo <= 0) return 0;
+  // NCHW: the NHWC copy and the permuted weights; both layouts: the last
+  // round's split partial tiles (the KML layout runs without a workspace too)
+  const size_t base = layout == UK_CONV_NCHW
+                          ? align256((size_t)N * H * W * C * 2) + align256((size_t)Oc * Kh * Kw * C * 2)
+                          : 0;
+  return base + tail_bytes(pair_tiles(N, Ho, Wo, Oc), Kh * Kw * (C / PairF16::BKE));
 }
 
 extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_t* Y, int N, int H, int W, int C,
@@ -1219,8 +1362,14 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
     if (int rc = uk::check_device_ptr(scale, "scale")) return rc;
   const uint16_t* Xn = X;   // NHWC input
   const uint16_t* Wk = Wt;  // [Oc][kh][kw][c] weights
+  float* part = (float*)workspace;  // the split partial tiles, after the NCHW layout's copies
+  size_t part_room = workspace != nullptr ? workspace_bytes : 0;
+  if (workspace != nullptr && !uk::aligned16(workspace))
+    return uk::fail(UK_EINVAL, "conv2d_f16: the workspace must be 16-byte aligned");
+  if (workspace != nullptr)
+    if (int rc = uk::check_device_ptr(workspace, "workspace")) return rc;
   if (layout == UK_CONV_NCHW) {
-    const size_t need = uk_cuda_conv2d_f16_workspace_size(N, H, W, C, Kh, Kw, Oc, pad, layout);
+    const size_t need = align256((size_t)N * H * W * C * 2) + align256((size_t)Oc * Kh * Kw * C * 2);
     if (workspace == nullptr || workspace_bytes < need)
       return uk::fail(UK_EINVAL, "conv2d_f16: needs a %zu-byte workspace (uk_cuda_conv2d_f16_workspace_size), got %zu",
                       need, workspace ? workspace_bytes : (size_t)0);
@@ -1253,6 +1402,8 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
     if (int rc = uk::check_launch("conv2d_f16(pre-pass)")) return rc;
     Xn = Xt;
     Wk = Wp;
+    part = (float*)((uint8_t*)workspace + need);
+    part_room = workspace_bytes - need;
   } else if (!uk::aligned16(X) || !uk::aligned16(Wt)) {
     return uk::fail(UK_EINVAL, "conv2d_f16: X and Wt must be 16-byte aligned");
   }
@@ -1285,6 +1436,8 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
   const int64_t tiles = (int64_t)N * p.tiles_h * p.tiles_w * p.tiles_oc;
   if (tiles > 2147483647LL) return uk::fail(UK_EINVAL, "conv2d_f16: too many tiles");
   p.num_tiles = (int)tiles;
+  const TailPlan tp = tail_plan(tiles, Kh * Kw * (C / PairF16::BKE), workspace != nullptr ? part_room : 0);
+  apply_tail(p, tp, part);
 
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -1295,9 +1448,8 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
       return uk::check_launch("conv2d_f16: smem attribute");
     attr_done[dev] = true;
   }
-  const int pairs = p.num_tiles < uk::sm_count() / 2 ? p.num_tiles : uk::sm_count() / 2;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.gridDim = dim3((unsigned)(2 * tp.pairs), 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = pair_smem_bytes<PairF16>();
   cfg.stream = st;
@@ -1310,5 +1462,10 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_pair<PairF16>, tx, tx, tw, tw, p);
   if (e != cudaSuccess) return uk::fail(UK_ECUDA, "conv2d_f16: launch: %s", cudaGetErrorString(e));
+  if (tp.splits >= 2) {
+    const int64_t total = (int64_t)(p.num_tiles - p.num_full) * 2 * BN * 128;
+    const int64_t g = std::min<int64_t>((total + 255) / 256, (int64_t)uk::sm_count() * 8);
+    k_conv_tail<__half><<<(unsigned)g, 256, 0, st>>>(p);
+  }
   return uk::check_launch("conv2d_f16(tcgen05 pair)");
 }

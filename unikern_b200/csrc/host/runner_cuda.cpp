@@ -136,7 +136,7 @@ struct OpCall {
         if (f16)  // fp16: kind::f16 tensor cores, the KML input read in place
           return uk_cuda_conv2d_f16((const uint16_t*)in0, (const uint16_t*)in1, (uint16_t*)out, 1, (int)d[0],
                                     (int)d[1], (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML,
-                                    nullptr, 0, st);
+                                    ws, ws_bytes, st);
         // fp32: tensor cores when C % 32 == 0 (workspace sized for it), else FFMA
         return uk_cuda_conv2d_f32_ws((const float*)in0, (const float*)in1, (float*)out, 1, (int)d[0], (int)d[1],
                                      (int)d[2], (int)d[3], (int)d[4], (int)d[5], 0, nullptr, UK_CONV_KML, ws,
@@ -202,9 +202,11 @@ bool stage_operands(OpCall* c, DevArena* ar, cudaStream_t st, std::string* err) 
                                : uk_cuda_reduce_workspace_size(1, c->d[0]);
   if (c->op == OpKind::Gemm && c->tc32)
     c->ws_bytes = uk_cuda_gemm_f32_workspace_size((int)c->d[0], (int)c->d[1], (int)c->d[2]);
-  if (c->op == OpKind::Conv && !c->f16)
-    c->ws_bytes = uk_cuda_conv2d_workspace_size(1, (int)c->d[0], (int)c->d[1], (int)c->d[2], (int)c->d[3],
-                                                (int)c->d[4], (int)c->d[5], 0, UK_CONV_KML);
+  if (c->op == OpKind::Conv)
+    c->ws_bytes = c->f16 ? uk_cuda_conv2d_f16_workspace_size(1, (int)c->d[0], (int)c->d[1], (int)c->d[2],
+                                                             (int)c->d[3], (int)c->d[4], (int)c->d[5], 0, UK_CONV_KML)
+                         : uk_cuda_conv2d_workspace_size(1, (int)c->d[0], (int)c->d[1], (int)c->d[2], (int)c->d[3],
+                                                         (int)c->d[4], (int)c->d[5], 0, UK_CONV_KML);
   if (c->ws_bytes) c->ws = ar->alloc(c->ws_bytes, "workspace");
   if (!ar->err.empty()) {
     *err = ar->err;
@@ -543,6 +545,9 @@ RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, co
                     : tree.op == OpKind::Conv && tree.dtype == DType::F32
                         ? uk_cuda_conv2d_workspace_size(1, tree.dims[0], tree.dims[1], tree.dims[2], tree.dims[3],
                                                         tree.dims[4], tree.dims[5], 0, UK_CONV_KML)
+                    : tree.op == OpKind::Conv
+                        ? uk_cuda_conv2d_f16_workspace_size(1, tree.dims[0], tree.dims[1], tree.dims[2], tree.dims[3],
+                                                            tree.dims[4], tree.dims[5], 0, UK_CONV_KML)
                     : timed.tc32 ? uk_cuda_gemm_f32_workspace_size(tree.dims[0], tree.dims[1], tree.dims[2])
                                  : 0;
   const int64_t payload = payload_bytes(tree, ws);

@@ -27,7 +27,8 @@ namespace uk {  // the tensor-core fp32 GEMM's stages (conv_tc.cu)
 size_t gemm_f32_tc_b_bytes(int N, int K);
 size_t gemm_f32_tc_a_bytes(int M, int K);
 int gemm_f32_tc_prep_b(const float* B, void* bws, int N, int K, cudaStream_t st);
-int gemm_f32_tc_run(const float* A, const void* bws, void* aws, float* C, int M, int N, int K, cudaStream_t st);
+int gemm_f32_tc_run(const float* A, const void* bws, void* aws, float* C, int M, int N, int K, cudaStream_t st,
+                    float* part, size_t part_room);
 }  // namespace uk
 
 namespace {
@@ -221,7 +222,7 @@ int streamed_block_gemms(const RingLayout& L, void* dB, uint8_t* base, int M, in
     const int rc = f16 ? uk_cuda_gemm_f16_ld((const uint16_t*)a, K, (const uint16_t*)dB, N, (uint16_t*)c, N, nr, N,
                                              K, st)
                    : L.tc ? uk::gemm_f32_tc_run((const float*)a, b_split, b_split + L.b_split, (float*)c, nr, N, K,
-                                                st)
+                                                st, nullptr, 0)
                           : uk_cuda_gemm_f32((const float*)a, (const float*)dB, (float*)c, nr, N, K, st);
     if (rc != UK_OK) return rc;
   }
@@ -293,7 +294,7 @@ extern "C" int uk_cuda_gemm_streamed(const void* hA, const void* hB, void* hC, v
     const int rc = f16 ? uk_cuda_gemm_f16_ld((const uint16_t*)a_buf[slot], K, (const uint16_t*)dB, N,
                                              (uint16_t*)c_buf[slot], N, (int)nr, N, K, stream)
                    : L.tc ? uk::gemm_f32_tc_run((const float*)a_buf[slot], b_split, a_split, (float*)c_buf[slot],
-                                                (int)nr, N, K, st)
+                                                (int)nr, N, K, st, nullptr, 0)
                           : uk_cuda_gemm_f32((const float*)a_buf[slot], (const float*)dB, (float*)c_buf[slot],
                                              (int)nr, N, K, stream);
     if (rc != UK_OK) return rc;
