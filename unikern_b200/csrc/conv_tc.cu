@@ -682,9 +682,17 @@ __global__ void __launch_bounds__(256) k_conv_tail(const ConvTc p) {
     if (ho >= p.Ho || wo >= p.Wo || oc >= p.Oc) continue;
     const float* src = p.part + ((size_t)((size_t)tt * p.splits * 2 + crank) * BN + ocl) * 128 + m;
     const size_t step = (size_t)2 * BN * 128;  // from one split's partial tile to the next
+    // the loads are independent (only the adds are ordered): 8 in flight
     float v = 0.f;
-#pragma unroll 4
-    for (int sidx = 0; sidx < p.splits; ++sidx) v += src[(size_t)sidx * step];
+    int sidx = 0;
+    for (; sidx + 8 <= p.splits; sidx += 8) {
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = __ldcs(src + (size_t)(sidx + u) * step);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v += t[u];
+    }
+    for (; sidx < p.splits; ++sidx) v += __ldcs(src + (size_t)sidx * step);
     out_store(Y + (((int64_t)n * p.Oc + oc) * p.Ho + ho) * p.Wo + wo, scale != nullptr ? v * out_scale(scale, oc) : v);
   }
 }
