@@ -76,6 +76,17 @@ def _hcs_with_vram(mib):
     return json.dumps(h)
 
 
+def test_streamed_fp32_picks_the_tensor_core_ring_when_it_fits():
+    # fp32 blocks of >= 2^30 multiply-adds take the split-tf32 tensor cores,
+    # whose ring also holds B^T's tf32 pairs; a tighter device tier falls
+    # back to the smaller FFMA ring
+    kml = '{"op":"gemm","dtype":"fp32","dims":[8192,1024,1024]}'
+    roomy = abi.kml_describe(kml, _hcs_with_vram(64))["placement"]
+    tight = abi.kml_describe(kml, _hcs_with_vram(40))["placement"]
+    assert "placement: streamed" in roomy and "split-tf32 tensor cores" in roomy
+    assert "placement: streamed" in tight and "FFMA" in tight
+
+
 @pytest.mark.parametrize("kml,mib,want", [
     ('{"op":"gemm","dtype":"fp16","dims":[4096,1024,1024]}', 16, "streamed"),   # 18 MiB > 0.85 x 16
     ('{"op":"gemm","dtype":"fp16","dims":[1024,1024,1024]}', 16, "resident"),   # 6 MiB fits
