@@ -11,8 +11,12 @@
 //      CUDA events on one stream; warm/iters as the reference (2/10, or 1/1
 //      when the payload exceeds 2 GiB; the fp16 gemm and the row ops warm once);
 //   3. the UNIKERN_RESULT line with the reference's tokens.
-// Resident only: a payload above 0.85 x the device's own reported memory is
-// refused (supports_streaming() is false), never silently streamed.
+// A payload above 0.85 x the device budget (the HCS's device tier, capped by
+// the device's own reported memory) runs streamed when it is a GEMM whose B
+// fits beside a ring of row blocks (scenario B: verified through the ring,
+// mode=streamed on the result line); anything else is refused with
+// stream_refused.  The file also holds the solver, the TAB file ledger and
+// calibration.
 #include "runner_cuda.hpp"
 
 #include <cuda_runtime.h>
