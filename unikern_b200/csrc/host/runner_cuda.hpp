@@ -8,8 +8,12 @@
 //                           src/runner_ocl.cpp (verify instance, warm/iters,
 //                           e2e and kernel-only spans, result line :834-841)
 //   BackendNvidia ......... IBackend, include/unikern/components.hpp:14-33
-//   FileLedger ............ src/runtime.cpp:20-170 (TAB rows, #VIOLATION events)
+//   FileLedger ............ src/runtime.cpp:20-170 (TAB rows, #VIOLATION events,
+//                           measured_rows :100-128)
 //   run flow .............. cmd_run, src/main.cpp:346-570
+//   scenario B ............ src/codegen_hip.cpp:1143-1238, :1485-1500
+//   calibrate ............. cmd_calibrate, src/main.cpp:573-652;
+//                           calibrated_link_bw, src/solver.cpp:188-245
 #pragma once
 
 #include <optional>
