@@ -21,6 +21,7 @@ _EMIT = None
 f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
 u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 I, L64 = C.c_int, C.c_int64
 
 
@@ -46,6 +47,7 @@ def lib():
             "or_conv_f64": (None, [f32p, f32p, f64p, I, I, I, I, I, I, I]),
             "or_conv_nchw_f64": (None, [f32p, f32p, C.c_void_p, f64p] + [I] * 11),
             "or_conv_nchw_f32": (None, [f32p, f32p, C.c_void_p, f32p] + [I] * 11),
+            "or_conv_nchw_points_f64": (None, [f32p, f32p, C.c_void_p, i32p, I, f64p] + [I] * 7),
             "or_reduce_f32": (C.c_float, [f32p, L64]),
             "or_reduce_blocked_f32": (C.c_float, [f32p, L64, I]),
             "or_reduce_f64": (C.c_double, [f32p, L64]),
@@ -85,6 +87,9 @@ def ref():
         l.ref_emit_program.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, I]
         l.ref_workload.argtypes = [C.c_char_p, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]
         l.ref_solve_tile.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(I), C.POINTER(I)]
+        l.ref_ledger_lookup.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, I]
+        l.ref_ledger_commit.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, C.c_double, C.c_double]
+        l.ref_ledger_counts.argtypes = [C.c_char_p, C.POINTER(I)]
         _REF = l
     return _REF
 
@@ -230,6 +235,23 @@ def conv_nchw(x, w, s, pad, images=None, threads=None, f32=False):
     fn(x.reshape(-1), w.reshape(-1), sp, y.reshape(-1), N, Cc, H, W, Oc, Kh, Kw, pad,
        n0, n1, threads or nthreads())
     return y
+
+
+def conv_nchw_points_f64(x, w, s, pad, pts):
+    """f64 outputs y[n][oc][ho][wo] of the NCHW conv at the (n, oc, ho, wo)
+    rows of `pts` (the loop of or_conv_nchw_f64, src/reference.cpp:6-22)."""
+    x, w = _c(x, np.float32), _c(w, np.float32)
+    _, Cc, H, W = x.shape
+    Oc, _, Kh, Kw = w.shape
+    pts = np.ascontiguousarray(pts, np.int32).reshape(-1, 4)
+    out = np.zeros(len(pts), np.float64)
+    sp = None
+    if s is not None:
+        s = _c(s, np.float32)
+        sp = s.ctypes.data
+    lib().or_conv_nchw_points_f64(x.reshape(-1), w.reshape(-1), sp, pts.reshape(-1), len(pts), out, Cc, H, W, Oc,
+                                  Kh, Kw, pad)
+    return out
 
 
 def reduce_f32(x):

@@ -10,6 +10,7 @@
 
 #include <math.h>
 #include <stddef.h>
+#include <stdlib.h>
 #include <string.h>
 
 #ifdef _OPENMP
@@ -84,37 +85,45 @@ void or_gemm_f64(const float* A, const float* B, double* C, int M, int N, int K,
 }
 
 /* src/codegen_hip.cpp:1851-1862: the reference quantises to half on the host,
- * widens back with __half2float and hands the widened values to cpu_ref. */
+ * widens back with __half2float and hands the widened values to cpu_ref.
+ * Each C element is one fp32 accumulator fed the products A[i][k]*B[k][j] in
+ * ascending k, exactly cpu_ref's sequence; the loops run i -> k -> j over a
+ * row of accumulators (so B streams by rows, widened to fp32 once), which
+ * leaves every element's operation sequence, and so its bits, unchanged. */
+#define UK_GEMM_F16_ROWS(ACC_T)                                                      \
+  float* Bf = (float*)malloc((size_t)K * N * sizeof(float));                         \
+  if (!Bf) return;                                                                    \
+  for (size_t t = 0; t < (size_t)K * N; ++t) Bf[t] = or_f16_to_f32(B[t]);            \
+  UK_OMP_FOR(threads)                                                                 \
+  for (int i = row0; i < row1; ++i) {                                                 \
+    ACC_T* acc = C + (size_t)i * N;                                                   \
+    for (int j = 0; j < N; ++j) acc[j] = 0;                                           \
+    for (int k = 0; k < K; ++k) {                                                     \
+      const ACC_T a = (ACC_T)or_f16_to_f32(A[(size_t)i * K + k]);                     \
+      const float* b = Bf + (size_t)k * N;                                            \
+      for (int j = 0; j < N; ++j) acc[j] += a * (ACC_T)b[j];                          \
+    }                                                                                 \
+  }                                                                                   \
+  free(Bf);
+
+#ifdef _OPENMP
+#define UK_PRAGMA(x) _Pragma(#x)
+#define UK_OMP_FOR(t) UK_PRAGMA(omp parallel for schedule(dynamic, 1) num_threads(UK_NT(t)))
+#else
+#define UK_OMP_FOR(t)
+#endif
+
 void or_gemm_f16(const uint16_t* A, const uint16_t* B, float* C, int M, int N,
                  int K, int row0, int row1, int threads) {
   (void)M;
-#ifdef _OPENMP
-#pragma omp parallel for schedule(dynamic, 1) num_threads(UK_NT(threads))
-#endif
-  for (int i = row0; i < row1; ++i)
-    for (int j = 0; j < N; ++j) {
-      float s = 0.f;
-      for (int k = 0; k < K; ++k)
-        s += or_f16_to_f32(A[(size_t)i * K + k]) * or_f16_to_f32(B[(size_t)k * N + j]);
-      C[(size_t)i * N + j] = s;
-    }
+  UK_GEMM_F16_ROWS(float)
   (void)threads;
 }
 
 void or_gemm_f16_f64(const uint16_t* A, const uint16_t* B, double* C, int M,
                      int N, int K, int row0, int row1, int threads) {
   (void)M;
-#ifdef _OPENMP
-#pragma omp parallel for schedule(dynamic, 1) num_threads(UK_NT(threads))
-#endif
-  for (int i = row0; i < row1; ++i)
-    for (int j = 0; j < N; ++j) {
-      double s = 0.0;
-      for (int k = 0; k < K; ++k)
-        s += (double)or_f16_to_f32(A[(size_t)i * K + k]) *
-             (double)or_f16_to_f32(B[(size_t)k * N + j]);
-      C[(size_t)i * N + j] = s;
-    }
+  UK_GEMM_F16_ROWS(double)
   (void)threads;
 }
 
@@ -233,6 +242,27 @@ void or_conv_nchw_f64(const float* x, const float* w, const float* s, double* y,
   (void)threads;
   UK_CONV_NCHW_BODY(double)
 #endif
+}
+
+void or_conv_nchw_points_f64(const float* x, const float* w, const float* s, const int* pts, int npts,
+                             double* out, int C, int H, int W, int Oc, int Kh, int Kw, int pad) {
+  (void)Oc;
+  for (int i = 0; i < npts; ++i) {
+    const int n = pts[4 * i], oc = pts[4 * i + 1], ho = pts[4 * i + 2], wo = pts[4 * i + 3];
+    double acc = 0;
+    for (int c = 0; c < C; ++c)
+      for (int kh = 0; kh < Kh; ++kh) {
+        const int hi = ho + kh - pad;
+        if (hi < 0 || hi >= H) continue;
+        for (int kw = 0; kw < Kw; ++kw) {
+          const int wi = wo + kw - pad;
+          if (wi < 0 || wi >= W) continue;
+          acc += (double)x[(((size_t)n * C + c) * H + hi) * W + wi] *
+                 (double)w[(((size_t)oc * C + c) * Kh + kh) * Kw + kw];
+        }
+      }
+    out[i] = acc * (s ? (double)s[oc] : 1.0);
+  }
 }
 
 void or_conv_nchw_f32(const float* x, const float* w, const float* s, float* y,

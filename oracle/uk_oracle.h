@@ -81,6 +81,11 @@ void or_conv_f64(const float* x, const float* wt, double* y, int H, int W,
 void or_conv_nchw_f64(const float* x, const float* w, const float* s, double* y,
                       int N, int C, int H, int W, int Oc, int Kh, int Kw,
                       int pad, int n0, int n1, int threads);
+/* The f64 yardstick of or_conv_nchw_f64 at `npts` single output points
+ * pts[4 * i .. 4 * i + 3] = (n, oc, ho, wo) -> out[i]; for sampled checks of
+ * full-batch runs whose every image would take too long on the host. */
+void or_conv_nchw_points_f64(const float* x, const float* w, const float* s, const int* pts, int npts,
+                             double* out, int C, int H, int W, int Oc, int Kh, int Kw, int pad);
 /* same, fp32 accumulator in the reference's c->kh->kw order (timing arm) */
 void or_conv_nchw_f32(const float* x, const float* w, const float* s, float* y,
                       int N, int C, int H, int W, int Oc, int Kh, int Kw,

@@ -1,7 +1,9 @@
 """Worker for tests/test_gpu_multi.py (launched by torchrun, one rank per GPU):
 the batch-sharded conv with the NCCL all-gather of Y must leave on every rank
 the same full Y, bit for bit, as a single-GPU run of the same kernel over the
-whole batch."""
+whole batch (to the fp32 gate: see below), and images of every rank's shard
+must agree with the fp64 oracle of the reference's cpu_conv
+(src/reference.cpp:6-22) on every rank."""
 import datetime
 import os
 import sys
@@ -13,6 +15,7 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 import unikern_b200.abi as abi  # noqa: E402
+from oracle import oracle as O  # noqa: E402
 from unikern_b200 import shard  # noqa: E402
 
 
@@ -43,6 +46,14 @@ def main():
         # tile count: a different grouping in the tensor cores' accumulator
         # there (~2e-5 of the output scale), so the fp32 gate, not bitwise
         ok = ok and rel <= 1e-4 and not torch.isnan(Y).any().item()
+        # the first and last image (different ranks' shards) against fp64
+        xs, ws_, ss = x.cpu().numpy(), w.cpu().numpy(), s.cpu().numpy()
+        Yh = Y.cpu().numpy()
+        for n in sorted({0, N - 1}):
+            ref_n = O.conv_nchw(xs[n:n + 1], ws_, ss, pad)
+            err = O.rel_err(Yh[n:n + 1], ref_n, O.rms(ref_n))
+            print("rank %d conv image %d vs f64: %.3e" % (rank, n, err), flush=True)
+            ok = ok and err <= 1e-4
         dist.barrier()
     dist.destroy_process_group()
     return 0 if ok else 1

@@ -2,7 +2,9 @@
 the decode layer with its weight columns sharded over the ranks and the
 all-gather fused into the GEMM's store must leave on every rank the full
 Y[B][N] of a single-GPU run (up to f16 rounding: the K split of a narrow
-shard sums in a different order)."""
+shard sums in a different order), and that Y must agree on every rank with
+the fp64 oracle of the op-by-op chain (the reference's fp32 RMSNorm rounded to
+f16, then the product in fp64) within the f16 GEMM gate."""
 import datetime
 import os
 import sys
@@ -13,7 +15,10 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
+import numpy as np  # noqa: E402
+
 import unikern_b200.abi as abi  # noqa: E402
+from oracle import oracle as O  # noqa: E402
 from unikern_b200 import shard  # noqa: E402
 
 
@@ -43,6 +48,13 @@ def main():
         print("rank %d decode %dx%dx%d max|Y - single GPU| = %g (of %g) fault=%d" % (rank, B, K, N, diff, scale,
                                                                                    fault), flush=True)
         ok = ok and diff <= 2e-3 * scale and fault == 0 and not torch.isnan(Y.float()).any().item()
+        Wh = W.cpu().view(torch.int16).numpy().view(np.uint16)
+        ref = O.gemm_f16_f64(O.f32_to_f16(O.rmsnorm_f32(X.cpu().numpy(), gamma.cpu().numpy(), 1e-5)), Wh,
+                             threads=O.nthreads())
+        got = O.f16_to_f32(Y.cpu().view(torch.int16).numpy().view(np.uint16))
+        err = O.rel_err(got, ref, O.rms(ref))
+        print("rank %d decode %dx%dx%d full Y vs f64: %.3e" % (rank, B, K, N, err), flush=True)
+        ok = ok and err <= 2e-2
         dist.barrier()
         plan.close()
         del Y

@@ -1,6 +1,10 @@
 """Worker for tests/test_gpu_multi.py (launched by torchrun, one rank per GPU):
-the N-sharded f16 GEMM with the fused all-gather must leave the same full C
-on every rank as a single-GPU GEMM of the same inputs."""
+the N-sharded f16 GEMM with the fused all-gather must leave on every rank
+(1) the same full C as a single-GPU GEMM of the same inputs, bit for bit, and
+(2) a C whose sampled full rows (every rank's column block) agree with the
+fp64 oracle of the half inputs within the f16 gate, and within 2x of the
+reference algorithm's own error (src/codegen_hip.cpp:1851-1862).  The last
+case is BASELINE configs[3] itself: 8192^3 with A, B ~ N(0, 0.02)."""
 import datetime
 import os
 import sys
@@ -11,8 +15,27 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
+import numpy as np  # noqa: E402
+
 import unikern_b200.abi as abi  # noqa: E402
+from oracle import oracle as O  # noqa: E402
 from unikern_b200 import shard  # noqa: E402
+
+F16_TOL = 2e-2
+
+
+def host_f16(t):
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def oracle_rows(A, B, C, rows):
+    """(error of C's rows vs f64, error of the reference algorithm vs f64)."""
+    Ah, Bh = host_f16(A), host_f16(B)
+    got = O.f16_to_f32(host_f16(C)[rows])
+    ref = O.gemm_f16_f64(Ah[rows], Bh, threads=O.nthreads())
+    algo = O.f16_to_f32(O.f32_to_f16(O.gemm_f16(Ah[rows], Bh, threads=O.nthreads())))
+    tau = O.rms(ref)
+    return O.rel_err(got, ref, tau), O.rel_err(algo, ref, tau)
 
 
 def main():
@@ -21,11 +44,12 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", int(os.environ["LOCAL_RANK"])))
     ok = True
-    for (M, N, K) in [(1024, 2048, 512), (384, 1000, 264), (8192, 8192, 1024)]:
+    for (M, N, K, sd) in [(1024, 2048, 512, 0.5), (384, 1000, 264, 0.5), (8192, 8192, 1024, 0.5),
+                          (8192, 8192, 8192, 0.02)]:
         g = torch.Generator(device="cuda")
         g.manual_seed(M + N + K)
-        A = (torch.randn((M, K), generator=g, device="cuda") * 0.5).half()
-        B = (torch.randn((K, N), generator=g, device="cuda") * 0.5).half()
+        A = (torch.randn((M, K), generator=g, device="cuda") * sd).half()
+        B = (torch.randn((K, N), generator=g, device="cuda") * sd).half()
         C = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
         plan = shard.GemmAllGather(C, M, N, K)
         for _ in range(2):
@@ -35,8 +59,11 @@ def main():
         torch.cuda.synchronize()
         diff = (C.float() - ref.float()).abs().max().item()
         fault = abi.lib().uk_cuda_pipeline_fault()
-        print("rank %d %dx%dx%d max|C - single GPU| = %g fault=%d" % (rank, M, N, K, diff, fault), flush=True)
-        ok = ok and diff == 0.0 and fault == 0
+        rows = np.unique(np.random.default_rng(rank * 7 + M).choice(M, min(M, 16), replace=False))
+        err, err_algo = oracle_rows(A, B, C, rows)
+        print("rank %d %dx%dx%d max|C - single GPU| = %g fault=%d; %d full rows vs f64: %.3e (reference "
+              "algorithm %.3e)" % (rank, M, N, K, diff, fault, len(rows), err, err_algo), flush=True)
+        ok = ok and diff == 0.0 and fault == 0 and err <= F16_TOL and err <= 2.0 * err_algo
         dist.barrier()
         plan.close()
         del C

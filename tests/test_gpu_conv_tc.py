@@ -6,7 +6,8 @@ gate as the FFMA kernel: rel_err <= 1e-4 with the output-scale floor.
 Shapes cover both layouts, channel counts that are multiples of 32 (the
 tensor-core path), output widths above the 64-pixel tile, more than 256
 output channels (two channel tiles), 1x1 and 3x3 filters, padding 0 and 1,
-and the full BASELINE configuration.  Shapes the tensor cores do not take
+and the KML BASELINE declaration (the full NCHW BASELINE batch is in
+tests/test_gpu_baseline_parity.py).  Shapes the tensor cores do not take
 (C not a multiple of 32) must run the FFMA kernel and give its bits.
 """
 import numpy as np
@@ -116,18 +117,3 @@ def test_conv_tc_missing_workspace_is_refused():
     rc = abi.lib().uk_cuda_conv2d_f32_ws(x.data_ptr(), w.data_ptr(), y.data_ptr(), 1, 8, 8, 32, 3, 3, 8, 1, None,
                                          abi.UK_CONV_NCHW, None, 0, None)
     assert rc == 2 and "workspace" in abi.lib().uk_cuda_last_error().decode()
-
-
-def test_conv_tc_baseline_shape_sampled_images():
-    # N=32, 256->256, 56x56, 3x3, pad 1, channel scale;
-    # the full batch on the GPU, two images checked in full against fp64
-    N, Cc, H, W, Oc = 32, 256, 56, 56, 256
-    rng = np.random.default_rng(2024)
-    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
-    w = rng.normal(0, np.sqrt(2.0 / (9 * 256)), (Oc, Cc, 3, 3)).astype(np.float32)
-    s = rng.uniform(0.5, 1.5, Oc).astype(np.float32)
-    got = run_nchw(x, w, s, 1)
-    for n in (0, 31):
-        ref = O.conv_nchw(x[n:n + 1], w, s, 1)
-        assert O.rel_err(got[n:n + 1], ref, SUM_TAU * O.rms(ref)) <= F32_TOL
-    assert abi.lib().uk_cuda_pipeline_fault() == 0

@@ -39,9 +39,14 @@ def test_gemm_f32_vs_f64(M, N, K):
     B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
     ref = O.gemm_f64(A, B, threads=8)
     tau = SUM_TAU * O.rms(ref)
-    assert O.rel_err(gemm32(A, B), ref, tau) <= F32_TOL
+    err = O.rel_err(gemm32(A, B), ref, tau)
+    assert err <= F32_TOL
     # the gate is one the reference's own fp32 loop passes
-    assert O.rel_err(O.gemm_f32(A, B, threads=8), ref, tau) <= F32_TOL
+    err_ref = O.rel_err(O.gemm_f32(A, B, threads=8), ref, tau)
+    assert err_ref <= F32_TOL
+    # and, tighter, within 4x of that loop's own error (floor 1e-6 of the
+    # output scale for the shapes where the reference's sums are near exact)
+    assert err <= max(4.0 * err_ref, 1e-6), (err, err_ref)
 
 
 def test_gemm_f32_k0_writes_zeros():
@@ -70,7 +75,13 @@ def test_gemm_f16_vs_f64(M, N, K):
     A = O.f32_to_f16(rng.normal(0, 0.02, (M, K)).astype(np.float32) * 25)
     B = O.f32_to_f16(rng.normal(0, 0.02, (K, N)).astype(np.float32) * 25)
     ref = O.gemm_f16_f64(A, B, threads=8)
-    assert O.rel_err(gemm16(A, B), ref, SUM_TAU * O.rms(ref)) <= F16_TOL
+    tau = SUM_TAU * O.rms(ref)
+    err = O.rel_err(gemm16(A, B), ref, tau)
+    assert err <= F16_TOL
+    # tighter: within 2x of the reference algorithm's own error (fp32 sum,
+    # one f16 rounding: half an f16 ulp)
+    err_ref = O.rel_err(O.f16_to_f32(O.f32_to_f16(O.gemm_f16(A, B, threads=8))), ref, tau)
+    assert err <= 2.0 * err_ref, (err, err_ref)
 
 
 # ---- conv --------------------------------------------------------------------
@@ -109,19 +120,3 @@ def test_conv_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):
     abi.conv2d(dev(x), dev(w), y, N, H, W, Cc, K, K, Oc, pad, dev(s) if scaled else None, abi.UK_CONV_NCHW)
     ref = O.conv_nchw(x, w, s, pad)
     assert O.rel_err(host(y), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
-
-
-def test_conv_nchw_baseline_shape_sampled_images():
-    # the BASELINE configuration (N=32, 256->256, 56x56, 3x3, pad 1, scale):
-    # full-size run on the GPU, two images checked in full against f64
-    N, Cc, H, W, Oc = 32, 256, 56, 56, 256
-    rng = np.random.default_rng(2024)
-    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
-    w = rng.normal(0, np.sqrt(2.0 / (9 * 256)), (Oc, Cc, 3, 3)).astype(np.float32)
-    s = rng.uniform(0.5, 1.5, Oc).astype(np.float32)
-    y = empty((N, Oc, H, W))
-    abi.conv2d(dev(x), dev(w), y, N, H, W, Cc, 3, 3, Oc, 1, dev(s), abi.UK_CONV_NCHW)
-    got = host(y)
-    for n in (0, 31):
-        ref = O.conv_nchw(x[n:n + 1], w, s, 1)
-        assert O.rel_err(got[n:n + 1], ref, SUM_TAU * O.rms(ref)) <= F32_TOL
