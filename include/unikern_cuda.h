@@ -110,8 +110,9 @@ int uk_cuda_reduce_f16_width(const uint16_t* X, uint16_t* Y, int64_t rows, int64
  * exits.  Limit: a shape whose plan needs more than 8192 partial sums is
  * rejected with UK_EINVAL (on a 148-SM B200 the plan never needs more than
  * about 1800, so every shape fits).  The first call on each device looks up
- * the array's device address with that device current; make that first call
- * before any stream capture.  All calls share the one array: calls that
+ * the array's device address with that device current (and looks it up again
+ * after that device's context changed, e.g. after cudaDeviceReset); make that
+ * first call before any stream capture.  All calls share the one array: calls that
  * overlap on the GPU (different streams, or threads, on the same device)
  * race and must be serialised, e.g. on one stream.  The array keeps the last
  * call's contents; nothing in it has to start at zero.
@@ -333,7 +334,7 @@ int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int 
  *   hcs_fingerprint / the ledger key (src/kml_front.cpp:75-251,
  *   src/kml.cpp:60-177, src/hcs.cpp:52-115, src/main.cpp:217-219).
  * uk_run_kml: import the HCS and the KML tree, look the ledger key up in the
- *   TAB-separated file ledger (a hit reuses the recorded tile), solve on a
+ *   ledger (a hit reuses the recorded tile), solve on a
  *   miss, run the tree on the current device (verify instance checked on the
  *   GPU in fp64 against the dtype's gate, then e2e and kernel-only timing at
  *   the declared dims), and commit a verified run when write_ledger != 0.
@@ -343,8 +344,24 @@ int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int 
  *   infeasible, 5 residency violation.  ledger_path may be NULL (no ledger).
  *   Replaces cmd_run's execute branch + run_ocl/run_hip (src/main.cpp:346-570,
  *   src/runner_ocl.cpp); allocates its own device and pinned buffers (this is
- *   the runner, not a hot call). */
+ *   the runner, not a hot call).
+ * Ledgers (both entry points, and uk_calibrate): a path ending in ".jsonl"
+ *   is the reference's TAB-separated file ledger (src/runtime.cpp:20-170);
+ *   any other path is an SQLite database with the reference's solutions /
+ *   violations tables, one row per key, each write in BEGIN IMMEDIATE ..
+ *   COMMIT (src/sqlite_ledger.cpp:44-133; the choice is src/main.cpp:61-70's).
+ *   The SQLite engine is the system's libsqlite3.so.0, loaded on first use;
+ *   without it a non-.jsonl path is refused with exit code 2.
+ * uk_solve_kml: `unikern solve`'s nvidia branch (src/main.cpp:276-343): the
+ *   gap check, a ledger lookup (LEDGER HIT reuses the recorded tile) or the
+ *   solver on `sms` multiprocessors (0 = the HCS's compute_units), and, when
+ *   write_ledger != 0, a solve-time row (measured_ms = c_ms, kernel_ms = 0; a
+ *   later run of the same key overwrites it).  Transcript (LEDGER HIT ... or
+ *   SOLVED  x* tile=MxN  c_ms=...) to out.  Returns 0, 2 bad input /
+ *   unsupported tree / ledger error, 3 infeasible.  No GPU needed. */
 int uk_kml_describe(const char* kml_json, const char* hcs_json, int sms, char* out, size_t out_cap);
+int uk_solve_kml(const char* hcs_json, const char* kml_json, const char* ledger_path, int write_ledger, int sms,
+                 char* out, size_t out_cap);
 int uk_run_kml(const char* hcs_json, const char* kml_json, const char* ledger_path, int write_ledger, char* out,
                size_t out_cap);
 

@@ -8,8 +8,10 @@ TEST INFRASTRUCTURE ONLY.  Outputs:
 * ``oracle/_ref/libukref.so``  -- the UNIKERN reference's own C++ sources
   (``src/reference.cpp``, ``src/kml.cpp``, ``src/kml_front.cpp``,
   ``src/json_flat.cpp``, ``src/runtime.cpp``, ``src/hcs.cpp``,
-  ``src/solver.cpp``, ``src/codegen_hip.cpp``) compiled unchanged with g++
-  straight from the reference tree, plus ``ref_shim.cpp`` (extern "C"
+  ``src/solver.cpp``, ``src/codegen_hip.cpp``, ``src/sqlite_ledger.cpp``)
+  compiled unchanged with g++ straight from the reference tree (the SQLite
+  ledger against the reference's vendored ``sqlite3.h``, linked to the
+  system's ``libsqlite3.so.0``), plus ``ref_shim.cpp`` (extern "C"
   forwarding only).  Nothing is copied into the repository.
 * ``oracle/_ref/libukemit.so``  -- the CPU reference functions that the
   reference embeds as text in its generated programs (gemm ``cpu_ref``,
@@ -17,8 +19,10 @@ TEST INFRASTRUCTURE ONLY.  Outputs:
   ``cpu_reduce_ref`` and the sawtooth initialisers), cut out of the program
   text that ``libukref.so`` emits and compiled on their own.
 
-The ``_ref`` libraries need the reference tree and are only built where it
-exists; they are git-ignored but travel with the snapshot.
+The ``_ref`` libraries need the reference tree, named by the environment
+variable ``UK_REFERENCE_TREE`` (the UNIKERN project root), and are only built
+where it is set and exists; they are git-ignored but travel with the
+snapshot.
 """
 from __future__ import annotations
 
@@ -32,11 +36,21 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
-REFERENCE = Path(os.environ.get("UK_REFERENCE_TREE", "/root/reference"))
+
+
+def reference_tree():
+    """The UNIKERN source tree named by UK_REFERENCE_TREE (its project root,
+    holding src/ and include/), or None: there is no default location."""
+    t = os.environ.get("UK_REFERENCE_TREE")
+    return Path(t) if t else None
+
 
 CFLAGS = ["-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-fopenmp"]
 REF_SOURCES = ["reference", "kml", "kml_front", "json_flat", "runtime", "hcs",
-               "solver", "codegen_hip"]
+               "solver", "codegen_hip", "sqlite_ledger"]
+# the reference's SQLite ledger is compiled against its vendored sqlite3.h and
+# linked to the system's SQLite library (the same engine the product loads)
+SQLITE_LIB = "-l:libsqlite3.so.0"
 
 
 def _run(cmd):
@@ -174,13 +188,14 @@ def _cut_function(text: str, name: str) -> str:
 
 def build_ref(force: bool = False) -> bool:
     """Compile the reference's sources (only where the reference tree exists)."""
-    src = REFERENCE / "src"
-    if not (src / "reference.cpp").exists():
+    REFERENCE = reference_tree()
+    if REFERENCE is None or not (REFERENCE / "src" / "reference.cpp").exists():
         return False
+    src = REFERENCE / "src"
     REF_OUT.mkdir(exist_ok=True)
     objdir = REF_OUT / "obj"
     objdir.mkdir(exist_ok=True)
-    inc = ["-I", str(REFERENCE / "include"), "-I", str(src)]
+    inc = ["-I", str(REFERENCE / "include"), "-I", str(src), "-I", str(REFERENCE / "third_party" / "sqlite")]
     objs = []
     for name in REF_SOURCES:
         s = src / (name + ".cpp")
@@ -192,7 +207,7 @@ def build_ref(force: bool = False) -> bool:
     lib = REF_OUT / "libukref.so"
     if force or _stale(lib, objs + [str(shim)]):
         _run(["g++", "-std=c++20", "-O2", "-ffp-contract=off", "-fPIC", "-shared", *inc,
-              str(shim), *objs, "-o", str(lib)])
+              str(shim), *objs, "-o", str(lib), SQLITE_LIB])
 
     emit_lib = REF_OUT / "libukemit.so"
     if not force and not _stale(emit_lib, [str(lib), __file__]):

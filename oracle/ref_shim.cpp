@@ -12,7 +12,11 @@
 //   hcs_import / hcs_fingerprint ................... src/hcs.cpp:52-115
 //   workload_of .................................... src/kml.cpp:125-177
 //   hip_runnable_program (emitted CPU references) .. src/codegen_hip.cpp:132
+//   make_file_ledger / make_sqlite_ledger .......... src/runtime.cpp,
+//     src/sqlite_ledger.cpp, chosen by suffix as src/main.cpp:61-70 does
+#include <cstdio>
 #include <cstring>
+#include <memory>
 #include <string>
 
 #include "unikern/codegen.hpp"
@@ -113,6 +117,68 @@ int ref_solve_tile(const char* kml_json, const char* hcs_json, int* tm, int* tn)
   *tm = s.best.tile_m;
   *tn = s.best.tile_n;
   return s.feasible_count;
+}
+
+namespace {
+std::unique_ptr<ILedger> open_ledger(const std::string& path) {
+  const std::string sfx = ".jsonl";
+  if (path.size() >= sfx.size() && path.compare(path.size() - sfx.size(), sfx.size(), sfx) == 0)
+    return make_file_ledger(path);
+  return make_sqlite_ledger(path);
+}
+Key key_of(const KmlTree& t, const Hcs& h) {
+  return Key{op_signature(t), hcs_fingerprint(h), fnv1a_hex(canonical_form(t))};
+}
+}  // namespace
+
+// The reference ledger's lookup of a tree's key: 1 hit (out gets
+// "c_ms tm tn placement"), 0 miss, -1 bad input or an unopenable ledger.
+int ref_ledger_lookup(const char* path, const char* kml_json, const char* hcs_json, char* out, int cap) {
+  auto t = kml_import(kml_json, nullptr);
+  auto h = hcs_import(hcs_json, nullptr);
+  if (!t || !h) return -1;
+  try {
+    auto l = open_ledger(path);
+    auto hit = l->lookup(key_of(*t, *h));
+    if (!hit) return 0;
+    char num[64];
+    std::snprintf(num, sizeof num, "%.17g", hit->c_ms);
+    put(std::string(num) + " " + std::to_string(hit->best.tile_m) + " " + std::to_string(hit->best.tile_n) + " " +
+            hit->placement_record,
+        out, cap);
+    return 1;
+  } catch (...) {
+    return -1;
+  }
+}
+
+// The reference's solve of the tree committed to its ledger: measured_ms < 0
+// commits a solve-time row (measured = c_ms, as cmd_solve does), otherwise a
+// run's row with the given measured / kernel times.  0 ok, -1 error.
+int ref_ledger_commit(const char* path, const char* kml_json, const char* hcs_json, double measured_ms,
+                      double kernel_ms) {
+  auto t = kml_import(kml_json, nullptr);
+  auto h = hcs_import(hcs_json, nullptr);
+  if (!t || !h) return -1;
+  try {
+    auto l = open_ledger(path);
+    const Solution s = solve(*h, *t);
+    l->commit(key_of(*t, *h), s, measured_ms < 0 ? s.c_ms : measured_ms, kernel_ms);
+    return 0;
+  } catch (...) {
+    return -1;
+  }
+}
+
+// rows (solutions) and violation events in the reference ledger's view; -1 error
+int ref_ledger_counts(const char* path, int* violations) {
+  try {
+    auto l = open_ledger(path);
+    *violations = l->violation_count();
+    return l->size();
+  } catch (...) {
+    return -1;
+  }
 }
 
 // The emitted AMD program text; its embedded CPU references are extracted by

@@ -1,7 +1,7 @@
 """Generate tests/golden/reference_vectors.npz from the UNIKERN reference itself.
 
-Run in a container that holds the reference tree (default /root/reference, or
-$UK_REFERENCE_TREE):  ``python tests/golden/make_golden.py``.
+Run where the reference tree is present, named by $UK_REFERENCE_TREE (the
+UNIKERN project root):  ``UK_REFERENCE_TREE=<tree> python tests/golden/make_golden.py``.
 
 Every output below is computed by the reference's own code, compiled by
 oracle/build.py straight from the reference sources:
@@ -127,7 +127,7 @@ def main():
     emit.emit_channelscale(X, S, Y, 6, 33)
     out.update(channelscale_X=X, channelscale_S=S, channelscale_Y=Y)
 
-    hcs = (obuild.REFERENCE / "samples" / "hcs_amd.json").read_text()
+    hcs = (obuild.reference_tree() / "samples" / "hcs_amd.json").read_text()
     kml = {"hcs_amd": hcs, "cases": []}
     for k in KML_CASES:
         rc, canon = O.ref_str(ref.ref_kml_check, k)

@@ -62,6 +62,7 @@ PROTOTYPES = {
     "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
+    "uk_solve_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, i32, C.c_char_p, sz]),
     "uk_calibrate": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz, C.c_char_p, sz]),
 }
 
@@ -312,6 +313,15 @@ def run_kml(hcs_json: str, kml_json: str, ledger: str | None = None, write_ledge
     buf = C.create_string_buffer(1 << 16)
     rc = lib().uk_run_kml(hcs_json.encode(), kml_json.encode(), ledger.encode() if ledger else None,
                           int(write_ledger), buf, len(buf))
+    return rc, buf.value.decode()
+
+
+def solve_kml(hcs_json: str, kml_json: str, ledger: str | None = None, write_ledger: bool = True, sms: int = 0):
+    """The nvidia branch of `unikern solve`: returns (exit code, transcript).
+    No GPU needed."""
+    buf = C.create_string_buffer(1 << 14)
+    rc = lib().uk_solve_kml(hcs_json.encode(), kml_json.encode(), ledger.encode() if ledger else None,
+                            int(write_ledger), sms, buf, len(buf))
     return rc, buf.value.decode()
 
 

@@ -522,9 +522,11 @@ std::string hcs_export(const Hcs& h) {
   return os.str();
 }
 
-std::string ledger_key(const Hcs& h, const KmlTree& t) {
-  return op_signature(t) + "|" + hcs_fingerprint(h) + "|" + fnv1a_hex(canonical_form(t));
+LedgerKey ledger_key_parts(const Hcs& h, const KmlTree& t) {
+  return LedgerKey{op_signature(t), hcs_fingerprint(h), fnv1a_hex(canonical_form(t))};
 }
+
+std::string ledger_key(const Hcs& h, const KmlTree& t) { return ledger_key_parts(h, t).str(); }
 
 double tolerance_for(DType d) { return d == DType::F16 ? 0.0625 : d == DType::I8 ? 0.0 : 0.03125; }
 

@@ -84,7 +84,13 @@ std::string hcs_fingerprint(const Hcs& h);
 // (src/hcs.cpp:117-148 of UNIKERN); calibration writes its HCS with it
 std::string hcs_export(const Hcs& h);
 
-// "op_sig|hcs_fp|tree_hash"
+// the ledger key (src/main.cpp:217-219): its three parts, and the composite
+// "op_sig|hcs_fp|tree_hash" both ledger formats file a row under
+struct LedgerKey {
+  std::string op_sig, hcs_fp, tree_hash;
+  std::string str() const { return op_sig + "|" + hcs_fp + "|" + tree_hash; }
+};
+LedgerKey ledger_key_parts(const Hcs& h, const KmlTree& t);
 std::string ledger_key(const Hcs& h, const KmlTree& t);
 
 // tolerance gate of the verify instance, by declared dtype (2^-5, 2^-4, 0)

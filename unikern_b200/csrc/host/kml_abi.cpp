@@ -1,6 +1,6 @@
 // kml_abi.cpp -- C entry points of the host runner (declared in
-// include/unikern_cuda.h): the KML contract queries (no GPU needed) and the
-// nvidia branch of the reference's `run`/`verify` flow.
+// include/unikern_cuda.h): the KML contract queries and `solve` (no GPU
+// needed), and the nvidia branch of the reference's `run`/`verify` flow.
 #include <cstring>
 #include <sstream>
 #include <string>
@@ -74,6 +74,19 @@ int uk_run_kml(const char* hcs_json, const char* kml_json, const char* ledger_pa
   }
   std::string transcript;
   const int rc = ukb::run_kml(hcs_json, kml_json, ledger_path ? ledger_path : "", write_ledger != 0, &transcript);
+  if (out != nullptr && out_cap > 0) put(transcript, out, out_cap);
+  return rc;
+}
+
+int uk_solve_kml(const char* hcs_json, const char* kml_json, const char* ledger_path, int write_ledger, int sms,
+                 char* out, size_t out_cap) {
+  if (hcs_json == nullptr || kml_json == nullptr) {
+    put("hcs_json and kml_json are required", out, out_cap);
+    return 2;
+  }
+  std::string transcript;
+  const int rc =
+      ukb::solve_kml(hcs_json, kml_json, ledger_path ? ledger_path : "", write_ledger != 0, sms, &transcript);
   if (out != nullptr && out_cap > 0) put(transcript, out, out_cap);
   return rc;
 }

@@ -368,103 +368,6 @@ Solution solve_b200(const Hcs& h, const KmlTree& t, int sms) {
   return s;
 }
 
-// ---- ledger --------------------------------------------------------------------
-
-namespace {
-const char kSep = '\t';
-const char* kViolation = "#VIOLATION";
-
-std::vector<std::string> split_tabs(const std::string& line) {
-  std::vector<std::string> f;
-  size_t pos = 0;
-  while (true) {
-    const size_t tab = line.find(kSep, pos);
-    f.push_back(line.substr(pos, tab == std::string::npos ? std::string::npos : tab - pos));
-    if (tab == std::string::npos) break;
-    pos = tab + 1;
-  }
-  return f;
-}
-}  // namespace
-
-std::optional<Solution> FileLedger::lookup(const std::string& key) const {
-  std::ifstream in(path_);
-  std::string line;
-  while (std::getline(in, line)) {
-    const std::vector<std::string> f = split_tabs(line);
-    if (f.size() < 4 || f[0] != key) continue;
-    Solution s;
-    try {
-      s.c_ms = std::stod(f[1]);
-      if (f.size() >= 7) {  // key c_ms measured kernel tm tn placement
-        s.best.tile_m = std::stoi(f[4]);
-        s.best.tile_n = std::stoi(f[5]);
-        s.placement_record = f[6];
-      } else if (f.size() >= 6) {  // key c_ms measured tm tn placement
-        s.best.tile_m = std::stoi(f[3]);
-        s.best.tile_n = std::stoi(f[4]);
-        s.placement_record = f[5];
-      } else {
-        s.placement_record = f[3];
-      }
-    } catch (...) {
-      continue;  // a corrupt row is skipped, never surfaced as a solution
-    }
-    s.from_ledger = true;
-    s.feasible_count = 1;
-    return s;
-  }
-  return std::nullopt;
-}
-
-std::vector<MeasuredRow> FileLedger::measured_rows(const std::string& hcs_fp) const {
-  std::vector<MeasuredRow> out;
-  std::ifstream in(path_);
-  std::string line;
-  while (std::getline(in, line)) {
-    const std::vector<std::string> f = split_tabs(line);
-    if (f.size() < 4) continue;
-    // key = op_sig|hcs_fp|tree_hash (violation rows start with their marker)
-    const size_t b1 = f[0].find('|'), b2 = b1 == std::string::npos ? b1 : f[0].find('|', b1 + 1);
-    if (b2 == std::string::npos || f[0].compare(b1 + 1, b2 - b1 - 1, hcs_fp) != 0) continue;
-    MeasuredRow r;
-    r.op_sig = f[0].substr(0, b1);
-    try {
-      r.c_ms = std::stod(f[1]);
-      r.measured_ms = std::stod(f[2]);
-      if (f.size() >= 7) r.kernel_ms = std::stod(f[3]);  // only the 7-field row carries it
-    } catch (...) {
-      continue;  // a corrupt row is no calibration material
-    }
-    if (r.measured_ms > 0) out.push_back(r);
-  }
-  return out;
-}
-
-void FileLedger::commit(const std::string& key, const Solution& s, double measured_ms, double kernel_ms) const {
-  std::ofstream out(path_, std::ios::app);
-  out.precision(std::numeric_limits<double>::max_digits10);
-  out << key << kSep << s.c_ms << kSep << measured_ms << kSep << kernel_ms << kSep << s.best.tile_m << kSep
-      << s.best.tile_n << kSep << s.placement_record << "\n";
-}
-
-void FileLedger::record_violation(const std::string& key, double rate, double threshold, int migrations, int checks,
-                                  unsigned long long vram_free) const {
-  std::ofstream out(path_, std::ios::app);
-  out.precision(std::numeric_limits<double>::max_digits10);
-  out << kViolation << kSep << key << kSep << rate << kSep << threshold << kSep << migrations << kSep << checks
-      << kSep << vram_free << "\n";
-}
-
-int FileLedger::size() const {
-  std::ifstream in(path_);
-  std::string line;
-  int n = 0;
-  while (std::getline(in, line))
-    if (!line.empty() && line.rfind(kViolation, 0) != 0) ++n;
-  return n;
-}
-
 // ---- run_cuda ------------------------------------------------------------------
 
 RunOutcome run_cuda(const Solution& sol, const Hcs& hcs, const KmlTree& tree, const std::string& workdir) {
@@ -912,7 +815,13 @@ int calibrate(const std::string& hcs_json, const std::string& ledger_path, bool 
     return done(3);
   }
   const std::string fp = hcs_fingerprint(*hcs);
-  const std::vector<MeasuredRow> rows = FileLedger(ledger_path).measured_rows(fp);
+  std::string lerr;
+  const std::unique_ptr<Ledger> ledger = make_ledger(ledger_path, &lerr);
+  if (!ledger) {
+    out << "LEDGER " << lerr << "\n";
+    return done(2);
+  }
+  const std::vector<MeasuredRow> rows = ledger->measured_rows(fp);
   if (rows.empty()) {
     out << "CALIBRATE SKIP: no measured rows for hcs_fp=" << fp.substr(0, 8) << " (run first, then calibrate)\n";
     return done(3);
@@ -934,6 +843,67 @@ int calibrate(const std::string& hcs_json, const std::string& ledger_path, bool 
       << detail << "\n"
       << "PREDICTED demo c_ms " << solve_b200(*hcs, demo, sms).c_ms << " -> " << solve_b200(cal, demo, sms).c_ms
       << "\n";
+  return done(0);
+}
+
+// ---- cmd_solve's nvidia branch ---------------------------------------------------
+
+int solve_kml(const std::string& hcs_json, const std::string& kml_json, const std::string& ledger_path,
+              bool write_ledger, int sms, std::string* transcript) {
+  std::ostringstream out;
+  auto done = [&](int rc) {
+    if (transcript) *transcript = out.str();
+    return rc;
+  };
+  std::string err;
+  const std::optional<Hcs> hcs = hcs_import(hcs_json, &err);
+  if (!hcs) {
+    out << "HCS " << err << "\n";
+    return done(2);
+  }
+  const std::optional<KmlTree> tree = kml_import(kml_json, &err);
+  if (!tree) {
+    out << "KML " << err << "\n";
+    return done(2);
+  }
+  BackendNvidia be;
+  const std::string gap = be.capability_gap(*tree);
+  if (!gap.empty()) {
+    out << "UNSUPPORTED: " << gap << " - solve writes no ledger row for this tree. [backend=" << be.name() << "]\n";
+    return done(2);
+  }
+  const LedgerKey key = ledger_key_parts(*hcs, *tree);
+  std::unique_ptr<Ledger> ledger;
+  if (!ledger_path.empty()) {
+    ledger = make_ledger(ledger_path, &err);
+    if (!ledger) {
+      out << "LEDGER " << err << "\n";
+      return done(2);
+    }
+    if (auto hit = ledger->lookup(key)) {
+      out << "LEDGER HIT  c_cached_ms=" << hit->c_ms << "  tile=" << hit->best.tile_m << "x" << hit->best.tile_n
+          << "\n"
+          << hit->placement_record << "\n";
+      return done(0);
+    }
+  }
+  const int n_sm = sms > 0 ? sms : (hcs->compute_units > 0 ? hcs->compute_units : 148);
+  const Solution sol = solve_b200(*hcs, *tree, n_sm);
+  if (sol.feasible_count == 0) {
+    out << "INFEASIBLE: no tile for " << canonical_form(*tree) << "\n";
+    return done(3);
+  }
+  out << "SOLVED  x* tile=" << sol.best.tile_m << "x" << sol.best.tile_n << "  c_ms=" << sol.c_ms
+      << "  |X|=" << sol.feasible_count << "  hcs_fp=" << key.hcs_fp.substr(0, 8) << "\n"
+      << sol.placement_record << "\n";
+  if (write_ledger && ledger) {
+    // solve has no measurement: measured_ms is seeded with c_ms, and a run
+    // of the same key overwrites it (src/main.cpp:332-335)
+    if (!ledger->commit(key, sol, sol.c_ms, 0.0, &err)) {
+      out << "LEDGER " << err << "\n";
+      return done(2);
+    }
+  }
   return done(0);
 }
 
@@ -964,10 +934,18 @@ int run_kml(const std::string& hcs_json, const std::string& kml_json, const std:
         << be.name() << "]\n";
     return done(2);
   }
-  const std::string key = ledger_key(*hcs, *tree);
-  FileLedger ledger(ledger_path);
+  const LedgerKey key = ledger_key_parts(*hcs, *tree);
+  std::unique_ptr<Ledger> ledger;
+  if (!ledger_path.empty()) {
+    std::string lerr;
+    ledger = make_ledger(ledger_path, &lerr);
+    if (!ledger) {
+      out << "LEDGER " << lerr << "\n";
+      return done(2);
+    }
+  }
   Solution sol;
-  if (auto rec = ledger_path.empty() ? std::nullopt : ledger.lookup(key)) {
+  if (auto rec = ledger ? ledger->lookup(key) : std::nullopt) {
     sol = *rec;
     out << "LEDGER HIT  c_cached_ms=" << sol.c_ms << "  tile=" << sol.best.tile_m << "x" << sol.best.tile_n
         << "  (from ledger)\n"
@@ -994,8 +972,9 @@ int run_kml(const std::string& hcs_json, const std::string& kml_json, const std:
     out << "UNIKERN_VIOLATION what=migration_rate rate=" << rate << " threshold=0 migrations=" << r.migrations
         << " checks=" << r.checks << " exit=" << r.exit_code << " vram_free=" << r.vram_free
         << " vram_total=" << r.vram_total << " committed=no\n";
-    if (write_ledger && !ledger_path.empty())
-      ledger.record_violation(key, rate, 0.0, r.migrations, r.checks, r.vram_free);
+    std::string werr;
+    if (write_ledger && ledger && !ledger->record_violation(key, rate, 0.0, r.migrations, r.checks, r.vram_free, &werr))
+      out << "LEDGER " << werr << "\n";
     // cudaMalloc memory does not migrate on this device, so a violation means
     // something outside the plan's control: record it and stop
     out << "RESOLVE STOP: nvidia:cuda allocates device memory only; violation recorded, nothing committed.\n";
@@ -1005,11 +984,15 @@ int run_kml(const std::string& hcs_json, const std::string& kml_json, const std:
     out << "RUN FAILED; solution NOT committed to ledger\n";
     return done(1);
   }
-  if (!write_ledger || ledger_path.empty()) {
+  if (!write_ledger || !ledger) {
     out << "VERIFY PASS (no ledger write)\n";
     return done(0);
   }
-  ledger.commit(key, sol, r.measured_ms, r.kernel_ms);
+  std::string werr;
+  if (!ledger->commit(key, sol, r.measured_ms, r.kernel_ms, &werr)) {
+    out << "LEDGER " << werr << "; solution NOT committed\n";
+    return done(1);
+  }
   const double eps_abs = std::fabs(r.measured_ms - sol.c_ms);
   out << "LEDGER COMMIT predicted_ms=" << sol.c_ms << " measured_ms=" << r.measured_ms << " epsilon_abs=" << eps_abs
       << " epsilon_rel=" << eps_abs / std::max(sol.c_ms, 1e-9) << "\n";

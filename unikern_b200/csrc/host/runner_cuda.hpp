@@ -8,8 +8,10 @@
 //                           src/runner_ocl.cpp (verify instance, warm/iters,
 //                           e2e and kernel-only spans, result line :834-841)
 //   BackendNvidia ......... IBackend, include/unikern/components.hpp:14-33
-//   FileLedger ............ src/runtime.cpp:20-170 (TAB rows, #VIOLATION events,
-//                           measured_rows :100-128)
+//   ledger ................ ledger.hpp: TAB file ledger for .jsonl paths
+//                           (src/runtime.cpp:20-170), SQLite for the rest
+//                           (src/sqlite_ledger.cpp, src/main.cpp:61-70)
+//   solve ................. cmd_solve, src/main.cpp:276-343
 //   run flow .............. cmd_run, src/main.cpp:346-570
 //   scenario B ............ src/codegen_hip.cpp:1143-1238, :1485-1500
 //   calibrate ............. cmd_calibrate, src/main.cpp:573-652;
@@ -21,20 +23,9 @@
 #include <vector>
 
 #include "kml.hpp"
+#include "ledger.hpp"
 
 namespace ukb {
-
-struct Instance {
-  int tile_m = 0, tile_n = 0, k_block = 0, stages = 0;
-};
-
-struct Solution {
-  Instance best;
-  double c_ms = 0;  // predicted end-to-end time (roofline + host link copies)
-  int feasible_count = 0;
-  bool from_ledger = false;
-  std::string placement_record;
-};
 
 // Pure function of (hcs, tree, sms): the tile the library launches for the
 // tree (uk_cuda_tile_plan) and its predicted cost from the HCS constants.
@@ -64,29 +55,6 @@ class BackendNvidia {
   std::string capability_gap(const KmlTree& t) const;  // "" = supported
 };
 
-// one measured ledger row under an HCS fingerprint (calibration input)
-struct MeasuredRow {
-  std::string op_sig;      // carries the dims, e.g. "gemm:fp32:1024x1024x1024"
-  double c_ms = 0;         // predicted at record time
-  double measured_ms = 0;  // end to end per pass
-  double kernel_ms = 0;    // kernel only; 0 in rows that predate it
-};
-
-class FileLedger {
- public:
-  explicit FileLedger(std::string path) : path_(std::move(path)) {}
-  std::optional<Solution> lookup(const std::string& key) const;
-  // rows with a measurement (> 0) recorded under hcs_fp, in file order
-  std::vector<MeasuredRow> measured_rows(const std::string& hcs_fp) const;
-  void commit(const std::string& key, const Solution& s, double measured_ms, double kernel_ms) const;
-  void record_violation(const std::string& key, double rate, double threshold, int migrations, int checks,
-                        unsigned long long vram_free) const;
-  int size() const;
-
- private:
-  std::string path_;
-};
-
 // The effective host link bandwidth (GB/s) from measured rows: per row the
 // compulsory bytes of its signature's tree over measured_ms - kernel_ms, and
 // the median over usable rows (the mean of the middle two for an even
@@ -100,6 +68,15 @@ double calibrated_link_bw(const std::vector<MeasuredRow>& rows, std::string* det
 // HCS without allow_unified, no measured rows, or no usable row).
 int calibrate(const std::string& hcs_json, const std::string& ledger_path, bool allow_unified,
               std::string* hcs_out, std::string* transcript);
+
+// cmd_solve's nvidia branch (src/main.cpp:276-343): ledger lookup (a hit
+// reuses the recorded tile) or solve_b200 on `sms` multiprocessors (0 = the
+// HCS's compute_units), then a solve-time row (measured_ms seeded with c_ms,
+// kernel_ms 0; a later run overwrites it) when write_ledger.  No GPU needed.
+// Returns 0 solved or hit, 2 bad input / unsupported tree / ledger error,
+// 3 infeasible; the transcript (LEDGER HIT / SOLVED lines) goes to *transcript.
+int solve_kml(const std::string& hcs_json, const std::string& kml_json, const std::string& ledger_path,
+              bool write_ledger, int sms, std::string* transcript);
 
 // cmd_run's nvidia branch (run: write_ledger = true; verify: false).  Returns
 // cmd_run's exit code: 0 committed / verified, 1 run failed, 2 bad input or
