@@ -10,6 +10,7 @@
 //   * reductions are warp shuffles + a fixed-order cross-warp step, so the
 //     result bits are the same on every call (deterministic);
 //   * grids are sized from the SM count (148 on B200), not from a label.
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <cmath>
@@ -382,21 +383,55 @@ ReducePlan plan_reduce(int64_t rows, int64_t cols) { return uk::plan_reduce(rows
 constexpr int64_t kReduceScratchFloats = 8192;
 static __device__ __align__(256) float g_reduce_scratch[kReduceScratchFloats];
 
-// Device address of g_reduce_scratch on the current device, looked up once per
-// device (the first call on each device does it, with that device current).
+// The current context's unique id (cuCtxGetId, reached through the runtime's
+// driver entry points, so the library needs no link to libcuda); false when
+// the driver cannot say.
+bool current_context_id(unsigned long long* id) {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = (GetCurrent)f;
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = (GetId)f;
+  });
+  CUcontext ctx = nullptr;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of g_reduce_scratch on the current device.  The set-up (the
+// cudaGetSymbolAddress call, with the device current) runs on the first call
+// on each device and again whenever that device's context changed since (a
+// cudaDeviceReset, or a context torn down and made again, retires the old
+// address); where the driver cannot identify the context, every call looks
+// the address up again.
 int reduce_scratch_address(float** out) {
   static std::mutex mu;
   static float* addr[64] = {nullptr};
+  static unsigned long long ctx_of[64] = {0};
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return uk::fail(UK_ECUDA, "reduce_noalloc: no usable current device");
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  unsigned long long id = 0;
+  const bool known = current_context_id(&id) && id != 0;
+  if (addr[dev] == nullptr || !known || ctx_of[dev] != id) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_reduce_scratch);
     if (e != cudaSuccess || p == nullptr)
       return uk::fail(UK_ECUDA, "reduce_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
     addr[dev] = (float*)p;
+    unsigned long long now = 0;
+    ctx_of[dev] = current_context_id(&now) ? now : 0;
   }
   *out = addr[dev];
   return UK_OK;
