@@ -1,20 +1,24 @@
 #!/usr/bin/env python
-"""bench.py -- throughput of the B200 KML operator set (one JSON line).
+"""bench.py -- throughput of the B200 KML operator set (JSON lines, headline last).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--op OP]
 
-Headline workload (``value``): f16 GEMM, C(f16) = A(f16) * B(f16) with f32
-accumulation, M = N = K = 8192 row-major; at N GPUs
-the columns of B and C are split over the ranks (strong scaling, total work
-fixed).  A step is one GEMM over inputs already resident in HBM; ``e2e`` is
-the same metric through the C ABI with pinned host buffers copied in and the
-result copied out inside the timed region.
+Headline workload (``value``, the LAST line): f16 GEMM, C(f16) = A(f16) * B(f16)
+with f32 accumulation, M = N = K = 8192 row-major; at N
+GPUs the columns of B and C are split over the ranks (strong scaling, total
+work fixed).  A step is one GEMM over inputs already resident in HBM; ``e2e``
+is the same metric through the C ABI with pinned host buffers copied in and
+the result copied out inside the timed region.
 
-The line also carries ``ops``: the other KML ops at their BASELINE sizes on
-rank 0 (row reduce / RMSNorm / softmax over [8192 x 16384], channelscale,
-the KML scalar reduce, the conv N=32 256->256 56x56 3x3 pad 1 with the fused
-channel scale, the f32 GEMM 512^3 and the decode chain), each with its own
-roofline and a CPU baseline on a bounded sample.
+Before the headline, one compact JSON line per other BASELINE op (rank 0,
+one GPU): the f32 GEMM 512^3, the row reduce, the KML scalar reduce, RMSNorm
+and softmax over [8192 x 16384], the conv N=32 256->256 56x56 3x3 pad 1 with
+the fused channel scale (split-tf32 tensor cores, with the FFMA kernel
+beside it) and the decode chain.  Each carries ``roofline``, ``e2e`` (the op
+through the C ABI with its inputs uploaded from and its outputs downloaded to
+pinned host memory inside the timed region, the reference's measured_ms,
+src/codegen_hip.cpp:692-744) and ``cpu_baseline`` (the reference's CPU code on
+this host's cores).  The fp16 widenings and channelscale print first.
 
 Timing: W untimed steps, then exactly K steps between CUDA events on the
 launching stream, barrier + synchronize on both sides, max over ranks.
@@ -33,15 +37,18 @@ import sys
 import tempfile
 import threading
 import time
+import warnings
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+warnings.filterwarnings("ignore")  # stdout/stderr carry the JSON lines only
 
 METRIC = json.loads((ROOT / "BASELINE.json").read_text())["metric"] if (ROOT / "BASELINE.json").exists() else \
     "f16 GEMM TFLOP/s; reduce/norm/softmax HBM GB/s; % roofline at 1/2/4/8 B200"
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 FP32_SIMT_TFLOPS = 2 * 148 * 128 * 1.965e9 / 1e12  # nominal FFMA peak (no measured figure exists)
+SUSTAINED_LAUNCHES = 2000  # the headline GEMM back to back for ~1.7 s (burst vs power-capped clocks)
 
 
 def peaks():
@@ -53,6 +60,10 @@ def peaks():
     d = dict(FALLBACK)
     d["source"] = "fallback"
     return d
+
+
+def emit(d):
+    print(json.dumps(d, separators=(",", ":")), flush=True)
 
 
 # ---------------------------------------------------------------------------
@@ -76,6 +87,7 @@ class ClockSampler:
                                          stdout=self.file, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+        return self
 
     def stop(self):
         if self.proc is None:
@@ -124,7 +136,7 @@ class Ctx:
         self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
-    def time_steps(self, step, steps, warmup, flush=None):
+    def time_steps(self, step, steps, warmup):
         """ms per step over exactly `steps` launches (events on the launching stream)."""
         torch = self.torch
         for _ in range(warmup):
@@ -141,6 +153,33 @@ class Ctx:
         self.barrier()
         torch.cuda.synchronize()
         return self.max_over_ranks(e0.elapsed_time(e1) / steps)
+
+
+def pinned(t):
+    """A page-locked host copy of device tensor t."""
+    return t.cpu().pin_memory()
+
+
+def time_e2e(ctx, launch, ins, outs, steps, warmup=3):
+    """The op end to end, as the reference's measured_ms: every step uploads
+    each (device, pinned host) pair of `ins`, launches, and downloads each
+    pair of `outs`, all on the launching stream between CUDA events.
+    Returns (ms per step, H2D bytes per step, D2H bytes per step)."""
+    def step():
+        for d, h in ins:
+            d.copy_(h, non_blocking=True)
+        launch()
+        for d, h in outs:
+            h.copy_(d, non_blocking=True)
+    ms = ctx.time_steps(step, steps, warmup)
+    nb = lambda pairs: sum(h.numel() * h.element_size() for _, h in pairs)  # noqa: E731
+    return ms, nb(ins), nb(outs)
+
+
+def e2e_record(work, unit, ms, h2d, d2h):
+    """work per step (bytes for GB/s, flops for TFLOP/s) over the e2e time."""
+    v = work / ms / (1e6 if unit == "GB/s" else 1e9)
+    return {"value": round(v, 3), "h2d": h2d, "d2h": d2h}
 
 
 # ---------------------------------------------------------------------------
@@ -164,9 +203,16 @@ def run_threads(fn, n):
     return time.perf_counter() - t0
 
 
-def cpu_gemm_f16(M, N, K, budget_s=10.0, rows=None):
+def gemm_f16_cpu_rows():
+    """Rows of the 8192^3 product the CPU baseline computes; the headline's
+    cpu_baseline and the reference arm use the same count."""
+    return 4 * cpu_threads()
+
+
+def cpu_gemm_f16(M, N, K, rows=None):
     """Rows of C = A * B (8192^3 f16 config) with the reference's cpu_ref loop
-    (src/codegen_hip.cpp:1124-1132 on half-quantised inputs); one row per thread."""
+    (src/codegen_hip.cpp:1124-1132 on half-quantised inputs); rows dealt
+    round-robin over the host threads."""
     import numpy as np
     from oracle import oracle as O
     nt = cpu_threads()
@@ -174,7 +220,7 @@ def cpu_gemm_f16(M, N, K, budget_s=10.0, rows=None):
     Bh = O.f32_to_f16(rng.normal(0, 0.02, (K, N)).astype(np.float32))
     e = O.emit()
     kind = "reference" if e is not None else "port"
-    nrows = rows or nt
+    nrows = rows or gemm_f16_cpu_rows()
     Ah = O.f32_to_f16(rng.normal(0, 0.02, (nrows, K)).astype(np.float32))
     if e is not None:
         Bf = O.f16_to_f32(Bh)
@@ -188,19 +234,20 @@ def cpu_gemm_f16(M, N, K, budget_s=10.0, rows=None):
         dt = run_threads(work, min(nt, nrows))
     else:
         t0 = time.perf_counter()
-        O.gemm_f16(np.vstack([Ah, np.zeros((0, K), np.uint16)]), Bh, rows=(0, nrows), threads=nt)
+        O.gemm_f16(Ah, Bh, threads=nt)
         dt = time.perf_counter() - t0
     flops = 2.0 * nrows * N * K
     return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": min(nt, nrows), "kind": kind,
-            "sample": "%d rows x %d cols of C (K=%d), %.2f s, extrapolated to the full %dx%dx%d GEMM by rate"
-                      % (nrows, N, K, dt, M, N, K), "seconds": dt}
+            "sample": "%d rows of C, %.2f s, extrapolated by rate" % (nrows, dt), "seconds": dt}
 
 
-def cpu_rowop(op, L, C, budget_rows=None):
+def cpu_rowop(op, L, C):
+    """The whole [L x C] workload with the reference's CPU code, one block of
+    rows per host thread."""
     import numpy as np
     from oracle import oracle as O
     nt = cpu_threads()
-    rows = budget_rows or L  # the whole workload: it takes well under a minute on the host
+    rows = L
     rng = np.random.default_rng(6)
     X = rng.normal(0, 1, (rows, C)).astype(np.float32)
     W = rng.normal(1, 0.1, C).astype(np.float32)
@@ -237,9 +284,8 @@ def cpu_rowop(op, L, C, budget_rows=None):
     dt = run_threads(work, nt)
     nbytes = rows * C * 4 * (1 if op == "reduce" else 2)
     return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": nt, "kind": kind,
-            "sample": "%d of %d rows (C=%d, one contiguous block of rows per thread), %.2f s%s" % (rows, L, C, dt,
-                                                           "; eps fixed at 1e-6 in the reference" if op == "rmsnorm" else ""),
-            "seconds": dt}
+            "sample": "all %d rows (C=%d), %.2f s%s" % (rows, C, dt, "; eps 1e-6" if op == "rmsnorm" else ""),
+            "short": "all rows" + (", eps 1e-6" if op == "rmsnorm" else ""), "seconds": dt}
 
 
 def cpu_conv(N, Cc, H, W, Oc, pad):
@@ -263,7 +309,7 @@ def cpu_conv(N, Cc, H, W, Oc, pad):
     dt = run_threads(work, nt)
     flops = 2.0 * nt * H * W * Cc * 9 * Oc
     return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": nt, "kind": "reference" if r else "port",
-            "sample": "%d images of %d (one per thread), %.2f s" % (nt, N, dt), "seconds": dt}
+            "sample": "%d of %d images, %.2f s" % (nt, N, dt), "short": "%d images, by rate" % nt, "seconds": dt}
 
 
 def cpu_gemm_f32(M=512, N=512, K=512):
@@ -292,7 +338,7 @@ def cpu_gemm_f32(M=512, N=512, K=512):
         dt = time.perf_counter() - t0
     return {"value": 2.0 * M * N * K / dt / 1e12, "unit": "TFLOP/s", "cores": nt,
             "kind": "reference" if e is not None else "port",
-            "sample": "the whole %dx%dx%d GEMM, rows split over %d threads, %.3f s" % (M, N, K, nt, dt), "seconds": dt}
+            "sample": "whole %d^3 GEMM, %.3f s" % (M, dt), "short": "whole", "seconds": dt}
 
 
 def cpu_reduce_scalar(L=134217728):
@@ -311,7 +357,7 @@ def cpu_reduce_scalar(L=134217728):
         O.reduce_blocked_f32(X, 1024)
     dt = time.perf_counter() - t0
     return {"value": L * 4 / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "reference" if r is not None else "port",
-            "sample": "the whole vector (L = %d), %.3f s" % (L, dt), "seconds": dt}
+            "sample": "whole vector L=%d, %.3f s" % (L, dt), "short": "whole, 1 thread", "seconds": dt}
 
 
 def cpu_decode(Bt=32, H=4096, F=14336, heads=32, S=8192):
@@ -347,12 +393,14 @@ def cpu_decode(Bt=32, H=4096, F=14336, heads=32, S=8192):
     dt = time.perf_counter() - t0
     nbytes = Bt * H * 4 + H * 4 + H * F * 2 + Bt * F * 2 + 2 * Bt * heads * S * 4
     return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": nt, "kind": "reference",
-            "sample": "the whole chain (B = %d), %.3f s" % (Bt, dt), "seconds": dt}
+            "sample": "whole chain B=%d, %.3f s" % (Bt, dt), "short": "whole", "seconds": dt}
 
 
-def strip(d):
-    return None if d is None else {k: (round(v, 6) if isinstance(v, float) else v) for k, v in d.items()
-                                   if k != "seconds"}
+def cpu_short(d):
+    """The cpu_baseline object of a per-op line."""
+    if d is None:
+        return None
+    return {"value": round(d["value"], 6), "cores": d["cores"], "kind": d["kind"], "sample": d["short"]}
 
 
 # ---------------------------------------------------------------------------
@@ -368,6 +416,30 @@ def gen(torch, shape, kind, seed, dtype=None, scale=1.0, lo=0.0, hi=1.0):
     return t.to(dtype) if dtype is not None else t
 
 
+def check_gemm_f16(A, B, Cm, rows, points=0, seed=0):
+    """Sampled check of a computed C against float64 dot products of the half
+    inputs (numpy on the host; a checker beside the timing, never timed):
+    `rows` full rows of C (every rank's column block) and `points` random
+    elements.  Returns the worst |C - ref| / max(|ref|, RMS(ref))."""
+    import numpy as np
+    M, N = Cm.shape
+    rng = np.random.default_rng(seed)
+    idx = np.unique(np.concatenate([[0, M - 1], rng.choice(M, max(0, rows - 2), replace=False)]))
+    Bf = B.double().cpu().numpy()
+    ref = A[idx].double().cpu().numpy() @ Bf
+    got = Cm[idx].double().cpu().numpy()
+    tau = float(np.sqrt(np.mean(ref * ref)))
+    err = float(np.max(np.abs(got - ref) / np.maximum(np.abs(ref), tau)))
+    if points:
+        import torch
+        i = rng.integers(0, M, points)
+        j = rng.integers(0, N, points)
+        refp = np.einsum("pk,kp->p", A[i].double().cpu().numpy(), Bf[:, j])
+        gotp = Cm[torch.as_tensor(i, device=Cm.device), torch.as_tensor(j, device=Cm.device)].double().cpu().numpy()
+        err = max(err, float(np.max(np.abs(gotp - refp) / np.maximum(np.abs(refp), tau))))
+    return err, len(idx)
+
+
 def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
     import unikern_b200.abi as abi
     torch = ctx.torch
@@ -375,9 +447,11 @@ def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
     A = gen(torch, (M, K), "normal", 1, torch.float16, 0.02)
     B = gen(torch, (K, N), "normal", 2, torch.float16, 0.02)
     Cm = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    plan = None
     if world == 1:
-        def step():
+        def launch():
             abi.gemm_f16(A, B, Cm)
+        step = launch
         launches_per_step = 1
         parallelism = "single GPU"
         Bs = B
@@ -385,124 +459,200 @@ def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
         from unikern_b200 import shard
         plan = shard.GemmAllGather(Cm, M, N, K)
         Bs = plan.b_shard(B)
-        kev = []  # (start, end) events around this rank's GEMM launch in each timed step
+
+        def launch():
+            plan.launch(A, Bs)
 
         def step():
-            if timing[0]:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(ctx.stream)
-                plan.launch(A, Bs)
-                e1.record(ctx.stream)
-                kev.append((e0, e1))
-            else:
-                plan.launch(A, Bs)
+            launch()
             plan.barrier()
         launches_per_step = plan.launches_per_step
         parallelism = plan.describe()
-    timing = [False]
-    for _ in range(warmup):
-        step()
-    timing[0] = True
-    ms = ctx.time_steps(step, steps, 0)
-    timing[0] = False
+    sampler = ClockSampler(ctx.local_rank).start()
+    ms = ctx.time_steps(step, steps, warmup)
+    clocks = sampler.stop()
+    # the dominant kernel's own launch time: events on the launching stream
+    # around each GEMM alone (at N > 1 the barrier falls outside), max over ranks
+    kev = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ctx.stream)
+        launch()
+        e1.record(ctx.stream)
+        kev.append((e0, e1))
+        if plan is not None:
+            plan.barrier()
+    torch.cuda.synchronize()
+    kernel_ms = ctx.max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / len(kev))
     flops = 2.0 * M * N * K
-    if world == 1:
-        kernel_ms, flops_per_launch = ms, flops
-    else:
-        # the dominant kernel's own launch time: events on the launching stream
-        # around each GEMM (the barrier is outside), max over ranks
-        kernel_ms = ctx.max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / len(kev))
-        flops_per_launch = 2.0 * M * (plan.n1 - plan.n0) * K
+    flops_per_launch = flops if world == 1 else 2.0 * M * (plan.n1 - plan.n0) * K
     res = {"ms": ms, "value": flops / ms / 1e9, "flops_per_step": flops, "launches": launches_per_step * steps,
-           "parallelism": parallelism, "kernel_ms": kernel_ms,
-           "kernel_tflops": flops_per_launch / kernel_ms / 1e9}
-    # e2e through the C ABI with pinned host buffers (rank-local inputs): on
-    # one GPU the pipelined host-to-host entry point (uploads of A row blocks,
-    # their GEMMs and the downloads of C blocks overlapped); on N GPUs each
-    # rank uploads A and its B block, runs the sharded GEMM and downloads C
-    Ah = A.cpu().pin_memory()
-    Bh = Bs.contiguous().cpu().pin_memory()
-    Ch = torch.empty((M, N), dtype=torch.float16).pin_memory()
-    Bd = torch.empty_like(Bh, device="cuda")
+           "parallelism": parallelism, "kernel_ms": kernel_ms, "kernel_tflops": flops_per_launch / kernel_ms / 1e9,
+           "clocks": clocks}
 
-    def e2e_step():
-        if world == 1:
-            abi.gemm_f16_host(Ah, Bh, Ch, A, Bd, Cm)
-            return
-        A.copy_(Ah, non_blocking=True)
-        Bd.copy_(Bh, non_blocking=True)
-        plan.run(A, Bd, Cm)
-        Ch.copy_(Cm, non_blocking=True)
-    e2e_ms = ctx.time_steps(e2e_step, max(2, min(steps, 10)), 1)
+    # sustained: the same step back to back for ~1.7 s with clocks sampled,
+    # so the power-capped rate is measured beside the burst figure above
+    sampler = ClockSampler(ctx.local_rank).start()
+    sms = ctx.time_steps(step, SUSTAINED_LAUNCHES, 0)
+    sclk = sampler.stop()
+    res["sustained"] = {"launches": SUSTAINED_LAUNCHES, "value": round(flops / sms / 1e9, 2),
+                        "sm_mhz": sclk["sm_mhz"] if sclk else None,
+                        "reasons": sclk["reasons"] if sclk else None}
+
+    # e2e through the C ABI with pinned host buffers: on one GPU the pipelined
+    # host-to-host entry point (uploads of A row blocks, their GEMMs and the
+    # downloads of C blocks overlapped); on N GPUs the sharded host path
+    if world == 1:
+        Ah, Bh = pinned(A), pinned(B)
+        Ch = torch.empty((M, N), dtype=torch.float16).pin_memory()
+        Bd = torch.empty_like(B)
+        e2e_step = lambda: abi.gemm_f16_host(Ah, Bh, Ch, A, Bd, Cm)  # noqa: E731
+        h2d, d2h = Ah.numel() * 2 + Bh.numel() * 2, Ch.numel() * 2
+    else:
+        host = shard.HostGemmF16(plan, A, B)
+        e2e_step = host.step
+        h2d, d2h = host.h2d_bytes, host.d2h_bytes
+    e2e_ms = ctx.time_steps(e2e_step, max(3, min(steps, 10)), 3)
+    res["e2e"] = {"value": round(flops / e2e_ms / 1e9, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                  "d2h_bytes_per_step": d2h}
     if world > 1:
-        # every rank must hold the same full C: spot-check against a column
-        # block computed locally on this GPU
-        ref = torch.empty((M, 64), dtype=torch.float16, device="cuda")
-        j0 = ((rank + 1) % world) * (N // world)
-        abi.gemm_f16(A, B[:, j0:j0 + 64], ref)
-        step()
-        torch.cuda.synchronize()
-        res["allgather_max_abs_diff"] = float((Cm[:, j0:j0 + 64].float() - ref.float()).abs().max().item())
+        # the host C the sharded e2e path assembled: every rank's block
+        res["e2e"]["check"] = host.check_host(step_fn=e2e_step)
+        host.close()
+
+    # correctness of the timed product (a checker, after the timing): at N=1
+    # 64 full rows + 4096 elements, at N>1 16 full rows of this rank's gathered
+    # C (every rank's column block), each against float64 dot products; max over ranks
+    step()
+    torch.cuda.synchronize()
+    err, nrows = check_gemm_f16(A, B, Cm, 64 if world == 1 else 16, 4096 if world == 1 else 0, seed=rank)
+    err = ctx.max_over_ranks(err)
+    res["check"] = {"rows": nrows, "points": 4096 if world == 1 else 0, "err_vs_f64": float("%.3g" % err),
+                    "pass": err <= 2e-2}
+    if plan is not None:
         plan.close()
-    res["e2e"] = {"value": flops / e2e_ms / 1e9, "unit": "TFLOP/s",
-                  "h2d_bytes_per_step": Ah.numel() * 2 + Bh.numel() * 2, "d2h_bytes_per_step": Ch.numel() * 2,
-                  "ms_per_step": e2e_ms}
     return res
 
 
-def bench_rowop(ctx, op, steps, warmup, L=8192, C=16384):
-    import unikern_b200.abi as abi
-    torch = ctx.torch
+def rowop_tensors(torch, op, L=8192, C=16384):
     X = gen(torch, (L, C), "normal", 3, None, 2.0 if op == "softmax" else 1.0)
     W = gen(torch, (C,), "normal", 4, None, 0.1) + 1.0
-    Y = torch.empty((L, C), device="cuda")
-    R = torch.empty((L,), device="cuda")
-    if op == "rmsnorm":
-        step = lambda: abi.rmsnorm(X, W, Y, 1e-5)  # noqa: E731
-        nbytes = 2 * L * C * 4 + C * 4
-    elif op == "softmax":
-        step = lambda: abi.softmax(X, Y)  # noqa: E731
-        nbytes = 2 * L * C * 4
-    elif op == "channelscale":
-        step = lambda: abi.channelscale(X, W, Y)  # noqa: E731
-        nbytes = 2 * L * C * 4 + C * 4
-    elif op == "reduce":
-        step = lambda: abi.reduce(X, R)  # noqa: E731
-        nbytes = L * C * 4 + L * 4
-    elif op == "reduce_scalar":
-        Xs = X.view(1, L * C)
-        ws = torch.empty(max(1, abi.reduce_workspace_size(1, L * C) // 4), device="cuda")
-        step = lambda: abi.reduce(Xs, R[:1], ws)  # noqa: E731
-        nbytes = L * C * 4 + 4
-    ms = ctx.time_steps(step, steps, warmup)
-    return {"ms": ms, "value": nbytes / ms / 1e6, "bytes_per_step": nbytes}
+    return X, W
 
 
-def bench_conv(ctx, steps, warmup, N=32, Cc=256, H=56, W=56, Oc=256, pad=1):
+def measure_rowop(ctx, op, steps, warmup, pk, L=8192, C=16384, e2e=True):
+    """Row reduce / RMSNorm / softmax / channelscale / KML scalar reduce at
+    the BASELINE row shape: device-resident rate, then e2e."""
     import unikern_b200.abi as abi
     torch = ctx.torch
+    X, W = rowop_tensors(torch, op, L, C)
+    Y = torch.empty((L, C), device="cuda")
+    R = torch.empty((L,), device="cuda")
+    ins, outs = [(X, pinned(X))], []
+    if op == "rmsnorm":
+        launch = lambda: abi.rmsnorm(X, W, Y, 1e-5)  # noqa: E731
+        nbytes = 2 * L * C * 4 + C * 4
+        ins.append((W, pinned(W)))
+        outs.append((Y, torch.empty_like(Y, device="cpu").pin_memory()))
+    elif op == "softmax":
+        launch = lambda: abi.softmax(X, Y)  # noqa: E731
+        nbytes = 2 * L * C * 4
+        outs.append((Y, torch.empty_like(Y, device="cpu").pin_memory()))
+    elif op == "channelscale":
+        launch = lambda: abi.channelscale(X, W, Y)  # noqa: E731
+        nbytes = 2 * L * C * 4 + C * 4
+        ins.append((W, pinned(W)))
+        outs.append((Y, torch.empty_like(Y, device="cpu").pin_memory()))
+    elif op == "reduce":
+        launch = lambda: abi.reduce(X, R)  # noqa: E731
+        nbytes = L * C * 4 + L * 4
+        outs.append((R, torch.empty_like(R, device="cpu").pin_memory()))
+    else:  # reduce_scalar: the KML reduce, one vector of L*C floats to a scalar
+        Xs = X.view(1, L * C)
+        ws = torch.empty(max(1, abi.reduce_workspace_size(1, L * C) // 4), device="cuda")
+        launch = lambda: abi.reduce(Xs, R[:1], ws)  # noqa: E731
+        nbytes = L * C * 4 + 4
+        outs.append((R[:1], torch.empty(1).pin_memory()))
+    ms = ctx.time_steps(launch, steps, warmup)
+    val = nbytes / ms / 1e6
+    rec = {"value": val, "unit": "GB/s", "ms": ms, "bytes_per_step": nbytes,
+           "roofline": roofline("hbm", val, pk, traffic_for("rowop_" + op))}
+    if e2e:
+        ems, h2d, d2h = time_e2e(ctx, launch, ins, outs, max(3, min(steps, 10)))
+        rec["e2e"] = e2e_record(nbytes, "GB/s", ems, h2d, d2h)
+    return rec
+
+
+def conv_tensors(torch, N=32, Cc=256, H=56, W=56, Oc=256):
     x = gen(torch, (N, Cc, H, W), "uniform", 8)
     w = gen(torch, (Oc, Cc, 3, 3), "normal", 9, None, (2.0 / (9 * Cc)) ** 0.5)
     s = gen(torch, (Oc,), "uniform", 10, None, lo=0.5, hi=1.5)
+    return x, w, s
+
+
+def measure_conv(ctx, steps, warmup, pk, N=32, Cc=256, H=56, W=56, Oc=256, pad=1, ffma=True, e2e=True):
+    """the split-tf32 tensor-core conv (step includes its
+    NCHW->NHWC hi/lo pre-pass) and, beside it, the FFMA kernel the north star
+    names for the fp32 path."""
+    import unikern_b200.abi as abi
+    torch = ctx.torch
+    x, w, s = conv_tensors(torch, N, Cc, H, W, Oc)
     y = torch.empty((N, Oc, H, W), device="cuda")
     ws = abi.conv2d_workspace(N, H, W, Cc, 3, 3, Oc, pad, abi.UK_CONV_NCHW)
-    step = lambda: abi.conv2d_tc(x, w, y, N, H, W, Cc, 3, 3, Oc, pad, s, abi.UK_CONV_NCHW, ws)  # noqa: E731
-    ms = ctx.time_steps(step, steps, warmup)
+    launch = lambda: abi.conv2d_tc(x, w, y, N, H, W, Cc, 3, 3, Oc, pad, s, abi.UK_CONV_NCHW, ws)  # noqa: E731
+    ms = ctx.time_steps(launch, steps, warmup)
     flops = 2.0 * N * H * W * Cc * 9 * Oc
-    return {"ms": ms, "value": flops / ms / 1e9, "flops_per_step": flops}
+    val = flops / ms / 1e9
+    rec = {"value": val, "unit": "TFLOP/s", "ms": ms, "path": "3xTF32 tcgen05 SM pairs",
+           "roofline": roofline("tensor_3xtf32", val, pk)}
+    if e2e:
+        ins = [(x, pinned(x)), (w, pinned(w)), (s, pinned(s))]
+        outs = [(y, torch.empty_like(y, device="cpu").pin_memory())]
+        ems, h2d, d2h = time_e2e(ctx, launch, ins, outs, max(3, min(steps, 10)))
+        rec["e2e"] = e2e_record(flops, "TFLOP/s", ems, h2d, d2h)
+    if ffma:
+        fl = lambda: abi.conv2d(x, w, y, N, H, W, Cc, 3, 3, Oc, pad, s, abi.UK_CONV_NCHW)  # noqa: E731
+        fms = ctx.time_steps(fl, max(3, min(steps, 5)), 3)
+        fval = flops / fms / 1e9
+        rec["ffma"] = {"value": round(fval, 2), "frac": round(fval / FP32_SIMT_TFLOPS, 4)}
+    return rec
 
 
-def bench_gemm_f32(ctx, steps, warmup, M=512, N=512, K=512):
+def capture(ctx, fn):
+    """fn's launches as a CUDA graph on the bench stream (after two eager
+    warm-up calls that set up per-device state)."""
+    torch = ctx.torch
+    fn()
+    fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):  # captured on a side stream, replayed on the bench stream
+        fn()
+    torch.cuda.synchronize()
+    return graph
+
+
+def measure_gemm_f32(ctx, steps, warmup, pk, M=512, N=512, K=512, e2e=True):
+    """the FFMA GEMM at 512^3 (a few microseconds of
+    device time: the device-resident step replays a CUDA graph of the one
+    launch so host launch overhead stays out; e2e calls the C ABI directly)."""
     import unikern_b200.abi as abi
     torch = ctx.torch
     A = gen(torch, (M, K), "uniform", 11, lo=-1, hi=1)
     B = gen(torch, (K, N), "uniform", 12, lo=-1, hi=1)
     Cm = torch.empty((M, N), device="cuda")
-    # a 512^3 GEMM is a few microseconds of device time: the step replays a
-    # CUDA graph of the one launch so host launch overhead stays out
-    graph = capture(ctx, lambda: abi.gemm_f32(A, B, Cm))
+    launch = lambda: abi.gemm_f32(A, B, Cm)  # noqa: E731
+    graph = capture(ctx, launch)
     ms = ctx.time_steps(graph.replay, steps, warmup)
-    return {"ms": ms, "value": 2.0 * M * N * K / ms / 1e9, "graph": True}
+    flops = 2.0 * M * N * K
+    val = flops / ms / 1e9
+    rec = {"value": val, "unit": "TFLOP/s", "ms": ms, "graph": True, "roofline": roofline("fp32", val, pk)}
+    if e2e:
+        ins = [(A, pinned(A)), (B, pinned(B))]
+        outs = [(Cm, torch.empty_like(Cm, device="cpu").pin_memory())]
+        ems, h2d, d2h = time_e2e(ctx, launch, ins, outs, max(10, steps))
+        rec["e2e"] = e2e_record(flops, "TFLOP/s", ems, h2d, d2h)
+    return rec
 
 
 def bench_gemm_f32_tc(ctx, steps, warmup, M=8192, N=8192, K=8192):
@@ -518,10 +668,13 @@ def bench_gemm_f32_tc(ctx, steps, warmup, M=8192, N=8192, K=8192):
     return {"ms": ms, "value": 2.0 * M * N * K / ms / 1e9}
 
 
-def bench_decode(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
+def measure_decode(ctx, steps, warmup, pk, Bt=32, H=4096, F=14336, heads=32, S=8192, e2e=True):
     """Decode-layer chain: RMSNorm [B x 4096] fused into
-    the f16 skinny GEMM [B x 4096] x [4096 x 14336] (one kernel), then softmax
-    over [B*32 x 8192] scores.  HBM-bound: the 112 MiB of weights dominate."""
+    the f16 skinny GEMM [B x 4096] x [4096 x 14336], then softmax over
+    [B*32 x 8192] scores.  HBM-bound: the 112 MiB of weights dominate.
+    e2e: the layer weight and gamma stay resident (model state); each step
+    uploads the token rows and the scores and downloads the GEMM output and
+    the probabilities."""
     import unikern_b200.abi as abi
     torch = ctx.torch
     x = gen(torch, (Bt, H), "normal", 13)
@@ -530,7 +683,6 @@ def bench_decode(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
     out = torch.empty((Bt, F), dtype=torch.float16, device="cuda")
     sc = gen(torch, (Bt * heads, S), "normal", 16)
     pr = torch.empty_like(sc)
-
     ws = abi.decode_workspace(Bt, H)
     side = torch.cuda.Stream()
 
@@ -548,7 +700,16 @@ def bench_decode(ctx, steps, warmup, Bt=32, H=4096, F=14336, heads=32, S=8192):
     graph = capture(ctx, chain)
     ms = ctx.time_steps(graph.replay, steps, warmup)
     nbytes = Bt * H * 4 + H * 4 + H * F * 2 + Bt * F * 2 + 2 * Bt * heads * S * 4
-    return {"ms": ms, "value": nbytes / ms / 1e6, "bytes_per_step": nbytes, "batch": Bt, "graph": True}
+    val = nbytes / ms / 1e6
+    rec = {"value": val, "unit": "GB/s", "ms": ms, "graph": True, "roofline": roofline("hbm", val, pk)}
+    if e2e:
+        ins = [(x, pinned(x)), (sc, pinned(sc))]
+        outs = [(out, torch.empty_like(out, device="cpu").pin_memory()),
+                (pr, torch.empty_like(pr, device="cpu").pin_memory())]
+        ems, h2d, d2h = time_e2e(ctx, graph.replay, ins, outs, max(5, min(steps, 20)))
+        rec["e2e"] = e2e_record(nbytes, "GB/s", ems, h2d, d2h)
+    del graph
+    return rec
 
 
 def bench_gemm_streamed(ctx, steps, warmup, M=32768, N=32768, K=32768, f16=False, block_rows=4096):
@@ -577,20 +738,6 @@ def bench_gemm_streamed(ctx, steps, warmup, M=32768, N=32768, K=32768, f16=False
     host_bytes = (M * K + K * N + M * N) * es
     return {"ms": ms, "value": 2.0 * M * N * K / ms / 1e9, "link_GBps": host_bytes / ms / 1e6,
             "host_bytes": host_bytes, "blocks": (M + block_rows - 1) // block_rows}
-
-
-def capture(ctx, fn):
-    """fn's launches as a CUDA graph on the bench stream (after two eager
-    warm-up calls that set up per-device state)."""
-    torch = ctx.torch
-    fn()
-    fn()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):  # captured on a side stream, replayed on the bench stream
-        fn()
-    torch.cuda.synchronize()
-    return graph
 
 
 def bench_rowop_f16(ctx, op, steps, warmup, L=8192, C=16384):
@@ -708,17 +855,38 @@ def roofline(bound, achieved, pk, traffic=None):
     if bound == "tensor":
         peak, unit, src = pk.get("bf16_tflops", FALLBACK["bf16_tflops"]), "TFLOP/s", pk["source"] + " bf16 burst"
     elif bound == "fp32":
-        peak, unit, src = FP32_SIMT_TFLOPS, "TFLOP/s", "nominal FFMA"
+        peak, unit, src = round(FP32_SIMT_TFLOPS, 1), "TFLOP/s", "nominal FFMA"
     elif bound == "tensor_3xtf32":
         # fp32-accurate split-tf32: 3 tf32 MMAs per product at half the bf16
         # rate -> one sixth of the measured bf16 peak, in fp32-equivalent flop/s
         peak = round(pk.get("bf16_tflops", FALLBACK["bf16_tflops"]) / 6.0, 2)
-        unit, src = "TFLOP/s", pk["source"] + " bf16 burst / 6 (3 tf32 MMAs at half rate)"
+        unit, src = "TFLOP/s", pk["source"] + " bf16 burst / 6"
     else:
         peak, unit, src = pk.get("hbm_gbs", FALLBACK["hbm_gbs"]), "GB/s", pk["source"] + " copy"
     return {"bound": "tensor" if bound.startswith("tensor") else ("hbm" if bound == "hbm" else "fp32"),
             "achieved": round(achieved, 2), "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
-            "peak_source": src, "traffic": traffic, "scope": "one launch of the kernel on one GPU"}
+            "peak_source": src, "traffic": traffic}
+
+
+def op_line(name, rec, cpu=None, **extra):
+    """One compact JSON line per op: value, roofline (peak_source kept
+    short), e2e and cpu_baseline."""
+    roof = dict(rec["roofline"])
+    for k in ("achieved", "unit", "peak_source"):  # = value, = unit, in the peaks line
+        roof.pop(k, None)
+    if roof.get("traffic") is None:
+        roof.pop("traffic", None)
+    d = {"op": name, "value": round(rec["value"], 3), "unit": rec["unit"], "ms": round(rec["ms"], 5),
+         "roofline": roof}
+    if "e2e" in rec:
+        d["e2e"] = rec["e2e"]
+    if cpu is not None:
+        d["cpu_baseline"] = cpu_short(cpu)
+    for k in ("ffma",):
+        if k in rec:
+            d[k] = rec[k]
+    d.update(extra)
+    return d
 
 
 NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (900 nominal)
@@ -727,8 +895,8 @@ NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (900
 def fused_roofline(g, M, N, K, world, pk):
     """Roofline of the N-sharded GEMM with the all-gather fused into its store:
     the target time per launch is the slower of its flops at the measured
-    bf16 peak and the bytes it must push over NVLink (its C block to every
-    peer: M * N/world * 2 B * (world - 1)) at the measured 770 GB/s per
+    bf16 peak and the bytes this GPU must receive over NVLink (every peer's C
+    block: M * N/world * 2 B * (world - 1)) at the measured 770 GB/s per
     direction; frac = target / measured kernel time."""
     peak = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
     flops = 2.0 * M * (N / world) * K
@@ -738,11 +906,9 @@ def fused_roofline(g, M, N, K, world, pk):
     target = max(t_tensor, t_link)
     return {"bound": "tensor" if t_tensor >= t_link else "nvlink", "achieved": round(g["kernel_tflops"], 2),
             "peak": peak, "unit": "TFLOP/s", "frac": round(target / g["kernel_ms"], 4),
-            "peak_source": "%s bf16 burst; NVLink %.0f GB/s per direction (measured peer copy)" % (pk["source"],
-                                                                                                 NVLINK_GBS),
+            "peak_source": "%s bf16 burst; NVLink %.0f GB/s" % (pk["source"], NVLINK_GBS),
             "target_ms": round(target, 5), "tensor_ms": round(t_tensor, 5), "nvlink_ms": round(t_link, 5),
-            "nvlink_bytes_per_launch": link_bytes, "kernel_ms": round(g["kernel_ms"], 5), "traffic": None,
-            "scope": "one launch of this rank's fused GEMM + all-gather kernel"}
+            "kernel_ms": round(g["kernel_ms"], 5), "traffic": None}
 
 
 def run_reference(args, world, rank):
@@ -752,7 +918,7 @@ def run_reference(args, world, rank):
     M = N = K = 8192
     vals, last = [], None
     for i in range(args.warmup + args.steps):
-        r = cpu_gemm_f16(M, N, K)
+        r = cpu_gemm_f16(M, N, K, rows=gemm_f16_cpu_rows())
         if i >= args.warmup:
             vals.append(r["value"])
             last = r
@@ -766,55 +932,56 @@ def run_reference(args, world, rank):
             "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     line["cpu_baseline"]["value"] = round(v, 6)
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
+SINGLE_OPS = ["gemm_f16", "reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar", "conv", "gemm_f32",
+              "decode", "softmax_f16", "rmsnorm_f16", "channelscale_f16", "conv_f16", "gemm_streamed",
+              "gemm_streamed_f16", "gemm_f32_tc", "reduce_f16"]
+
+
 def run_single(args, ctx, pk):
-    """One op alone at its BASELINE size (used for per-op numbers and profiling)."""
+    """One op alone at its BASELINE size (per-op numbers and profiling)."""
     op = args.op
     extra = {}
     if op in ("reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar"):
-        r = bench_rowop(ctx, op, args.steps, args.warmup)
-        val, unit, bound = r["value"], "GB/s", "hbm"
+        r = measure_rowop(ctx, op, args.steps, args.warmup, pk, e2e=not args.no_e2e)
     elif op == "conv":
-        r = bench_conv(ctx, args.steps, args.warmup)
-        val, unit, bound = r["value"], "TFLOP/s", "tensor_3xtf32"
+        r = measure_conv(ctx, args.steps, args.warmup, pk, ffma=not args.no_e2e, e2e=not args.no_e2e)
+    elif op == "gemm_f32":
+        r = measure_gemm_f32(ctx, args.steps, args.warmup, pk, e2e=not args.no_e2e)
+    elif op == "decode":
+        r = measure_decode(ctx, args.steps, args.warmup, pk, e2e=not args.no_e2e)
     elif op in ("softmax_f16", "rmsnorm_f16", "channelscale_f16", "reduce_f16"):
         r = bench_rowop_f16(ctx, op[:-4], args.steps, args.warmup)
-        val, unit, bound = r["value"], "GB/s", "hbm"
+        r.update(unit="GB/s", roofline=roofline("hbm", r["value"], pk))
     elif op == "conv_f16":
         r = bench_conv_f16(ctx, args.steps, args.warmup)
-        val, unit, bound = r["value"], "TFLOP/s", "tensor"
-    elif op == "gemm_f32":
-        r = bench_gemm_f32(ctx, args.steps, args.warmup)
-        val, unit, bound = r["value"], "TFLOP/s", "fp32"
+        r.update(unit="TFLOP/s", roofline=roofline("tensor", r["value"], pk))
     elif op == "gemm_f32_tc":
         M, N, K = (int(v) for v in args.gemm_shape.split(","))
         r = bench_gemm_f32_tc(ctx, args.steps, args.warmup, M, N, K)
-        val, unit, bound = r["value"], "TFLOP/s", "tensor_3xtf32"
+        r.update(unit="TFLOP/s", roofline=roofline("tensor_3xtf32", r["value"], pk))
         extra = {"config": {"workload": "fp32 GEMM %dx%dx%d, split-tf32 tensor cores, pre-passes included" % (M, N, K)}}
-    elif op in ("gemm_streamed", "gemm_streamed_f16"):
+    else:  # gemm_streamed, gemm_streamed_f16
         M, N, K = (int(v) for v in args.gemm_shape.split(",")) if args.gemm_shape != "8192,8192,8192" else \
             (32768, 32768, 32768)
-        r = bench_gemm_streamed(ctx, args.steps, args.warmup, M, N, K, f16=op.endswith("f16"))
-        val, unit, bound = r["value"], "TFLOP/s", "tensor" if op.endswith("f16") else "tensor_3xtf32"
-        es = 2 if op.endswith("f16") else 4
-        extra = {"e2e": {"value": round(val, 3), "unit": unit, "h2d_bytes_per_step": (M * K + K * N) * es,
-                         "d2h_bytes_per_step": M * N * es},
-                 "config": {"workload": "GEMM %dx%dx%d %s streamed from pinned host memory, B resident, %d row "
-                                        "blocks in a two-slot ring" % (M, N, K, "f16" if es == 2 else "fp32",
+        f16 = op.endswith("f16")
+        r = bench_gemm_streamed(ctx, args.steps, args.warmup, M, N, K, f16=f16)
+        es = 2 if f16 else 4
+        r.update(unit="TFLOP/s", roofline=roofline("tensor" if f16 else "tensor_3xtf32", r["value"], pk),
+                 e2e={"value": round(r["value"], 3), "h2d": (M * K + K * N) * es, "d2h": M * N * es})
+        extra = {"config": {"workload": "GEMM %dx%dx%d %s streamed from pinned host memory, B resident, %d row "
+                                        "blocks in a two-slot ring" % (M, N, K, "f16" if f16 else "fp32",
                                                                        r["blocks"])},
-                 "host_link_GBps": round(r["link_GBps"], 2), "seconds_per_step": round(r["ms"] / 1e3, 4)}
-    else:
-        r = bench_decode(ctx, args.steps, args.warmup)
-        val, unit, bound = r["value"], "GB/s", "hbm"
+                 "host_link_GBps": round(r["link_GBps"], 2)}
     if ctx.rank == 0:
-        line = {"metric": METRIC, "op": op, "value": round(val, 3), "unit": unit, "n_gpus": ctx.world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 5),
-                "higher_is_better": True, "roofline": roofline(bound, val, pk)}
+        line = op_line(op, r)
+        line.update({"metric": METRIC, "n_gpus": ctx.world, "steps": args.steps, "warmup": args.warmup,
+                     "higher_is_better": True})
         line.update(extra)
-        print(json.dumps(line), flush=True)
+        emit(line)
     return 0
 
 
@@ -824,13 +991,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="all",
-                    choices=["all", "gemm_f16", "reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar",
-                             "conv", "gemm_f32", "decode", "softmax_f16", "rmsnorm_f16", "channelscale_f16",
-                             "conv_f16", "gemm_streamed", "gemm_streamed_f16", "gemm_f32_tc", "reduce_f16"],
-                    help="all = headline f16 GEMM + every other op; otherwise one op alone (profiling)")
+    ap.add_argument("--op", default="all", choices=["all"] + SINGLE_OPS,
+                    help="all = every op, headline f16 GEMM last; otherwise one op alone (profiling)")
     ap.add_argument("--gemm-shape", default="8192,8192,8192", help="M,N,K of the f16 GEMM")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--no-e2e", action="store_true", help="single-op runs: device-resident timing only")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -855,84 +1020,82 @@ def main():
     if args.op not in ("all", "gemm_f16"):
         return run_single(args, ctx, pk)
     M, N, K = (int(v) for v in args.gemm_shape.split(","))
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    g = bench_gemm_f16(ctx, args.steps, args.warmup, M, N, K)
-    clocks = sampler.stop()
+    want_cpu = not args.no_cpu
 
-    ops = {}
+    if rank == 0:
+        emit({"peaks": {"hbm": [pk.get("hbm_gbs"), "GB/s", pk["source"] + " copy"],
+                        "tensor": [pk.get("bf16_tflops"), "TFLOP/s", pk["source"] + " bf16 burst"],
+                        "tensor_sustained": [pk.get("bf16_tflops_sustained"), "TFLOP/s", pk["source"]],
+                        "tensor_3xtf32": [round(pk.get("bf16_tflops", FALLBACK["bf16_tflops"]) / 6.0, 2), "TFLOP/s",
+                                          "bf16 burst / 6 (3 tf32 MMAs at half rate)"],
+                        "fp32": [round(FP32_SIMT_TFLOPS, 1), "TFLOP/s", "nominal FFMA"]},
+              "cpu_threads": cpu_threads()})
     if args.op == "all" and world == 1:
+        one = Ctx(1, 0, local_rank)
         s = max(5, min(args.steps, 20))
-        for op in ("reduce", "rmsnorm", "softmax", "channelscale", "reduce_scalar"):
-            r = bench_rowop(Ctx(1, 0, local_rank), op, s, 3)
-            ops[op] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
-                       "roofline": roofline("hbm", r["value"], pk, traffic_for("rowop_" + op))}
-        r = bench_conv(Ctx(1, 0, local_rank), max(3, s // 2), 3)
-        ops["conv_n32_256_56_3x3_pad1_scaled"] = {
-            "TFLOP/s": round(r["value"], 2), "ms": round(r["ms"], 4),
-            "path": "split-tf32 (3xTF32) implicit GEMM on tcgen05; the step includes the NCHW->NHWC hi/lo pre-pass",
-            "roofline": roofline("tensor_3xtf32", r["value"], pk)}
-        r = bench_gemm_f32(Ctx(1, 0, local_rank), s, 3)
-        ops["gemm_f32_512"] = {"TFLOP/s": round(r["value"], 3), "ms": round(r["ms"], 5),
-                               "roofline": roofline("fp32", r["value"], pk)}
-        r = bench_decode(Ctx(1, 0, local_rank), s, 3)
-        ops["decode_chain_b32"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
-                                   "roofline": roofline("hbm", r["value"], pk)}
-        # fp16 variants (beyond the reference's dtype interval)
+        # widenings beyond the reference's dtype interval, and channelscale
+        # (BASELINE runs it fused into the conv): printed first
         for op in ("softmax", "rmsnorm", "channelscale", "reduce"):
-            r = bench_rowop_f16(Ctx(1, 0, local_rank), op, s, 3)
-            ops[op + "_f16"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
-                                "roofline": roofline("hbm", r["value"], pk)}
-        r = bench_conv_f16(Ctx(1, 0, local_rank), max(3, s // 2), 3)
-        ops["conv_f16_n32_256_56_3x3_pad1_scaled"] = {"TFLOP/s": round(r["value"], 2), "ms": round(r["ms"], 4),
-                                                     "roofline": roofline("tensor", r["value"], pk)}
-        # last: the only op that holds ~3 GB and runs seconds-long tensor-core
-        # work; it runs after the memory-bound ops so it cannot perturb them
-        r = bench_gemm_f32_tc(Ctx(1, 0, local_rank), max(3, s // 2), 3)
-        ops["gemm_f32_8192_tensor_cores"] = {
-            "TFLOP/s": round(r["value"], 2), "ms": round(r["ms"], 4),
-            "path": "split-tf32 on the convolution's SM-pair kernel, fp32 promotion every 1024 k; pre-passes included",
-            "roofline": roofline("tensor_3xtf32", r["value"], pk)}
-        if not args.no_cpu:
-            # the reference's CPU path for every op, timed on this host in this run
-            for op in ("reduce", "rmsnorm", "softmax", "channelscale"):
-                ops[op]["cpu_baseline"] = strip(cpu_rowop(op, 8192, 16384))
-            ops["reduce_scalar"]["cpu_baseline"] = strip(cpu_reduce_scalar())
-            ops["conv_n32_256_56_3x3_pad1_scaled"]["cpu_baseline"] = strip(cpu_conv(32, 256, 56, 56, 256, 1))
-            ops["gemm_f32_512"]["cpu_baseline"] = strip(cpu_gemm_f32())
-            ops["decode_chain_b32"]["cpu_baseline"] = strip(cpu_decode())
+            r = bench_rowop_f16(one, op, s, 3)
+            emit({"op": op + "_f16", "value": round(r["value"], 1), "unit": "GB/s", "ms": round(r["ms"], 5),
+                  "roofline": {"bound": "hbm", "peak": pk["hbm_gbs"], "frac": round(r["value"] / pk["hbm_gbs"], 4)}})
+        r = bench_conv_f16(one, max(3, s // 2), 3)
+        tp = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
+        emit({"op": "conv_f16", "value": round(r["value"], 2), "unit": "TFLOP/s", "ms": round(r["ms"], 5),
+              "roofline": {"bound": "tensor", "peak": tp, "frac": round(r["value"] / tp, 4)}})
+        r = bench_gemm_f32_tc(one, max(3, s // 2), 3)
+        emit({"op": "gemm_f32_8192_3xtf32", "value": round(r["value"], 2), "unit": "TFLOP/s", "ms": round(r["ms"], 4),
+              "roofline": {"bound": "tensor", "peak": round(tp / 6, 2), "frac": round(r["value"] / (tp / 6), 4)}})
+        r = measure_rowop(one, "channelscale", s, 3, pk)
+        emit(op_line("channelscale", r, cpu_rowop("channelscale", 8192, 16384) if want_cpu else None))
+        torch.cuda.empty_cache()
+
+        # the BASELINE rows, compact, last before the headline
+        r = measure_gemm_f32(one, s, 3, pk)
+        emit(op_line("gemm_f32_512", r, cpu_gemm_f32() if want_cpu else None))
+        for op in ("reduce", "reduce_scalar", "rmsnorm", "softmax"):
+            r = measure_rowop(one, op, s, 3, pk)
+            cpu = (cpu_reduce_scalar() if op == "reduce_scalar" else cpu_rowop(op, 8192, 16384)) if want_cpu else None
+            emit(op_line(op, r, cpu))
+            torch.cuda.empty_cache()
+        r = measure_conv(one, max(3, s // 2), 3, pk)
+        emit(op_line("conv_n32", r, cpu_conv(32, 256, 56, 56, 256, 1) if want_cpu else None))
+        torch.cuda.empty_cache()
+        r = measure_decode(one, s, 3, pk)
+        emit(op_line("decode_b32", r, cpu_decode() if want_cpu else None))
+        torch.cuda.empty_cache()
 
     if args.op == "all" and world > 1:
         r = bench_conv_sharded(ctx, max(3, min(args.steps, 10)), 3)
-        ops["conv_n32_batch_sharded"] = {"TFLOP/s": round(r["value"], 2), "ms": round(r["ms"], 4),
-                                         "parallelism": r["parallelism"], "scaling": "strong"}
+        if rank == 0:
+            emit({"op": "conv_n32_batch_sharded", "value": round(r["value"], 2), "unit": "TFLOP/s",
+                  "ms": round(r["ms"], 4), "n_gpus": world, "parallelism": r["parallelism"], "scaling": "strong"})
         r = bench_decode_sharded(ctx, max(5, min(args.steps, 20)), 3)
-        ops["decode_chain_b32_column_sharded"] = {"GB/s": round(r["value"], 1), "ms": round(r["ms"], 4),
-                                                  "parallelism": r["parallelism"], "scaling": "strong"}
+        if rank == 0:
+            emit({"op": "decode_b32_column_sharded", "value": round(r["value"], 1), "unit": "GB/s",
+                  "ms": round(r["ms"], 4), "n_gpus": world, "parallelism": r["parallelism"], "scaling": "strong"})
 
-    tflops = g["value"]
-    line = {"metric": METRIC, "value": round(tflops, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(g["ms"], 5), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,0.02) fp16 on device)",
-            "config": {"workload": "f16 GEMM C=A*B, f32 accumulation, f16 out, M=%d N=%d K=%d row-major "
-                                   "(BASELINE configs[3])" % (M, N, K), "M": M, "N": N, "K": K,
-                       "parallelism": g["parallelism"], "l2": "inputs (256 MiB) larger than L2"},
-            "roofline": roofline("tensor", g["kernel_tflops"], pk,
-                                 traffic_for("gemm_f16_%dx%dx%d_n%d" % (M, N, K, world))) if world == 1 else
-            fused_roofline(g, M, N, K, world, pk),
-            "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in g["e2e"].items()},
-            "gpu_launches": g["launches"], "clocks": clocks}
-    line["e2e"]["value"] = round(g["e2e"]["value"], 3)
-    if "allgather_max_abs_diff" in g:
-        line["config"]["allgather_check_max_abs_diff"] = g["allgather_max_abs_diff"]
-    if world == 1 and not args.no_cpu:
-        cb = cpu_gemm_f16(M, N, K, rows=10 * cpu_threads())  # ~10 s of host work
+    g = bench_gemm_f16(ctx, args.steps, args.warmup, M, N, K)
+    clocks = g["clocks"]
+    if clocks:
+        clocks.pop("samples", None)
+
+    roof = roofline("tensor", g["kernel_tflops"], pk, traffic_for("gemm_f16_%dx%dx%d_n%d" % (M, N, K, world))) \
+        if world == 1 else fused_roofline(g, M, N, K, world, pk)
+    roof.pop("peak_source", None)  # in the peaks line
+    line = {"metric": METRIC, "value": round(g["value"], 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(g["ms"], 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic N(0,0.02)",
+            "config": {"workload": "f16 GEMM %dx%dx%d (configs[3])" % (M, N, K), "M": M, "N": N, "K": K,
+                       "parallelism": g["parallelism"] if world > 1 else "1 GPU", "l2": "inputs > L2"},
+            "roofline": roof, "e2e": g["e2e"], "gpu_launches": g["launches"], "clocks": clocks,
+            "sustained": g["sustained"], "check": g["check"]}
+    if world == 1 and want_cpu:
+        cb = cpu_gemm_f16(M, N, K, rows=gemm_f16_cpu_rows())
         line["cpu_baseline"] = {k: (round(v, 6) if isinstance(v, float) else v) for k, v in cb.items()
                                 if k != "seconds"}
-    if ops:
-        line["ops"] = ops
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

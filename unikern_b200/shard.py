@@ -11,10 +11,41 @@ tells every rank its C is complete.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 from . import abi
 
 MAX_RANKS = 8  # the kernel stores to at most 8 copies of C
+_CUDART = None
+CUDA_MEMCPY_DEFAULT = 4
+CUDA_HOST_REGISTER_PORTABLE = 1
+
+
+def cudart():
+    """The CUDA runtime torch loaded (for stream-ordered strided host copies
+    of the host-to-host sharded path; the library's own entry points link a
+    static runtime and are not involved)."""
+    global _CUDART
+    if _CUDART is None:
+        import torch  # noqa: F401  (loads libcudart.so.12 into the process)
+        lib = C.CDLL("libcudart.so.12")
+        lib.cudaMemcpy2DAsync.restype = C.c_int
+        lib.cudaMemcpy2DAsync.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                          C.c_int, C.c_void_p]
+        lib.cudaHostRegister.restype = C.c_int
+        lib.cudaHostRegister.argtypes = [C.c_void_p, C.c_size_t, C.c_uint]
+        lib.cudaHostUnregister.restype = C.c_int
+        lib.cudaHostUnregister.argtypes = [C.c_void_p]
+        _CUDART = lib
+    return _CUDART
+
+
+def copy2d(dst, dpitch, src, spitch, width, height, stream):
+    """height rows of `width` bytes, stream-ordered (cudaMemcpyDefault: either
+    side may be host or device memory)."""
+    rc = cudart().cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, CUDA_MEMCPY_DEFAULT, stream)
+    if rc != 0:
+        raise RuntimeError("cudaMemcpy2DAsync failed with CUDA error %d" % rc)
 
 
 def column_split(N: int, world: int, rank: int, align: int = 8):
@@ -90,6 +121,7 @@ class GemmAllGather:
         order = store_order(self.world, self.rank)
         self.c_list = (C.c_void_p * self.world)(*[self.peers.ptrs[r] for r in order])
         self.ldc = C_full.stride(0)
+        self.c_tensor, self.c_local = C_full, C_full.data_ptr()
         self.flag = torch.zeros(1, device="cuda")
         self.launches_per_step = 1  # this library's kernels per step (the barrier is NCCL's)
 
@@ -117,6 +149,120 @@ class GemmAllGather:
 
     def close(self):
         self.peers.close()
+
+
+class HostGemmF16:
+    """The N-sharded f16 GEMM from and to host memory, as a user of a node's
+    GPUs calls it: A[M][K] and B[K][N] in, C[M][N] out, one host copy of each
+    shared by the ranks (files in /dev/shm mapped by every rank and
+    registered as page-locked memory; private pinned copies where /dev/shm is
+    too small).  Each step, on the launching stream:
+
+    1. rank r uploads its row block of A and its column block of B (a strided
+       2-D copy) over its own host link, so every host byte crosses the host
+       links once per step instead of once per rank;
+    2. an NCCL all-gather over NVLink replicates A (its row blocks are
+       contiguous);
+    3. the GEMM with the fused all-gather of C (GemmAllGather.run);
+    4. rank r downloads only its column block of C (a strided 2-D copy) into
+       the shared host C.
+    """
+
+    def __init__(self, plan, A_src, B_src):
+        import torch
+        import torch.distributed as dist
+        self.plan = plan
+        M, N, K = plan.M, plan.N, plan.K
+        w, r = plan.world, plan.rank
+        self.split_a = M % w == 0
+        self.r0, self.r1 = (M // w * r, M // w * (r + 1)) if self.split_a else (0, M)
+        self.n0, self.n1 = plan.n0, plan.n1
+        need = (M * K + K * N + M * N) * 2
+        st = os.statvfs("/dev/shm") if os.path.isdir("/dev/shm") else None
+        ok = st is not None and st.f_bavail * st.f_frsize > 2 * need
+        self.shared = bool(gather_objects(ok, plan.group) == [True] * w)
+        self.paths = []
+        if self.shared:
+            tag = "uk_e2e_%s_%d_%dx%dx%d" % (os.environ.get("MASTER_PORT", "0"), os.getppid(), M, N, K)
+            bufs = []
+            for name, n in (("A", M * K), ("B", K * N), ("C", M * N)):
+                path = "/dev/shm/%s_%s" % (tag, name)
+                self.paths.append(path)
+                if r == 0:
+                    t = torch.from_file(path, shared=True, size=n, dtype=torch.float16)
+                dist.barrier(group=plan.group)
+                if r != 0:
+                    t = torch.from_file(path, shared=True, size=n, dtype=torch.float16)
+                bufs.append(t)
+            self.Ah, self.Bh, self.Ch = bufs[0].view(M, K), bufs[1].view(K, N), bufs[2].view(M, N)
+            if r == 0:
+                self.Ah.copy_(A_src.cpu())
+                self.Bh.copy_(B_src.cpu())
+            for t in (self.Ah, self.Bh, self.Ch):
+                rc = cudart().cudaHostRegister(t.data_ptr(), t.numel() * 2, CUDA_HOST_REGISTER_PORTABLE)
+                if rc != 0:
+                    raise RuntimeError("cudaHostRegister failed with CUDA error %d" % rc)
+            dist.barrier(group=plan.group)
+        else:
+            self.Ah = A_src.cpu().pin_memory()
+            self.Bh = B_src.cpu().pin_memory()
+            self.Ch = torch.empty((M, N), dtype=torch.float16).pin_memory()
+        self.Ad = torch.empty((M, K), dtype=torch.float16, device="cuda")
+        self.Bd = torch.empty((K, self.n1 - self.n0), dtype=torch.float16, device="cuda")
+        # whole-job bytes per step (the sum over the ranks' links)
+        self.h2d_bytes = (M * K if self.split_a else w * M * K) * 2 + K * N * 2
+        self.d2h_bytes = M * N * 2
+
+    def step(self, stream=None):
+        import torch
+        import torch.distributed as dist
+        p = self.plan
+        s = (stream or torch.cuda.current_stream()).cuda_stream
+        M, N, K = p.M, p.N, p.K
+        nb = self.n1 - self.n0
+        rows = self.r1 - self.r0
+        copy2d(self.Ad.data_ptr() + self.r0 * K * 2, K * 2, self.Ah.data_ptr() + self.r0 * K * 2, K * 2, K * 2,
+               rows, s)
+        copy2d(self.Bd.data_ptr(), nb * 2, self.Bh.data_ptr() + self.n0 * 2, N * 2, nb * 2, K, s)
+        if self.split_a and p.world > 1:
+            dist.all_gather_into_tensor(self.Ad, self.Ad[self.r0:self.r1], group=p.group)
+        p.run(self.Ad, self.Bd, None)
+        copy2d(self.Ch.data_ptr() + self.n0 * 2, N * 2, p.c_local + self.n0 * 2, p.ldc * 2, nb * 2, M, s)
+
+    def check_host(self, step_fn=None):
+        """After one step: the host C against this rank's device C (the full
+        gathered C): max |difference| over the rank's view of the host C (all
+        of it when shared, its own block otherwise), max over ranks."""
+        import torch
+        import torch.distributed as dist
+        (step_fn or self.step)()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.plan.group)
+        dev = self.plan.c_tensor.cpu()
+        cols = slice(None) if self.shared else slice(self.n0, self.n1)
+        d = float((dev[:, cols].float() - self.Ch[:, cols].float()).abs().max().item())
+        t = torch.tensor([d], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.plan.group)
+        return {"max_abs_diff_host_vs_device": float(t.item()), "host_c": "shared" if self.shared else "per rank"}
+
+    def close(self):
+        import torch.distributed as dist
+        torch_sync()
+        if self.shared:
+            for t in (self.Ah, self.Bh, self.Ch):
+                cudart().cudaHostUnregister(t.data_ptr())
+            dist.barrier(group=self.plan.group)
+            if self.plan.rank == 0:
+                for path in self.paths:
+                    try:
+                        os.unlink(path)
+                    except OSError:
+                        pass
+
+
+def torch_sync():
+    import torch
+    torch.cuda.synchronize()
 
 
 def batch_split(N: int, world: int, rank: int):
