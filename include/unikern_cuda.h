@@ -365,6 +365,32 @@ int uk_solve_kml(const char* hcs_json, const char* kml_json, const char* ledger_
 int uk_run_kml(const char* hcs_json, const char* kml_json, const char* ledger_path, int write_ledger, char* out,
                size_t out_cap);
 
+/* run_cuda as a C call: run one tree on the current device exactly as
+ * uk_run_kml does (verify instance checked in fp64 on the GPU against the
+ * dtype's gate, then e2e and kernel-only timing at the declared dims, the
+ * UNIKERN_RESULT line), without the ledger and without solving: tile_m /
+ * tile_n are the caller's solution's tile, reported on the result line.  The
+ * fields of *out are RunOutcome's (include/unikern/codegen.hpp:49-83), so a
+ * reference-side run_cuda(Solution, Hcs, KmlTree, workdir) fills its
+ * RunOutcome from them field by field (src/runner.cpp:195-237 parses the
+ * same values from a HIP program's result line).  migrations / checks are -1
+ * when the run never reached a result line; stream_path is "pinned" once it
+ * ran.  log gets the transcript (UNIKERN_INFO / UNIKERN_RESULT lines, or the
+ * reason it did not run).  Returns UK_OK when *out was filled (the run's own
+ * status is out->exit_code: 0 pass, 1 verify FAIL, 2 unsupported tree, 4 no
+ * usable device or a CUDA error, 5 residency violation), UK_EINVAL when the
+ * HCS or KML is rejected (log gets the reason). */
+typedef struct uk_run_outcome {
+  int built, ran, verified;
+  double max_rel, measured_ms, kernel_ms;
+  int migrations, checks;
+  unsigned long long vram_free, vram_total;
+  int exit_code;
+  char stream_path[16];
+} uk_run_outcome;
+int uk_run_cuda(const char* hcs_json, const char* kml_json, int tile_m, int tile_n, uk_run_outcome* out, char* log,
+                size_t log_cap);
+
 /* `unikern calibrate` (src/main.cpp:573-652, src/solver.cpp:188-245): read the
  * rows the ledger at ledger_path measured under the HCS's fingerprint, take
  * per usable row (measured_ms > kernel_ms > 0) the compulsory bytes of its

@@ -8,8 +8,10 @@ TEST INFRASTRUCTURE ONLY.  Outputs:
 * ``oracle/_ref/libukref.so``  -- the UNIKERN reference's own C++ sources
   (``src/reference.cpp``, ``src/kml.cpp``, ``src/kml_front.cpp``,
   ``src/json_flat.cpp``, ``src/runtime.cpp``, ``src/hcs.cpp``,
-  ``src/solver.cpp``, ``src/codegen_hip.cpp``, ``src/sqlite_ledger.cpp``)
-  compiled unchanged with g++ straight from the reference tree (the SQLite
+  ``src/solver.cpp``, ``src/codegen_hip.cpp``, ``src/sqlite_ledger.cpp``,
+  and the backend registry ``src/backends.cpp`` with the runners and
+  emitters it links: ``src/runner.cpp``, ``src/runner_ocl.cpp``,
+  ``src/runner_metal_stub.cpp``, ``src/codegen_other.cpp``) compiled unchanged with g++ straight from the reference tree (the SQLite
   ledger against the reference's vendored ``sqlite3.h``, linked to the
   system's ``libsqlite3.so.0``), plus ``ref_shim.cpp`` (extern "C"
   forwarding only).  Nothing is copied into the repository.
@@ -47,7 +49,11 @@ def reference_tree():
 
 CFLAGS = ["-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-fopenmp"]
 REF_SOURCES = ["reference", "kml", "kml_front", "json_flat", "runtime", "hcs",
-               "solver", "codegen_hip", "sqlite_ledger"]
+               "solver", "codegen_hip", "sqlite_ledger",
+               # the backend registry (make_backends) and what it links: the
+               # runners (the OpenCL and Metal ones compile to their stubs
+               # without those SDKs) and the other emitters
+               "backends", "runner", "runner_ocl", "runner_metal_stub", "codegen_other"]
 # the reference's SQLite ledger is compiled against its vendored sqlite3.h and
 # linked to the system's SQLite library (the same engine the product loads)
 SQLITE_LIB = "-l:libsqlite3.so.0"

@@ -63,6 +63,7 @@ PROTOTYPES = {
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_solve_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, i32, C.c_char_p, sz]),
+    "uk_run_cuda": (i32, [C.c_char_p, C.c_char_p, i32, i32, vp, C.c_char_p, sz]),
     "uk_calibrate": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz, C.c_char_p, sz]),
 }
 
@@ -314,6 +315,24 @@ def run_kml(hcs_json: str, kml_json: str, ledger: str | None = None, write_ledge
     rc = lib().uk_run_kml(hcs_json.encode(), kml_json.encode(), ledger.encode() if ledger else None,
                           int(write_ledger), buf, len(buf))
     return rc, buf.value.decode()
+
+
+class RunOutcome(C.Structure):
+    """uk_run_outcome: the fields of the reference's RunOutcome."""
+    _fields_ = [("built", i32), ("ran", i32), ("verified", i32), ("max_rel", C.c_double),
+                ("measured_ms", C.c_double), ("kernel_ms", C.c_double), ("migrations", i32), ("checks", i32),
+                ("vram_free", C.c_ulonglong), ("vram_total", C.c_ulonglong), ("exit_code", i32),
+                ("stream_path", C.c_char * 16)]
+
+
+def run_cuda(hcs_json: str, kml_json: str, tile_m: int = 0, tile_n: int = 0):
+    """run_cuda of one tree (no ledger): returns (RunOutcome, log)."""
+    o = RunOutcome()
+    buf = C.create_string_buffer(1 << 16)
+    rc = lib().uk_run_cuda(hcs_json.encode(), kml_json.encode(), tile_m, tile_n, C.byref(o), buf, len(buf))
+    if rc != 0:
+        raise UkError(rc, buf.value.decode())
+    return o, buf.value.decode()
 
 
 def solve_kml(hcs_json: str, kml_json: str, ledger: str | None = None, write_ledger: bool = True, sms: int = 0):

@@ -1,6 +1,7 @@
 // kml_abi.cpp -- C entry points of the host runner (declared in
 // include/unikern_cuda.h): the KML contract queries and `solve` (no GPU
 // needed), and the nvidia branch of the reference's `run`/`verify` flow.
+#include <cstdio>
 #include <cstring>
 #include <sstream>
 #include <string>
@@ -89,6 +90,45 @@ int uk_solve_kml(const char* hcs_json, const char* kml_json, const char* ledger_
       ukb::solve_kml(hcs_json, kml_json, ledger_path ? ledger_path : "", write_ledger != 0, sms, &transcript);
   if (out != nullptr && out_cap > 0) put(transcript, out, out_cap);
   return rc;
+}
+
+int uk_run_cuda(const char* hcs_json, const char* kml_json, int tile_m, int tile_n, uk_run_outcome* out, char* log,
+                size_t log_cap) {
+  if (hcs_json == nullptr || kml_json == nullptr || out == nullptr) {
+    put("hcs_json, kml_json and out are required", log, log_cap);
+    return UK_EINVAL;
+  }
+  std::string err;
+  const auto hcs = ukb::hcs_import(hcs_json, &err);
+  if (!hcs) {
+    put("HCS " + err, log, log_cap);
+    return UK_EINVAL;
+  }
+  const auto tree = ukb::kml_import(kml_json, &err);
+  if (!tree) {
+    put("KML " + err, log, log_cap);
+    return UK_EINVAL;
+  }
+  ukb::Solution sol;
+  sol.best.tile_m = tile_m;
+  sol.best.tile_n = tile_n;
+  sol.feasible_count = 1;
+  const ukb::RunOutcome r = ukb::run_cuda(sol, *hcs, *tree, "");
+  *out = uk_run_outcome{};
+  out->built = r.built;
+  out->ran = r.ran;
+  out->verified = r.verified;
+  out->max_rel = r.max_rel;
+  out->measured_ms = r.measured_ms;
+  out->kernel_ms = r.kernel_ms;
+  out->migrations = r.migrations;
+  out->checks = r.checks;
+  out->vram_free = r.vram_free;
+  out->vram_total = r.vram_total;
+  out->exit_code = r.exit_code;
+  std::snprintf(out->stream_path, sizeof out->stream_path, "%s", r.stream_path.c_str());
+  if (log != nullptr && log_cap > 0) put(r.log, log, log_cap);
+  return UK_OK;
 }
 
 int uk_calibrate(const char* hcs_json, const char* ledger_path, int allow_unified, char* hcs_out, size_t hcs_cap,
