@@ -440,7 +440,7 @@ def check_gemm_f16(A, B, Cm, rows, points=0, seed=0):
     return err, len(idx)
 
 
-def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
+def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192, profile_only=False):
     import unikern_b200.abi as abi
     torch = ctx.torch
     world, rank = ctx.world, ctx.rank
@@ -490,6 +490,10 @@ def bench_gemm_f16(ctx, steps, warmup, M=8192, N=8192, K=8192):
            "parallelism": parallelism, "kernel_ms": kernel_ms, "kernel_tflops": flops_per_launch / kernel_ms / 1e9,
            "clocks": clocks}
 
+    if profile_only:  # --no-e2e: the timed steps alone (ncu captures of this kernel)
+        if plan is not None:
+            plan.close()
+        return res
     # sustained: the same step back to back for ~1.7 s with clocks sampled,
     # so the power-capped rate is measured beside the burst figure above
     sampler = ClockSampler(ctx.local_rank).start()
@@ -995,7 +999,7 @@ def main():
                     help="all = every op, headline f16 GEMM last; otherwise one op alone (profiling)")
     ap.add_argument("--gemm-shape", default="8192,8192,8192", help="M,N,K of the f16 GEMM")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
-    ap.add_argument("--no-e2e", action="store_true", help="single-op runs: device-resident timing only")
+    ap.add_argument("--no-e2e", action="store_true", help="one op's device-resident timing only (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1075,7 +1079,16 @@ def main():
             emit({"op": "decode_b32_column_sharded", "value": round(r["value"], 1), "unit": "GB/s",
                   "ms": round(r["ms"], 4), "n_gpus": world, "parallelism": r["parallelism"], "scaling": "strong"})
 
-    g = bench_gemm_f16(ctx, args.steps, args.warmup, M, N, K)
+    g = bench_gemm_f16(ctx, args.steps, args.warmup, M, N, K, profile_only=args.no_e2e)
+    if args.no_e2e:
+        if rank == 0:
+            emit({"op": "gemm_f16", "value": round(g["value"], 3), "unit": "TFLOP/s", "ms": round(g["ms"], 5),
+                  "kernel_ms": round(g["kernel_ms"], 5), "n_gpus": world, "steps": args.steps,
+                  "config": {"M": M, "N": N, "K": K}, "note": "--no-e2e: timed steps only"})
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return 0
     clocks = g["clocks"]
     if clocks:
         clocks.pop("samples", None)

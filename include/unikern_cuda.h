@@ -63,6 +63,25 @@ int uk_cuda_device_supported(void);
 #define UK_OP_CHANNELSCALE 5
 int uk_cuda_tile_plan(int op, int f16, const int64_t* dims, int sms, int* out4);
 
+/* The GEMM solve behind that plan (op = UK_OP_GEMM; dims M, N, K): the
+ * re-target of the reference's solver (src/solver.cpp:14-186: candidate
+ * grid, feasibility, pure cost, lexicographic argmin) to this library's
+ * kernels.  Candidates are kernel families with their tile and K split:
+ * the FFMA tiles 128x128, 64x64 and 32x64 (the last with K split over 2, 4 or
+ * 8 CTAs), and for fp32 with allow_tc the split-tf32 pair kernel (K % 32,
+ * N % 64, from 2^30 multiply-adds); for f16 (the tensor-core shape rules
+ * hold) the single-SM 128x256 and SM-pair 256x256 tcgen05 kernels.  Cost =
+ * predicted device time from wave counts at each family's measured
+ * efficiency, pre-passes, folds and launches.  out8 = {family (0 FFMA, 1
+ * tcgen05 single-SM, 2 tcgen05 pair, 3 split-tf32 pair), tile_m, tile_n,
+ * k_block, stages, k_split, feasible candidates, predicted ns}.  The GEMM
+ * launchers take the same argmin.  Host only; with sms > 0 it needs no GPU. */
+int uk_cuda_solve_plan(int op, int f16, const int64_t* dims, int sms, int allow_tc, int* out8);
+/* The plan of the last GEMM launched on the calling thread, as out6 =
+ * {family, tile_m, tile_n, k_block, stages, k_split} (family -1 before any):
+ * how a caller sees the solver's choice reach the launcher. */
+int uk_cuda_last_launch(int* out6);
+
 /* ---- channelscale ----------------------------------------------------------
  * Y[i*C + c] = X[i*C + c] * S[c] for i < L, c < C.  Bit-exact to the reference.
  * Replaces uk_channelscale (src/codegen_hip.cpp:2329-2335). */

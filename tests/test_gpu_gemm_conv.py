@@ -120,3 +120,35 @@ def test_conv_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):
     abi.conv2d(dev(x), dev(w), y, N, H, W, Cc, K, K, Oc, pad, dev(s) if scaled else None, abi.UK_CONV_NCHW)
     ref = O.conv_nchw(x, w, s, pad)
     assert O.rel_err(host(y), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+
+
+# ---- the solver's choice reaches the launcher ----------------------------------
+
+@pytest.mark.parametrize("M,N,K,f16", [(640, 15104, 4096, True), (640, 16384, 4096, True), (512, 512, 512, False),
+                                       (1024, 768, 1000, False), (4096, 4096, 4096, False)])
+def test_launcher_runs_the_solver_argmin(M, N, K, f16):
+    # the GEMM entry point launches the kernel family, tile and K split the
+    # solver chose (uk_cuda_last_launch), and its result passes the gate
+    want = abi.solve_plan(M, N, K, f16)
+    rng = np.random.default_rng(M + N + K)
+    rows = [0, M // 2, M - 1]
+    if f16:
+        A = O.f32_to_f16(rng.normal(0, 0.5, (M, K)).astype(np.float32))
+        B = O.f32_to_f16(rng.normal(0, 0.5, (K, N)).astype(np.float32))
+        got = gemm16(A, B)
+        ref = O.gemm_f16_f64(A[rows], B, threads=8)
+        tol = F16_TOL
+    else:
+        A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+        B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+        Cm = empty((M, N))
+        if want["family"] == "tcgen05-2sm-3xtf32":
+            abi.gemm_f32_tc(dev(A), dev(B), Cm)
+        else:
+            abi.gemm_f32(dev(A), dev(B), Cm)
+        got = host(Cm)
+        ref = O.gemm_f64(A[rows], B, threads=8)
+        tol = F32_TOL
+    ran = abi.last_launch()
+    assert (ran["family"], ran["tile"], ran["k_split"]) == (want["family"], want["tile"], want["k_split"]), (ran, want)
+    assert O.rel_err(got[rows], ref, SUM_TAU * O.rms(ref)) <= tol

@@ -88,9 +88,12 @@ def test_verify_mode_writes_no_ledger(tmp_path):
 def test_oversized_payload_is_refused_when_b_does_not_fit(tmp_path):
     # B alone is 262144^2 fp32 = 256 GiB: beyond 0.85 x HBM, so not even the
     # streamed GEMM (B resident) can run it
-    rc, out = abi.run_kml(HCS, '{"op":"gemm","dtype":"fp32","dims":[1024,262144,262144]}', str(tmp_path / "l"))
+    import sqlite3
+    ledger = tmp_path / "ledger.sqlite3"
+    rc, out = abi.run_kml(HCS, '{"op":"gemm","dtype":"fp32","dims":[1024,262144,262144]}', str(ledger))
     assert rc == 1 and "UNIKERN_ERROR what=stream_refused" in out
-    assert not (tmp_path / "l").exists()
+    with sqlite3.connect(ledger) as db:  # opened (as the reference opens it), nothing committed
+        assert db.execute("SELECT count(*) FROM solutions").fetchone()[0] == 0
 
 
 def small_vram_hcs(mib):
@@ -161,9 +164,9 @@ def test_reduce_width_knob(tmp_path, monkeypatch):
     assert abi.result_tokens(out)["max_rel"] == "0.000000e+00"
     for bad in ("100", "2000000", "abc"):
         monkeypatch.setenv("UK_REDUCE_WIDTH", bad)
-        rc, out = abi.run_kml(HCS, kml, str(tmp_path / "l"), write_ledger=True)
+        rc, out = abi.run_kml(HCS, kml, str(tmp_path / "l.jsonl"), write_ledger=True)
         assert rc == 1 and "UNIKERN_ERROR what=reduce_width_pin_unfit value=" + bad in out, out
-        assert not (tmp_path / "l").exists()
+        assert not (tmp_path / "l.jsonl").exists()
 
 
 def test_stream_path_knob(tmp_path, monkeypatch):
@@ -177,3 +180,37 @@ def test_stream_path_knob(tmp_path, monkeypatch):
         monkeypatch.setenv("UK_GEMM_STREAM_PATH", bad)
         rc, out = abi.run_kml(small_vram_hcs(16), kml, None, write_ledger=False)
         assert rc == 1 and "UNIKERN_ERROR what=stream_path_pin_unfit val=" + bad in out, out
+
+
+def test_run_commits_an_sqlite_row_both_tools_read(tmp_path):
+    # the reference's default ledger is SQLite (src/main.cpp:37, :61-70): a
+    # verified run's row is a HIT for the reference's own lookup, a second
+    # run is a HIT here that replaces the row, and a row the reference
+    # commits is a HIT for uk_run_kml
+    import ctypes as C
+    import sqlite3
+
+    from oracle import oracle as O
+    ledger = tmp_path / "ledger.sqlite3"
+    kml = '{"op":"gemm","dtype":"fp32","dims":[512,512,512]}'
+    rc, out = abi.run_kml(HCS, kml, str(ledger))
+    assert rc == 0 and "LEDGER COMMIT" in out, out
+    with sqlite3.connect(ledger) as db:
+        rows = db.execute("SELECT key, c_ms, measured_ms, kernel_ms, tm, tn FROM solutions").fetchall()
+    assert len(rows) == 1 and rows[0][0] == abi.kml_describe(kml, HCS)["ledger_key"]
+    assert rows[0][2] > rows[0][3] > 0  # measured_ms (e2e) > kernel_ms > 0
+    rc, out = abi.run_kml(HCS, kml, str(ledger))
+    assert rc == 0 and "LEDGER HIT" in out, out
+    with sqlite3.connect(ledger) as db:
+        assert db.execute("SELECT count(*) FROM solutions").fetchone()[0] == 1
+    r = O.ref()
+    if r is None:
+        return
+    buf = C.create_string_buffer(4096)
+    assert r.ref_ledger_lookup(str(ledger).encode(), kml.encode(), HCS.encode(), buf, len(buf)) == 1
+    c_ms, tm, tn, _ = buf.value.decode().split(" ", 3)
+    assert (int(tm), int(tn)) == rows[0][4:6]
+    other = '{"op":"reduce","dtype":"fp32","dims":[1048576]}'
+    assert r.ref_ledger_commit(str(ledger).encode(), other.encode(), HCS.encode(), -1.0, 0.0) == 0
+    rc, out = abi.run_kml(HCS, other, str(ledger))
+    assert rc == 0 and "LEDGER HIT" in out, out

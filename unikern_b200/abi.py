@@ -60,6 +60,8 @@ PROTOTYPES = {
     "uk_cuda_gemm_streamed_ring_size": (sz, [i32, i32, i32, i32, i32]),
     "uk_cuda_gemm_streamed": (i32, [vp, vp, vp, vp, vp, sz, i32, i32, i32, i32, i32, vp]),
     "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
+    "uk_cuda_solve_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, i32, C.POINTER(C.c_int)]),
+    "uk_cuda_last_launch": (i32, [C.POINTER(C.c_int)]),
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_solve_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, i32, C.c_char_p, sz]),
@@ -292,6 +294,25 @@ def tile_plan(op: str, dims, f16: bool = False, sms: int = 0):
     out = (C.c_int * 4)()
     check(lib().uk_cuda_tile_plan(UK_OP[op], int(f16), d, sms, out))
     return tuple(out)
+
+
+FAMILIES = {0: "ffma", 1: "tcgen05-1sm", 2: "tcgen05-2sm", 3: "tcgen05-2sm-3xtf32"}
+
+
+def solve_plan(M: int, N: int, K: int, f16: bool = False, sms: int = 0, allow_tc: bool = True):
+    """The GEMM solve: dict(family, tile, k_block, stages, k_split, feasible, ns)."""
+    d = (C.c_int64 * 6)(M, N, K, 0, 0, 0)
+    out = (C.c_int * 8)()
+    check(lib().uk_cuda_solve_plan(UK_OP["gemm"], int(f16), d, sms, int(allow_tc), out))
+    return {"family": FAMILIES.get(out[0], out[0]), "tile": (out[1], out[2]), "k_block": out[3], "stages": out[4],
+            "k_split": out[5], "feasible": out[6], "ns": out[7]}
+
+
+def last_launch():
+    """The plan of the last GEMM this thread launched: dict(family, tile, k_split)."""
+    out = (C.c_int * 6)()
+    check(lib().uk_cuda_last_launch(out))
+    return {"family": FAMILIES.get(out[0], out[0]), "tile": (out[1], out[2]), "k_split": out[5]}
 
 
 def kml_describe(kml_json: str, hcs_json: str | None = None, sms: int = 0):

@@ -36,6 +36,7 @@
 
 #include "sm100_ptx.cuh"
 #include "uk_common.cuh"
+#include "uk_plan.cuh"
 
 namespace uk {
 __device__ unsigned int g_conv_fault = 0;
@@ -1203,6 +1204,7 @@ int gemm_f32_tc_run(const float* A, const void* bws, void* aws, float* C, int M,
   if (int rc = uk::check_launch("gemm_f32(split)")) return rc;
   const float* Th = (const float*)bws;
   const float* Tl = (const float*)((const uint8_t*)bws + align256((size_t)N * K * 4));
+  note_launch(Candidate{kFamTf32x3, kConvPairF32Tile, 1, 0.0});
   return run_tc(Th, Tl, Ah, Al, C, nullptr, 1, N / 64, 64, K, 1, 1, M, 0, part, part_room, st);
 }
 
@@ -1214,9 +1216,10 @@ extern "C" size_t uk_cuda_gemm_f32_workspace_size(int M, int N, int K) {
 }
 
 extern "C" int uk_cuda_gemm_f32_prefers_tc(int M, int N, int K) {
-  // from about 2^30 multiply-adds the tensor cores win; below, the FFMA
-  // kernel is as fast and needs no workspace
-  return uk::gemm_f32_tc_shape(M, N, K) && (int64_t)M * N * K >= ((int64_t)1 << 30);
+  // the solver's argmin over the FFMA and split-tf32 candidates (the latter
+  // only from 2^30 multiply-adds; below, its pre-passes are never repaid)
+  if (!uk::gemm_f32_tc_shape(M, N, K)) return 0;
+  return uk::solve_gemm(M, N, K, false, true, uk::sm_count()).family == uk::kFamTf32x3;
 }
 
 extern "C" int uk_cuda_gemm_f32_ws(const float* A, const float* B, float* C, int M, int N, int K, void* workspace,

@@ -329,19 +329,29 @@ int gemm_f16_tc_2sm(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t l
 // before its next tile: measured on 8 GPUs, the single-SM kernel is faster
 // there (0.186 vs 0.284 ms per step).  UNIKERN_GEMM_F16_PAIR=0 selects the
 // single-SM kernel everywhere (for comparisons).
-static bool use_pair_kernel(int M, int nc) {
-  static int env = -1;
+// With one or two copies the solver's argmin decides between the two kernels
+// (wave quantization of 128 x 256 tiles on SMs against 256 x 256 on pairs);
+// UNIKERN_GEMM_F16_PAIR=1 / =0 pins the pair / single-SM kernel instead (for
+// measuring the alternative to the solver's choice).
+static bool use_pair_kernel(int M, int N, int K, int nc) {
+  static int env = -1;  // -1 unread, 0 single, 1 pair, 2 solver
   if (env < 0) {
     const char* e = getenv("UNIKERN_GEMM_F16_PAIR");
-    env = (e != nullptr && e[0] == '0') ? 0 : 1;
+    env = e == nullptr || e[0] == 0 ? 2 : e[0] == '0' ? 0 : 1;
   }
-  return env == 1 && M > 128 && nc <= 2;
+  if (env == 0 || nc > 2 || M <= 128) return false;
+  if (env == 1) return true;
+  return solve_gemm(M, N, K, true, false, sm_count()).family == kFamF16Pair;
 }
 
 int gemm_f16_tc(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, uint16_t* const* Cs, int nc,
                 int64_t ldc, int M, int N, int K, cudaStream_t st) {
   if (nc < 1 || nc > MAX_OUT) return fail(UK_EINVAL, "gemm_f16: 1..%d outputs, got %d", MAX_OUT, nc);
-  if (use_pair_kernel(M, nc)) return gemm_f16_tc_2sm(A, lda, B, ldb, Cs, nc, ldc, M, N, K, st);
+  if (use_pair_kernel(M, N, K, nc)) {
+    note_launch(Candidate{kFamF16Pair, kGemmF16PairTile, 1, 0.0});
+    return gemm_f16_tc_2sm(A, lda, B, ldb, Cs, nc, ldc, M, N, K, st);
+  }
+  note_launch(Candidate{kFamF16Single, kGemmF16Tile, 1, 0.0});
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM)) return rc;
   if (int rc = make_map(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK)) return rc;

@@ -16,6 +16,9 @@
 // cluster in rank order -- deterministic, no workspace.
 #include <cuda_fp16.h>
 
+#include <cstdio>
+#include <cstdlib>
+
 #include "sm100_ptx.cuh"
 #include "uk_common.cuh"
 #include "uk_plan.cuh"
@@ -293,26 +296,49 @@ void launch_split(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda
   else cudaLaunchKernelEx(&cfg, k_sgemm<32, 64, BK, 4, 4, false, T, KS>, A, B, C, M, N, K, lda, ldb, ldc);
 }
 
-// tile choice (uk::sgemm_tile): the largest tile that still gives every SM a
-// CTA; small problems fall to smaller tiles (512^3: 128 CTAs of 32x64), and
-// when even those leave the GPU short of work, K is split over a cluster
-// (uk::sgemm_ksplit: 512^3 -> 4 CTAs per tile, 512 CTAs)
+// A pinned FFMA plan from UK_SGEMM_PLAN="bm,bn,ks" (a measurement knob, like
+// the reference's UK_CONV_TILE): one of the compiled variants 128,128,1 /
+// 64,64,1 / 32,64,{1,2,4,8}.  Returns 0 with *c set, 1 when unset, 2 when
+// the value names no compiled variant (the call is then refused).
+int pinned_plan(uk::Candidate* c) {
+  const char* e = getenv("UK_SGEMM_PLAN");
+  if (e == nullptr || e[0] == 0) return 1;
+  int bm = 0, bn = 0, ks = 0;
+  if (sscanf(e, "%d,%d,%d", &bm, &bn, &ks) != 3) return 2;
+  const bool ok = (bm == 128 && bn == 128 && ks == 1) || (bm == 64 && bn == 64 && ks == 1) ||
+                  (bm == 32 && bn == 64 && (ks == 1 || ks == 2 || ks == 4 || ks == 8));
+  if (!ok) return 2;
+  *c = uk::Candidate{uk::kFamSgemm, uk::Tile{bm, bn, bm == 32 ? 16 : 8, 2}, ks, 0.0};
+  return 0;
+}
+
+// tile and K split: the solver's argmin over the FFMA candidates
+// (uk::solve_gemm; 512^3 -> 32 x 64 tiles, K split over 4-CTA clusters)
 template <typename T>
-void simt_gemm(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
-               cudaStream_t st) {
-  const int64_t sms = uk::sm_count();
-  const uk::Tile t = uk::sgemm_tile(M, N, sms);
-  if (t.bm == 128) {
+int simt_gemm(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
+              cudaStream_t st) {
+  uk::Candidate c = uk::solve_gemm(M, N, K, /*f16*/ false, /*allow_tc*/ false, uk::sm_count());
+  const int pin = pinned_plan(&c);
+  if (pin == 2)
+    return uk::fail(UK_EINVAL, "gemm: UK_SGEMM_PLAN=%s names no compiled FFMA plan (128,128,1 64,64,1 32,64,{1,2,4,8})",
+                    getenv("UK_SGEMM_PLAN"));
+  if (pin == 0 && c.ksplit > 1 && K / c.ksplit < 16)
+    return uk::fail(UK_EINVAL, "gemm: UK_SGEMM_PLAN k split %d leaves less than 16 of K=%d per CTA", c.ksplit, K);
+  uk::note_launch(c);
+  if (c.tile.bm == 128) {
     launch<128, 128, 8, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
-  } else if (t.bm == 64) {
+  } else if (c.tile.bm == 64) {
     launch<64, 64, 8, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  } else if (c.ksplit == 8) {
+    launch_split<8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  } else if (c.ksplit == 4) {
+    launch_split<4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  } else if (c.ksplit == 2) {
+    launch_split<2>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   } else {
-    const int ks = uk::sgemm_ksplit(M, N, K, sms);
-    if (ks == 8) launch_split<8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
-    else if (ks == 4) launch_split<4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
-    else if (ks == 2) launch_split<2>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
-    else launch<32, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    launch<32, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   }
+  return UK_OK;
 }
 
 }  // namespace
@@ -328,7 +354,7 @@ int gemm_f16_simt(const __half* A, int64_t lda, const __half* B, int64_t ldb, __
   }
   const bool vec = K % 4 == 0 && N % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 && ldc % 4 == 0 &&
                    ((uintptr_t)A & 7) == 0 && ((uintptr_t)B & 7) == 0 && ((uintptr_t)C & 7) == 0;
-  simt_gemm<__half>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  if (int rc = simt_gemm<__half>(A, B, C, M, N, K, lda, ldb, ldc, vec, st)) return rc;
   return check_launch("gemm_f16(simt)");
 }
 }  // namespace uk
@@ -346,6 +372,6 @@ extern "C" int uk_cuda_gemm_f32(const float* A, const float* B, float* C, int M,
   if (int rc = uk::check_device_ptr(B, "B")) return rc;
   if ((M + 31) / 32 > 65535) return uk::fail(UK_EINVAL, "gemm_f32: M=%d exceeds the grid limit", M);
   const bool vec = K % 4 == 0 && N % 4 == 0 && uk::aligned16(A) && uk::aligned16(B) && uk::aligned16(C);
-  simt_gemm<float>(A, B, C, M, N, K, K, N, N, vec, st);
+  if (int rc = simt_gemm<float>(A, B, C, M, N, K, K, N, N, vec, st)) return rc;
   return uk::check_launch("gemm_f32");
 }

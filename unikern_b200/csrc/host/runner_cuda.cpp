@@ -329,6 +329,23 @@ Solution solve_b200(const Hcs& h, const KmlTree& t, int sms) {
   if (uk_cuda_tile_plan(uk_op_of(t.op), t.dtype == DType::F16, dims, sms, tile) != UK_OK) return s;
   s.best = {tile[0], tile[1], tile[2], tile[3]};
   s.feasible_count = 1;
+  // a GEMM is solved over the candidate grid (kernel family x tile x K split);
+  // |X| is the number of feasible candidates, the tile the argmin's
+  std::string family;
+  int ksplit = 1;
+  double device_us = 0;
+  if (t.op == OpKind::Gemm) {
+    const bool f16 = t.dtype == DType::F16;
+    int plan[8] = {0};
+    if (uk_cuda_solve_plan(UK_OP_GEMM, f16 && dims[1] % 8 == 0 && dims[2] % 8 == 0, dims, sms, !f16, plan) ==
+        UK_OK) {
+      static const char* names[] = {"ffma", "tcgen05-1sm", "tcgen05-2sm", "tcgen05-2sm-3xtf32"};
+      family = plan[0] >= 0 && plan[0] < 4 ? names[plan[0]] : "?";
+      ksplit = plan[5];
+      s.feasible_count = plan[6];
+      device_us = plan[7] / 1000.0;
+    }
+  }
   // predicted time: compute or device memory, whichever binds, scaled by the
   // SMs a tile grid leaves idle; plus the host link copies that the measured
   // (end-to-end) time includes
@@ -364,6 +381,8 @@ Solution solve_b200(const Hcs& h, const KmlTree& t, int sms) {
     pr << "placement: resident on " << h.device << " (sm_100a) tile=" << tile[0] << "x" << tile[1]
        << " k_block=" << tile[2] << " stages=" << tile[3] << " path=pinned-copy";
   }
+  if (!family.empty())
+    pr << " kernel=" << family << " k_split=" << ksplit << " predicted_device_us=" << device_us;
   s.placement_record = pr.str();
   return s;
 }

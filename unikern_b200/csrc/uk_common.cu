@@ -9,6 +9,9 @@
 namespace uk {
 
 static thread_local std::string g_last_error;
+static thread_local Candidate g_last_launch;
+
+void note_launch(const Candidate& c) { g_last_launch = c; }
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
@@ -76,18 +79,47 @@ int uk_cuda_device_supported(void) {
   return major == 10 && minor == 0;
 }
 
+int uk_cuda_solve_plan(int op, int f16, const int64_t* dims, int sms, int allow_tc, int* out8) {
+  if (dims == nullptr || out8 == nullptr) return uk::fail(UK_EINVAL, "solve_plan: NULL dims or out8");
+  if (op != UK_OP_GEMM) return uk::fail(UK_EINVAL, "solve_plan: the candidate grid covers op=gemm (%d given)", op);
+  if (sms < 0 || dims[0] < 0 || dims[1] < 0 || dims[2] < 0) return uk::fail(UK_EINVAL, "solve_plan: negative size");
+  const int64_t n_sm = sms > 0 ? sms : uk::sm_count();
+  int nf = 0;
+  const uk::Candidate c = uk::solve_gemm(dims[0], dims[1], dims[2], f16 != 0, allow_tc != 0, n_sm, &nf);
+  out8[0] = c.family;
+  out8[1] = c.tile.bm;
+  out8[2] = c.tile.bn;
+  out8[3] = c.tile.bk;
+  out8[4] = c.tile.stages;
+  out8[5] = c.ksplit;
+  out8[6] = nf;
+  out8[7] = (int)(c.us * 1000.0 + 0.5);  // ns
+  return UK_OK;
+}
+
+int uk_cuda_last_launch(int* out6) {
+  if (out6 == nullptr) return uk::fail(UK_EINVAL, "last_launch: NULL out6");
+  const uk::Candidate& c = uk::g_last_launch;
+  out6[0] = c.family;
+  out6[1] = c.tile.bm;
+  out6[2] = c.tile.bn;
+  out6[3] = c.tile.bk;
+  out6[4] = c.tile.stages;
+  out6[5] = c.ksplit;
+  return UK_OK;
+}
+
 int uk_cuda_tile_plan(int op, int f16, const int64_t* dims, int sms, int* out4) {
   if (dims == nullptr || out4 == nullptr) return uk::fail(UK_EINVAL, "tile_plan: NULL dims or out4");
   if (sms < 0) return uk::fail(UK_EINVAL, "tile_plan: sms < 0");
   const int64_t n_sm = sms > 0 ? sms : uk::sm_count();
   uk::Tile t{0, 0, 0, 0};
   switch (op) {
-    case UK_OP_GEMM:  // dims M, N, K
-      if (f16 && dims[2] % 8 == 0 && dims[1] % 8 == 0) t = dims[0] > 128 ? uk::kGemmF16PairTile : uk::kGemmF16Tile;
-      else if (!f16 && uk_cuda_gemm_f32_prefers_tc((int)dims[0], (int)dims[1], (int)dims[2]))
-        t = uk::kConvPairF32Tile;  // split-tf32 on the convolution's pair kernel
-      else t = uk::sgemm_tile(dims[0], dims[1], n_sm);
+    case UK_OP_GEMM: {  // dims M, N, K: the solver's argmin (the launchers take the same)
+      const bool tc16 = f16 && dims[2] % 8 == 0 && dims[1] % 8 == 0;
+      t = uk::solve_gemm(dims[0], dims[1], dims[2], tc16, /*allow_tc*/ !f16, n_sm).tile;
       break;
+    }
     case UK_OP_CONV: {  // KML dims H, W, C, Kh, Kw, Oc (one image, valid)
       const int64_t npix = (dims[0] - dims[3] + 1) * (dims[1] - dims[4] + 1);
       if (f16) t = uk::kConvPairF16Tile;

@@ -28,6 +28,10 @@ int check_launch(const char* what);
 
 int sm_count();  // multiprocessors of the current device (cached per device)
 
+struct Candidate;
+// the plan of the last GEMM this thread launched (uk_cuda_last_launch)
+void note_launch(const Candidate& c);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace uk

@@ -24,27 +24,6 @@ struct Tile {
 constexpr Tile kGemmF16Tile = {128, 256, 64, 4};
 constexpr Tile kGemmF16PairTile = {256, 256, 64, 6};
 
-// f32 FFMA GEMM (and the CUDA-core f16 path): the largest tile that still
-// gives every SM a CTA; double-buffered shared memory (2 stages)
-inline Tile sgemm_tile(int64_t M, int64_t N, int64_t sms) {
-  auto ctas = [&](int bm, int bn) { return ((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
-  if (ctas(128, 128) >= sms) return {128, 128, 8, 2};
-  if (ctas(64, 64) >= sms) return {64, 64, 8, 2};
-  return {32, 64, 16, 2};
-}
-
-// K split of the smallest f32 tile (32 x 64): CTAs per tile (a cluster along
-// K) so that up to UK_SGEMM_SPLIT_CAP CTAs per SM run, each keeping >= 64 of K
-#ifndef UK_SGEMM_SPLIT_CAP
-#define UK_SGEMM_SPLIT_CAP 4
-#endif
-inline int sgemm_ksplit(int64_t M, int64_t N, int64_t K, int64_t sms) {
-  const int64_t ctas = ((M + 31) / 32) * ((N + 63) / 64);
-  int ks = 1;
-  while (ks < 8 && ctas * ks * 2 <= UK_SGEMM_SPLIT_CAP * sms && K / (ks * 2) >= 64) ks *= 2;
-  return ks;
-}
-
 // the tensor-core convolutions on SM pairs (also the fp32 GEMM run as a 1 x 1
 // convolution): 256 output channels x 256 pixels per pair, 32 fp32 channels
 // (split-tf32, 3 stages) or 64 fp16 channels (6 stages) per k-step
@@ -99,6 +78,184 @@ inline ReducePlan plan_reduce(int64_t rows, int64_t cols, int64_t sms) {
   chunk = (chunk + 3) / 4 * 4;
   splits = (cols + chunk - 1) / chunk;
   return {3, splits, chunk};
+}
+
+// ---- solve: the Blackwell candidate grid ---------------------------------------
+//
+// The re-target of the reference's solver (src/solver.cpp): sketch a grid of
+// candidates (:14-47), keep the feasible ones (:54-77), cost each with a pure
+// function of the shape and the machine (:81-120), and take the lexicographic
+// argmin of (cost, candidate key) (:153-179).  Here a candidate is a kernel
+// family with its tile, K split and stage count, and the cost is device time:
+//   waves x (work one SM does per wave) / (its peak x the family's measured
+//   efficiency), plus the fixed latency of a tile, the pre-passes the family
+//   needs, the split fold and one launch per kernel;
+// and never less than the compulsory bytes over HBM bandwidth.  The launchers
+// call the same argmin, so the solver's choice is the kernel that runs, and
+// uk_cuda_tile_plan / the ledger's tm, tn report it.
+
+enum Family : int {
+  kFamSgemm = 0,      // FFMA register-blocked GEMM (gemm_f32.cu)
+  kFamF16Single = 1,  // tcgen05 cta_group::1, 128 x 256 per SM (gemm_f16.cu)
+  kFamF16Pair = 2,    // tcgen05 cta_group::2, 256 x 256 per SM pair (gemm_f16_2sm.cu)
+  kFamTf32x3 = 3,     // fp32 as split-tf32 on the conv pair kernel (conv_tc.cu)
+  kFamConvFfma = 4,   // FFMA implicit-GEMM conv (conv_f32.cu)
+  kFamConvPair = 5,   // tcgen05 conv on SM pairs, split-tf32 or f16 (conv_tc.cu)
+};
+
+inline const char* family_name(int f) {
+  switch (f) {
+    case kFamSgemm: return "ffma";
+    case kFamF16Single: return "tcgen05-1sm";
+    case kFamF16Pair: return "tcgen05-2sm";
+    case kFamTf32x3: return "tcgen05-2sm-3xtf32";
+    case kFamConvFfma: return "ffma-conv";
+    case kFamConvPair: return "tcgen05-2sm-conv";
+  }
+  return "?";
+}
+
+struct Candidate {
+  int family = -1;
+  Tile tile{0, 0, 0, 0};
+  int ksplit = 1;
+  double us = 0;  // predicted device time
+};
+
+// The machine model: a B200 at 1965 MHz.  Peaks: the measured dense f16
+// tensor rate and copy bandwidth of this pool's B200s, the nominal FFMA rate.
+// Efficiencies are the measured fraction of peak each family sustains in
+// steady state (tensor-pipe activity in ncu for the tcgen05 kernels: 92 % for
+// the pair GEMM, 81 % single-SM, 91 % for the split-tf32 pair kernel; the
+// FFMA tiles from their measured rates), and lat_us the fixed cost of one
+// tile (pipeline fill and epilogue drain).
+struct CostModel {
+  double f16_tflops = 1620.0;
+  double ffma_tflops = 74.4;
+  double hbm_gbs = 6544.0;
+  double launch_us = 2.0;
+};
+
+namespace detail {
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// time of `units` equal work items of `flops` each on `slots` processors
+// (SMs or SM pairs), each slot at `rate` flop/s; items go round-robin
+inline double waves_us(int64_t units, int64_t slots, double flops, double rate, double lat_us) {
+  const int64_t waves = cdiv(units, slots > 0 ? slots : 1);
+  return (double)waves * (flops / rate * 1e6 + lat_us);
+}
+
+// FFMA tile shapes the sgemm kernel is compiled for: {bm, bn, bk, threads}
+// with the measured fraction of the FFMA peak one SM reaches with it
+struct SgemmShape {
+  int bm, bn, bk, threads;
+  double eff;
+};
+constexpr SgemmShape kSgemmShapes[] = {{128, 128, 8, 256, 0.70}, {64, 64, 8, 256, 0.55}, {32, 64, 16, 128, 0.45}};
+
+}  // namespace detail
+
+// f32 / CUDA-core GEMM on the FFMA pipes: every compiled tile, and K splits
+// of the smallest tile over a cluster of up to 8 CTAs (each keeping >= 64 of K)
+inline void sgemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms, const CostModel& cm,
+                             Candidate* out, int* n) {
+  const double sm_rate = cm.ffma_tflops * 1e12 / (double)sms;
+  for (const auto& s : detail::kSgemmShapes) {
+    const int64_t tiles = detail::cdiv(M, s.bm) * detail::cdiv(N, s.bn);
+    for (int ks = 1; ks <= 8; ks *= 2) {
+      if (ks > 1 && (s.bm != 32 || K / ks < 64)) continue;  // splits: the 32 x 64 tile only
+      const int64_t ctas = tiles * ks;
+      // resident CTAs per SM: 2048 threads, at most 16 CTAs; a wave is one
+      // round of resident CTAs, and too few warps per SM cost latency hiding
+      const int64_t per_sm = 2048 / s.threads < 16 ? 2048 / s.threads : 16;
+      const int64_t load = detail::cdiv(ctas, sms);  // CTAs the busiest SM runs
+      const int64_t warps = (load < per_sm ? load : per_sm) * s.threads / 32;
+      const double hide = warps >= 16 ? 1.0 : (double)warps / 16.0;
+      const double flops_sm = (double)load * 2.0 * s.bm * s.bn * (double)K / ks;
+      double us = flops_sm / (sm_rate * s.eff * hide) * 1e6 + 1.0 * detail::cdiv(load, per_sm);
+      if (ks > 1) us += 0.3 * ks;  // the distributed-shared-memory fold
+      us += cm.launch_us;
+      out[(*n)++] = Candidate{kFamSgemm, Tile{s.bm, s.bn, s.bk, 2}, ks, us};
+    }
+  }
+}
+
+// f16 GEMM on the tensor cores: the single-SM and the SM-pair kernel (the
+// pair needs two 128-row blocks of M)
+inline void f16_gemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms, const CostModel& cm,
+                                Candidate* out, int* n) {
+  const double sm_rate = cm.f16_tflops * 1e12 / (double)sms;
+  {
+    const Tile t = kGemmF16Tile;
+    const int64_t tiles = detail::cdiv(M, t.bm) * detail::cdiv(N, t.bn);
+    const double us = detail::waves_us(tiles, sms, 2.0 * t.bm * t.bn * K, sm_rate * 0.81, 1.5) + cm.launch_us;
+    out[(*n)++] = Candidate{kFamF16Single, t, 1, us};
+  }
+  if (M > 128) {
+    const Tile t = kGemmF16PairTile;
+    const int64_t tiles = detail::cdiv(M, t.bm) * detail::cdiv(N, t.bn);
+    const double us =
+        detail::waves_us(tiles, sms / 2, 2.0 * t.bm * t.bn * K, 2.0 * sm_rate * 0.92, 1.5) + cm.launch_us;
+    out[(*n)++] = Candidate{kFamF16Pair, t, 1, us};
+  }
+}
+
+// fp32 GEMM as the 1 x 1 convolution on the split-tf32 pair kernel (K % 32,
+// N % 64): the tf32 (hi, lo) pre-passes of A and B^T, then 256 x 256 tiles at a
+// sixth of the f16 rate (three tf32 MMAs at half rate), the last round of
+// tiles split along K over the pairs it would leave idle
+inline void tf32x3_gemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms, const CostModel& cm,
+                                   Candidate* out, int* n) {
+  if (K % 32 != 0 || N % 64 != 0) return;
+  const Tile t = kConvPairF32Tile;
+  const double pair_rate = 2.0 * cm.f16_tflops * 1e12 / (double)sms / 6.0 * 0.91;
+  const int64_t tiles = detail::cdiv(M, t.bm) * detail::cdiv(N, t.bn);
+  const int64_t pairs = sms / 2;
+  const int64_t full = tiles / pairs, last = tiles % pairs;
+  const double tile_us = 2.0 * t.bm * t.bn * K / pair_rate * 1e6 + 2.0;
+  double us = (double)full * tile_us;
+  if (last > 0) us += tile_us * (double)last / (double)pairs + 2.0 + cm.launch_us;  // split last round + its fold
+  const double prepass_bytes = 3.0 * (double)(M + N) * (double)K * 4.0;
+  us += prepass_bytes / (cm.hbm_gbs * 1e9) * 1e6 + 3.0 * cm.launch_us;
+  out[(*n)++] = Candidate{kFamTf32x3, t, 1, us};
+}
+
+// a candidate's key for the lexicographic tie-break (src/solver.cpp:153-179)
+inline bool candidate_less(const Candidate& a, const Candidate& b) {
+  if (a.us != b.us) return a.us < b.us;
+  if (a.family != b.family) return a.family < b.family;
+  if (a.tile.bm != b.tile.bm) return a.tile.bm < b.tile.bm;
+  if (a.tile.bn != b.tile.bn) return a.tile.bn < b.tile.bn;
+  return a.ksplit < b.ksplit;
+}
+
+inline Candidate argmin(const Candidate* c, int n) {
+  Candidate best{};
+  for (int i = 0; i < n; ++i)
+    if (best.family < 0 || candidate_less(c[i], best)) best = c[i];
+  return best;
+}
+
+constexpr int kMaxCandidates = 16;
+
+// The GEMM solve.  f16: the tensor-core families (the caller checks the
+// tensor-core shape rules).  fp32: the FFMA candidates, and with allow_tc the
+// split-tf32 one, which is taken only from 2^30 multiply-adds (below that its
+// pre-passes and launches are never repaid on a B200: measured).
+inline Candidate solve_gemm(int64_t M, int64_t N, int64_t K, bool f16, bool allow_tc, int64_t sms,
+                            int* n_feasible = nullptr, const CostModel& cm = CostModel{}) {
+  Candidate c[kMaxCandidates];
+  int n = 0;
+  if (f16) {
+    f16_gemm_candidates(M, N, K, sms, cm, c, &n);
+  } else {
+    sgemm_candidates(M, N, K, sms, cm, c, &n);
+    if (allow_tc && M * N * K >= ((int64_t)1 << 30)) tf32x3_gemm_candidates(M, N, K, sms, cm, c, &n);
+  }
+  if (n_feasible) *n_feasible = n;
+  return argmin(c, n);
 }
 
 }  // namespace uk
