@@ -39,11 +39,12 @@ def test_without_the_tensor_cores_fp32_stays_on_ffma():
 
 
 def test_smaller_parts_shift_the_choice():
-    # on 16 SMs the 64 tiles of 64 x 64 already give every SM four CTAs, so
-    # neither the smaller tile nor a K split pays
+    # on 148 SMs the 128 tiles of 32 x 64 leave SMs idle and K is split over
+    # 4-CTA clusters; on a 16-SM part the same tiles give every SM eight CTAs,
+    # and a split only adds its fold
     assert abi.solve_plan(512, 512, 512, False, sms=148)["k_split"] == 4
     p = abi.solve_plan(512, 512, 512, False, sms=16)
-    assert p["tile"] == (64, 64) and p["k_split"] == 1
+    assert p["tile"] == (32, 64) and p["k_split"] == 1
 
 
 def test_deterministic_and_costed():

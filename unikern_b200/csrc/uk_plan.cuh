@@ -12,6 +12,8 @@
 
 #include <stdint.h>
 
+#include <cmath>
+
 namespace uk {
 
 struct Tile {
@@ -125,13 +127,17 @@ struct Candidate {
 // The machine model: a B200 at 1965 MHz.  Peaks: the measured dense f16
 // tensor rate and copy bandwidth of this pool's B200s, the nominal FFMA rate.
 // Efficiencies are the measured fraction of peak each family sustains in
-// steady state (tensor-pipe activity in ncu for the tcgen05 kernels: 92 % for
-// the pair GEMM, 81 % single-SM, 91 % for the split-tf32 pair kernel; the
-// FFMA tiles from their measured rates), and lat_us the fixed cost of one
-// tile (pipeline fill and epilogue drain).
+// steady state: the tcgen05 kernels' tensor-pipe activity in ncu (92 % for
+// the pair GEMM, 91 % for the split-tf32 pair kernel) and the single-SM GEMM's
+// measured rate at 8192^3 (86 %); the FFMA tiles' rates from a sweep of every
+// compiled tile and K split on a B200 (128 x 128: 60 % of the nominal FFMA
+// peak, 64 x 64: 42 %, 32 x 64: 45 % once 16 warps per SM hide latency,
+// falling with the square root of the warps below that; a K-split fold costs
+// about 0.6 us per CTA of the cluster); a tile's fixed cost (pipeline fill,
+// epilogue drain) is 1-2 us, a launch 2 us.
 struct CostModel {
-  double f16_tflops = 1620.0;
-  double ffma_tflops = 74.4;
+  double f16_tflops_sm = 1620.0 / 148;  // per SM (a part with fewer SMs has proportionally less)
+  double ffma_tflops_sm = 74.4 / 148;
   double hbm_gbs = 6544.0;
   double launch_us = 2.0;
 };
@@ -153,7 +159,7 @@ struct SgemmShape {
   int bm, bn, bk, threads;
   double eff;
 };
-constexpr SgemmShape kSgemmShapes[] = {{128, 128, 8, 256, 0.70}, {64, 64, 8, 256, 0.55}, {32, 64, 16, 128, 0.45}};
+constexpr SgemmShape kSgemmShapes[] = {{128, 128, 8, 256, 0.60}, {64, 64, 8, 256, 0.42}, {32, 64, 16, 128, 0.45}};
 
 }  // namespace detail
 
@@ -161,7 +167,7 @@ constexpr SgemmShape kSgemmShapes[] = {{128, 128, 8, 256, 0.70}, {64, 64, 8, 256
 // of the smallest tile over a cluster of up to 8 CTAs (each keeping >= 64 of K)
 inline void sgemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms, const CostModel& cm,
                              Candidate* out, int* n) {
-  const double sm_rate = cm.ffma_tflops * 1e12 / (double)sms;
+  const double sm_rate = cm.ffma_tflops_sm * 1e12;
   for (const auto& s : detail::kSgemmShapes) {
     const int64_t tiles = detail::cdiv(M, s.bm) * detail::cdiv(N, s.bn);
     for (int ks = 1; ks <= 8; ks *= 2) {
@@ -172,10 +178,10 @@ inline void sgemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms, const
       const int64_t per_sm = 2048 / s.threads < 16 ? 2048 / s.threads : 16;
       const int64_t load = detail::cdiv(ctas, sms);  // CTAs the busiest SM runs
       const int64_t warps = (load < per_sm ? load : per_sm) * s.threads / 32;
-      const double hide = warps >= 16 ? 1.0 : (double)warps / 16.0;
+      const double hide = warps >= 16 ? 1.0 : std::sqrt((double)warps / 16.0);
       const double flops_sm = (double)load * 2.0 * s.bm * s.bn * (double)K / ks;
       double us = flops_sm / (sm_rate * s.eff * hide) * 1e6 + 1.0 * detail::cdiv(load, per_sm);
-      if (ks > 1) us += 0.3 * ks;  // the distributed-shared-memory fold
+      if (ks > 1) us += 0.6 * ks;  // the cluster barrier and distributed-shared-memory fold
       us += cm.launch_us;
       out[(*n)++] = Candidate{kFamSgemm, Tile{s.bm, s.bn, s.bk, 2}, ks, us};
     }
@@ -186,11 +192,11 @@ inline void sgemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms, const
 // pair needs two 128-row blocks of M)
 inline void f16_gemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms, const CostModel& cm,
                                 Candidate* out, int* n) {
-  const double sm_rate = cm.f16_tflops * 1e12 / (double)sms;
+  const double sm_rate = cm.f16_tflops_sm * 1e12;
   {
     const Tile t = kGemmF16Tile;
     const int64_t tiles = detail::cdiv(M, t.bm) * detail::cdiv(N, t.bn);
-    const double us = detail::waves_us(tiles, sms, 2.0 * t.bm * t.bn * K, sm_rate * 0.81, 1.5) + cm.launch_us;
+    const double us = detail::waves_us(tiles, sms, 2.0 * t.bm * t.bn * K, sm_rate * 0.86, 1.5) + cm.launch_us;
     out[(*n)++] = Candidate{kFamF16Single, t, 1, us};
   }
   if (M > 128) {
@@ -210,7 +216,7 @@ inline void tf32x3_gemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms,
                                    Candidate* out, int* n) {
   if (K % 32 != 0 || N % 64 != 0) return;
   const Tile t = kConvPairF32Tile;
-  const double pair_rate = 2.0 * cm.f16_tflops * 1e12 / (double)sms / 6.0 * 0.91;
+  const double pair_rate = 2.0 * cm.f16_tflops_sm * 1e12 / 6.0 * 0.91;
   const int64_t tiles = detail::cdiv(M, t.bm) * detail::cdiv(N, t.bn);
   const int64_t pairs = sms / 2;
   const int64_t full = tiles / pairs, last = tiles % pairs;
