@@ -104,3 +104,59 @@ def test_conv_batch_gather_gloo_world2(N):
         assert p.exitcode == 0
     for rank, col in results:
         assert col == [float(b) for b in range(N)]
+
+
+# ---- failure detection: a rank that leaves or stalls between steps ------------------
+
+def _watch_worker(rank, world, port, mode, q):
+    import time
+
+    def report_and_exit(msg):
+        # the queue's feeder thread must flush before the process ends abruptly
+        q.put(msg)
+        q.close()
+        q.join_thread()
+        os._exit(0)
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    watch = shard.PeerWatch(timeout_s=1.5)
+    done = []
+    for step in range(4):
+        if rank == world - 1 and step == 2:
+            if mode == "leave":  # between steps, with no collective in flight
+                report_and_exit((rank, "left", done))
+            time.sleep(4.0)  # "stall": past the peers' limit
+        t0 = time.monotonic()
+        try:
+            watch.step()
+        except shard.PeerLost as e:
+            report_and_exit((rank, "lost", done + [(step, str(e), time.monotonic() - t0)]))
+        done.append(step)
+    report_and_exit((rank, "ok", done))
+
+
+@pytest.mark.parametrize("mode", ["leave", "stall"])
+def test_peer_watch_reports_a_missing_rank_within_its_limit(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 3
+    procs = [ctx.Process(target=_watch_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        rank, what, info = q.get(timeout=120)
+        res[rank] = (what, info)
+    for p in procs:
+        p.join(timeout=60)
+    # the ranks that stayed all stop at step 2 with PeerLost, naming rank 2,
+    # within about their 1.5 s limit -- none hangs
+    for r in (0, 1):
+        what, info = res[r]
+        assert what == "lost", res
+        step, msg, waited = info[-1]
+        assert step == 2 and "[2]" in msg and waited < 10.0, info
+        assert info[:-1] == [0, 1]
+    assert res[2][0] in ("left", "lost", "ok")

@@ -322,25 +322,21 @@ namespace uk {
 int gemm_f16_tc_2sm(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, uint16_t* const* Cs, int nc,
                     int64_t ldc, int M, int N, int K, cudaStream_t st);  // gemm_f16_2sm.cu
 
-// Kernel choice: the SM-pair kernel (256 x 256 tiles over two SMs) once M has
-// two 128-row blocks and the tiles go to at most two copies of C.  With more
-// copies (the all-gather over 4-8 GPUs) each tile's epilogue is bound by
-// NVLink stores, and a pair must wait for the slower of its two epilogues
-// before its next tile: measured on 8 GPUs, the single-SM kernel is faster
-// there (0.186 vs 0.284 ms per step).  UNIKERN_GEMM_F16_PAIR=0 selects the
-// single-SM kernel everywhere (for comparisons).
-// With one or two copies the solver's argmin decides between the two kernels
-// (wave quantization of 128 x 256 tiles on SMs against 256 x 256 on pairs);
-// UNIKERN_GEMM_F16_PAIR=1 / =0 pins the pair / single-SM kernel instead (for
-// measuring the alternative to the solver's choice).
+// Kernel choice: the SM-pair kernel (256 x 256 tiles over two SMs) needs M
+// to have two 128-row blocks.  With one copy of C the solver's argmin decides
+// between it and the single-SM kernel; with more copies (the all-gather of
+// the N-sharded GEMM over 2-8 GPUs) the pair kernel runs its TMA-store
+// epilogue, which hands the accumulator back before the NVLink stores drain.
+// UNIKERN_GEMM_F16_PAIR=0 / =1 pins the single-SM / pair kernel (for
+// measuring the alternative).
 static bool use_pair_kernel(int M, int N, int K, int nc) {
   static int env = -1;  // -1 unread, 0 single, 1 pair, 2 solver
   if (env < 0) {
     const char* e = getenv("UNIKERN_GEMM_F16_PAIR");
     env = e == nullptr || e[0] == 0 ? 2 : e[0] == '0' ? 0 : 1;
   }
-  if (env == 0 || nc > 2 || M <= 128) return false;
-  if (env == 1) return true;
+  if (env == 0 || M <= 128) return false;
+  if (env == 1 || nc > 1) return true;
   return solve_gemm(M, N, K, true, false, sm_count()).family == kFamF16Pair;
 }
 

@@ -20,6 +20,14 @@
 //   warps 2-5   epilogue of this CTA's 128 rows (as the single-SM kernel:
 //               tcgen05.ld, f16, swizzled staging, 128-byte row stores), then
 //               a remote arrive on the leader's tile-empty barrier
+// The all-gather of the N-sharded multi-GPU GEMM writes each tile to every
+// copy of C.  A second epilogue (TMA_OUT, opt-in) stores through the TMA:
+// each warp stages its 32 x 64 block in one of two 4 KiB slots with the
+// 128-byte swizzle a tensor map expects, one lane issues a TMA tensor store
+// of the block to every copy (peers' buffers over NVLink included) and the
+// accumulator goes back to the MMA issuer as soon as the tile is staged.
+// Measured on 2 and 4 GPUs it is no faster than the lane stores (0.294 vs
+// 0.273 ms per launch on 4), so the lane stores stay the default.
 // Every mbarrier wait is bounded (2 s); a timeout sets the fault word and the
 // CTA unwinds; both CTAs pass the same cluster barriers on every path.  Each
 // TMA load is a plain load of this GPU's memory into the issuing CTA's own
@@ -66,6 +74,12 @@ struct OutList {
   int n;
 };
 
+// TMA_OUT: one tensor map per copy of C ([M][N] at stride ldc, box 64 x 32,
+// 128-byte swizzle)
+struct OutMaps {
+  CUtensorMap m[MAX_OUT];
+};
+
 struct SmemCtl {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -77,8 +91,11 @@ struct SmemCtl {
 };
 
 constexpr int STG_BYTES = 32 * 64 * 2;
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + EPI_WARPS * STG_BYTES + sizeof(SmemCtl) + 1024;
-static_assert(SMEM_BYTES <= 232448, "shared memory per block on sm_100");
+template <bool TMA_OUT>
+constexpr size_t smem_bytes() {
+  return (size_t)STAGES * STAGE_BYTES + EPI_WARPS * (TMA_OUT ? 2 : 1) * STG_BYTES + sizeof(SmemCtl) + 1024;
+}
+static_assert(smem_bytes<true>() <= 232448 && smem_bytes<false>() <= 232448, "shared memory per block on sm_100");
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
@@ -95,13 +112,14 @@ __device__ __forceinline__ void raise_fault(SmemCtl* ctl, unsigned bit) {
   ctl->abort = 1;
 }
 
+template <bool TMA_OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    k_gemm_f16_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, OutList out,
-                   int M, int N, int K, int64_t ldc) {
+    k_gemm_f16_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ OutMaps omaps, OutList out, int M, int N, int K, int64_t ldc) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* staging = smem + (size_t)STAGES * STAGE_BYTES;
-  SmemCtl* ctl = (SmemCtl*)(staging + EPI_WARPS * STG_BYTES);
+  uint8_t* staging = smem + (size_t)STAGES * STAGE_BYTES;  // 1024-byte aligned: the swizzle atom
+  SmemCtl* ctl = (SmemCtl*)(staging + EPI_WARPS * (TMA_OUT ? 2 : 1) * STG_BYTES);
   volatile int* abort = &ctl->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -204,10 +222,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- epilogue (warps 2 .. 5, both CTAs) ----------------
     const int q = warp & 3;
-    uint8_t* stg = staging + (warp - 2) * STG_BYTES;
+    uint8_t* stg = staging + (warp - 2) * (TMA_OUT ? 2 : 1) * STG_BYTES;
     const uint32_t tempty_leader[2] = {uk_mapa(uk_smem_u32(&ctl->tempty[0]), 0),
                                        uk_mapa(uk_smem_u32(&ctl->tempty[1]), 0)};
     uint32_t tl = 0;
+    int slot = 0;  // TMA_OUT: the staging slot of the next block (two per warp)
     for (int t = pair; t < num_tiles && !*abort; t += npairs, ++tl) {
       int mb, nb;
       tile_coords(t, num_m, num_n, mb, nb);
@@ -226,6 +245,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uk_tmem_ld32(taddr, v0);
         uk_tmem_ld32(taddr + 32, v1);
         uk_tmem_ld_wait();
+        uint8_t* blk = stg;
+        if constexpr (TMA_OUT) {
+          blk = stg + slot * STG_BYTES;
+          // the stores issued from this slot two blocks ago have read it
+          if (lane == 0) uk_bulk_wait_read<1>();
+          __syncwarp();
+        }
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint32_t* src = c < 4 ? &v0[(c & 3) * 8] : &v1[(c & 3) * 8];
@@ -235,7 +261,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             __half2 h2 = __floats2half2_rn(__uint_as_float(src[2 * i]), __uint_as_float(src[2 * i + 1]));
             w[i] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(blk + lane * 128 + ((c ^ (lane & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        if constexpr (TMA_OUT) {
+          // staging writes -> async proxy, then one lane stores the block to
+          // every copy (boxes wholly past M or N are skipped; partial ones
+          // are clipped by the tensor map)
+          uk_fence_proxy_async_smem();
+          __syncwarp();
+          const int bx = n0 + h * 64;
+          if (lane == 0 && bx < N && row0 < M) {
+            for (int o = 0; o < out.n; ++o) uk_tma_store_2d(&omaps.m[o], blk, bx, row0);
+            uk_bulk_commit();
+          }
+          slot ^= 1;
+          continue;
         }
         __syncwarp();
         const int c = lane & 7;
@@ -255,6 +295,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uk_tc_fence_before();
       __syncwarp();
       if (lane == 0) uk_mbar_arrive_cluster(tempty_leader[buf]);
+    }
+    // TMA_OUT: every store this warp issued has been performed before the
+    // CTA retires; stores into other GPUs' buffers are made visible
+    // system-wide (the host orders the ranks after the kernel)
+    if constexpr (TMA_OUT) {
+      if (lane == 0) uk_bulk_wait<0>();
+      __syncwarp();
     }
     if (out.n > 1) __threadfence_system();
   }
@@ -320,23 +367,42 @@ int gemm_f16_tc_2sm(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t l
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BMC)) return rc;
   if (int rc = make_map(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK)) return rc;
-  static bool attr_done[64] = {false};
+  // copies of C go out through the lane stores of the one-copy epilogue;
+  // UNIKERN_GEMM_F16_TMA_OUT=1 selects the TMA-store epilogue instead (on 4
+  // GPUs the lane stores measured 0.273 ms per launch against 0.294)
+  static int tma_env = -1;
+  if (tma_env < 0) {
+    const char* e = getenv("UNIKERN_GEMM_F16_TMA_OUT");
+    tma_env = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  const bool tma_out = nc > 1 && tma_env == 1;
+  static bool attr_done[2][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_f16_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+  if (dev >= 0 && dev < 64 && !attr_done[tma_out][dev]) {
+    const cudaError_t e =
+        tma_out ? cudaFuncSetAttribute(k_gemm_f16_tc2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem_bytes<true>())
+                : cudaFuncSetAttribute(k_gemm_f16_tc2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem_bytes<false>());
     if (e != cudaSuccess) return fail(UK_ECUDA, "gemm_f16: smem attribute: %s", cudaGetErrorString(e));
-    attr_done[dev] = true;
+    attr_done[tma_out][dev] = true;
   }
   OutList out{};
   for (int i = 0; i < nc; ++i) out.c[i] = Cs[i];
   out.n = nc;
+  // the copies' tensor maps: [M][N] at stride ldc (each copy already offset
+  // to this rank's first column), 64 x 32 boxes, 128-byte swizzle
+  OutMaps omaps{};
+  if (tma_out)
+    for (int i = 0; i < nc; ++i)
+      if (int rc = make_map(&omaps.m[i], Cs[i], (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 64, 32)) return rc;
   const int tiles = ((M + 2 * BMC - 1) / (2 * BMC)) * ((N + BN - 1) / BN);
   const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = tma_out ? smem_bytes<true>() : smem_bytes<false>();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -345,7 +411,8 @@ int gemm_f16_tc_2sm(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t l
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_f16_tc2, ta, tb, out, M, N, K, ldc);
+  const cudaError_t e = tma_out ? cudaLaunchKernelEx(&cfg, k_gemm_f16_tc2<true>, ta, tb, omaps, out, M, N, K, ldc)
+                                : cudaLaunchKernelEx(&cfg, k_gemm_f16_tc2<false>, ta, tb, omaps, out, M, N, K, ldc);
   if (e != cudaSuccess) return fail(UK_ECUDA, "gemm_f16(2sm): launch: %s", cudaGetErrorString(e));
   return check_launch("gemm_f16(tcgen05 pair)");
 }

@@ -88,6 +88,33 @@ __device__ __forceinline__ void uk_tma_load_2d(void* dst, const CUtensorMap* map
       : "memory");
 }
 
+// TMA tensor store of one 2-D box from this CTA's shared memory to global
+// memory (this GPU's or a peer's, through a tensor map of its address),
+// tracked in the issuing thread's bulk async-group.  x, y >= 0 (x * elem_size
+// a multiple of 16 bytes); the parts of the box outside the tensor are not
+// written.  The source must have been made visible to the async proxy
+// (uk_fence_proxy_async_smem by every writing thread) before the store.
+__device__ __forceinline__ void uk_tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(uk_smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+// close the bulk async-group of the stores issued so far by this thread
+__device__ __forceinline__ void uk_bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's bulk groups still read their shared
+// memory sources (the sources of older groups may be rewritten)
+template <int N>
+__device__ __forceinline__ void uk_bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until at most N of this thread's bulk groups are incomplete (their
+// writes performed)
+template <int N>
+__device__ __forceinline__ void uk_bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---- tcgen05 -----------------------------------------------------------------
 __device__ __forceinline__ void uk_tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(uk_smem_u32(dst_smem)),

@@ -75,6 +75,69 @@ def gather_objects(obj, group=None):
     return out
 
 
+class PeerLost(RuntimeError):
+    """A peer rank left or stopped stepping: the runner's exit code 4."""
+
+    code = 4
+
+
+class PeerWatch:
+    """Host-side liveness of the ranks between steps.
+
+    Before a step's GPU work, every rank posts "step n" to the process
+    group's key-value store and waits, for at most `timeout_s`, until every
+    peer has posted the same step.  A peer that exited, crashed or stopped
+    stepping is found here, on the host and before this rank launches a
+    kernel that stores into that peer's memory, and the wait ends with
+    PeerLost naming the missing ranks: an error status, never a hang (the
+    reference's runner, likewise, ends a failed run with an exit code,
+    src/main.cpp:469-539).  Keys of finished steps are removed as the ranks
+    move on."""
+
+    def __init__(self, timeout_s: float = 5.0, group=None, prefix: str = "uk_hb"):
+        import torch.distributed as dist
+        from torch.distributed import distributed_c10d as c10d
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.store = c10d._get_default_store()
+        self.timeout_s = timeout_s
+        self.prefix = prefix
+        self.n = 0
+
+    def _key(self, step, rank):
+        return "%s/%d/%d" % (self.prefix, step, rank)
+
+    def step(self):
+        """Post this rank's next step and wait for every peer's; returns the
+        step number, raises PeerLost when a peer does not post in time."""
+        import datetime
+        n = self.n
+        self.store.set(self._key(n, self.rank), b"1")
+        keys = [self._key(n, r) for r in range(self.world) if r != self.rank]
+        try:
+            if keys:
+                self.store.wait(keys, datetime.timedelta(seconds=self.timeout_s))
+        except Exception as e:  # the store's timeout, or its server (rank 0) gone
+            missing = []
+            for r in range(self.world):
+                if r == self.rank:
+                    continue
+                try:
+                    if not self.store.check([self._key(n, r)]):
+                        missing.append(r)
+                except Exception:
+                    missing.append(r)
+            raise PeerLost("step %d: rank(s) %s did not reach the step within %.1f s (%s)"
+                           % (n, missing or "?", self.timeout_s, type(e).__name__)) from None
+        if n >= 2:  # every peer has posted step n, so all are past step n - 2
+            try:
+                self.store.delete_key(self._key(n - 2, self.rank))
+            except Exception:
+                pass
+        self.n = n + 1
+        return n
+
+
 class PeerBuffers:
     """Device pointers of every rank's copy of one buffer (peers via CUDA IPC)."""
 
@@ -143,7 +206,11 @@ class GemmAllGather:
         import torch.distributed as dist
         dist.all_reduce(self.flag, group=self.group)
 
-    def run(self, A, B_shard, C_full, stream=None):
+    def run(self, A, B_shard, C_full, stream=None, watch=None):
+        """One step; with a PeerWatch, every peer is confirmed alive on the
+        host before the kernel stores into its C."""
+        if watch is not None:
+            watch.step()
         self.launch(A, B_shard, stream)
         self.barrier()
 
