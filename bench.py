@@ -582,7 +582,16 @@ def measure_rowop(ctx, op, steps, warmup, pk, L=8192, C=16384, e2e=True):
     rec = {"value": val, "unit": "GB/s", "ms": ms, "bytes_per_step": nbytes,
            "roofline": roofline("hbm", val, pk, traffic_for("rowop_" + op))}
     if e2e:
-        ems, h2d, d2h = time_e2e(ctx, launch, ins, outs, max(3, min(steps, 10)))
+        if op == "reduce_scalar":  # one row: upload, reduce, download in turn
+            ems, h2d, d2h = time_e2e(ctx, launch, ins, outs, max(3, min(steps, 10)))
+        else:  # uk_cuda_rowop_host: row blocks pipelined, both link directions at once
+            Xh = ins[0][1]
+            Wh = ins[1][1] if len(ins) > 1 else None
+            Yd, Yh = outs[0]
+            ems = ctx.time_steps(lambda: abi.rowop_host(op, Xh, Wh, Yh, X, W if Wh is not None else None, Yd,
+                                                        1e-5), max(3, min(steps, 10)), 3)
+            h2d = sum(h.numel() * h.element_size() for _, h in ins)
+            d2h = Yh.numel() * Yh.element_size()
         rec["e2e"] = e2e_record(nbytes, "GB/s", ems, h2d, d2h)
     return rec
 
@@ -796,6 +805,7 @@ def bench_conv_sharded(ctx, steps, warmup, N=32, Cc=256, H=56, W=56, Oc=256, pad
     y = torch.empty((N, Oc, H, W), device="cuda")
     ms = ctx.time_steps(lambda: plan.run(x, w, y, s), steps, warmup)
     flops = 2.0 * N * H * W * Cc * 9 * Oc
+    plan.close()
     return {"ms": ms, "value": flops / ms / 1e9, "parallelism": plan.describe()}
 
 

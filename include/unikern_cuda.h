@@ -79,7 +79,10 @@ int uk_cuda_tile_plan(int op, int f16, const int64_t* dims, int sms, int* out4);
 int uk_cuda_solve_plan(int op, int f16, const int64_t* dims, int sms, int allow_tc, int* out8);
 /* The plan of the last GEMM launched on the calling thread, as out6 =
  * {family, tile_m, tile_n, k_block, stages, k_split} (family -1 before any):
- * how a caller sees the solver's choice reach the launcher. */
+ * how a caller sees the solver's choice reach the launcher.  Families beyond
+ * the solver's: 6 the decode chain's skinny GEMM (tile = 128 weight columns x
+ * 32 token rows, k_split = its K-split cluster size), 7 the FFMA 32 x 64 tile
+ * with K split over warp groups of one CTA (k_split = the groups). */
 int uk_cuda_last_launch(int* out6);
 
 /* ---- channelscale ----------------------------------------------------------
@@ -213,6 +216,23 @@ int uk_cuda_gemm_f16_ld(const uint16_t* A, int64_t lda, const uint16_t* B, int64
 int uk_cuda_gemm_f16_host(const uint16_t* hA, const uint16_t* hB, uint16_t* hC, uint16_t* dA,
                           uint16_t* dB, uint16_t* dC, int M, int N, int K, int chunks, void* stream);
 
+/* The row ops from and to HOST memory (page-locked hX[L][C], hW[C] for
+ * RMSNorm's gamma or channelscale's S, hY[L][C] -- or hY[L] for the reduce),
+ * through the caller's device buffers dX, dW, dY of the same shapes: op is
+ * UK_OP_REDUCE, UK_OP_SOFTMAX, UK_OP_RMSNORM (eps) or UK_OP_CHANNELSCALE.
+ * The copies are pipelined over `chunks` row blocks (0 = 8): W uploads
+ * first, then each block of X; a block's op runs once its rows landed and its
+ * rows of Y download while later blocks upload, so both directions of the
+ * host link run at once.  The reduce takes the workspace of
+ * uk_cuda_reduce_workspace_size(rows, C) for a block's rows (NULL when that
+ * is 0).  Asynchronous on `stream`, complete (Y included) when `stream` is;
+ * shares the copy streams of uk_cuda_gemm_f16_host.  The reference measures
+ * each op end to end (upload, run, download: src/codegen_hip.cpp:2036-2126);
+ * this overlaps those phases. */
+int uk_cuda_rowop_host(int op, const float* hX, const float* hW, float* hY, float* dX, float* dW, float* dY,
+                       int64_t L, int64_t C, float eps, int chunks, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 /* GEMM larger than the device (the reference's streamed scenario B,
  * src/codegen_hip.cpp:1143-1238): C = A * B from and to page-locked host
  * memory with only B resident (dB, K*N elements) and A, C passing through a
@@ -265,6 +285,47 @@ int uk_cuda_decode_rmsnorm_gemm_f16(const float* X, const float* gamma, float ep
                                     uint16_t* const* Y_list, int n_y, int64_t ldy, int B, int N_shard, int K,
                                     int64_t col_offset, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- multi-GPU from a C/C++ host, over NCCL (one process per GPU) ----------
+ * NCCL is resolved at run time (the process's loaded libnccl, else
+ * libnccl.so.2); these calls return UK_ECUDA when it is absent.
+ * uk_nccl_get_unique_id: rank 0's id (uk_nccl_unique_id_size() bytes), which
+ *   the caller hands to every rank (file, socket, MPI ...).
+ * uk_nccl_comm_init: ncclCommInitRankConfig with a non-blocking config,
+ *   polled (ncclCommGetAsyncError) for at most timeout_ns: a rank that never
+ *   joins ends it with ncclCommAbort and UK_ECUDA instead of a hang.
+ * uk_nccl_comm_destroy: aborts (frees) the communicator without a collective
+ *   (the peers may be gone); a communicator this library already aborted
+ *   after a failure is left alone.
+ * uk_shard_gemm_f16_create: for C[M][ldc] on this rank (the full C), this
+ *   rank's column block of the N-sharded GEMM (multiples of 8 columns, as
+ *   even as possible: uk_shard_gemm_f16_columns) and every rank's C opened
+ *   over CUDA IPC, the handles exchanged once with an NCCL all-gather (bounded
+ *   by timeout_ns).  Set-up, not a hot call: it allocates a few bytes.
+ * uk_shard_gemm_f16_run: one step on `stream`: a one-float NCCL all-reduce
+ *   that proves every peer alive and past its previous step, the GEMM of this
+ *   rank's column block with its all-gather fused into the store (every
+ *   tile into every rank's C, uk_cuda_gemm_f16_allgather), then a second
+ *   all-reduce after which every rank's C is complete.  With timeout_ns > 0
+ *   the host waits on each all-reduce for at most timeout_ns, polling the
+ *   communicator's asynchronous error: a peer that left, stalled or failed
+ *   is caught before this rank's kernel stores into its memory, and the call
+ *   aborts the communicator and returns UK_ECUDA (the runner's exit code 4)
+ *   -- never a hang.  With timeout_ns = 0 the step is enqueued asynchronously.
+ *   B_shard is this rank's [K][n1 - n0] column block of B (leading dim ldb).
+ * No reference counterpart (the reference is single-GPU; its failure
+ * protocol, an exit code per outcome, src/main.cpp:469-539, is kept). */
+size_t uk_nccl_unique_id_size(void);
+int uk_nccl_get_unique_id(void* out);
+int uk_nccl_comm_init(const void* unique_id, int nranks, int rank, uint64_t timeout_ns, void** comm_out);
+int uk_nccl_comm_destroy(void* comm);
+typedef struct uk_shard_gemm uk_shard_gemm;
+int uk_shard_gemm_f16_create(void* comm, int rank, int nranks, uint16_t* C, int64_t ldc, int M, int N, int K,
+                             uint64_t timeout_ns, uk_shard_gemm** out);
+int uk_shard_gemm_f16_columns(const uk_shard_gemm* h, int64_t* n0, int64_t* n1);
+int uk_shard_gemm_f16_run(uk_shard_gemm* h, const uint16_t* A, int64_t lda, const uint16_t* B_shard, int64_t ldb,
+                          void* stream, uint64_t timeout_ns);
+int uk_shard_gemm_f16_destroy(uk_shard_gemm* h);
+
 /* CUDA IPC: export a device buffer (handle of uk_cuda_ipc_handle_size() bytes
  * plus the offset of `ptr` inside its allocation), open a peer's export as a
  * pointer on this device, close it.  No reference counterpart. */
@@ -272,6 +333,21 @@ size_t uk_cuda_ipc_handle_size(void);
 int uk_cuda_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
 int uk_cuda_ipc_import(const void* handle, uint64_t offset, void** ptr_out);
 int uk_cuda_ipc_close(void* ptr, uint64_t offset);
+
+/* Device-side barrier of the ranks of one node (one process per GPU): a
+ * one-warp kernel on `stream` posts `epoch` into every rank's flag array at
+ * this rank's slot (flag_list[r] = rank r's array of n unsigned ints, in rank
+ * order, this rank's own included; peers' arrays opened with
+ * uk_cuda_ipc_import), with a system-scope release that makes everything this
+ * GPU wrote earlier on the stream (the sharded GEMM's peer stores included)
+ * visible first; it then waits until every rank's post of `epoch` (or a later
+ * one) is in its own array.  Epochs only grow (the caller counts steps from
+ * 1; arrays start at 0).  A wait longer than timeout_ns (1 us .. 60 s) gives
+ * up and sets bit 32 of uk_cuda_pipeline_fault: an error status, never a
+ * hang.  Each rank runs it on its own GPU: ranks that share a GPU must not use
+ * it.  No reference counterpart (the reference is single-GPU). */
+int uk_cuda_peer_barrier(unsigned* const* flag_list, int n, int rank, unsigned epoch, uint64_t timeout_ns,
+                         void* stream);
 
 /* Fault word of the tensor-core pipelines: 0 when no bounded wait inside a
  * kernel of this library expired since the last call, otherwise a bit mask
@@ -338,6 +414,20 @@ int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_t* Y, int N
 int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W,
                           int C, int Kh, int Kw, int Oc, int pad, const float* scale,
                           int layout, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The NCHW tensor-core fp32 conv (uk_cuda_conv2d_f32_ws, C a multiple of 32)
+ * with its output stored into n_y (<= 8) copies of Y: Y_list[0] on this GPU,
+ * Y_list[1..] other GPUs' buffers opened with uk_cuda_ipc_import, each
+ * pointing at the same place (this rank's first image).  That is the
+ * batch-sharded conv with its all-gather fused into the store: rank r passes
+ * its image block X[b0:b1] (N = b1 - b0) and every rank's Y + b0 * Oc * Ho * Wo,
+ * and orders the ranks after the call (uk_cuda_peer_barrier) before reading
+ * Y.  Same workspace as uk_cuda_conv2d_f32_ws.  No reference counterpart (the
+ * reference is single-GPU); the batch split and all-gather are the north
+ * star's multi-GPU plan for the conv. */
+int uk_cuda_conv2d_f32_allgather(const float* X, const float* Wt, float* const* Y_list, int n_y, int N, int H, int W,
+                                 int C, int Kh, int Kw, int Oc, int pad, const float* scale, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* ---- KML runner (host side; the nvidia branch of `unikern run`) -----------
  * uk_kml_describe: the KML contract for one declaration, no GPU needed.

@@ -46,6 +46,7 @@ def main():
         # tile count: a different grouping in the tensor cores' accumulator
         # there (~2e-5 of the output scale), so the fp32 gate, not bitwise
         ok = ok and rel <= 1e-4 and not torch.isnan(Y).any().item()
+        print("rank %d conv gather: %s" % (rank, plan.describe()), flush=True)
         # the first and last image (different ranks' shards) against fp64
         xs, ws_, ss = x.cpu().numpy(), w.cpu().numpy(), s.cpu().numpy()
         Yh = Y.cpu().numpy()
@@ -55,6 +56,7 @@ def main():
             print("rank %d conv image %d vs f64: %.3e" % (rank, n, err), flush=True)
             ok = ok and err <= 1e-4
         dist.barrier()
+        plan.close()
     dist.destroy_process_group()
     return 0 if ok else 1
 

@@ -71,6 +71,40 @@ def test_decode_full_layer_width_sampled():
     assert abi.lib().uk_cuda_pipeline_fault() == 0
 
 
+@pytest.mark.parametrize("N,splits", [
+    (1792, (1, 2, 3, 5, 7, 10, 16)),   # 14 tiles: one CTA per SM up to 10, two at 16
+    (14336, (1, 4, 5, 6)),             # 112 tiles: four or five CTAs share an SM (shallow rings)
+])
+def test_decode_every_k_split_matches_oracle(N, splits, monkeypatch):
+    """The K split pinned to each cluster size (UK_DECODE_KSPLIT), non-powers
+    of two included: ragged k-block ranges per rank and ragged row slices in
+    the distributed-shared-memory fold.  Each plan must reach the launcher
+    and match the oracle on sampled columns."""
+    import unikern_b200.abi as abi
+    B, K = 32, 4096
+    rng = np.random.default_rng(N)
+    X = rng.normal(0, 1, (B, K)).astype(np.float32)
+    g = rng.normal(1, 0.1, K).astype(np.float32)
+    Wh = O.f32_to_f16(rng.normal(0, 0.02, (K, N)).astype(np.float32))
+    cols = np.unique(np.concatenate([np.arange(0, 256), rng.choice(N, 128, replace=False), np.arange(N - 128, N)]))
+    ref = oracle_chain(X, g, np.ascontiguousarray(Wh[:, cols]), 1e-5)
+    Xd, gd, Wd = dev(X), dev(g), dev(Wh)
+    for cs in splits:
+        monkeypatch.setenv("UK_DECODE_KSPLIT", str(cs))
+        Y = empty((B, N), "f16")
+        abi.decode_rmsnorm_gemm(Xd, gd, Wd, Y, 1e-5)
+        plan = abi.last_launch()
+        assert plan["family"] == "tcgen05-skinny" and plan["k_split"] == cs, plan
+        got = O.f16_to_f32(host(Y))
+        err = O.rel_err(got[:, cols], ref, O.rms(ref))
+        assert err <= F16_TOL, (cs, err)
+        assert abi.lib().uk_cuda_pipeline_fault() == 0
+    monkeypatch.delenv("UK_DECODE_KSPLIT")
+    Y = empty((B, N), "f16")
+    abi.decode_rmsnorm_gemm(Xd, gd, Wd, Y, 1e-5)
+    assert abi.last_launch()["family"] == "tcgen05-skinny"
+
+
 def test_decode_bad_shapes_are_refused():
     import unikern_b200.abi as abi
     X = empty((33, 64))

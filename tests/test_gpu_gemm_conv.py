@@ -49,6 +49,39 @@ def test_gemm_f32_vs_f64(M, N, K):
     assert err <= max(4.0 * err_ref, 1e-6), (err, err_ref)
 
 
+PLANS = ["128,128,1", "64,64,1", "32,64,1", "32,64,2", "32,64,4", "32,64,8", "32,64,1,2", "32,64,1,4", "32,64,1,8"]
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (300, 200, 264), (33, 47, 130)])
+def test_gemm_f32_every_compiled_plan(M, N, K, monkeypatch):
+    """Every compiled FFMA plan pinned through UK_SGEMM_PLAN (the vectorised
+    path, and the scalar one when K is not a multiple of 4) against f64; the
+    K split over warp groups of one CTA gives the same bits as the same split
+    over a cluster (same K ranges, same fold order)."""
+    rng = np.random.default_rng(M + N + K)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    ref = O.gemm_f64(A, B, threads=8)
+    tau = SUM_TAU * O.rms(ref)
+    got = {}
+    for plan in PLANS:
+        monkeypatch.setenv("UK_SGEMM_PLAN", plan)
+        got[plan] = gemm32(A, B)
+        launched = abi.last_launch()
+        parts = [int(x) for x in plan.split(",")]
+        if len(parts) == 4:
+            assert launched["family"] == "ffma-kgroups" and launched["k_split"] == parts[3], launched
+        else:
+            assert launched["family"] == "ffma" and launched["tile"] == (parts[0], parts[1]), launched
+            assert launched["k_split"] == parts[2], launched
+        assert O.rel_err(got[plan], ref, tau) <= F32_TOL, plan
+    for kg in (2, 4, 8):
+        assert np.array_equal(got["32,64,1,%d" % kg], got["32,64,%d" % kg]), kg
+    monkeypatch.setenv("UK_SGEMM_PLAN", "32,64,2,4")
+    with pytest.raises(abi.UkError):
+        gemm32(A, B)
+
+
 def test_gemm_f32_k0_writes_zeros():
     Cm = empty((3, 5))
     Cm.fill_(5.0)

@@ -192,3 +192,32 @@ def test_host_pointer_refused_with_code_5():
                                             t.cuda.current_stream().cuda_stream)
     assert rc == 5
     assert "device-resident" in abi.lib().uk_cuda_last_error().decode()
+
+
+# ---- the row ops from and to host memory (uk_cuda_rowop_host) -------------------------
+
+@pytest.mark.parametrize("op", ["softmax", "rmsnorm", "channelscale", "reduce"])
+@pytest.mark.parametrize("L,C,chunks", [(1024, 4096, 0), (1000, 1000, 7), (5, 2048, 8), (3, 100, 1)])
+def test_rowop_host_equals_the_device_op(op, L, C, chunks):
+    # rows are independent and each block runs the same per-row plan, so the
+    # pipelined host-to-host call gives the device op's bits
+    import torch
+    rng = np.random.default_rng(L + C + chunks)
+    X = rng.normal(0, 2.0, (L, C)).astype(np.float32)
+    W = rng.normal(1, 0.1, C).astype(np.float32)
+    Xd, Wd = dev(X), dev(W)
+    want = empty((L,)) if op == "reduce" else empty((L, C))
+    if op == "softmax":
+        abi.softmax(Xd, want)
+    elif op == "rmsnorm":
+        abi.rmsnorm(Xd, Wd, want, 1e-5)
+    elif op == "channelscale":
+        abi.channelscale(Xd, Wd, want)
+    else:
+        abi.reduce(Xd, want)
+    Xh, Wh = torch.from_numpy(X).pin_memory(), torch.from_numpy(W).pin_memory()
+    Yh = torch.empty(tuple(want.shape)).pin_memory()
+    Xs, Ws, Ys = torch.empty_like(Xd), torch.empty_like(Wd), torch.empty_like(want)
+    abi.rowop_host(op, Xh, Wh, Yh, Xs, Ws, Ys, 1e-5, chunks)
+    torch.cuda.synchronize()
+    assert np.array_equal(Yh.numpy(), host(want))

@@ -41,9 +41,11 @@ PROTOTYPES = {
     "uk_cuda_conv2d_f32": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp]),
     "uk_cuda_conv2d_workspace_size": (sz, [i32] * 9),
     "uk_cuda_conv2d_f32_ws": (i32, [vp, vp, vp] + [i32] * 8 + [vp, i32, vp, sz, vp]),
+    "uk_cuda_conv2d_f32_allgather": (i32, [vp, vp, C.POINTER(vp), i32] + [i32] * 8 + [vp, vp, sz, vp]),
     "uk_cuda_pipeline_fault": (C.c_uint, []),
     "uk_cuda_selftest_wait": (i32, [i32, C.c_uint64, vp, vp]),
     "uk_cuda_gemm_f16_allgather": (i32, [vp, i64, vp, i64, C.POINTER(vp), i32, i64, i32, i32, i32, i64, vp]),
+    "uk_cuda_peer_barrier": (i32, [C.POINTER(vp), i32, i32, C.c_uint, C.c_uint64, vp]),
     "uk_cuda_ipc_handle_size": (sz, []),
     "uk_cuda_ipc_export": (i32, [vp, vp, C.POINTER(C.c_uint64)]),
     "uk_cuda_ipc_import": (i32, [vp, C.c_uint64, C.POINTER(vp)]),
@@ -52,6 +54,7 @@ PROTOTYPES = {
     "uk_cuda_decode_rmsnorm_gemm_f16": (i32, [vp, vp, f32, vp, i64, C.POINTER(vp), i32, i64, i32, i32, i32, i64,
                                                vp, sz, vp]),
     "uk_cuda_gemm_f16_host": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+    "uk_cuda_rowop_host": (i32, [i32, vp, vp, vp, vp, vp, vp, i64, i64, f32, i32, vp, sz, vp]),
     "uk_cuda_softmax_f16": (i32, [vp, vp, i64, i64, vp]),
     "uk_cuda_rmsnorm_f16": (i32, [vp, vp, vp, i64, i64, f32, vp]),
     "uk_cuda_channelscale_f16": (i32, [vp, vp, vp, i64, i64, vp]),
@@ -62,6 +65,14 @@ PROTOTYPES = {
     "uk_cuda_tile_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, C.POINTER(C.c_int)]),
     "uk_cuda_solve_plan": (i32, [i32, i32, C.POINTER(C.c_int64), i32, i32, C.POINTER(C.c_int)]),
     "uk_cuda_last_launch": (i32, [C.POINTER(C.c_int)]),
+    "uk_nccl_unique_id_size": (sz, []),
+    "uk_nccl_get_unique_id": (i32, [vp]),
+    "uk_nccl_comm_init": (i32, [vp, i32, i32, C.c_uint64, C.POINTER(vp)]),
+    "uk_nccl_comm_destroy": (i32, [vp]),
+    "uk_shard_gemm_f16_create": (i32, [vp, i32, i32, vp, i64, i32, i32, i32, C.c_uint64, C.POINTER(vp)]),
+    "uk_shard_gemm_f16_columns": (i32, [vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "uk_shard_gemm_f16_run": (i32, [vp, vp, i64, vp, i64, vp, C.c_uint64]),
+    "uk_shard_gemm_f16_destroy": (i32, [vp]),
     "uk_kml_describe": (i32, [C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_run_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, C.c_char_p, sz]),
     "uk_solve_kml": (i32, [C.c_char_p, C.c_char_p, C.c_char_p, i32, i32, C.c_char_p, sz]),
@@ -239,6 +250,15 @@ def gemm_f16_host(Ah, Bh, Ch, Ad, Bd, Cd, chunks=0, stream=None):
                                       _stream(stream)))
 
 
+def rowop_host(op, Xh, Wh, Yh, Xd, Wd, Yd, eps=1e-5, chunks=0, workspace=None, stream=None):
+    """A row op from and to pinned host tensors through device buffers, the
+    copies pipelined against the op over row blocks."""
+    L, Cc = Xh.shape
+    ws = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(lib().uk_cuda_rowop_host(UK_OP[op], _p(Xh), _p(Wh), _p(Yh), _p(Xd), _p(Wd), _p(Yd), L, Cc, eps, chunks,
+                                   _p(workspace), ws, _stream(stream)))
+
+
 def gemm_streamed(Ah, Bh, Ch, Bd, ring, block_rows, stream=None, ffma=False):
     """C = A * B (host tensors, f16 or fp32) with only B resident and A / C
     streamed through a two-slot device ring of block_rows-row blocks (fp32:
@@ -296,7 +316,8 @@ def tile_plan(op: str, dims, f16: bool = False, sms: int = 0):
     return tuple(out)
 
 
-FAMILIES = {0: "ffma", 1: "tcgen05-1sm", 2: "tcgen05-2sm", 3: "tcgen05-2sm-3xtf32"}
+FAMILIES = {0: "ffma", 1: "tcgen05-1sm", 2: "tcgen05-2sm", 3: "tcgen05-2sm-3xtf32", 4: "ffma-conv",
+            5: "tcgen05-2sm-conv", 6: "tcgen05-skinny", 7: "ffma-kgroups"}
 
 
 def solve_plan(M: int, N: int, K: int, f16: bool = False, sms: int = 0, allow_tc: bool = True):
@@ -309,10 +330,11 @@ def solve_plan(M: int, N: int, K: int, f16: bool = False, sms: int = 0, allow_tc
 
 
 def last_launch():
-    """The plan of the last GEMM this thread launched: dict(family, tile, k_split)."""
+    """The plan of the last GEMM this thread launched: dict(family, tile,
+    stages, k_split)."""
     out = (C.c_int * 6)()
     check(lib().uk_cuda_last_launch(out))
-    return {"family": FAMILIES.get(out[0], out[0]), "tile": (out[1], out[2]), "k_split": out[5]}
+    return {"family": FAMILIES.get(out[0], out[0]), "tile": (out[1], out[2]), "stages": out[4], "k_split": out[5]}
 
 
 def kml_describe(kml_json: str, hcs_json: str | None = None, sms: int = 0):

@@ -72,9 +72,15 @@ struct SmemCtl {
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(SmemCtl);
 static_assert(SMEM_BYTES <= 232448, "shared memory per block on sm_100");
 
+constexpr int MAX_COPIES = 7;  // copies of Y beyond p.y (the fused all-gather over up to 8 GPUs)
+
 struct ConvTc {
   void* y;            // float (fp32 conv) or __half (fp16 conv)
   const void* scale;  // same type as y
+  // more copies of Y (other GPUs' buffers over NVLink, at the same offsets):
+  // every output the pair kernel and the tail store goes to y and to these
+  void* yc[MAX_COPIES];
+  int nyc;
   int N, Ho, Wo, Oc, C, Kh, Kw, pad;
   int tiles_w, tiles_h, tiles_oc, num_tiles;
   // SM-pair kernel work items: tiles [0, num_full) whole, then each of the
@@ -630,14 +636,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int r = 0; r < 32 / RPR; ++r) {
             const int oi = r * RPR + lane / LPR, oc = ocj + oi;
             if (oc < p.Oc && ho_w < p.Ho && wo < p.Wo) {
-              Out* dst = Y + (((int64_t)n * p.Oc + oc) * p.Ho + ho_w) * p.Wo + wo;
+              const int64_t off = (((int64_t)n * p.Oc + oc) * p.Ho + ho_w) * p.Wo + wo;
               const Out* src = stg + oi * 32 + px;
-              if (vec_ok && wo + VEC <= p.Wo) {
-                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-              } else {
+              for (int o = 0; o <= p.nyc; ++o) {
+                Out* dst = (o == 0 ? Y : (Out*)p.yc[o - 1]) + off;
+                if (vec_ok && wo + VEC <= p.Wo) {
+                  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+                } else {
 #pragma unroll
-                for (int e = 0; e < VEC; ++e)
-                  if (wo + e < p.Wo) dst[e] = src[e];
+                  for (int e = 0; e < VEC; ++e)
+                    if (wo + e < p.Wo) dst[e] = src[e];
+                }
               }
             }
           }
@@ -648,6 +657,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) uk_mbar_arrive_cluster(tempty_leader[buf]);
     }
+    // stores into other GPUs' copies are visible system-wide before the CTA
+    // retires (the ranks are ordered after the kernel)
+    if (p.nyc > 0) __threadfence_system();
   }
 
   if (warp == 1 && lane == 0) {
@@ -694,8 +706,11 @@ __global__ void __launch_bounds__(256) k_conv_tail(const ConvTc p) {
       for (int u = 0; u < 8; ++u) v += t[u];
     }
     for (; sidx < p.splits; ++sidx) v += __ldcs(src + (size_t)sidx * step);
-    out_store(Y + (((int64_t)n * p.Oc + oc) * p.Ho + ho) * p.Wo + wo, scale != nullptr ? v * out_scale(scale, oc) : v);
+    const int64_t off = (((int64_t)n * p.Oc + oc) * p.Ho + ho) * p.Wo + wo;
+    const float out = scale != nullptr ? v * out_scale(scale, oc) : v;
+    for (int o = 0; o <= p.nyc; ++o) out_store((o == 0 ? Y : (Out*)p.yc[o - 1]) + off, out);
   }
+  if (p.nyc > 0) __threadfence_system();
 }
 
 // ---- pre-pass: fp32 -> (hi, lo) tf32 pairs, NCHW -> NHWC ------------------------
@@ -995,7 +1010,8 @@ void apply_tail(ConvTc& p, const TailPlan& tp, float* part) {
 // the split-tf32 kernel over prepared operands: Xh/Xl the input as NHWC
 // (hi, lo) pairs, Wh/Wl the weights as [Oc][kh][kw][c] pairs
 int run_tc(const float* Xh, const float* Xl, const float* Wh, const float* Wl, float* Y, const float* scale, int N,
-           int H, int W, int C, int Kh, int Kw, int Oc, int pad, float* part, size_t part_room, cudaStream_t st) {
+           int H, int W, int C, int Kh, int Kw, int Oc, int pad, float* part, size_t part_room, cudaStream_t st,
+           float* const* ycopies = nullptr, int nyc = 0) {
   const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
   // tensor maps: input [N][H][W][C] as 4-D (C innermost), weights [Oc][K]
   CUtensorMap txh, txl, twh, twl;
@@ -1015,6 +1031,10 @@ int run_tc(const float* Xh, const float* Xl, const float* Wh, const float* Wl, f
   ConvTc p{};
   p.y = Y;
   p.scale = scale;
+  if (nyc < 0 || nyc > MAX_COPIES) return uk::fail(UK_EINVAL, "conv2d: %d extra copies of Y (0..%d)", nyc, MAX_COPIES);
+  if (nyc > 0 && !pair) return uk::fail(UK_EINVAL, "conv2d: copies of Y need the SM-pair kernel");
+  for (int i = 0; i < nyc; ++i) p.yc[i] = ycopies[i];
+  p.nyc = nyc;
   p.N = N;
   p.Ho = Ho;
   p.Wo = Wo;
@@ -1092,17 +1112,22 @@ extern "C" size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int 
   return 2 * xs + 2 * ws + tail;
 }
 
-extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh,
-                                     int Kw, int Oc, int pad, const float* scale, int layout, void* workspace,
-                                     size_t workspace_bytes, void* stream) {
+namespace {
+
+// the tensor-core fp32 conv, its output stored into Y and the nyc copies
+int conv2d_f32_tc(const float* X, const float* Wt, float* Y, float* const* ycopies, int nyc, int N, int H, int W,
+                  int C, int Kh, int Kw, int Oc, int pad, const float* scale, int layout, void* workspace,
+                  size_t workspace_bytes, void* stream) {
   const cudaStream_t st = (cudaStream_t)stream;
   if (layout != UK_CONV_KML && layout != UK_CONV_NCHW)
     return uk::fail(UK_EINVAL, "conv2d: unknown layout %d", layout);
   if (N < 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0 || pad < 0)
     return uk::fail(UK_EINVAL, "conv2d: invalid dims N=%d H=%d W=%d C=%d Kh=%d Kw=%d Oc=%d pad=%d", N, H, W, C, Kh,
                     Kw, Oc, pad);
-  if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout))
+  if (!tc_applies(N, H, W, C, Kh, Kw, Oc, pad, layout)) {
+    if (nyc > 0) return uk::fail(UK_EINVAL, "conv2d: copies of Y need the tensor-core path (C a multiple of 32)");
     return uk::conv2d_ffma(X, Wt, Y, N, H, W, C, Kh, Kw, Oc, pad, scale, layout, st);
+  }
   // the operand pairs are required; the split partials of the last round
   // are used when the workspace has room for them (the size query includes it)
   const size_t need = 2 * align256((size_t)N * H * W * C * 4) + 2 * align256((size_t)Oc * Kh * Kw * C * 4);
@@ -1162,7 +1187,33 @@ extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, 
   if (int rc = uk::check_launch("conv2d(split)")) return rc;
 
   return run_tc(Xh, Xl, Wh, Wl, Y, scale, N, H, W, C, Kh, Kw, Oc, pad, (float*)((uint8_t*)workspace + need),
-                workspace_bytes - need, st);
+                workspace_bytes - need, st, ycopies, nyc);
+}
+
+}  // namespace
+
+extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh,
+                                     int Kw, int Oc, int pad, const float* scale, int layout, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  return conv2d_f32_tc(X, Wt, Y, nullptr, 0, N, H, W, C, Kh, Kw, Oc, pad, scale, layout, workspace, workspace_bytes,
+                       stream);
+}
+
+extern "C" int uk_cuda_conv2d_f32_allgather(const float* X, const float* Wt, float* const* Y_list, int n_y, int N,
+                                            int H, int W, int C, int Kh, int Kw, int Oc, int pad, const float* scale,
+                                            void* workspace, size_t workspace_bytes, void* stream) {
+  if (Y_list == nullptr || n_y < 1 || n_y > MAX_COPIES + 1)
+    return uk::fail(UK_EINVAL, "conv2d_allgather: 1..%d copies of Y, got %d", MAX_COPIES + 1, n_y);
+  for (int i = 1; i < n_y; ++i) {
+    cudaPointerAttributes a{};
+    if (Y_list[i] == nullptr || cudaPointerGetAttributes(&a, Y_list[i]) != cudaSuccess ||
+        a.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      return uk::fail(UK_ERESIDENCY, "conv2d_allgather: Y_list[%d] is not device memory", i);
+    }
+  }
+  return conv2d_f32_tc(X, Wt, Y_list[0], Y_list + 1, n_y - 1, N, H, W, C, Kh, Kw, Oc, pad, scale, UK_CONV_NCHW,
+                       workspace, workspace_bytes, stream);
 }
 
 // ---- the fp32 GEMM as a 1 x 1 convolution -------------------------------------------

@@ -22,7 +22,14 @@
 //   flight.  When N gives too few 128-column tiles to fill the GPU (a
 //   weight-column shard on 8 GPUs: 14 tiles), K is split over a
 //   thread-block cluster and the partial tiles are summed through
-//   distributed shared memory in a fixed rank order (deterministic).
+//   distributed shared memory in a fixed rank order (deterministic).  Any
+//   cluster size up to 16 folds correctly (ragged k-block ranges and row
+//   slices); a split that puts several CTAs on one SM gets a shallower ring
+//   so the bytes in flight per SM stay about the same.  Splitting the full
+//   Llama-3-8B width (112 tiles) over 4-, 5- or 6-CTA clusters, so that all
+//   148 SMs stream, measured slower than the unsplit 112 CTAs (44.4 / 54.7 /
+//   47.1 us against 40.8 us per chain), so the split is only taken when the
+//   tiles alone leave most of the GPU idle.
 //   The f16 result can be stored into up to 8 copies of Y (other GPUs'
 //   buffers over NVLink): the weight-column sharding of the decode layer with
 //   its all-gather fused into the store.
@@ -34,10 +41,13 @@
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "sm100_ptx.cuh"
 #include "uk_common.cuh"
+#include "uk_plan.cuh"
 
 namespace uk {
 __device__ unsigned int g_decode_fault = 0;
@@ -48,13 +58,6 @@ namespace {
 constexpr int TM = 128;        // W columns per tile (UMMA M)
 constexpr int BP = 32;         // token rows, zero-padded (UMMA N)
 constexpr int BK = 64;         // K per k-block (one 128-byte swizzle row of f16)
-#ifndef UK_DECODE_STAGES
-#define UK_DECODE_STAGES 8
-#endif
-#ifndef UK_DECODE_MIN_CTAS
-#define UK_DECODE_MIN_CTAS 100
-#endif
-constexpr int STAGES = UK_DECODE_STAGES;
 constexpr int CL_MAX = 16;     // CTAs per cluster (K split)
 constexpr int THREADS = 128;   // 4 warps = the 4 TMEM lane quadrants
 constexpr int MAX_OUT = 8;
@@ -71,6 +74,7 @@ struct YList {
   int n;
 };
 
+template <int STAGES>
 struct Ctl {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -80,13 +84,17 @@ struct Ctl {
   int acc_ok;
 };
 
+template <int STAGES>
+constexpr size_t smem_bytes() {
+  return 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(Ctl<STAGES>);
+}
+static_assert(smem_bytes<8>() <= 232448, "shared memory per block on sm_100");
 // the fp32 partial tile of a K-split cluster reuses the ring (all loads have
 // landed once the last MMA completed)
-static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "partial tile fits in the ring");
-constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(Ctl);
-static_assert(SMEM_BYTES <= 232448, "shared memory per block on sm_100");
+static_assert(RED_BYTES <= 2 * STAGE_BYTES, "partial tile fits in the shallowest ring");
 
-__device__ __forceinline__ void fault(Ctl* ctl, unsigned bit) {
+template <class CtlT>
+__device__ __forceinline__ void fault(CtlT* ctl, unsigned bit) {
   atomicOr(&uk::g_decode_fault, bit);
   ctl->abort = 1;
 }
@@ -145,13 +153,14 @@ __global__ void __launch_bounds__(RMS_THREADS) k_rms_f16(const float* __restrict
 }
 
 // ---- 2. skinny GEMM -------------------------------------------------------------
+template <int STAGES>
 __global__ void __launch_bounds__(THREADS)
     k_skinny_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, YList out,
                   int64_t ldy, int B, int N, int K, int64_t col_offset, int kb_per_cta) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* red = smem;
-  Ctl* ctl = (Ctl*)(smem + (size_t)STAGES * STAGE_BYTES);
+  Ctl<STAGES>* ctl = (Ctl<STAGES>*)(smem + (size_t)STAGES * STAGE_BYTES);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t crank = uk_cluster_ctarank();
@@ -275,8 +284,9 @@ __global__ void __launch_bounds__(THREADS)
       *reinterpret_cast<uint4*>(red + m * 128 + ((c ^ (m & 7)) * 16)) =
           make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
     uk_cluster_sync();
-    const int rows = TM / (int)csize;
-    const int m_lo = (int)crank * rows;
+    const int per = (TM + (int)csize - 1) / (int)csize;
+    const int m_lo = min(TM, (int)crank * per);
+    const int rows = min(TM, m_lo + per) - m_lo;
     for (int idx = tid; idx < rows * 8; idx += THREADS) {
       const int mm = m_lo + idx % rows, c = idx / rows;
       const uint32_t a = uk_smem_u32(red + mm * 128 + ((c ^ (mm & 7)) * 16));
@@ -347,6 +357,132 @@ int make_map_f16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t oute
   return UK_OK;
 }
 
+using SkinnyFn = void (*)(CUtensorMap, CUtensorMap, YList, int64_t, int, int, int, int64_t, int);
+
+// ---- the K split ------------------------------------------------------------
+// A plan runs `tiles` clusters of cs CTAs; CTA r of a cluster streams k-blocks
+// [r * ceil(kb/cs), ...).  Policy (measured): no split while the tiles alone
+// give about 100 CTAs; otherwise the smallest power-of-two cs that does, each
+// CTA keeping at least one k-block, halved while the GPU cannot co-schedule
+// the cluster (its own occupancy answer).  per_sm = ceil(tiles * cs / SMs)
+// CTAs share the busiest SM; the ring is 8 stages for one CTA per SM and
+// shallower for more (4 for two, 3 for three, 2 for four or five), with the
+// dynamic shared memory padded so that no SM takes more than per_sm.
+// UK_DECODE_KSPLIT=<cs> pins any cluster size up to 16 (a measurement knob;
+// refused when the cluster cannot be scheduled or needs more than five CTAs
+// per SM).
+struct SplitPlan {
+  int cs = 1, per_sm = 1, stages = 8;
+  size_t smem = 0;
+  SkinnyFn kernel = nullptr;
+};
+
+constexpr int kMaxPerSm = 5;
+constexpr int kMinCtas = 100;
+
+int stages_for(int per_sm) { return per_sm <= 1 ? 8 : per_sm == 2 ? 4 : per_sm == 3 ? 3 : 2; }
+
+SkinnyFn kernel_for(int stages) {
+  switch (stages) {
+    case 8: return k_skinny_gemm<8>;
+    case 4: return k_skinny_gemm<4>;
+    case 3: return k_skinny_gemm<3>;
+    default: return k_skinny_gemm<2>;
+  }
+}
+
+size_t ring_smem(int stages) {
+  switch (stages) {
+    case 8: return smem_bytes<8>();
+    case 4: return smem_bytes<4>();
+    case 3: return smem_bytes<3>();
+    default: return smem_bytes<2>();
+  }
+}
+
+void launch_config(const SplitPlan& plan, int tiles, cudaStream_t st, cudaLaunchConfig_t* cfg,
+                   cudaLaunchAttribute* attr) {
+  *cfg = cudaLaunchConfig_t{};
+  cfg->gridDim = dim3((unsigned)plan.cs, (unsigned)tiles, 1);
+  cfg->blockDim = dim3(THREADS, 1, 1);
+  cfg->dynamicSmemBytes = plan.smem;
+  cfg->stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)plan.cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg->attrs = attr;
+  cfg->numAttrs = 2;
+}
+
+// shared memory that fits at most per_sm CTAs on one SM (at least the ring)
+size_t padded_smem(int stages, int per_sm, int sm_smem, int reserved) {
+  const size_t ring = ring_smem(stages);
+  if (per_sm >= kMaxPerSm) return ring;
+  // one CTA more than per_sm must not fit: (per_sm + 1) * (smem + reserved) > sm_smem
+  const size_t cap = (size_t)sm_smem / (size_t)(per_sm + 1) - (size_t)reserved + 1024;
+  return std::max(ring, std::min(cap, (size_t)232448));
+}
+
+// the plan for cluster size cs, or false when the GPU cannot co-schedule it
+bool make_plan(int dev, int cs, int tiles, int nsm, int sm_smem, int reserved, SplitPlan* c) {
+  c->cs = cs;
+  c->per_sm = (int)(((long)tiles * cs + nsm - 1) / nsm);
+  if (c->per_sm > kMaxPerSm) return false;
+  c->stages = stages_for(c->per_sm);
+  c->kernel = kernel_for(c->stages);
+  c->smem = padded_smem(c->stages, c->per_sm, sm_smem, reserved);
+  if (cs == 1) return true;
+  // the answer per (device, cluster size, per_sm) is asked once: 1 yes, -1 no
+  static signed char fits[64][CL_MAX + 1][kMaxPerSm + 1] = {};
+  signed char* slot = (dev >= 0 && dev < 64) ? &fits[dev][cs][c->per_sm] : nullptr;
+  if (slot && *slot != 0) return *slot > 0;
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[2];
+  launch_config(*c, tiles, nullptr, &cfg, attr);
+  int active = 0;
+  const bool ok = cudaOccupancyMaxActiveClusters(&active, c->kernel, &cfg) == cudaSuccess && active > 0;
+  cudaGetLastError();
+  if (slot) *slot = ok ? 1 : -1;
+  return ok;
+}
+
+int plan_split(int dev, int tiles, int kb_total, SplitPlan* out) {
+  int nsm = 0, sm_smem = 0, reserved = 0;
+  if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess)
+    return uk::check_launch("decode_rmsnorm_gemm: device attributes");
+  static std::once_flag attr_once[64];
+  static int attr_rc[64] = {};
+  if (dev >= 0 && dev < 64) {
+    std::call_once(attr_once[dev], [&] {
+      for (int stg : {8, 4, 3, 2}) {
+        const SkinnyFn f = kernel_for(stg);
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+          attr_rc[dev] = 1;
+      }
+    });
+    if (attr_rc[dev]) return uk::check_launch("decode_rmsnorm_gemm: function attributes");
+  }
+  if (const char* e = getenv("UK_DECODE_KSPLIT")) {
+    const int pin = atoi(e);
+    if (pin < 1 || pin > CL_MAX || !make_plan(dev, pin, tiles, nsm, sm_smem, reserved, out))
+      return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: UK_DECODE_KSPLIT=%s cannot be scheduled (1..%d, at most %d "
+                      "CTAs per SM)", e, CL_MAX, kMaxPerSm);
+    return UK_OK;
+  }
+  int cs = 1;
+  while (tiles * cs < kMinCtas && cs < CL_MAX && kb_total >= 2 * cs) cs *= 2;
+  for (; cs > 1; cs /= 2)
+    if (make_plan(dev, cs, tiles, nsm, sm_smem, reserved, out)) return UK_OK;
+  make_plan(dev, 1, tiles, nsm, sm_smem, reserved, out);
+  return UK_OK;
+}
+
 }  // namespace
 
 namespace uk {
@@ -408,68 +544,37 @@ extern "C" int uk_cuda_decode_rmsnorm_gemm_f16(const float* X, const float* gamm
   }
   out.n = n_y;
 
-  // K split: none while the 128-column tiles alone give ~100+ CTAs; otherwise
-  // the smallest power-of-two cluster that does (a weight-column shard)
   const int kb_total = (K + BK - 1) / BK;
   const int tiles = (N_shard + TM - 1) / TM;
   if (tiles > 65535) return uk::fail(UK_EINVAL, "decode_rmsnorm_gemm: N_shard too large");
-  int csize = 1;
-  while (tiles * csize < UK_DECODE_MIN_CTAS && csize < CL_MAX && kb_total >= 2 * csize) csize *= 2;
 
   CUtensorMap tmW, tmX;
   if (int rc = make_map_f16(&tmW, W, (uint64_t)N_shard, (uint64_t)K, (uint64_t)ldw, 64, BK)) return rc;
   if (int rc = make_map_f16(&tmX, workspace, (uint64_t)K, (uint64_t)B, (uint64_t)K, BK, BP)) return rc;
 
-  static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(k_skinny_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(k_skinny_gemm, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-      return uk::check_launch("decode_rmsnorm_gemm: function attributes");
-    attr_done[dev] = true;
-  }
+  SplitPlan plan;
+  if (int rc = plan_split(dev, tiles, kb_total, &plan)) return rc;
   const cudaStream_t st = (cudaStream_t)stream;
   cudaLaunchConfig_t cfg{};
-  cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
-  cfg.stream = st;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  // a cluster the GPU cannot co-schedule is halved until it can (the answer
-  // per device and cluster size is asked once: 1 yes, -1 no)
-  static signed char cluster_fits[64][5] = {};
-  for (;; csize /= 2) {
-    cfg.gridDim = dim3((unsigned)csize, (unsigned)tiles, 1);
-    attr[0].val.clusterDim.x = (unsigned)csize;
-    if (csize == 1) break;
-    int lg = 0;
-    while ((1 << lg) < csize) ++lg;
-    signed char* fit = (dev >= 0 && dev < 64) ? &cluster_fits[dev][lg] : nullptr;
-    if (fit == nullptr || *fit == 0) {
-      int nclusters = 0;
-      const bool ok = cudaOccupancyMaxActiveClusters(&nclusters, k_skinny_gemm, &cfg) == cudaSuccess && nclusters > 0;
-      cudaGetLastError();
-      if (fit) *fit = ok ? 1 : -1;
-      if (ok) break;
-    } else if (*fit > 0) {
-      break;
-    }
+  launch_config(plan, tiles, st, &cfg, attr);
+  const int kb_per_cta = (kb_total + plan.cs - 1) / plan.cs;
+  {
+    uk::Candidate c;  // the skinny decode GEMM (tile = W columns x token rows x k-block)
+    c.family = uk::kFamSkinny;
+    c.tile = uk::Tile{TM, BP, BK, plan.stages};
+    c.ksplit = plan.cs;
+    c.us = 0.0;
+    uk::note_launch(c);
   }
-  const int kb_per_cta = (kb_total + csize - 1) / csize;
 
   k_rms_f16<<<B, RMS_THREADS, 0, st>>>(X, gamma, eps, (__half*)workspace, K);
   if (int rc = uk::check_launch("decode_rmsnorm_gemm(norm)")) return rc;
 
   const cudaError_t e =
-      cudaLaunchKernelEx(&cfg, k_skinny_gemm, tmW, tmX, out, ldy, B, N_shard, K, col_offset, kb_per_cta);
+      cudaLaunchKernelEx(&cfg, plan.kernel, tmW, tmX, out, ldy, B, N_shard, K, col_offset, kb_per_cta);
   if (e != cudaSuccess) return uk::fail(UK_ECUDA, "decode_rmsnorm_gemm: launch: %s", cudaGetErrorString(e));
   return uk::check_launch("decode_rmsnorm_gemm");
 }

@@ -444,6 +444,7 @@ namespace uk {
 unsigned decode_fault_take();  // decode.cu
 unsigned conv_fault_take();    // conv_tc.cu
 unsigned fault_take_2sm();     // gemm_f16_2sm.cu
+unsigned peer_fault_take();    // peer.cu
 }
 
 // the bounded wait of every pipeline, run alone on one mbarrier: when nothing
@@ -475,5 +476,5 @@ extern "C" unsigned uk_cuda_pipeline_fault(void) {
   if (cudaMemcpyFromSymbol(&v, uk::g_fault_word, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
   const unsigned zero = 0;
   cudaMemcpyToSymbol(uk::g_fault_word, &zero, sizeof(zero));
-  return v | uk::decode_fault_take() | uk::conv_fault_take() | uk::fault_take_2sm();
+  return v | uk::decode_fault_take() | uk::conv_fault_take() | uk::fault_take_2sm() | uk::peer_fault_take();
 }

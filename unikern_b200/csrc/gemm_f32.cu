@@ -18,6 +18,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 
 #include "sm100_ptx.cuh"
 #include "uk_common.cuh"
@@ -65,26 +66,17 @@ struct SgemmCfg {
   static_assert(BK % 4 == 0, "BK must be a multiple of 4");
 };
 
-template <int BM, int BN, int BK, int TM, int TN, bool VEC, typename T, int KS = 1>
-__global__ void __launch_bounds__((BM / TM) * (BN / TN))
-    k_sgemm(const T* __restrict__ A, const T* __restrict__ B, T* __restrict__ C, int M, int N, int K,
-            int64_t lda, int64_t ldb, int64_t ldc) {
+// One tile's main loop: acc += A[m0 : m0 + BM, kbeg : kend) * B[kbeg : kend, n0 : n0 + BN)
+// by the NT threads (tid) that share As / Bs; `sync` is their barrier (the
+// whole CTA, or one warp group of a CTA that splits K over its groups).
+template <int BM, int BN, int BK, int TM, int TN, bool VEC, typename T, class Sync>
+__device__ __forceinline__ void sgemm_mainloop(const T* __restrict__ A, const T* __restrict__ B, int M, int N,
+                                               int64_t lda, int64_t ldb, int m0, int n0, int kbeg, int kend, int tid,
+                                               float (*As)[BK][SgemmCfg<BM, BN, BK, TM, TN, VEC>::APAD],
+                                               float (*Bs)[BK][BN], float (&acc)[TM][TN], Sync sync) {
   using Cfg = SgemmCfg<BM, BN, BK, TM, TN, VEC>;
   constexpr int NT = Cfg::NT, NTX = Cfg::NTX, NTY = Cfg::NTY;
-  __shared__ __align__(16) float As[2][BK][Cfg::APAD];
-  __shared__ __align__(16) float Bs[2][BK][BN];
-
-  const int tid = threadIdx.x;
   const int tx = tid % NTX, ty = tid / NTX;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  // this CTA's K range: all of K, or its share of a K-split cluster (grid z)
-  int kbeg = 0, kend = K;
-  if constexpr (KS > 1) {
-    const int kc = ((K + KS - 1) / KS + BK - 1) / BK * BK;
-    kbeg = min(K, (int)blockIdx.z * kc);
-    kend = min(K, kbeg + kc);
-  }
-
   float ra[Cfg::A_PER][4], rb[Cfg::B_PER][4];
 
   // global -> registers for the slab starting at k0 (zero outside the matrix)
@@ -148,7 +140,6 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     }
   };
 
-  float acc[TM][TN];
 #pragma unroll
   for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -159,7 +150,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     load_slab(kbeg);
     store_slab(0);
   }
-  __syncthreads();
+  sync();
   for (int s = 0; s < nslab; ++s) {
     const int buf = s & 1;
     if (s + 1 < nslab) load_slab(kbeg + (s + 1) * BK);
@@ -182,8 +173,37 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
     if (s + 1 < nslab) store_slab(buf ^ 1);
-    __syncthreads();
+    sync();
   }
+}
+
+// the K range of part `part` of `parts` (each a whole number of BK slabs)
+template <int BK>
+__device__ __forceinline__ void k_range(int K, int part, int parts, int* kbeg, int* kend) {
+  const int kc = ((K + parts - 1) / parts + BK - 1) / BK * BK;
+  *kbeg = min(K, part * kc);
+  *kend = min(K, *kbeg + kc);
+}
+
+template <int BM, int BN, int BK, int TM, int TN, bool VEC, typename T, int KS = 1>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+    k_sgemm(const T* __restrict__ A, const T* __restrict__ B, T* __restrict__ C, int M, int N, int K,
+            int64_t lda, int64_t ldb, int64_t ldc) {
+  using Cfg = SgemmCfg<BM, BN, BK, TM, TN, VEC>;
+  constexpr int NT = Cfg::NT, NTX = Cfg::NTX, NTY = Cfg::NTY;
+  __shared__ __align__(16) float As[2][BK][Cfg::APAD];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+
+  const int tid = threadIdx.x;
+  const int tx = tid % NTX, ty = tid / NTX;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  // this CTA's K range: all of K, or its share of a K-split cluster (grid z)
+  int kbeg = 0, kend = K;
+  if constexpr (KS > 1) k_range<BK>(K, (int)blockIdx.z, KS, &kbeg, &kend);
+
+  float acc[TM][TN];
+  sgemm_mainloop<BM, BN, BK, TM, TN, VEC, T>(A, B, M, N, lda, ldb, m0, n0, kbeg, kend, tid, As, Bs, acc,
+                                              [] { __syncthreads(); });
 
   if constexpr (KS > 1) {
     // the partial tile into shared memory (the slab buffers are free after the
@@ -257,6 +277,78 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     }
 }
 
+// The 32 x 64 tile with K split over KG warp groups of one CTA (128 threads
+// each, named barrier g + 1 for group g): each group walks its K range through
+// its own slab buffers, the partial tiles meet in the CTA's shared memory, and
+// every element is summed over the groups in group order -- the arithmetic of
+// the KS = KG cluster split (same K ranges, same fold order: the same bits)
+// without the cluster barrier and the distributed-shared-memory reads.
+constexpr int KG_BM = 32, KG_BN = 64, KG_BK = 16;
+using KgCfg = SgemmCfg<KG_BM, KG_BN, KG_BK, 4, 4, true>;
+constexpr int KG_GROUP_FLOATS = 2 * KG_BK * KgCfg::APAD + 2 * KG_BK * KG_BN;
+static_assert(KG_BM * KG_BN <= KG_GROUP_FLOATS, "a group's partial tile fits in its slab buffers");
+template <int KG>
+constexpr size_t kg_smem_bytes() {
+  return (size_t)KG * KG_GROUP_FLOATS * sizeof(float);
+}
+
+template <int KG, bool VEC, typename T>
+__global__ void __launch_bounds__(128 * KG)
+    k_sgemm_kg(const T* __restrict__ A, const T* __restrict__ B, T* __restrict__ C, int M, int N, int K,
+               int64_t lda, int64_t ldb, int64_t ldc) {
+  constexpr int BM = KG_BM, BN = KG_BN, BK = KG_BK, TM = 4, TN = 4;
+  using Cfg = SgemmCfg<BM, BN, BK, TM, TN, VEC>;
+  constexpr int NT = Cfg::NT, NTX = Cfg::NTX, NTY = Cfg::NTY;
+  static_assert(NT == 128 && KG >= 2 && KG <= 8, "groups of 128 threads, named barriers 1..8");
+  extern __shared__ __align__(16) float kg_smem[];
+  const int g = (int)threadIdx.x / NT, tid = (int)threadIdx.x % NT;
+  const int tx = tid % NTX, ty = tid / NTX;
+  float* gs = kg_smem + g * KG_GROUP_FLOATS;
+  auto As = reinterpret_cast<float (*)[BK][Cfg::APAD]>(gs);
+  auto Bs = reinterpret_cast<float (*)[BK][BN]>(gs + 2 * BK * Cfg::APAD);
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  int kbeg, kend;
+  k_range<BK>(K, g, KG, &kbeg, &kend);
+
+  float acc[TM][TN];
+  sgemm_mainloop<BM, BN, BK, TM, TN, VEC, T>(A, B, M, N, lda, ldb, m0, n0, kbeg, kend, tid, As, Bs, acc, [g] {
+    asm volatile("bar.sync %0, %1;" ::"r"(g + 1), "r"(NT) : "memory");
+  });
+
+  // the group's partial tile into its own slab buffers (its last barrier has
+  // passed), then every element summed over the groups in group order
+  float* red = gs;
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    const int lm = ty * 4 + i, ln = tx * 4;
+    *reinterpret_cast<float4*>(red + lm * BN + ln) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  }
+  __syncthreads();
+  for (int idx = (int)threadIdx.x; idx < BM * BN / 4; idx += NT * KG) {
+    const int lm = idx / (BN / 4), ln = (idx % (BN / 4)) * 4;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < KG; ++r) {
+      const float4 q = *reinterpret_cast<const float4*>(kg_smem + r * KG_GROUP_FLOATS + lm * BN + ln);
+      v[0] += q.x;
+      v[1] += q.y;
+      v[2] += q.z;
+      v[3] += q.w;
+    }
+    const int gm = m0 + lm, gn = n0 + ln;
+    if (gm < M) {
+      T* c = C + (size_t)gm * ldc + gn;
+      if (VEC && gn + 3 < N) {
+        st4(c, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (gn + j < N) st1(c + j, v[j]);
+      }
+    }
+  }
+}
+
 template <int BM, int BN, int BK, int TM, int TN, typename T>
 void launch(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
             cudaStream_t st) {
@@ -296,17 +388,49 @@ void launch_split(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda
   else cudaLaunchKernelEx(&cfg, k_sgemm<32, 64, BK, 4, 4, false, T, KS>, A, B, C, M, N, K, lda, ldb, ldc);
 }
 
-// A pinned FFMA plan from UK_SGEMM_PLAN="bm,bn,ks" (a measurement knob, like
-// the reference's UK_CONV_TILE): one of the compiled variants 128,128,1 /
-// 64,64,1 / 32,64,{1,2,4,8}.  Returns 0 with *c set, 1 when unset, 2 when
-// the value names no compiled variant (the call is then refused).
+// the 32 x 64 tile with K split over KG warp groups of one CTA
+template <int KG, typename T>
+int launch_groups(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
+                  cudaStream_t st) {
+  static std::once_flag once[64];
+  static int rc[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64) {
+    std::call_once(once[dev], [&] {
+      if (cudaFuncSetAttribute(k_sgemm_kg<KG, true, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kg_smem_bytes<KG>()) != cudaSuccess ||
+          cudaFuncSetAttribute(k_sgemm_kg<KG, false, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kg_smem_bytes<KG>()) != cudaSuccess)
+        rc[dev] = 1;
+    });
+    if (rc[dev]) return uk::check_launch("gemm: k-group kernel attributes");
+  }
+  const dim3 grid((unsigned)((N + KG_BN - 1) / KG_BN), (unsigned)((M + KG_BM - 1) / KG_BM));
+  if (vec) k_sgemm_kg<KG, true, T><<<grid, 128 * KG, kg_smem_bytes<KG>(), st>>>(A, B, C, M, N, K, lda, ldb, ldc);
+  else k_sgemm_kg<KG, false, T><<<grid, 128 * KG, kg_smem_bytes<KG>(), st>>>(A, B, C, M, N, K, lda, ldb, ldc);
+  return UK_OK;
+}
+
+// A pinned FFMA plan from UK_SGEMM_PLAN="bm,bn,ks[,kg]" (a measurement knob,
+// like the reference's UK_CONV_TILE): one of the compiled variants 128,128,1 /
+// 64,64,1 / 32,64,{1,2,4,8} (K split over a cluster of ks CTAs) /
+// 32,64,1,{2,4,8} (K split over kg warp groups of one CTA).  Returns 0 with
+// *c set, 1 when unset, 2 when the value names no compiled variant (the call
+// is then refused).
 int pinned_plan(uk::Candidate* c) {
   const char* e = getenv("UK_SGEMM_PLAN");
   if (e == nullptr || e[0] == 0) return 1;
-  int bm = 0, bn = 0, ks = 0;
-  if (sscanf(e, "%d,%d,%d", &bm, &bn, &ks) != 3) return 2;
-  const bool ok = (bm == 128 && bn == 128 && ks == 1) || (bm == 64 && bn == 64 && ks == 1) ||
-                  (bm == 32 && bn == 64 && (ks == 1 || ks == 2 || ks == 4 || ks == 8));
+  int bm = 0, bn = 0, ks = 0, kg = 1;
+  const int got = sscanf(e, "%d,%d,%d,%d", &bm, &bn, &ks, &kg);
+  if (got != 3 && got != 4) return 2;
+  if (kg > 1) {
+    if (!(bm == 32 && bn == 64 && ks == 1 && (kg == 2 || kg == 4 || kg == 8))) return 2;
+    *c = uk::Candidate{uk::kFamSgemmGroups, uk::Tile{32, 64, 16, 2}, kg, 0.0};
+    return 0;
+  }
+  const bool ok = kg == 1 && ((bm == 128 && bn == 128 && ks == 1) || (bm == 64 && bn == 64 && ks == 1) ||
+                              (bm == 32 && bn == 64 && (ks == 1 || ks == 2 || ks == 4 || ks == 8)));
   if (!ok) return 2;
   *c = uk::Candidate{uk::kFamSgemm, uk::Tile{bm, bn, bm == 32 ? 16 : 8, 2}, ks, 0.0};
   return 0;
@@ -320,11 +444,18 @@ int simt_gemm(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, in
   uk::Candidate c = uk::solve_gemm(M, N, K, /*f16*/ false, /*allow_tc*/ false, uk::sm_count());
   const int pin = pinned_plan(&c);
   if (pin == 2)
-    return uk::fail(UK_EINVAL, "gemm: UK_SGEMM_PLAN=%s names no compiled FFMA plan (128,128,1 64,64,1 32,64,{1,2,4,8})",
+    return uk::fail(UK_EINVAL,
+                    "gemm: UK_SGEMM_PLAN=%s names no compiled FFMA plan (128,128,1 64,64,1 32,64,{1,2,4,8} "
+                    "32,64,1,{2,4,8})",
                     getenv("UK_SGEMM_PLAN"));
   if (pin == 0 && c.ksplit > 1 && K / c.ksplit < 16)
     return uk::fail(UK_EINVAL, "gemm: UK_SGEMM_PLAN k split %d leaves less than 16 of K=%d per CTA", c.ksplit, K);
   uk::note_launch(c);
+  if (c.family == uk::kFamSgemmGroups) {
+    if (c.ksplit == 8) return launch_groups<8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    if (c.ksplit == 4) return launch_groups<4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    return launch_groups<2>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  }
   if (c.tile.bm == 128) {
     launch<128, 128, 8, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   } else if (c.tile.bm == 64) {

@@ -134,6 +134,81 @@ extern "C" int uk_cuda_gemm_f16_host(const uint16_t* hA, const uint16_t* hB, uin
   return UK_OK;
 }
 
+// ---- row ops from and to host memory ------------------------------------------
+// The same pipeline for the row ops (their rows are independent): the copy-in
+// stream uploads W (RMSNorm's gamma, channelscale's S), then the row blocks of
+// X; the caller's stream runs the op on each block once it landed; the
+// copy-out stream brings each block of Y home while later blocks upload, so
+// the two PCIe directions run at once instead of one after the other.
+extern "C" int uk_cuda_rmsnorm_f32(const float* X, const float* W, float* Y, int64_t L, int64_t C, float eps,
+                                   void* stream);
+extern "C" int uk_cuda_softmax_f32(const float* X, float* Y, int64_t L, int64_t C, void* stream);
+extern "C" int uk_cuda_channelscale_f32(const float* X, const float* S, float* Y, int64_t L, int64_t C,
+                                        void* stream);
+extern "C" int uk_cuda_reduce_f32(const float* X, float* Y, int64_t rows, int64_t cols, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+extern "C" int uk_cuda_rowop_host(int op, const float* hX, const float* hW, float* hY, float* dX, float* dW,
+                                  float* dY, int64_t L, int64_t C, float eps, int chunks, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (op != UK_OP_REDUCE && op != UK_OP_SOFTMAX && op != UK_OP_RMSNORM && op != UK_OP_CHANNELSCALE)
+    return uk::fail(UK_EINVAL, "rowop_host: op %d is not reduce, softmax, rmsnorm or channelscale", op);
+  if (L < 0 || C < 0) return uk::fail(UK_EINVAL, "rowop_host: negative size L=%lld C=%lld", (long long)L, (long long)C);
+  if (chunks < 0 || chunks > MAX_CHUNKS) return uk::fail(UK_EINVAL, "rowop_host: chunks %d (0..%d)", chunks, MAX_CHUNKS);
+  if (L == 0) return UK_OK;
+  const bool has_w = op == UK_OP_RMSNORM || op == UK_OP_CHANNELSCALE;
+  if (int rc = check_host(hX, "hX")) return rc;
+  if (int rc = check_host(hY, "hY")) return rc;
+  if (has_w)
+    if (int rc = check_host(hW, "hW")) return rc;
+  if (int rc = uk::check_device_ptr(dX, "dX")) return rc;
+  if (int rc = uk::check_device_ptr(dY, "dY")) return rc;
+  if (has_w)
+    if (int rc = uk::check_device_ptr(dW, "dW")) return rc;
+  DevPipe* p = nullptr;
+  if (int rc = get_pipe(&p)) return rc;
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (chunks == 0) chunks = 8;
+  const int64_t rows = (L + chunks - 1) / chunks;
+  const int nblk = (int)((L + rows - 1) / rows);
+  const int64_t ycols = op == UK_OP_REDUCE ? 1 : C;  // Y per row: one sum, or a row
+  if (cudaEventRecord(p->start, st) != cudaSuccess || cudaStreamWaitEvent(p->in, p->start, 0) != cudaSuccess ||
+      cudaStreamWaitEvent(p->out, p->start, 0) != cudaSuccess)
+    return uk::check_launch("rowop_host: ordering");
+  if (has_w && (cudaMemcpyAsync(dW, hW, (size_t)C * 4, cudaMemcpyHostToDevice, p->in) != cudaSuccess ||
+                cudaEventRecord(p->b_ready, p->in) != cudaSuccess))
+    return uk::check_launch("rowop_host: upload W");
+  for (int i = 0; i < nblk; ++i) {
+    const int64_t r0 = (int64_t)i * rows, r1 = r0 + rows < L ? r0 + rows : L;
+    if (cudaMemcpyAsync(dX + r0 * C, hX + r0 * C, (size_t)(r1 - r0) * C * 4, cudaMemcpyHostToDevice, p->in) !=
+            cudaSuccess ||
+        cudaEventRecord(p->a_ready[i], p->in) != cudaSuccess)
+      return uk::check_launch("rowop_host: upload X");
+  }
+  for (int i = 0; i < nblk; ++i) {
+    const int64_t r0 = (int64_t)i * rows, r1 = r0 + rows < L ? r0 + rows : L, n = r1 - r0;
+    if ((i == 0 && has_w && cudaStreamWaitEvent(st, p->b_ready, 0) != cudaSuccess) ||
+        cudaStreamWaitEvent(st, p->a_ready[i], 0) != cudaSuccess)
+      return uk::check_launch("rowop_host: wait");
+    int rc = UK_OK;
+    float* x = dX + r0 * C;
+    float* y = dY + r0 * ycols;
+    switch (op) {
+      case UK_OP_SOFTMAX: rc = uk_cuda_softmax_f32(x, y, n, C, stream); break;
+      case UK_OP_RMSNORM: rc = uk_cuda_rmsnorm_f32(x, dW, y, n, C, eps, stream); break;
+      case UK_OP_CHANNELSCALE: rc = uk_cuda_channelscale_f32(x, dW, y, n, C, stream); break;
+      default: rc = uk_cuda_reduce_f32(x, y, n, C, workspace, workspace_bytes, stream); break;
+    }
+    if (rc != UK_OK) return rc;
+    if (cudaEventRecord(p->c_ready[i], st) != cudaSuccess || cudaStreamWaitEvent(p->out, p->c_ready[i], 0) != cudaSuccess ||
+        cudaMemcpyAsync(hY + r0 * ycols, y, (size_t)n * ycols * 4, cudaMemcpyDeviceToHost, p->out) != cudaSuccess)
+      return uk::check_launch("rowop_host: download Y");
+  }
+  if (cudaEventRecord(p->done, p->out) != cudaSuccess || cudaStreamWaitEvent(st, p->done, 0) != cudaSuccess)
+    return uk::check_launch("rowop_host: join");
+  return UK_OK;
+}
+
 // ---- streamed GEMM (payload larger than the device) -------------------------
 // Only B is resident; A and C pass through a two-slot ring of row blocks in
 // the caller's device buffer.  Block i uses slot i % 2: its upload waits until

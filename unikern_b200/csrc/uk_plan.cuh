@@ -103,6 +103,8 @@ enum Family : int {
   kFamTf32x3 = 3,     // fp32 as split-tf32 on the conv pair kernel (conv_tc.cu)
   kFamConvFfma = 4,   // FFMA implicit-GEMM conv (conv_f32.cu)
   kFamConvPair = 5,   // tcgen05 conv on SM pairs, split-tf32 or f16 (conv_tc.cu)
+  kFamSkinny = 6,     // tcgen05 skinny GEMM of the decode chain, K split over a cluster (decode.cu)
+  kFamSgemmGroups = 7,  // FFMA 32 x 64 tile with K split over warp groups of one CTA (gemm_f32.cu)
 };
 
 inline const char* family_name(int f) {
@@ -113,6 +115,8 @@ inline const char* family_name(int f) {
     case kFamTf32x3: return "tcgen05-2sm-3xtf32";
     case kFamConvFfma: return "ffma-conv";
     case kFamConvPair: return "tcgen05-2sm-conv";
+    case kFamSkinny: return "tcgen05-skinny";
+    case kFamSgemmGroups: return "ffma-kgroups";
   }
   return "?";
 }

@@ -4,9 +4,9 @@ The north star splits the columns of B and C over the GPUs of one node and
 all-gathers C.  Here the all-gather is fused into the GEMM: every rank holds a
 full C[M][N]; rank r computes its column block and its kernel stores each
 tile into its own C and into every peer's C (CUDA IPC mappings over NVLink).
-torch.distributed is the plumbing: it carries the IPC handles once, and an
-all-reduce of one float after each GEMM is the stream-ordered barrier that
-tells every rank its C is complete.
+torch.distributed is the plumbing: it carries the IPC handles once.  After
+each GEMM a device-side barrier (flags posted into every rank's memory over
+NVLink, waited for with a time limit) tells every rank its C is complete.
 """
 from __future__ import annotations
 
@@ -167,6 +167,50 @@ class PeerBuffers:
         self._opened = []
 
 
+class DeviceBarrier:
+    """Stream-ordered barrier of the ranks on the GPUs themselves
+    (uk_cuda_peer_barrier): each rank's flag array (one unsigned per rank) is
+    opened by every peer once; a step posts an ever-growing epoch into every
+    rank's array and waits, bounded by timeout_s, for every rank's post in its
+    own.  It replaces a one-float NCCL all-reduce (about 25 us on 8 GPUs) after
+    the sharded kernels; UK_BARRIER=nccl keeps the all-reduce (for
+    comparison).  A wait that runs out sets bit 32 of uk_cuda_pipeline_fault."""
+
+    def __init__(self, group=None, timeout_s: float = 2.0):
+        import torch
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.kind = "nccl" if os.environ.get("UK_BARRIER", "device") == "nccl" else "device"
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.epoch = 0
+        self.flag = torch.zeros(1, device="cuda")
+        self.peers = None
+        if self.kind == "device" and self.world > 1:
+            self.flags = torch.zeros(MAX_RANKS, dtype=torch.int32, device="cuda")
+            self.peers = PeerBuffers(self.flags, group)
+            self.ptrs = (C.c_void_p * self.world)(*self.peers.ptrs)
+
+    def __call__(self, stream=None):
+        import torch.distributed as dist
+        if self.world == 1:
+            return
+        if self.kind == "nccl":
+            dist.all_reduce(self.flag, group=self.group)
+            return
+        self.epoch += 1
+        abi.check(abi.lib().uk_cuda_peer_barrier(self.ptrs, self.world, self.rank, self.epoch & 0xFFFFFFFF,
+                                                 self.timeout_ns, abi._stream(stream)))
+
+    def close(self):
+        if self.peers is not None:
+            import torch
+            torch.cuda.synchronize()
+            self.peers.close()
+            self.peers = None
+
+
 class GemmAllGather:
     """C = A * B on `world` GPUs: B and C split by columns, C all-gathered."""
 
@@ -185,12 +229,13 @@ class GemmAllGather:
         self.c_list = (C.c_void_p * self.world)(*[self.peers.ptrs[r] for r in order])
         self.ldc = C_full.stride(0)
         self.c_tensor, self.c_local = C_full, C_full.data_ptr()
-        self.flag = torch.zeros(1, device="cuda")
-        self.launches_per_step = 1  # this library's kernels per step (the barrier is NCCL's)
+        self.sync = DeviceBarrier(group)
+        # this library's kernels per step: the GEMM, and the device barrier
+        self.launches_per_step = 2 if self.sync.kind == "device" else 1
 
     def describe(self):
         return "N-sharded over %d GPUs (%d columns each), all-gather fused into the GEMM epilogue " \
-               "(peer stores over NVLink) + NCCL barrier" % (self.world, self.n1 - self.n0)
+               "(peer stores over NVLink) + %s barrier" % (self.world, self.n1 - self.n0, self.sync.kind)
 
     def b_shard(self, B):
         return B[:, self.n0:self.n1]
@@ -201,10 +246,9 @@ class GemmAllGather:
             A.data_ptr(), A.stride(0), B_shard.data_ptr(), B_shard.stride(0), self.c_list, self.world, self.ldc,
             self.M, self.n1 - self.n0, self.K, self.n0, abi._stream(stream)))
 
-    def barrier(self):
+    def barrier(self, stream=None):
         """Stream-ordered: after it, every rank's stores into this rank's C are done."""
-        import torch.distributed as dist
-        dist.all_reduce(self.flag, group=self.group)
+        self.sync(stream)
 
     def run(self, A, B_shard, C_full, stream=None, watch=None):
         """One step; with a PeerWatch, every peer is confirmed alive on the
@@ -212,9 +256,10 @@ class GemmAllGather:
         if watch is not None:
             watch.step()
         self.launch(A, B_shard, stream)
-        self.barrier()
+        self.barrier(stream)
 
     def close(self):
+        self.sync.close()
         self.peers.close()
 
 
@@ -347,8 +392,13 @@ class ConvBatchShard:
     `world` GPUs: the batch is split into contiguous image blocks, weights and
     scale are replicated, and the output is all-gathered so every rank holds
     the full Y[N][Oc][Ho][Wo].  Images are independent, so the only exchange is
-    the gather (NCCL over NVLink): in place into Y when the blocks are equal,
-    through a padded staging buffer otherwise."""
+    the gather.  On the tensor-core path it is fused into the conv's store:
+    each rank's kernel writes its image block into every rank's Y (CUDA IPC
+    mappings over NVLink, opened on the first run) and a device barrier orders
+    the ranks, so the exchange overlaps the compute tile by tile.  Otherwise
+    (and with UK_CONV_GATHER=nccl) an NCCL all-gather after the conv: in place
+    into Y when the blocks are equal, through a padded staging buffer
+    otherwise."""
 
     def __init__(self, N, Cc, H, W, Oc, Kh, Kw, pad, group=None):
         import torch.distributed as dist
@@ -365,26 +415,57 @@ class ConvBatchShard:
         # the shape runs the FFMA kernel)
         self.ws = abi.conv2d_workspace(max(1, self.b1 - self.b0), H, W, Cc, Kh, Kw, Oc, pad, abi.UK_CONV_NCHW) \
             if self.b1 > self.b0 else None
-        self.launches_per_step = 3  # the hi/lo pre-passes and the conv
+        self.fused = self.world > 1 and self.ws is not None and os.environ.get("UK_CONV_GATHER", "fused") != "nccl"
+        self._peers = None
+        self._ylist = None
+        self.sync = DeviceBarrier(group) if self.fused else None
+        # the hi/lo pre-passes and the conv (and the device barrier when fused)
+        self.launches_per_step = 4 if self.fused else 3
 
     def describe(self):
-        return "batch-sharded over %d GPUs (%d images each), NCCL all-gather of Y" % (self.world, self.b1 - self.b0)
+        return "batch-sharded over %d GPUs (%d images each), %s" % (
+            self.world, self.b1 - self.b0,
+            "all-gather fused into the conv's store (peer stores over NVLink) + device barrier" if self.fused else
+            "NCCL all-gather of Y")
+
+    def _bind(self, Y):
+        """Open every rank's Y once (a collective: every rank binds together)."""
+        if self._peers is not None:
+            if Y.data_ptr() != self._bound:
+                raise ValueError("ConvBatchShard: the fused gather is bound to one Y buffer")
+            return
+        self._peers = PeerBuffers(Y, self.group)
+        self._bound = Y.data_ptr()
+        off = self.b0 * self.Oc * self.Ho * self.Wo * Y.element_size()
+        order = store_order(self.world, self.rank)
+        self._ylist = (C.c_void_p * self.world)(*[self._peers.ptrs[r] + off for r in order])
 
     def x_shard(self, X):
         return X[self.b0:self.b1]
 
     def launch(self, x_shard, Wt, Y, scale=None, stream=None):
-        """This rank's images into its block of Y."""
+        """This rank's images into its block of Y (and, fused, every rank's)."""
         n = self.b1 - self.b0
+        if self.fused:
+            self._bind(Y)
+            ws = self.ws
+            abi.check(abi.lib().uk_cuda_conv2d_f32_allgather(
+                x_shard.data_ptr(), Wt.data_ptr(), self._ylist, self.world, n, self.H, self.W, self.C, self.Kh,
+                self.Kw, self.Oc, self.pad, None if scale is None else scale.data_ptr(), ws.data_ptr(),
+                ws.numel() * ws.element_size(), abi._stream(stream)))
+            return
         if n:
             abi.conv2d_tc(x_shard, Wt, Y[self.b0:self.b1], n, self.H, self.W, self.C, self.Kh, self.Kw, self.Oc,
                           self.pad, scale, abi.UK_CONV_NCHW, self.ws, stream)
 
-    def gather(self, Y):
+    def gather(self, Y, stream=None):
         """Every rank's block into every rank's Y."""
         import torch
         import torch.distributed as dist
         if self.world == 1:
+            return
+        if self.fused:  # the blocks were stored by the conv itself: order the ranks
+            self.sync(stream)
             return
         def gather_into(out, mine):
             # NCCL gathers in place (the input is this rank's slot of the
@@ -409,7 +490,14 @@ class ConvBatchShard:
 
     def run(self, x_shard, Wt, Y, scale=None, stream=None):
         self.launch(x_shard, Wt, Y, scale, stream)
-        self.gather(Y)
+        self.gather(Y, stream)
+
+    def close(self):
+        if self.sync is not None:
+            self.sync.close()
+        if self._peers is not None:
+            self._peers.close()
+            self._peers = None
 
 
 class DecodeColumnShard:
@@ -433,9 +521,9 @@ class DecodeColumnShard:
         self.y_list = (C.c_void_p * self.world)(*[self.peers.ptrs[r] for r in order])
         self.ldy = Y_full.stride(0)
         self.ws = abi.decode_workspace(B, K)
-        import torch
-        self.flag = torch.zeros(1, device="cuda")
-        self.launches_per_step = 2  # the norm kernel and the GEMM
+        self.sync = DeviceBarrier(group)
+        # the norm kernel and the GEMM, and the device barrier
+        self.launches_per_step = 3 if self.sync.kind == "device" else 2
 
     def describe(self):
         return "weight columns sharded over %d GPUs (%d each), all-gather fused into the store" % (
@@ -450,13 +538,13 @@ class DecodeColumnShard:
             self.ldy, self.B, self.n1 - self.n0, self.K, self.n0, self.ws.data_ptr(),
             self.ws.numel() * self.ws.element_size(), abi._stream(stream)))
 
-    def barrier(self):
-        import torch.distributed as dist
-        dist.all_reduce(self.flag, group=self.group)
+    def barrier(self, stream=None):
+        self.sync(stream)
 
     def run(self, X, gamma, W_shard, eps=1e-5, stream=None):
         self.launch(X, gamma, W_shard, eps, stream)
-        self.barrier()
+        self.barrier(stream)
 
     def close(self):
+        self.sync.close()
         self.peers.close()
