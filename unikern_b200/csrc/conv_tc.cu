@@ -896,6 +896,35 @@ __global__ void k_split_weights(const float* __restrict__ Wt, float* __restrict_
   }
 }
 
+// NCHW weights [Oc][C][Kh][Kw] -> [Oc][kh][kw][c], one CTA per output channel:
+// its C * taps weights staged in shared memory (as fp32, exact for halves) by
+// contiguous loads, then written in the new order by contiguous stores.  F16:
+// binary16 in and out (O0); else fp32 in, tf32 (hi, lo) pairs out (O0, O1).
+// Needs C * taps * 4 <= kPermuteSmem.
+constexpr int kPermuteSmem = 48 * 1024;
+template <bool F16>
+__global__ void __launch_bounds__(256) k_permute_w(const void* __restrict__ Wt, void* __restrict__ O0,
+                                                   void* __restrict__ O1, int C, int taps) {
+  extern __shared__ float wst[];
+  const int K = C * taps;
+  const int64_t base = (int64_t)blockIdx.x * K;
+  for (int i = threadIdx.x; i < K; i += blockDim.x)
+    wst[i] = F16 ? __half2float(__ldg((const __half*)Wt + base + i)) : __ldg((const float*)Wt + base + i);
+  __syncthreads();
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    const int tap = i / C, c = i - tap * C;
+    const float v = wst[c * taps + tap];
+    if constexpr (F16) {
+      ((__half*)O0)[base + i] = __float2half_rn(v);  // exact: v came from a half
+    } else {
+      float hi, lo;
+      split(v, hi, lo);
+      ((float*)O0)[base + i] = hi;
+      ((float*)O1)[base + i] = lo;
+    }
+  }
+}
+
 // B[K][N] -> Bt[N][K] as (hi, lo) pairs, 32 x 32 tiles through shared memory
 // (K % 32 == 0 and N % 32 == 0: every tile is whole)
 __global__ void __launch_bounds__(256) k_split_transpose(const float* __restrict__ B, float* __restrict__ Th,
@@ -1179,7 +1208,9 @@ int conv2d_f32_tc(const float* X, const float* Wt, float* Y, float* const* ycopi
     k_split_flat<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 16), 256, 0, st>>>(X, Xh,
                                                                                                             Xl, n);
   }
-  {
+  if (layout == UK_CONV_NCHW && (int64_t)C * Kh * Kw * 4 <= kPermuteSmem) {
+    k_permute_w<false><<<(unsigned)Oc, 256, (size_t)C * Kh * Kw * 4, st>>>(Wt, Wh, Wl, C, Kh * Kw);
+  } else {
     const int64_t n = (int64_t)Oc * Kh * Kw * C;
     k_split_weights<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)uk::sm_count() * 8), 256, 0, st>>>(
         Wt, Wh, Wl, Oc, C, Kh, Kw, layout == UK_CONV_NCHW ? 1 : 0);
@@ -1459,8 +1490,11 @@ extern "C" int uk_cuda_conv2d_f16(const uint16_t* X, const uint16_t* Wt, uint16_
       k_row_nhwc_h<<<(unsigned)((int64_t)N * H), ROW_THREADS, plane, st>>>((const __half*)X, (__half*)Xt, C, H, W);
     }
     const int64_t nw = (int64_t)Oc * Kh * Kw * C;
-    k_permute_weights_h<<<(unsigned)std::min<int64_t>((nw + 255) / 256, (int64_t)uk::sm_count() * 8), 256, 0, st>>>(
-        (const __half*)Wt, (__half*)Wp, Oc, C, Kh, Kw);
+    if ((int64_t)C * Kh * Kw * 4 <= kPermuteSmem)
+      k_permute_w<true><<<(unsigned)Oc, 256, (size_t)C * Kh * Kw * 4, st>>>(Wt, Wp, nullptr, C, Kh * Kw);
+    else
+      k_permute_weights_h<<<(unsigned)std::min<int64_t>((nw + 255) / 256, (int64_t)uk::sm_count() * 8), 256, 0,
+                            st>>>((const __half*)Wt, (__half*)Wp, Oc, C, Kh, Kw);
     if (int rc = uk::check_launch("conv2d_f16(pre-pass)")) return rc;
     Xn = Xt;
     Wk = Wp;
