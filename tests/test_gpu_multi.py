@@ -2,9 +2,9 @@
 N-sharded f16 GEMM with the all-gather fused into its epilogue, the
 batch-sharded conv (NCCL all-gather of Y, or the gather fused into the conv's
 store) and the weight-column-sharded decode.  Each runs with the ranks
-ordered by a one-float NCCL all-reduce (the default) and by the device-side
-flag barrier with the fused conv gather (UK_BARRIER=device,
-UK_CONV_GATHER=fused).  Each worker compares every rank's full output with a
+ordered by the device-side flag barrier with the fused conv gather (the
+default) and by a one-float NCCL all-reduce with the NCCL all-gather of the
+conv (UK_BARRIER=nccl, UK_CONV_GATHER=nccl).  Each worker compares every rank's full output with a
 single-GPU run of the same inputs and with the f64 oracle."""
 import os
 import subprocess
@@ -16,7 +16,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-MODES = {"nccl": {}, "device": {"UK_BARRIER": "device", "UK_CONV_GATHER": "fused"}}
+MODES = {"device": {}, "nccl": {"UK_BARRIER": "nccl", "UK_CONV_GATHER": "nccl"}}
 
 
 def _torchrun(worker, port, mode="nccl"):

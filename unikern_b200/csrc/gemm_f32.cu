@@ -365,16 +365,18 @@ __global__ void k_zero2d(T* C, int M, int N, int64_t ldc) {
     st1(C + (i / N) * ldc + i % N, 0.f);
 }
 
-// the 32 x 64 tile with K split over a KS-CTA cluster (grid z)
+// a BM x BN tile (TM x TN per thread) with K split over a KS-CTA cluster
+// (grid z): the 32 x 64 tile with 4 x 4 per thread, and the 64 x 64 tile with
+// 8 x 8 per thread (twice the FFMAs per shared-memory load, 64 threads)
 #ifndef UK_SGEMM_SPLIT_BK
 #define UK_SGEMM_SPLIT_BK 16
 #endif
-template <int KS, typename T>
+template <int BM, int BN, int TM, int TN, int KS, typename T>
 void launch_split(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
                   cudaStream_t st) {
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)((N + 63) / 64), (unsigned)((M + 31) / 32), KS);
-  cfg.blockDim = dim3(128, 1, 1);
+  cfg.gridDim = dim3((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), KS);
+  cfg.blockDim = dim3((BM / TM) * (BN / TN), 1, 1);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -384,8 +386,8 @@ void launch_split(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   constexpr int BK = UK_SGEMM_SPLIT_BK;
-  if (vec) cudaLaunchKernelEx(&cfg, k_sgemm<32, 64, BK, 4, 4, true, T, KS>, A, B, C, M, N, K, lda, ldb, ldc);
-  else cudaLaunchKernelEx(&cfg, k_sgemm<32, 64, BK, 4, 4, false, T, KS>, A, B, C, M, N, K, lda, ldb, ldc);
+  if (vec) cudaLaunchKernelEx(&cfg, k_sgemm<BM, BN, BK, TM, TN, true, T, KS>, A, B, C, M, N, K, lda, ldb, ldc);
+  else cudaLaunchKernelEx(&cfg, k_sgemm<BM, BN, BK, TM, TN, false, T, KS>, A, B, C, M, N, K, lda, ldb, ldc);
 }
 
 // the 32 x 64 tile with K split over KG warp groups of one CTA
@@ -414,7 +416,8 @@ int launch_groups(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda
 
 // A pinned FFMA plan from UK_SGEMM_PLAN="bm,bn,ks[,kg]" (a measurement knob,
 // like the reference's UK_CONV_TILE): one of the compiled variants 128,128,1 /
-// 64,64,1 / 32,64,{1,2,4,8} (K split over a cluster of ks CTAs) /
+// 64,64,1 / 32,64,{1,2,4,8} (K split over a cluster of ks CTAs) / 64,64,{4,8}
+// (8 x 8 per thread, K split over a cluster) /
 // 32,64,1,{2,4,8} (K split over kg warp groups of one CTA).  Returns 0 with
 // *c set, 1 when unset, 2 when the value names no compiled variant (the call
 // is then refused).
@@ -429,10 +432,11 @@ int pinned_plan(uk::Candidate* c) {
     *c = uk::Candidate{uk::kFamSgemmGroups, uk::Tile{32, 64, 16, 2}, kg, 0.0};
     return 0;
   }
-  const bool ok = kg == 1 && ((bm == 128 && bn == 128 && ks == 1) || (bm == 64 && bn == 64 && ks == 1) ||
+  const bool ok = kg == 1 && ((bm == 128 && bn == 128 && ks == 1) ||
+                              (bm == 64 && bn == 64 && (ks == 1 || ks == 4 || ks == 8)) ||
                               (bm == 32 && bn == 64 && (ks == 1 || ks == 2 || ks == 4 || ks == 8)));
   if (!ok) return 2;
-  *c = uk::Candidate{uk::kFamSgemm, uk::Tile{bm, bn, bm == 32 ? 16 : 8, 2}, ks, 0.0};
+  *c = uk::Candidate{uk::kFamSgemm, uk::Tile{bm, bn, (bm == 32 || ks > 1) ? 16 : 8, 2}, ks, 0.0};
   return 0;
 }
 
@@ -445,8 +449,8 @@ int simt_gemm(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, in
   const int pin = pinned_plan(&c);
   if (pin == 2)
     return uk::fail(UK_EINVAL,
-                    "gemm: UK_SGEMM_PLAN=%s names no compiled FFMA plan (128,128,1 64,64,1 32,64,{1,2,4,8} "
-                    "32,64,1,{2,4,8})",
+                    "gemm: UK_SGEMM_PLAN=%s names no compiled FFMA plan (128,128,1 64,64,{1,4,8} "
+                    "32,64,{1,2,4,8} 32,64,1,{2,4,8})",
                     getenv("UK_SGEMM_PLAN"));
   if (pin == 0 && c.ksplit > 1 && K / c.ksplit < 16)
     return uk::fail(UK_EINVAL, "gemm: UK_SGEMM_PLAN k split %d leaves less than 16 of K=%d per CTA", c.ksplit, K);
@@ -458,14 +462,18 @@ int simt_gemm(const T* A, const T* B, T* C, int M, int N, int K, int64_t lda, in
   }
   if (c.tile.bm == 128) {
     launch<128, 128, 8, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  } else if (c.tile.bm == 64 && c.ksplit == 8) {
+    launch_split<64, 64, 8, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+  } else if (c.tile.bm == 64 && c.ksplit == 4) {
+    launch_split<64, 64, 8, 8, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   } else if (c.tile.bm == 64) {
     launch<64, 64, 8, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   } else if (c.ksplit == 8) {
-    launch_split<8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    launch_split<32, 64, 4, 4, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   } else if (c.ksplit == 4) {
-    launch_split<4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    launch_split<32, 64, 4, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   } else if (c.ksplit == 2) {
-    launch_split<2>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
+    launch_split<32, 64, 4, 4, 2>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   } else {
     launch<32, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, st);
   }

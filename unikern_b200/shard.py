@@ -172,8 +172,8 @@ class DeviceBarrier:
     (uk_cuda_peer_barrier): each rank's flag array (one unsigned per rank) is
     opened by every peer once; a step posts an ever-growing epoch into every
     rank's array and waits, bounded by timeout_s, for every rank's post in its
-    own.  UK_BARRIER=device selects it in place of the default one-float NCCL
-    all-reduce (about 25 us on 8 GPUs) after the sharded kernels.  A wait that
+    own.  It replaces a one-float NCCL all-reduce (about 25 us on 8 GPUs) after
+    the sharded kernels; UK_BARRIER=nccl keeps the all-reduce.  A wait that
     runs out sets bit 32 of uk_cuda_pipeline_fault."""
 
     def __init__(self, group=None, timeout_s: float = 2.0):
@@ -182,7 +182,7 @@ class DeviceBarrier:
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.kind = "device" if os.environ.get("UK_BARRIER", "nccl") == "device" else "nccl"
+        self.kind = "nccl" if os.environ.get("UK_BARRIER", "device") == "nccl" else "device"
         self.timeout_ns = int(timeout_s * 1e9)
         self.epoch = 0
         self.flag = torch.zeros(1, device="cuda")
@@ -392,13 +392,13 @@ class ConvBatchShard:
     `world` GPUs: the batch is split into contiguous image blocks, weights and
     scale are replicated, and the output is all-gathered so every rank holds
     the full Y[N][Oc][Ho][Wo].  Images are independent, so the only exchange is
-    the gather: by default an NCCL all-gather after the conv (in place into Y
-    when the blocks are equal, through a padded staging buffer otherwise).
-    With UK_CONV_GATHER=fused, on the tensor-core path, it is fused into the
-    conv's store instead: each rank's kernel writes its image block into every
-    rank's Y (CUDA IPC mappings over NVLink, opened on the first run) and a
-    barrier (UK_BARRIER) orders the ranks, so the exchange overlaps the compute
-    tile by tile."""
+    the gather.  On the tensor-core path it is fused into the conv's store:
+    each rank's kernel writes its image block into every rank's Y (CUDA IPC
+    mappings over NVLink, opened on the first run) and a barrier (UK_BARRIER)
+    orders the ranks, so the exchange overlaps the compute tile by tile.
+    Otherwise (and with UK_CONV_GATHER=nccl) an NCCL all-gather after the conv:
+    in place into Y when the blocks are equal, through a padded staging buffer
+    otherwise."""
 
     def __init__(self, N, Cc, H, W, Oc, Kh, Kw, pad, group=None):
         import torch.distributed as dist
@@ -415,7 +415,7 @@ class ConvBatchShard:
         # the shape runs the FFMA kernel)
         self.ws = abi.conv2d_workspace(max(1, self.b1 - self.b0), H, W, Cc, Kh, Kw, Oc, pad, abi.UK_CONV_NCHW) \
             if self.b1 > self.b0 else None
-        self.fused = self.world > 1 and self.ws is not None and os.environ.get("UK_CONV_GATHER", "nccl") == "fused"
+        self.fused = self.world > 1 and self.ws is not None and os.environ.get("UK_CONV_GATHER", "fused") != "nccl"
         self._peers = None
         self._ylist = None
         self.sync = DeviceBarrier(group) if self.fused else None
