@@ -19,11 +19,16 @@ B200_HCS = (abi.SAMPLES / "hcs_nvidia_b200.json").read_text()
     # pair grid needs 3 on 74 pairs
     (640, 15104, 4096, True, "tcgen05-1sm", (128, 256), 1),
     (640, 16384, 4096, True, "tcgen05-2sm", (256, 256), 1),   # 64 column tiles: 3 waves either way
-    (512, 512, 512, False, "ffma", (32, 64), 4),              # 128 tiles on 148 SMs: K split over 4-CTA clusters
+    # 512^3: 64 tiles of 64 x 64, 8 x 8 per thread, K split over 4-CTA clusters
+    # (16.7 us against 18.4 for 32 x 64 tiles split 4 ways, L2 flushed)
+    (512, 512, 512, False, "ffma", (64, 64), 4),
     (256, 256, 256, False, "ffma", (32, 64), 4),
     (2048, 2048, 2048, False, "tcgen05-2sm-3xtf32", (256, 256), 1),
     (4096, 4096, 4096, False, "tcgen05-2sm-3xtf32", (256, 256), 1),
     (4096, 4096, 4090, False, "ffma", (128, 128), 1),         # K % 32: no split-tf32 candidate
+    # mid sizes: the 64 x 64 tile with 8 x 8 per thread and K split over 4
+    # CTAs (measured 114 against 147 us for the 32 x 64 split, L2 flushed)
+    (1000, 3000, 700, False, "ffma", (64, 64), 4),
 ])
 def test_argmin_changes_with_shape(M, N, K, f16, family, tile, ks):
     p = abi.solve_plan(M, N, K, f16, sms=148)
@@ -34,17 +39,22 @@ def test_argmin_changes_with_shape(M, N, K, f16, family, tile, ks):
 
 def test_without_the_tensor_cores_fp32_stays_on_ffma():
     p = abi.solve_plan(4096, 4096, 4096, False, sms=148, allow_tc=False)
-    assert p["family"] == "ffma" and p["tile"] == (128, 128) and p["feasible"] == 6
-    assert abi.solve_plan(4096, 4096, 4096, False, sms=148)["feasible"] == 7
+    assert p["family"] == "ffma" and p["tile"] == (128, 128) and p["feasible"] == 8
+    assert abi.solve_plan(4096, 4096, 4096, False, sms=148)["feasible"] == 9
+    # without them, 2048^3 takes the 8 x 8 split tiles (measured 399 against
+    # 462 us for 128 x 128, whose 256 tiles are 1.7 waves on 148 SMs)
+    p = abi.solve_plan(2048, 2048, 2048, False, sms=148, allow_tc=False)
+    assert p["tile"] == (64, 64) and p["k_split"] == 4
 
 
 def test_smaller_parts_shift_the_choice():
-    # on 148 SMs the 128 tiles of 32 x 64 leave SMs idle and K is split over
-    # 4-CTA clusters; on a 16-SM part the same tiles give every SM eight CTAs,
-    # and a split only adds its fold
-    assert abi.solve_plan(512, 512, 512, False, sms=148)["k_split"] == 4
-    p = abi.solve_plan(512, 512, 512, False, sms=16)
-    assert p["tile"] == (32, 64) and p["k_split"] == 1
+    # 256^3 on 148 SMs: the 64 CTAs of the 8 x 8 split leave most SMs idle
+    # and the 32 x 64 tiles split 4 ways win; on a 16-SM part every SM is
+    # busy either way and the 8 x 8 micro-tiles' higher FFMA rate wins
+    p = abi.solve_plan(256, 256, 256, False, sms=148)
+    assert p["tile"] == (32, 64) and p["k_split"] == 4
+    p = abi.solve_plan(256, 256, 256, False, sms=16)
+    assert p["tile"] == (64, 64) and p["k_split"] == 4
 
 
 def test_deterministic_and_costed():
@@ -59,4 +69,4 @@ def test_solve_transcript_carries_the_grid():
     rc, out = abi.solve_kml(B200_HCS, '{"op":"gemm","dtype":"fp16","dims":[640,15104,4096]}', None)
     assert rc == 0 and "tile=128x256" in out and "|X|=2" in out and "kernel=tcgen05-1sm" in out, out
     rc, out = abi.solve_kml(B200_HCS, '{"op":"gemm","dtype":"fp32","dims":[512,512,512]}', None)
-    assert rc == 0 and "|X|=6" in out and "kernel=ffma k_split=4" in out, out
+    assert rc == 0 and "|X|=8" in out and "kernel=ffma k_split=4" in out, out

@@ -158,31 +158,43 @@ inline double waves_us(int64_t units, int64_t slots, double flops, double rate, 
 }
 
 // FFMA tile shapes the sgemm kernel is compiled for: {bm, bn, bk, threads}
-// with the measured fraction of the FFMA peak one SM reaches with it
+// with the measured fraction of the FFMA peak one SM reaches with it, and the
+// K splits (over a cluster) compiled for it as a bit mask of ks in {1,2,4,8}.
+// The 64 x 64 tile comes twice: 4 x 4 per thread (256 threads, whole K) and
+// 8 x 8 per thread (64 threads, twice the FFMAs per shared-memory load, K
+// split 4 or 8 ways); its 0.58 is fitted to one B200's times of every plan at
+// 256^3 .. 2048^3 and 1000 x 3000 x 700 with the L2 flushed before each run.
 struct SgemmShape {
   int bm, bn, bk, threads;
   double eff;
+  unsigned splits;  // bit (log2 ks) set when that split is compiled
 };
-constexpr SgemmShape kSgemmShapes[] = {{128, 128, 8, 256, 0.60}, {64, 64, 8, 256, 0.42}, {32, 64, 16, 128, 0.45}};
+constexpr SgemmShape kSgemmShapes[] = {{128, 128, 8, 256, 0.60, 0x1},
+                                       {64, 64, 8, 256, 0.42, 0x1},
+                                       {64, 64, 16, 64, 0.58, 0x4 | 0x8},
+                                       {32, 64, 16, 128, 0.45, 0x1 | 0x2 | 0x4 | 0x8}};
 
 }  // namespace detail
 
-// f32 / CUDA-core GEMM on the FFMA pipes: every compiled tile, and K splits
-// of the smallest tile over a cluster of up to 8 CTAs (each keeping >= 64 of K)
+// f32 / CUDA-core GEMM on the FFMA pipes: every compiled tile with each K
+// split compiled for it (a cluster of up to 8 CTAs, each keeping >= 64 of K)
 inline void sgemm_candidates(int64_t M, int64_t N, int64_t K, int64_t sms, const CostModel& cm,
                              Candidate* out, int* n) {
   const double sm_rate = cm.ffma_tflops_sm * 1e12;
   for (const auto& s : detail::kSgemmShapes) {
     const int64_t tiles = detail::cdiv(M, s.bm) * detail::cdiv(N, s.bn);
-    for (int ks = 1; ks <= 8; ks *= 2) {
-      if (ks > 1 && (s.bm != 32 || K / ks < 64)) continue;  // splits: the 32 x 64 tile only
+    for (int ks = 1, lg = 0; ks <= 8; ks *= 2, ++lg) {
+      if (!(s.splits & (1u << lg)) || (ks > 1 && K / ks < 64)) continue;
       const int64_t ctas = tiles * ks;
       // resident CTAs per SM: 2048 threads, at most 16 CTAs; a wave is one
-      // round of resident CTAs, and too few warps per SM cost latency hiding
+      // round of resident CTAs, and too few warps per SM cost latency hiding:
+      // 16 warps for a 4 x 4 micro-tile, fewer in proportion for larger ones
+      // (an 8 x 8 micro-tile has four times the independent FFMAs per load)
       const int64_t per_sm = 2048 / s.threads < 16 ? 2048 / s.threads : 16;
       const int64_t load = detail::cdiv(ctas, sms);  // CTAs the busiest SM runs
       const int64_t warps = (load < per_sm ? load : per_sm) * s.threads / 32;
-      const double hide = warps >= 16 ? 1.0 : std::sqrt((double)warps / 16.0);
+      const double need = 16.0 * 16.0 / ((double)s.bm * s.bn / s.threads);
+      const double hide = warps >= need ? 1.0 : std::sqrt((double)warps / need);
       const double flops_sm = (double)load * 2.0 * s.bm * s.bn * (double)K / ks;
       double us = flops_sm / (sm_rate * s.eff * hide) * 1e6 + 1.0 * detail::cdiv(load, per_sm);
       if (ks > 1) us += 0.6 * ks;  // the cluster barrier and distributed-shared-memory fold
