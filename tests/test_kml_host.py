@@ -120,7 +120,7 @@ def test_capability_gaps(kml, gap):
     ("gemm", (8192, 8192, 8192), True, (256, 256, 64, 6)),     # tcgen05 SM-pair tile
     ("gemm", (128, 4096, 4096), True, (128, 256, 64, 4)),      # one 128-row block: single-SM tile
     ("gemm", (8192, 8192, 8190), True, (128, 128, 8, 2)),      # K % 8: CUDA-core path
-    ("gemm", (512, 512, 512), False, (32, 64, 16, 2)),         # 128 CTAs of 32x64
+    ("gemm", (512, 512, 512), False, (64, 64, 16, 2)),         # 64 tiles of 64x64, 8x8 per thread, K split 4
     ("gemm", (4096, 4096, 4096), False, (256, 256, 32, 3)),    # split-tf32 on the conv pair kernel
     ("gemm", (4096, 4096, 4090), False, (128, 128, 8, 2)),     # K % 32: FFMA
     ("conv", (58, 58, 256, 3, 3, 256), False, (256, 256, 32, 3)),
