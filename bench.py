@@ -658,10 +658,16 @@ def measure_conv(ctx, steps, warmup, pk, N=32, Cc=256, H=56, W=56, Oc=256, pad=1
     rec = {"value": val, "unit": "TFLOP/s", "ms": ms, "path": "3xTF32 tcgen05 SM pairs",
            "roofline": roofline("tensor_3xtf32", val, pk)}
     if e2e:
-        ins = [(x, pinned(x)), (w, pinned(w)), (s, pinned(s))]
-        outs = [(y, torch.empty_like(y, device="cpu").pin_memory())]
-        ems, h2d, d2h = time_e2e(ctx, launch, ins, outs, max(3, min(steps, 10)))
-        rec["e2e"] = e2e_record(flops, "TFLOP/s", ems, h2d, d2h)
+        # uk_cuda_conv2d_f32_host: the weights, then blocks of images up, each
+        # block's conv, its Y down while later blocks upload
+        xh, wh, sh = pinned(x), pinned(w), pinned(s)
+        yh = torch.empty_like(y, device="cpu").pin_memory()
+        hws_n = abi.lib().uk_cuda_conv2d_f32_host_workspace_size(N, H, W, Cc, 3, 3, Oc, pad, 0)
+        hws = torch.empty(((hws_n + 15) // 16) * 4, device="cuda")
+        ems = ctx.time_steps(lambda: abi.conv2d_host(xh, wh, sh, yh, x, w, s, y, N, H, W, Cc, 3, 3, Oc, pad, 0, hws),
+                             max(3, min(steps, 10)), 3)
+        h2d = sum(t.numel() * t.element_size() for t in (xh, wh, sh))
+        rec["e2e"] = e2e_record(flops, "TFLOP/s", ems, h2d, yh.numel() * yh.element_size())
     if ffma:
         fl = lambda: abi.conv2d(x, w, y, N, H, W, Cc, 3, 3, Oc, pad, s, abi.UK_CONV_NCHW)  # noqa: E731
         fms = ctx.time_steps(fl, max(3, min(steps, 5)), 3)

@@ -233,6 +233,26 @@ int uk_cuda_rowop_host(int op, const float* hX, const float* hW, float* hY, floa
                        int64_t L, int64_t C, float eps, int chunks, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* The fp32 NCHW convolution (uk_cuda_conv2d_f32_ws) from and to page-locked
+ * host memory: hX [N][C][H][W], hW [Oc][C][Kh][Kw], hS [Oc] (or NULL, with dS
+ * NULL), hY [N][Oc][Ho][Wo], each with a device buffer of the same size (dX,
+ * dW, dS, dY).  Images are independent: the weights upload first, then the
+ * images in `chunks` blocks (0: 8); each block's convolution runs once it
+ * landed and its Y downloads while later blocks upload, so both directions
+ * of the host link run at once.  The workspace is that of one block's
+ * images: uk_cuda_conv2d_f32_host_workspace_size(N, ..., chunks) bytes (the
+ * split tail is used when it has room, as for the device call).
+ * Asynchronous on `stream`, complete (Y included) when `stream` is; shares
+ * the copy streams of uk_cuda_gemm_f16_host.  The reference measures its
+ * conv end to end (upload, run, download: measured_ms,
+ * src/codegen_hip.cpp:692-744); this overlaps those phases. */
+size_t uk_cuda_conv2d_f32_host_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc,
+                                              int pad, int chunks);
+int uk_cuda_conv2d_f32_host(const float* hX, const float* hW, const float* hS, float* hY, float* dX,
+                            float* dW, float* dS, float* dY, int N, int H, int W, int C, int Kh,
+                            int Kw, int Oc, int pad, int chunks, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* GEMM larger than the device (the reference's streamed scenario B,
  * src/codegen_hip.cpp:1143-1238): C = A * B from and to page-locked host
  * memory with only B resident (dB, K*N elements) and A, C passing through a

@@ -117,3 +117,46 @@ def test_conv_tc_missing_workspace_is_refused():
     rc = abi.lib().uk_cuda_conv2d_f32_ws(x.data_ptr(), w.data_ptr(), y.data_ptr(), 1, 8, 8, 32, 3, 3, 8, 1, None,
                                          abi.UK_CONV_NCHW, None, 0, None)
     assert rc == 2 and "workspace" in abi.lib().uk_cuda_last_error().decode()
+
+
+# ---- the conv from and to host memory (uk_cuda_conv2d_f32_host) ----------------------
+
+@pytest.mark.parametrize("N,Cc,H,W,Oc,K,pad,chunks,scaled", [
+    (7, 64, 13, 20, 48, 3, 1, 3, True),     # ragged last block (3 + 3 + 1 images)
+    (4, 32, 9, 9, 16, 1, 0, 0, False),       # default 8 chunks: one image per block, no scale
+    (5, 40, 8, 8, 24, 3, 1, 2, True),        # C % 32 != 0: each block runs the FFMA kernel
+])
+def test_conv_host_equals_the_device_op(N, Cc, H, W, Oc, K, pad, chunks, scaled):
+    """Blocks of images through the host pipeline match the same convolution
+    run on the whole batch on the device, and the f64 oracle."""
+    import torch
+    rng = np.random.default_rng(N * 31 + Cc + H)
+    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / (K * K * Cc)), (Oc, Cc, K, K)).astype(np.float32)
+    s = rng.uniform(0.5, 1.5, Oc).astype(np.float32) if scaled else None
+    Ho, Wo = H + 2 * pad - K + 1, W + 2 * pad - K + 1
+    pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
+    xh, wh = pin(x), pin(w)
+    sh = pin(s) if scaled else None
+    yh = torch.full((N, Oc, Ho, Wo), float("nan")).pin_memory()
+    xd, wd = empty(x.shape), empty(w.shape)
+    sd = empty((Oc,)) if scaled else None
+    yd = empty((N, Oc, Ho, Wo))
+    abi.conv2d_host(xh, wh, sh, yh, xd, wd, sd, yd, N, H, W, Cc, K, K, Oc, pad, chunks)
+    torch.cuda.synchronize()
+    got = yh.numpy()
+    ref = O.conv_nchw(x, w, s, pad)
+    assert O.rel_err(got, ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+    whole = run_nchw(x, w, s, pad)
+    assert O.rel_err(got, whole.astype(np.float64), SUM_TAU * O.rms(ref)) <= F32_TOL
+    assert abi.lib().uk_cuda_pipeline_fault() == 0
+
+
+def test_conv_host_refuses_a_half_given_scale():
+    import torch
+    x, w, y = empty((1, 32, 4, 4)), empty((8, 32, 1, 1)), empty((1, 8, 4, 4))
+    xh, wh = torch.zeros((1, 32, 4, 4)).pin_memory(), torch.zeros((8, 32, 1, 1)).pin_memory()
+    yh = torch.zeros((1, 8, 4, 4)).pin_memory()
+    sh = torch.ones(8).pin_memory()
+    with pytest.raises(abi.UkError):
+        abi.conv2d_host(xh, wh, sh, yh, x, w, None, y, 1, 4, 4, 32, 1, 1, 8, 0, 1)

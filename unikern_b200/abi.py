@@ -55,6 +55,8 @@ PROTOTYPES = {
                                                vp, sz, vp]),
     "uk_cuda_gemm_f16_host": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "uk_cuda_rowop_host": (i32, [i32, vp, vp, vp, vp, vp, vp, i64, i64, f32, i32, vp, sz, vp]),
+    "uk_cuda_conv2d_f32_host_workspace_size": (sz, [i32] * 9),
+    "uk_cuda_conv2d_f32_host": (i32, [vp, vp, vp, vp, vp, vp, vp, vp] + [i32] * 9 + [vp, sz, vp]),
     "uk_cuda_softmax_f16": (i32, [vp, vp, i64, i64, vp]),
     "uk_cuda_rmsnorm_f16": (i32, [vp, vp, vp, i64, i64, f32, vp]),
     "uk_cuda_channelscale_f16": (i32, [vp, vp, vp, i64, i64, vp]),
@@ -248,6 +250,20 @@ def gemm_f16_host(Ah, Bh, Ch, Ad, Bd, Cd, chunks=0, stream=None):
     N = Bh.shape[1]
     check(lib().uk_cuda_gemm_f16_host(_p(Ah), _p(Bh), _p(Ch), _p(Ad), _p(Bd), _p(Cd), M, N, K, chunks,
                                       _stream(stream)))
+
+
+def conv2d_host(Xh, Wh, Sh, Yh, Xd, Wd, Sd, Yd, N, H, W, Cc, Kh, Kw, Oc, pad=0, chunks=0, workspace=None,
+                stream=None):
+    """The fp32 NCHW conv from and to pinned host tensors through device
+    buffers, image blocks pipelined (uploads, convs and downloads overlap).
+    Allocates the workspace through torch when none is passed."""
+    import torch
+    if workspace is None:
+        n = lib().uk_cuda_conv2d_f32_host_workspace_size(N, H, W, Cc, Kh, Kw, Oc, pad, chunks)
+        workspace = torch.empty(((n + 15) // 16) * 4, dtype=torch.float32, device="cuda") if n else None
+    nbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(lib().uk_cuda_conv2d_f32_host(_p(Xh), _p(Wh), _p(Sh), _p(Yh), _p(Xd), _p(Wd), _p(Sd), _p(Yd), N, H, W,
+                                        Cc, Kh, Kw, Oc, pad, chunks, _p(workspace), nbytes, _stream(stream)))
 
 
 def rowop_host(op, Xh, Wh, Yh, Xd, Wd, Yd, eps=1e-5, chunks=0, workspace=None, stream=None):

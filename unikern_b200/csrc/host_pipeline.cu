@@ -209,6 +209,88 @@ extern "C" int uk_cuda_rowop_host(int op, const float* hX, const float* hW, floa
   return UK_OK;
 }
 
+// ---- fp32 conv from and to host memory ------------------------------------------
+// Images are independent: the copy-in stream uploads the weights (and the
+// scale), then the blocks of images of X; the caller's stream runs the
+// convolution (uk_cuda_conv2d_f32_ws, NCHW) on each block once it landed; the
+// copy-out stream brings each block of Y home while later blocks upload, so
+// both directions of the host link run at once.
+extern "C" size_t uk_cuda_conv2d_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad,
+                                                int layout);
+extern "C" int uk_cuda_conv2d_f32_ws(const float* X, const float* Wt, float* Y, int N, int H, int W, int C, int Kh,
+                                     int Kw, int Oc, int pad, const float* scale, int layout, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
+extern "C" size_t uk_cuda_conv2d_f32_host_workspace_size(int N, int H, int W, int C, int Kh, int Kw, int Oc, int pad,
+                                                         int chunks) {
+  if (N <= 0 || chunks < 0 || chunks > MAX_CHUNKS) return 0;
+  if (chunks == 0) chunks = 8;
+  const int per = (N + chunks - 1) / chunks;
+  return uk_cuda_conv2d_workspace_size(per, H, W, C, Kh, Kw, Oc, pad, UK_CONV_NCHW);
+}
+
+extern "C" int uk_cuda_conv2d_f32_host(const float* hX, const float* hW, const float* hS, float* hY, float* dX,
+                                       float* dW, float* dS, float* dY, int N, int H, int W, int C, int Kh, int Kw,
+                                       int Oc, int pad, int chunks, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  if (N < 0 || H <= 0 || W <= 0 || C <= 0 || Kh <= 0 || Kw <= 0 || Oc <= 0 || pad < 0)
+    return uk::fail(UK_EINVAL, "conv2d_host: invalid dims N=%d H=%d W=%d C=%d Kh=%d Kw=%d Oc=%d pad=%d", N, H, W, C,
+                    Kh, Kw, Oc, pad);
+  if (chunks < 0 || chunks > MAX_CHUNKS) return uk::fail(UK_EINVAL, "conv2d_host: chunks %d (0..%d)", chunks, MAX_CHUNKS);
+  const int Ho = H + 2 * pad - Kh + 1, Wo = W + 2 * pad - Kw + 1;
+  if (Ho <= 0 || Wo <= 0) return uk::fail(UK_EINVAL, "conv2d_host: the filter is larger than the padded input");
+  if (N == 0) return UK_OK;
+  if ((hS == nullptr) != (dS == nullptr))
+    return uk::fail(UK_EINVAL, "conv2d_host: the scale needs both its host (hS) and device (dS) buffer, or neither");
+  if (int rc = check_host(hX, "hX")) return rc;
+  if (int rc = check_host(hW, "hW")) return rc;
+  if (int rc = check_host(hY, "hY")) return rc;
+  if (hS)
+    if (int rc = check_host(hS, "hS")) return rc;
+  if (int rc = uk::check_device_ptr(dX, "dX")) return rc;
+  if (int rc = uk::check_device_ptr(dW, "dW")) return rc;
+  if (int rc = uk::check_device_ptr(dY, "dY")) return rc;
+  if (dS)
+    if (int rc = uk::check_device_ptr(dS, "dS")) return rc;
+  DevPipe* p = nullptr;
+  if (int rc = get_pipe(&p)) return rc;
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (chunks == 0) chunks = 8;
+  const int per = (N + chunks - 1) / chunks;
+  const int nblk = (N + per - 1) / per;
+  const size_t ximg = (size_t)C * H * W, yimg = (size_t)Oc * Ho * Wo;
+  if (cudaEventRecord(p->start, st) != cudaSuccess || cudaStreamWaitEvent(p->in, p->start, 0) != cudaSuccess ||
+      cudaStreamWaitEvent(p->out, p->start, 0) != cudaSuccess)
+    return uk::check_launch("conv2d_host: ordering");
+  if (cudaMemcpyAsync(dW, hW, (size_t)Oc * C * Kh * Kw * 4, cudaMemcpyHostToDevice, p->in) != cudaSuccess ||
+      (hS && cudaMemcpyAsync(dS, hS, (size_t)Oc * 4, cudaMemcpyHostToDevice, p->in) != cudaSuccess) ||
+      cudaEventRecord(p->b_ready, p->in) != cudaSuccess)
+    return uk::check_launch("conv2d_host: upload weights");
+  for (int i = 0; i < nblk; ++i) {
+    const int n0 = i * per, nb = n0 + per < N ? per : N - n0;
+    if (cudaMemcpyAsync(dX + n0 * ximg, hX + n0 * ximg, (size_t)nb * ximg * 4, cudaMemcpyHostToDevice, p->in) !=
+            cudaSuccess ||
+        cudaEventRecord(p->a_ready[i], p->in) != cudaSuccess)
+      return uk::check_launch("conv2d_host: upload X");
+  }
+  for (int i = 0; i < nblk; ++i) {
+    const int n0 = i * per, nb = n0 + per < N ? per : N - n0;
+    if ((i == 0 && cudaStreamWaitEvent(st, p->b_ready, 0) != cudaSuccess) ||
+        cudaStreamWaitEvent(st, p->a_ready[i], 0) != cudaSuccess)
+      return uk::check_launch("conv2d_host: wait");
+    if (int rc = uk_cuda_conv2d_f32_ws(dX + n0 * ximg, dW, dY + n0 * yimg, nb, H, W, C, Kh, Kw, Oc, pad, dS,
+                                       UK_CONV_NCHW, workspace, workspace_bytes, stream))
+      return rc;
+    if (cudaEventRecord(p->c_ready[i], st) != cudaSuccess || cudaStreamWaitEvent(p->out, p->c_ready[i], 0) != cudaSuccess ||
+        cudaMemcpyAsync(hY + n0 * yimg, dY + n0 * yimg, (size_t)nb * yimg * 4, cudaMemcpyDeviceToHost, p->out) !=
+            cudaSuccess)
+      return uk::check_launch("conv2d_host: download Y");
+  }
+  if (cudaEventRecord(p->done, p->out) != cudaSuccess || cudaStreamWaitEvent(st, p->done, 0) != cudaSuccess)
+    return uk::check_launch("conv2d_host: join");
+  return UK_OK;
+}
+
 // ---- streamed GEMM (payload larger than the device) -------------------------
 // Only B is resident; A and C pass through a two-slot ring of row blocks in
 // the caller's device buffer.  Block i uses slot i % 2: its upload waits until
