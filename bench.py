@@ -735,7 +735,7 @@ def measure_decode(ctx, steps, warmup, pk, Bt=32, H=4096, F=14336, heads=32, S=8
     [B*32 x 8192] scores.  HBM-bound: the 112 MiB of weights dominate.
     e2e: the layer weight and gamma stay resident (model state); each step
     uploads the token rows and the scores and downloads the GEMM output and
-    the probabilities."""
+    the probabilities, the scores' blocks pipelined through the softmax."""
     import unikern_b200.abi as abi
     torch = ctx.torch
     x = gen(torch, (Bt, H), "normal", 13)
@@ -764,10 +764,21 @@ def measure_decode(ctx, steps, warmup, pk, Bt=32, H=4096, F=14336, heads=32, S=8
     val = nbytes / ms / 1e6
     rec = {"value": val, "unit": "GB/s", "ms": ms, "graph": True, "roofline": roofline("hbm", val, pk)}
     if e2e:
-        ins = [(x, pinned(x)), (sc, pinned(sc))]
-        outs = [(out, torch.empty_like(out, device="cpu").pin_memory()),
-                (pr, torch.empty_like(pr, device="cpu").pin_memory())]
-        ems, h2d, d2h = time_e2e(ctx, graph.replay, ins, outs, max(5, min(steps, 20)))
+        # through the C ABI: the scores' blocks go up, through the softmax and
+        # back down pipelined (uk_cuda_rowop_host), and the token rows up,
+        # through the norm + GEMM and the GEMM's output back down
+        xh, sch = pinned(x), pinned(sc)
+        outh = torch.empty_like(out, device="cpu").pin_memory()
+        prh = torch.empty_like(pr, device="cpu").pin_memory()
+
+        def e2e_step():
+            abi.rowop_host("softmax", sch, None, prh, sc, None, pr, 1e-5, 8)
+            x.copy_(xh, non_blocking=True)
+            abi.decode_rmsnorm_gemm(x, g, Wt, out, 1e-5, ws)
+            outh.copy_(out, non_blocking=True)
+        ems = ctx.time_steps(e2e_step, max(5, min(steps, 20)), 3)
+        h2d = sum(t.numel() * t.element_size() for t in (xh, sch))
+        d2h = sum(t.numel() * t.element_size() for t in (outh, prh))
         rec["e2e"] = e2e_record(nbytes, "GB/s", ems, h2d, d2h)
     del graph
     return rec
