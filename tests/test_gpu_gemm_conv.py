@@ -156,6 +156,25 @@ def test_conv_nchw_vs_f64(N, Cc, H, W, Oc, K, pad, scaled):
     assert O.rel_err(host(y), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
 
 
+@pytest.mark.parametrize("plan", ["128,128,8", "128,128,16", "64,64,8", "32,64,16"])
+def test_conv_every_ffma_tile_vs_f64(plan, monkeypatch):
+    """Each compiled FFMA conv tile pinned through UK_FFMA_CONV_PLAN, on a
+    shape with ragged pixel and channel tiles in both layouts' NCHW form."""
+    N, Cc, H, W, Oc, K, pad = 2, 24, 11, 13, 40, 3, 1
+    rng = np.random.default_rng(7)
+    x = rng.uniform(0, 1, (N, Cc, H, W)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / (K * K * Cc)), (Oc, Cc, K, K)).astype(np.float32)
+    s = rng.uniform(0.5, 1.5, Oc).astype(np.float32)
+    monkeypatch.setenv("UK_FFMA_CONV_PLAN", plan)
+    y = empty((N, Oc, H, W))
+    abi.conv2d(dev(x), dev(w), y, N, H, W, Cc, K, K, Oc, pad, dev(s), abi.UK_CONV_NCHW)
+    ref = O.conv_nchw(x, w, s, pad)
+    assert O.rel_err(host(y), ref, SUM_TAU * O.rms(ref)) <= F32_TOL
+    monkeypatch.setenv("UK_FFMA_CONV_PLAN", "16,16,4")
+    with pytest.raises(abi.UkError):
+        abi.conv2d(dev(x), dev(w), y, N, H, W, Cc, K, K, Oc, pad, dev(s), abi.UK_CONV_NCHW)
+
+
 # ---- the solver's choice reaches the launcher ----------------------------------
 
 @pytest.mark.parametrize("M,N,K,f16", [(640, 15104, 4096, True), (640, 16384, 4096, True), (512, 512, 512, False),

@@ -13,6 +13,9 @@
 //   KML :  k = (kh, kw, c); x index ((ho+kh)*W + (wo+kw))*C + c   (N = 1, valid)
 // Output pixel p = n*Ho*Wo + q is stored at (n*Oc + oc)*Ho*Wo + q, which is
 // NCHW for the batch form and [Oc][Ho][Wo] for the KML form.
+#include <cstdio>
+#include <cstdlib>
+
 #include "uk_common.cuh"
 #include "uk_plan.cuh"
 
@@ -189,10 +192,30 @@ void launch(const ConvArgs& a, cudaStream_t st) {
     k_conv<BM, BN, BK, TM, TN, LAYOUT, 0><<<grid, NT, 0, st>>>(a);
 }
 
+// UK_FFMA_CONV_PLAN="bm,bn,bk" pins one compiled tile of this kernel (a
+// measurement knob, like the reference's UK_CONV_TILE for its own tiles):
+// 128,128,8 / 128,128,16 / 64,64,8 / 32,64,16.  Returns false when unset;
+// *bad when the value names no compiled tile.
+bool pinned_conv_tile(uk::Tile* t, bool* bad) {
+  *bad = false;
+  const char* e = getenv("UK_FFMA_CONV_PLAN");
+  if (e == nullptr || e[0] == 0) return false;
+  int bm = 0, bn = 0, bk = 0;
+  if (sscanf(e, "%d,%d,%d", &bm, &bn, &bk) != 3 ||
+      !((bm == 128 && bn == 128 && (bk == 8 || bk == 16)) || (bm == 64 && bn == 64 && bk == 8) ||
+        (bm == 32 && bn == 64 && bk == 16))) {
+    *bad = true;
+    return false;
+  }
+  *t = uk::Tile{bm, bn, bk, 2};
+  return true;
+}
+
 template <int LAYOUT>
-void dispatch(const ConvArgs& a, cudaStream_t st) {
-  const uk::Tile t = uk::conv_tile(a.npix, a.Oc, uk::sm_count());
-  if (t.bm == 128)
+void dispatch(const ConvArgs& a, cudaStream_t st, const uk::Tile& t) {
+  if (t.bm == 128 && t.bk == 16)
+    launch<128, 128, 16, 8, 8, LAYOUT>(a, st);
+  else if (t.bm == 128)
     launch<128, 128, 8, 8, 8, LAYOUT>(a, st);
   else if (t.bm == 64)
     launch<64, 64, 8, 4, 4, LAYOUT>(a, st);
@@ -242,7 +265,13 @@ int uk::conv2d_ffma(const float* X, const float* Wt, float* Y, int N, int H, int
   // the weight loader uses 16-byte loads when K % 4 == 0: refuse a misaligned
   // base instead of faulting
   if (!uk::aligned16(Wt) && a.K % 4 == 0) return uk::fail(UK_EINVAL, "conv2d: Wt must be 16-byte aligned");
-  if (layout == UK_CONV_NCHW) dispatch<UK_CONV_NCHW>(a, st);
-  else dispatch<UK_CONV_KML>(a, st);
+  uk::Tile t = uk::conv_tile(a.npix, a.Oc, uk::sm_count());
+  bool bad = false;
+  pinned_conv_tile(&t, &bad);
+  if (bad)
+    return uk::fail(UK_EINVAL, "conv2d: UK_FFMA_CONV_PLAN=%s names no compiled tile (128,128,8 128,128,16 64,64,8 "
+                    "32,64,16)", getenv("UK_FFMA_CONV_PLAN"));
+  if (layout == UK_CONV_NCHW) dispatch<UK_CONV_NCHW>(a, st, t);
+  else dispatch<UK_CONV_KML>(a, st, t);
   return uk::check_launch("conv2d");
 }
