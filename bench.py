@@ -18,7 +18,10 @@ beside it) and the decode chain.  Each carries ``roofline``, ``e2e`` (the op
 through the C ABI with its inputs uploaded from and its outputs downloaded to
 pinned host memory inside the timed region, the reference's measured_ms,
 src/codegen_hip.cpp:692-744) and ``cpu_baseline`` (the reference's CPU code on
-this host's cores).  The fp16 widenings and channelscale print first.
+this host's cores).  The fp16 widenings and channelscale print first.  Just
+before the headline, one short `baseline_rows` line repeats every BASELINE
+row's value, unit, roofline fraction, e2e and CPU baseline, so that all of
+them sit with the headline in the last ~1.5 KB of the output.
 
 Timing: W untimed steps, then exactly K steps between CUDA events on the
 launching stream, barrier + synchronize on both sides, max over ranks.
@@ -962,6 +965,14 @@ def op_line(name, rec, cpu=None, **extra):
     return d
 
 
+def summarize(rows, line):
+    """Record an op line's headline figures in `rows` (for the compact
+    baseline_rows line) and return the line unchanged."""
+    rows[line["op"]] = [line["value"], line["unit"], line["roofline"].get("frac"),
+                        (line.get("e2e") or {}).get("value"), (line.get("cpu_baseline") or {}).get("value")]
+    return line
+
+
 NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (900 nominal)
 
 
@@ -1099,6 +1110,7 @@ def main():
         return run_single(args, ctx, pk)
     M, N, K = (int(v) for v in args.gemm_shape.split(","))
     want_cpu = not args.no_cpu
+    rows = {}  # the BASELINE rows' headline figures (one GPU)
 
     if rank == 0:
         emit({"peaks": {"hbm": [pk.get("hbm_gbs"), "GB/s", pk["source"] + " copy"],
@@ -1130,14 +1142,14 @@ def main():
 
         # the BASELINE rows, compact, last before the headline
         r = measure_gemm_f32(one, s, 3, pk)
-        emit(op_line("gemm_f32_512", r, cpu_gemm_f32() if want_cpu else None))
+        emit(summarize(rows, op_line("gemm_f32_512", r, cpu_gemm_f32() if want_cpu else None)))
         for op in ("reduce", "reduce_scalar", "rmsnorm", "softmax"):
             r = measure_rowop(one, op, s, 3, pk)
             cpu = (cpu_reduce_scalar() if op == "reduce_scalar" else cpu_rowop(op, 8192, 16384)) if want_cpu else None
-            emit(op_line(op, r, cpu))
+            emit(summarize(rows, op_line(op, r, cpu)))
             torch.cuda.empty_cache()
         r = measure_conv(one, max(3, s // 2), 3, pk)
-        emit(op_line("conv_n32", r, cpu_conv(32, 256, 56, 56, 256, 1) if want_cpu else None))
+        emit(summarize(rows, op_line("conv_n32", r, cpu_conv(32, 256, 56, 56, 256, 1) if want_cpu else None)))
         torch.cuda.empty_cache()
         r = measure_decode(one, s, 3, pk)
         # the chain at every batch the decode config names (device-resident, GB/s)
@@ -1145,7 +1157,7 @@ def main():
         for b in (1, 2, 4, 8, 16):
             sweep[str(b)] = round(measure_decode(one, s, 3, pk, Bt=b, e2e=False)["value"], 1)
             torch.cuda.empty_cache()
-        emit(op_line("decode_b32", r, cpu_decode() if want_cpu else None, b_sweep_GBps=sweep))
+        emit(summarize(rows, op_line("decode_b32", r, cpu_decode() if want_cpu else None, b_sweep_GBps=sweep)))
         torch.cuda.empty_cache()
 
     if args.op == "all" and world > 1:
@@ -1187,6 +1199,10 @@ def main():
         line["cpu_baseline"] = {k: (round(v, 6) if isinstance(v, float) else v) for k, v in cb.items()
                                 if k != "seconds"}
     if rank == 0:
+        if rows:
+            # every BASELINE row again in one short line, so that the rows and the
+            # headline sit together in the last ~1.5 KB of the output
+            emit({"baseline_rows": {"fields": ["value", "unit", "roofline_frac", "e2e", "cpu_baseline"], **rows}})
         emit(line)
     if world > 1:
         torch.distributed.barrier()
